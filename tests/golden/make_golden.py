@@ -1,0 +1,382 @@
+"""Generate the golden fixtures the parity tests read.
+
+Test infrastructure, not product code. This script is the one place that
+imports the reference implementation (INSITU's numpy model). It runs only in a
+container that has the reference checked out; the fixtures it writes are small
+``.npz`` files committed next to it, so the tests need nothing but numpy on any
+machine.
+
+    python tests/golden/make_golden.py --ref /path/to/INSITU
+
+What it writes, and what each file pins:
+
+``tbvec_c64_k4v2.npz``
+    The reference's own shipped golden vectors (``tb/vectors/*.hex``, produced
+    by ``hw/vectors.py:emit`` at ctx 64, seed 0, 4b K / 2b V), parsed from the
+    hex text exactly as the RTL benches read them. Before parsing, the script
+    regenerates the whole directory from the reference (``hw/vectors.py:821``
+    ``build`` with ``cast_after_rope=False``, the setting the board results
+    were taken under, ``kernel.py:160-163``) and asserts every file is
+    byte-identical, so the fixture is the reference's answer twice over.
+
+``widths.npz``
+    Seeded synthetic k/v/q at every width pair the reference's tests use
+    ((4,2),(3,3),(3,2),(4,4),(6,6),(1,1)): rotations, norms, codes, packed
+    rows, scores, ``attend_online`` / ``attend_two_pass`` outputs and stats,
+    per-token online recurrence for a small case, a stress query with many
+    distinct rescale factors, and a saturating case where the 32-bit
+    accumulator clamp fires (``ops/attention.py:502-503``).
+
+``config1_ctx512.npz``
+    one Llama-3.2-1B-shaped attention layer (hidden 2048,
+    32 q heads, 8 KV heads, d 64, rope_theta 500000), W ~ N(0, 0.02) fp32 from
+    seed 0 through ``Weights.prepare`` (``weights.py:70``), x ~ N(0,1), 512
+    sequential decode steps through ``AttentionKernel.forward`` with the
+    online softmax. Stores the wire k/v of every step, the wire q and online
+    output of selected steps, and the final packed cache bytes.
+
+``tables.npz``
+    Codebook integers (gaussian and uniform, 1..8 bits), the exp table and its
+    constants, and PCG64 sign diagonals for a few seeds and round counts.
+"""
+
+from __future__ import annotations
+
+import argparse
+import filecmp
+import os
+import sys
+import tempfile
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _import_reference(ref: str):
+    pkg_root = tempfile.mkdtemp(prefix="insitu_refpkg_")
+    os.symlink(os.path.abspath(ref), os.path.join(pkg_root, "kernel"))
+    sys.path.insert(0, pkg_root)
+    import kernel  # noqa: F401  (the reference package)
+    return pkg_root
+
+
+# --------------------------------------------------------------------------
+# hex parsing (the format written by hw/vectors.py:emit, hw/vectors.py:108-121)
+# --------------------------------------------------------------------------
+
+def _fields(line: str, bits: int, count: int | None = None, signed: bool = True):
+    """One MSB-first hex line -> LSB-first fields of `bits` each."""
+    v = int(line.strip(), 16)
+    n = count if count is not None else max(1, (len(line.strip()) * 4) // bits)
+    mask = (1 << bits) - 1
+    out = []
+    for i in range(n):
+        f = (v >> (i * bits)) & mask
+        if signed and f >> (bits - 1):
+            f -= 1 << bits
+        out.append(f)
+    return out
+
+
+def _read(path: str):
+    with open(path) as f:
+        return [ln for ln in f.read().splitlines() if ln.strip()]
+
+
+def _arr(path, bits, count=None, signed=True):
+    return np.array([_fields(ln, bits, count, signed) for ln in _read(path)],
+                    dtype=np.int64)
+
+
+def _bytes_rows(path):
+    """Rows written as reversed bytes (hw/vectors.py:458-474)."""
+    rows = []
+    for ln in _read(path):
+        b = bytes.fromhex(ln.strip())[::-1]
+        rows.append(np.frombuffer(b, dtype=np.uint8))
+    return np.stack(rows)
+
+
+def make_tbvec(ref: str) -> dict:
+    from kernel.hw import vectors as V  # reference
+    tb = os.path.join(ref, "tb", "vectors")
+
+    # Regenerate and compare byte for byte before trusting the shipped files.
+    with tempfile.TemporaryDirectory() as tmp:
+        from kernel.config import KernelConfig, ModelConfig, QuantConfig
+        from kernel.kernel import AttentionKernel
+        m = ModelConfig(hidden_size=2048, num_heads=32, num_kv_heads=8, head_dim=64,
+                        max_position=max(4096, 64 * 2 + 2))
+        cfg = KernelConfig(model=m, quant=QuantConfig(key_bits=4, value_bits=2, seed=0))
+        k = AttentionKernel(cfg, capacity=65)
+        k.cast_after_rope = False
+        rng = np.random.default_rng(0)
+        k.forward(rng.standard_normal((64, 2048)).astype(np.float32) * 0.02)
+        step = rng.standard_normal((1, 2048)).astype(np.float32) * 0.02
+        vs = V.collect(k, step)
+        V.emit(vs, tmp)
+        names = sorted(os.listdir(tb))
+        same = [n for n in names if filecmp.cmp(os.path.join(tb, n), os.path.join(tmp, n),
+                                                 shallow=False)]
+        if len(same) != len(names):
+            raise AssertionError(f"regeneration differs: {sorted(set(names) - set(same))}")
+        print(f"tb/vectors: all {len(names)} files regenerate byte-identically")
+
+    p = lambda n: os.path.join(tb, n)
+    g = {}
+    for s in ("q", "k", "v"):
+        g[f"wire_{s}"] = _arr(p(f"wire_{s}.hex"), 24, 64)
+        g[f"rot_{s}"] = _arr(p(f"rot_{s}.hex"), 24, 64)
+    g["rot_signs_word"] = np.array([int(_read(p("rot_signs.hex"))[0], 16)], dtype=np.uint64)
+    g["rot_random_in"] = _arr(p("rot_random_in.hex"), 24, 64)
+    g["rot_random_out"] = _arr(p("rot_random_out.hex"), 24, 64)
+    g["enc_bounds_key"] = _arr(p("enc_bounds_key.hex"), 20, 1)[:, 0]
+    g["enc_bounds_value"] = _arr(p("enc_bounds_value.hex"), 20, 1)[:, 0]
+    g["cb_centroids_key"] = _arr(p("cb_centroids_key.hex"), 20, 1)[:, 0]
+    g["cb_centroids_value"] = _arr(p("cb_centroids_value.hex"), 20, 1)[:, 0]
+    g["enc_in"] = _arr(p("enc_in.hex"), 24, 64)
+    g["enc_norm"] = _arr(p("enc_norm.hex"), 16, 1, signed=False)[:, 0]
+    g["enc_idx_key"] = _arr(p("enc_idx_key.hex"), 8, 64, signed=False)
+    g["enc_idx_value"] = _arr(p("enc_idx_value.hex"), 8, 64, signed=False)
+    g["kv_rows"] = _bytes_rows(p("kv_rows.hex"))
+    g["cache_rows"] = np.stack([_bytes_rows(p(f"cache_rows_h{h}.hex")) for h in range(8)],
+                               axis=1)                                   # (65, 8, 52)
+    g["score_edge_rows"] = _bytes_rows(p("score_edge_rows.hex"))
+    g["score_edge_gold"] = _arr(p("score_edge_gold.hex"), 48, 1)[:, 0]
+    g["scores"] = _arr(p("scores.hex"), 48, 65)                          # (32, 65)
+    g["out_online"] = _arr(p("out.online.hex"), 24, 2048)                # (1, 2048)
+    g["out_two_pass"] = _arr(p("out.hex"), 24, 2048)
+    g["exp_table"] = _arr(p("exp_table.hex"), 16, 1, signed=False)[:, 0]
+    g["exp_in"] = _arr(p("exp_in.hex"), 48, 1, signed=False)[:, 0]
+    g["exp_out"] = _arr(p("exp_out.hex"), 16, 1, signed=False)[:, 0]
+    for pre in ("sm", "sm2"):
+        for name, bits in (("s", 48), ("m", 48), ("l", 48)):
+            g[f"{pre}_{name}"] = _arr(p(f"{pre}_{name}.hex"), bits, 4)
+        for name in ("p", "factor"):
+            g[f"{pre}_{name}"] = _arr(p(f"{pre}_{name}.hex"), 16, 4, signed=False)
+        g[f"{pre}_grew"] = _arr(p(f"{pre}_grew.hex"), 1, 4, signed=False)
+        acc = _arr(p(f"{pre}_acc.hex"), 32, 64)
+        g[f"{pre}_acc"] = acc.reshape(-1, 4, 64)
+    g["sm2_q"] = _arr(p("sm2_q.hex"), 24, 64)
+    g["fin_acc"] = _arr(p("fin_acc.hex"), 32, 64)
+    g["fin_l"] = _arr(p("fin_l.hex"), 48, 1, signed=False)[:, 0]
+    g["fin_recip"] = _arr(p("fin_recip.hex"), 32, 1, signed=False)[:, 0]
+    g["fin_shift"] = _arr(p("fin_shift.hex"), 8, 1, signed=False)[:, 0]
+    g["fin_out"] = _arr(p("fin_out.hex"), 48, 64)
+    return {n: (a.astype(np.int32) if a.dtype == np.int64 and a.size > 4096
+                and np.abs(a).max() < (1 << 31) else a) for n, a in g.items()}
+
+
+# --------------------------------------------------------------------------
+# seeded cases at every width
+# --------------------------------------------------------------------------
+
+WIDTHS = ((4, 2), (3, 3), (3, 2), (4, 4), (6, 6), (1, 1))
+
+
+def _wire(rng, shape, scale=1.0):
+    x = np.rint(rng.standard_normal(shape) * scale * 65536.0).astype(np.int64)
+    return np.clip(x, -(1 << 23), (1 << 23) - 1)
+
+
+def make_widths() -> dict:
+    from kernel.config import FixedFormat, QuantConfig
+    from kernel.ops.attention import CompressedAttention
+    from kernel.ops.quantize import KVQuantizer
+
+    fmt = FixedFormat()
+    out = {}
+    for kb, vb in WIDTHS:
+        tag = f"k{kb}v{vb}"
+        quant = QuantConfig(key_bits=kb, value_bits=vb, seed=0)
+        qz = KVQuantizer(64, quant, fmt)
+        att = CompressedAttention(qz, fmt, quant)
+        rng = np.random.default_rng(1000 + 10 * kb + vb)
+        T, H = 97, 4
+        k = _wire(rng, (T, 64))
+        v = _wire(rng, (T, 64))
+        q = _wire(rng, (H, 64), 1.0 / 8.0)
+        kr, vr, qr = qz.rotation.apply(k), qz.rotation.apply(v), qz.rotation.apply(q)
+        kv = qz.encode(kr, vr)
+        rows = qz.pack(kv)
+        s, ovf = att.scores(qr, kv)
+        on, st = att.attend_online(qr, kv)
+        tp, st2 = att.attend_two_pass(qr, kv)
+        out.update({
+            f"{tag}_k": k, f"{tag}_v": v, f"{tag}_q": q,
+            f"{tag}_k_rot": kr, f"{tag}_v_rot": vr, f"{tag}_q_rot": qr,
+            f"{tag}_k_idx": kv.k_idx.astype(np.int64), f"{tag}_v_idx": kv.v_idx.astype(np.int64),
+            f"{tag}_k_norm": kv.k_norm, f"{tag}_v_norm": kv.v_norm,
+            f"{tag}_rows": rows, f"{tag}_scores": s,
+            f"{tag}_online": on, f"{tag}_two_pass": tp,
+            f"{tag}_online_stats": np.array([st.n_tokens, st.rescale_events, st.score_overflows,
+                                             st.acc_overflows, st.max_abs_score, st.max_abs_acc]),
+            f"{tag}_two_pass_stats": np.array([st2.n_tokens, st2.rescale_events,
+                                               st2.score_overflows, st2.acc_overflows,
+                                               st2.max_abs_score, st2.max_abs_acc]),
+            f"{tag}_k_centroids": qz.key.codebook.centroids,
+            f"{tag}_k_bounds": qz.key.codebook.boundaries,
+            f"{tag}_v_centroids": qz.value.codebook.centroids,
+            f"{tag}_v_bounds": qz.value.codebook.boundaries,
+            f"{tag}_bytes_per_token": np.array([qz.bytes_per_token]),
+        })
+        print(f"widths {tag}: {qz.bytes_per_token} B/token, rescales {st.rescale_events}, "
+              f"acc_ovf {st.acc_overflows}")
+
+    # Stress: a query scaled so the running maximum moves in big jumps, giving
+    # many distinct rescale factors (the reasoning of hw/vectors.py:618-657).
+    quant = QuantConfig(key_bits=4, value_bits=2, seed=0)
+    qz = KVQuantizer(64, quant, fmt)
+    att = CompressedAttention(qz, fmt, quant)
+    rng = np.random.default_rng(77)
+    T = 300
+    k, v = _wire(rng, (T, 64)), _wire(rng, (T, 64))
+    q = np.clip(_wire(rng, (4, 64), 1.0 / 8.0) * 4, -(1 << 23), (1 << 23) - 1)
+    kr, vr, qr = qz.rotation.apply(k), qz.rotation.apply(v), qz.rotation.apply(q)
+    kv = qz.encode(kr, vr)
+    steps = []
+    att.on_step = lambda t, **kw: steps.append(
+        {n: (np.array(x, dtype=np.int64) if x is not None else None) for n, x in kw.items()})
+    on, st = att.attend_online(qr, kv)
+    att.on_step = None
+    fac = np.stack([s["factor"] if s["factor"] is not None else np.full(4, 32768)
+                    for s in steps])
+    out.update({
+        "stress_k": k, "stress_v": v, "stress_q": q, "stress_q_rot": qr,
+        "stress_rows": qz.pack(kv), "stress_online": on,
+        "stress_online_stats": np.array([st.n_tokens, st.rescale_events, st.score_overflows,
+                                         st.acc_overflows, st.max_abs_score, st.max_abs_acc]),
+        "stress_s": np.stack([s["s"] for s in steps]), "stress_m": np.stack([s["m"] for s in steps]),
+        "stress_p": np.stack([s["p"] for s in steps]), "stress_l": np.stack([s["l"] for s in steps]),
+        "stress_acc": np.stack([s["acc"] for s in steps]),
+        "stress_grew": np.stack([s["grew"] for s in steps]).astype(np.int64),
+        "stress_factor": fac,
+    })
+    g = st.rescale_events
+    print(f"stress: rescales {g}, distinct factors "
+          f"{len(set(fac[np.stack([s['grew'] for s in steps]).astype(bool)].tolist()))}")
+
+    # Saturation: identical, large v rows with a constant-sign pattern drive
+    # the accumulator into the 32-bit clamp, so acc_overflows > 0 and the
+    # per-token clamp order matters.
+    T = 1500
+    base = np.zeros(64, dtype=np.int64)
+    base[:] = (1 << 22) - 1
+    signs = qz.rotation.signs[0]
+    vsat = np.tile(base * signs, (T, 1))
+    vsat = np.clip(vsat, -(1 << 23), (1 << 23) - 1)
+    rng = np.random.default_rng(5)
+    ksat = _wire(rng, (T, 64), 0.25)
+    q = _wire(rng, (4, 64), 1.0 / 8.0)
+    kr, vr, qr = qz.rotation.apply(ksat), qz.rotation.apply(vsat), qz.rotation.apply(q)
+    kv = qz.encode(kr, vr)
+    on, st = att.attend_online(qr, kv)
+    tp, st2 = att.attend_two_pass(qr, kv)
+    out.update({
+        "sat_k": ksat, "sat_v": vsat, "sat_q": q, "sat_q_rot": qr, "sat_rows": qz.pack(kv),
+        "sat_online": on, "sat_two_pass": tp,
+        "sat_online_stats": np.array([st.n_tokens, st.rescale_events, st.score_overflows,
+                                      st.acc_overflows, st.max_abs_score, st.max_abs_acc]),
+        "sat_two_pass_stats": np.array([st2.n_tokens, st2.rescale_events, st2.score_overflows,
+                                        st2.acc_overflows, st2.max_abs_score, st2.max_abs_acc]),
+    })
+    print(f"saturation: acc_overflows {st.acc_overflows} (two-pass {st2.acc_overflows})")
+    if st.acc_overflows == 0:
+        raise AssertionError("saturation case does not saturate")
+    return {n: (a.astype(np.int32) if a.dtype == np.int64 and a.size > 4096
+                and np.abs(a).max() < (1 << 31) else a) for n, a in out.items()}
+
+
+# --------------------------------------------------------------------------
+# BASELINE config 1
+# --------------------------------------------------------------------------
+
+CONFIG1_STEPS = (0, 1, 2, 7, 63, 64, 255, 256, 257, 510, 511)
+
+
+def make_config1(n_steps: int = 512) -> dict:
+    from kernel.config import KernelConfig, ModelConfig, QuantConfig
+    from kernel.kernel import AttentionKernel
+    from kernel.ops.rotate import Rotation
+    from kernel.weights import Weights
+
+    m = ModelConfig(hidden_size=2048, num_heads=32, num_kv_heads=8, head_dim=64,
+                    rope_theta=500000.0, max_position=4096)
+    quant = QuantConfig(key_bits=4, value_bits=2, seed=0)
+    cfg = KernelConfig(model=m, quant=quant)
+    rot = Rotation.for_quant(quant, m.head_dim)
+    rng = np.random.default_rng(0)
+    w = lambda shape: rng.standard_normal(shape).astype(np.float32) * 0.02
+    weights = Weights.prepare(w((2048, 2048)), w((512, 2048)), w((512, 2048)),
+                              w((2048, 2048)), m, rot)
+    kern = AttentionKernel(cfg, weights, capacity=n_steps)
+    kern.softmax = "online"
+    xr = np.random.default_rng(1)
+    taps = {}
+    kern.on_stage = lambda name, val: taps.__setitem__(name, np.array(val, dtype=np.int64))
+    wk, wv, qsel, osel = [], [], [], []
+    for t in range(n_steps):
+        x = xr.standard_normal((1, 2048)).astype(np.float32)
+        kern.forward(x)
+        wk.append(taps["wire.k"][0])
+        wv.append(taps["wire.v"][0])
+        if t in CONFIG1_STEPS:
+            qsel.append(taps["wire.q"][0])
+            osel.append(taps["out"][0])
+        if t % 64 == 0:
+            print(f"config1 step {t}/{n_steps}")
+    return {
+        "wire_k": np.stack(wk).astype(np.int32), "wire_v": np.stack(wv).astype(np.int32),
+        "steps": np.array(CONFIG1_STEPS[:len(qsel)]),
+        "wire_q": np.stack(qsel).astype(np.int32), "out_online": np.stack(osel),
+        "cache": kern.cache.buf[:n_steps].copy(),
+    }
+
+
+# --------------------------------------------------------------------------
+# tables
+# --------------------------------------------------------------------------
+
+def make_tables() -> dict:
+    from kernel.config import FixedFormat
+    from kernel.ops.attention import ExpLut
+    from kernel.ops.codebook import Codebook
+    from kernel.ops.rotate import Rotation
+
+    g = {}
+    for b in range(1, 9):
+        for kind in ("gaussian", "uniform"):
+            cb = Codebook.build(kind, b)
+            g[f"{kind}{b}_centroids"] = cb.centroids
+            g[f"{kind}{b}_bounds"] = cb.boundaries
+    e = ExpLut(FixedFormat())
+    g["exp_table"] = e.table
+    g["exp_consts"] = np.array([int(e.log2e), int(e._delta_max), int(e._span)])
+    g["exp_flat"] = e._flat
+    for seed in (0, 1, 7, 12345):
+        for rounds in (1, 2):
+            g[f"signs_s{seed}_r{rounds}"] = Rotation.from_seed(64, seed, rounds).signs
+    g["signs_d32_s0_r1"] = Rotation.from_seed(32, 0, 1).signs
+    return g
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--skip-config1", action="store_true")
+    a = ap.parse_args(argv)
+    _import_reference(a.ref)
+    np.savez_compressed(os.path.join(HERE, "tbvec_c64_k4v2.npz"), **make_tbvec(a.ref))
+    np.savez_compressed(os.path.join(HERE, "tables.npz"), **make_tables())
+    np.savez_compressed(os.path.join(HERE, "widths.npz"), **make_widths())
+    if not a.skip_config1:
+        np.savez_compressed(os.path.join(HERE, "config1_ctx512.npz"), **make_config1())
+    for n in sorted(os.listdir(HERE)):
+        if n.endswith(".npz"):
+            print(f"{n}: {os.path.getsize(os.path.join(HERE, n)) / 1024:.0f} KiB")
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
