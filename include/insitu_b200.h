@@ -1,0 +1,208 @@
+/*
+ * insitu_b200 -- the C ABI of the B200 compressed-KV decode attention path.
+ *
+ * This is the drop-in boundary. Everything below it is hand-written CUDA for
+ * sm_100a; everything above it (the Python package `insitu_b200`, or any
+ * other host language through its FFI) mirrors the reference's operator
+ * interfaces and calls only these functions. No torch types cross: plain
+ * pointers, sizes and a cudaStream_t passed as `void *`.
+ *
+ * Citations are path:line inside the INSITU reference repository.
+ *
+ * Ownership. The handle owns the paged cache pool and its page tables, which
+ * it allocates at creation and never grows (capacity is fixed at
+ * construction, cache/base.py:30-36 and 67-73). Every other device buffer --
+ * q/k/v in, rotated q and outputs out, stats -- is owned by the caller.
+ *
+ * Ordering. Device work is enqueued on the caller's stream and returns
+ * without synchronising, except where a function says it blocks (the export,
+ * import and status readers, which move data to or from host memory).
+ *
+ * Errors. Every function returns an ins_status. Argument and capacity
+ * errors are detected on the host before anything is enqueued and leave the
+ * cache unchanged, the way the reference raises ValueError. Conditions only
+ * the device can see (a value outside the 24-bit wire range, a bounded wait
+ * that expired) are latched in a device status word that
+ * ins_cache_status() reads and clears.
+ */
+#ifndef INSITU_B200_H
+#define INSITU_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. The board protocol's numbering (host/attn_proto.h:47-55) is
+ * kept for the codes that have a meaning here. */
+typedef enum {
+    INS_OK = 0,
+    INS_EBADLEN = 4,   /* capacity exceeded, or a length/shape mismatch  */
+    INS_ETIMEOUT = 5,  /* a bounded device-side wait gave up              */
+    INS_ERANGE = 7,    /* a value escaped its fixed-point format          */
+    INS_EINVAL = 8,    /* bad argument or unsupported configuration       */
+    INS_ENOMEM = 9,    /* device or pinned allocation failed              */
+    INS_ECUDA = 10     /* a CUDA runtime call failed                      */
+} ins_status;
+
+/* The fixed-point contract, field for field from QuantConfig and FixedFormat
+ * (config.py:132-254), plus the cache geometry. */
+typedef struct {
+    int32_t head_dim;         /* d; this build supports 64                    */
+    int32_t n_kv_heads;       /* KV heads per layer                           */
+    int32_t kv_groups;        /* query heads per KV head: 1, 2, 4 or 8        */
+    int32_t key_bits;         /* 1..8                                         */
+    int32_t value_bits;       /* 1..8                                         */
+    int32_t norm_bits;        /* 16                                           */
+    int32_t norm_frac;        /* 9                                            */
+    int32_t qk_frac;          /* 16                                           */
+    int32_t centroid_frac;    /* 15                                           */
+    int32_t acc_frac;         /* 16                                           */
+    int32_t acc_width;        /* 32                                           */
+    int32_t score_width;      /* 48                                           */
+    int32_t prob_frac;        /* 15                                           */
+    int32_t exp_lut_bits;     /* 8                                            */
+    int32_t saturate;         /* 1                                            */
+    int32_t rot_rounds;       /* QuantConfig.rot_rounds                       */
+    int32_t rot_shift;        /* sqrt_shift(d), -1 when d is an odd power     */
+    int32_t rot_inv_sqrt_q15; /* round(2^15/sqrt(d)), used when rot_shift < 0 */
+    int32_t page_tokens;      /* tokens per cache page, a multiple of 16      */
+    int32_t max_seqs;         /* sequences the page table can hold            */
+    int32_t max_pages_per_seq;/* per-sequence capacity = this * page_tokens   */
+    int32_t reserved0;
+    int64_t n_pages;          /* pages in the pool                            */
+} ins_config;
+
+/* The integer tables (host pointers, copied at creation). They are format
+ * artefacts the host builds once: the PCG64 sign diagonal
+ * (ops/rotate.py:144-155), the Lloyd-Max codebooks (ops/codebook.py:67-120)
+ * and the exp table with its constants (ops/attention.py:104-151). */
+typedef struct {
+    const int64_t *signs;        /* rot_rounds * head_dim entries of +-1     */
+    const int64_t *k_centroids;  /* 2^key_bits                               */
+    const int64_t *k_bounds;     /* 2^key_bits - 1                           */
+    const int64_t *v_centroids;  /* 2^value_bits                             */
+    const int64_t *v_bounds;     /* 2^value_bits - 1                         */
+    const int64_t *exp_table;    /* 2^exp_lut_bits                           */
+    int64_t log2e;               /* round(log2(e) * 2^acc_frac)              */
+    int64_t delta_max;           /* ExpLut._delta_max                        */
+} ins_tables;
+
+/* AttentionStats (ops/attention.py:257-274), one per (sequence, KV head). */
+typedef struct {
+    int64_t n_tokens;
+    int64_t rescale_events;
+    int64_t score_overflows;
+    int64_t acc_overflows;
+    int64_t max_abs_score;
+    int64_t max_abs_acc;
+} ins_stats;
+
+typedef struct ins_cache ins_cache;
+
+/* Softmax forms of CompressedAttention (ops/attention.py:429-513). */
+typedef enum { INS_SOFTMAX_ONLINE = 0, INS_SOFTMAX_TWO_PASS = 1 } ins_softmax;
+
+/* Version of this ABI; bumped on any incompatible change. */
+int32_t ins_abi_version(void);
+
+/* Bytes of one compressed token of one KV head: QuantConfig.bytes_per_token
+ * (config.py:192-207). -1 for an invalid configuration. */
+int32_t ins_bytes_per_token(const ins_config *cfg);
+
+/* Create a paged compressed cache on `device`: the GPU form of
+ * CompressedCache.__init__ (cache/compressed.py:42-52) for max_seqs
+ * sequences at once. */
+int ins_cache_create(const ins_config *cfg, const ins_tables *tables, int32_t device,
+                     ins_cache **out);
+
+/* Free the pool, the page tables and the handle. NULL is a no-op. */
+int ins_cache_destroy(ins_cache *cache);
+
+/* KVCache.reset (cache/base.py:64-65) for one sequence (seq >= 0) or for all
+ * (seq < 0). Its pages return to the pool. Host-side only; ordered after
+ * work already enqueued by the caller's next synchronisation. */
+int ins_cache_reset(ins_cache *cache, int32_t seq);
+
+/* Tokens currently held for `seq` (KVCache.length), or -1. */
+int64_t ins_cache_length(const ins_cache *cache, int32_t seq);
+
+/* Tokens one sequence can hold (KVCache.capacity). */
+int64_t ins_cache_capacity(const ins_cache *cache);
+
+/* Flags of ins_ingress. */
+enum {
+    /* k and v (and q) are already rotated, as CompressedCache.append_rotated
+     * takes them (cache/compressed.py:64-86): skip the rotation and the 24-bit
+     * wire-range check. */
+    INS_INGRESS_PREROTATED = 1
+};
+
+/* The ingress: rotate q, k and v (Rotation.apply, ops/rotate.py:170-197),
+ * quantise k and v (KVQuantizer.encode, ops/quantize.py:164-212), bit-pack
+ * them (KVQuantizer.pack, ops/quantize.py:237-252) and append each token at
+ * its sequence's current length (CompressedCache.append_rotated,
+ * cache/compressed.py:64-86), in the kernel.py:271-284 order.
+ *
+ * n tokens; seq_ids (host, n) names each token's sequence, and tokens of one
+ * sequence are appended in the order given. q (device, [n, n_kv*groups, d]
+ * int32) may be NULL; when given, its rotation is written to q_rot (device,
+ * same shape). k and v are device [n, n_kv, d] int32, Q(qk_frac) in 24-bit
+ * lanes. EBADLEN, with nothing appended, if a sequence would exceed its
+ * capacity or the pool runs out of pages. */
+int ins_ingress(ins_cache *cache, int32_t n, const int32_t *seq_ids,
+                const int32_t *q, const int32_t *k, const int32_t *v, int32_t *q_rot,
+                uint32_t flags, void *stream);
+
+/* Rotation.apply (ops/rotate.py:170-197) alone: n vectors of head_dim int32
+ * on the device, x -> y (may alias). Same Q in and out, not clamped; a result
+ * that does not fit int32 latches INS_ERANGE. */
+int ins_rotate(ins_cache *cache, int64_t n, const int32_t *x, int32_t *y, void *stream);
+
+/* CompressedAttention.scores, fused mode (ops/attention.py:333-359): the
+ * kv_groups query heads q_rot (device, [groups, d] int32) against rows
+ * [t0, t0+n) of one sequence and KV head. s (device, [groups, n] int64,
+ * Q(acc_frac), clamped to score_width); ovf (device, one int64, may be NULL)
+ * receives the number of scores the clamp changed. */
+int ins_scores(ins_cache *cache, int32_t seq, int32_t kv_head, int64_t t0, int64_t n,
+               const int32_t *q_rot, int64_t *s, int64_t *ovf, void *stream);
+
+/* The code-domain scan: one decode step of attention for B sequences, every
+ * KV head, every query head of its group (kernel.py:338-346, with
+ * CompressedAttention.attend_online at ops/attention.py:451-513, or
+ * attend_two_pass at 429-449).
+ *
+ * seq_ids (host, B); lengths (host, B, may be NULL): how many leading tokens
+ * of each sequence to attend -- the causal prefix kv.select(slice(0, ctx))
+ * of kernel.py:387 -- or the whole current length when NULL; q_rot (device,
+ * [B, n_kv*groups, d] int32, already rotated and scaled); out (device,
+ * [B, n_kv*groups, d] int64, Q(acc_frac) in merge_heads order,
+ * ops/project.py:67-74); stats (device, [B, n_kv] ins_stats, may be NULL). */
+int ins_scan(ins_cache *cache, int32_t B, const int32_t *seq_ids, const int64_t *lengths,
+             const int32_t *q_rot, int64_t *out, ins_stats *stats, ins_softmax mode,
+             void *stream);
+
+/* Export rows [t0, t0+n) of one sequence and KV head in the reference's
+ * packed row format (KVQuantizer.pack, ops/quantize.py:237-252), the bytes
+ * CompressedCache.buf[t0:t0+n, kv_head] holds (cache/compressed.py:42-52).
+ * rows: host, n * bytes_per_token. Blocks until the copy is done. */
+int ins_cache_export(ins_cache *cache, int32_t seq, int32_t kv_head, int64_t t0, int64_t n,
+                     uint8_t *rows);
+
+/* Append n tokens given as packed rows (host, [n, n_kv, bytes_per_token],
+ * the layout of CompressedCache.buf) -- loading a cache image the way the
+ * board's CMD_LOAD does (host/attn_proto.h:36). Blocks. */
+int ins_cache_import(ins_cache *cache, int32_t seq, int64_t n, const uint8_t *rows);
+
+/* Read and clear the device status word latched by earlier kernels. Blocks
+ * on the stream. INS_OK when nothing went wrong. */
+int ins_cache_status(ins_cache *cache, void *stream);
+
+/* The last error message recorded on this thread ("" if none). */
+const char *ins_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,166 @@
+// Shared device-side definitions of the B200 compressed-KV attention path.
+//
+// Integer semantics follow the reference numpy model (INSITU, cited as
+// path:line): int64 everywhere a value can grow, arithmetic right shifts that
+// floor, and narrowing only at the named clamps.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "../../include/insitu_b200.h"
+
+namespace ins {
+
+constexpr int D = 64;                // head_dim this build supports
+constexpr int MAX_ROUNDS = 8;        // rotation rounds carried in the sign masks
+constexpr uint32_t FULL = 0xffffffffu;
+
+// Device status bits, latched by kernels and read by ins_cache_status().
+enum : int32_t { ST_RANGE = 1, ST_TIMEOUT = 2, ST_INTERNAL = 4 };
+
+// Tables, one copy per cache in device global memory.
+struct DevTables {
+    int64_t k_cent[256];
+    int64_t k_bound[256];
+    int64_t v_cent[256];
+    int64_t v_bound[256];
+    double k_cent_f64[256];          // the same key centroids as exact doubles
+    int32_t exp_tab[256];
+    uint64_t sign_mask[MAX_ROUNDS];  // bit j set: round negates channel j
+};
+
+// Geometry and the fixed-point contract, passed to kernels by value.
+struct Geo {
+    int32_t n_kv, H, kb, vb;
+    int32_t kbytes, vbytes, row_bytes;
+    int32_t P;                       // tokens per page
+    int32_t max_pages;               // page-table row length
+    int32_t norm_bits, norm_frac, qk_frac, centroid_frac, acc_frac, acc_width;
+    int32_t score_width, prob_frac, exp_lut_bits, saturate;
+    int32_t rounds, rot_shift, rot_inv;
+    int32_t score_shift, acc_shift, enc_shift;
+    int64_t head_bytes, page_bytes;
+    int64_t log2e, delta_max;
+};
+
+// Byte offsets of one (page, head) region's three planes: K codes (P rows of
+// kbytes), V codes (P rows of vbytes), norms (P rows of 4 bytes: k_norm then
+// v_norm, little-endian int16).
+__host__ __device__ inline int64_t region_off(const Geo &g, int64_t page, int32_t head) {
+    return page * g.page_bytes + (int64_t)head * g.head_bytes;
+}
+__host__ __device__ inline int64_t vplane_off(const Geo &g) { return (int64_t)g.P * g.kbytes; }
+__host__ __device__ inline int64_t nplane_off(const Geo &g) {
+    return (int64_t)g.P * (g.kbytes + g.vbytes);
+}
+
+__device__ __forceinline__ int64_t shfl_xor64(int64_t v, int m) {
+    return __shfl_xor_sync(FULL, v, m);
+}
+
+// Exact integer square root, digit by digit (two result bits per step), the
+// textbook method the reference's isqrt is checked against
+// (ops/quantize.py:42-60).
+__device__ __forceinline__ uint64_t isqrt_u64(uint64_t a) {
+    uint64_t r = 0, bit = 1ull << 62;
+    while (bit > a) bit >>= 2;
+    while (bit) {
+        if (a >= r + bit) {
+            a -= r + bit;
+            r = (r >> 1) + bit;
+        } else {
+            r >>= 1;
+        }
+        bit >>= 2;
+    }
+    return r;
+}
+
+// Round-half-to-even right shift (numerics/fixed.py:83-88).
+__device__ __forceinline__ int64_t rshift_even(int64_t a, int n) {
+    if (n == 0) return a;
+    const int64_t half = 1ll << (n - 1);
+    int64_t q = (a + half) >> n;
+    if ((a & ((1ll << n) - 1)) == half) q &= ~1ll;
+    return q;
+}
+
+__device__ __forceinline__ int64_t clamp_bits(int64_t a, int width, bool &hit) {
+    const int64_t lo = -(1ll << (width - 1)), hi = (1ll << (width - 1)) - 1;
+    hit = a < lo || a > hi;
+    return a < lo ? lo : (a > hi ? hi : a);
+}
+
+// Q.clamp with the wrap mode kept for completeness (numerics/fixed.py:161-168).
+__device__ __forceinline__ int64_t qclamp(int64_t a, int width, int saturate, bool &hit) {
+    const int64_t lo = -(1ll << (width - 1)), hi = (1ll << (width - 1)) - 1;
+    hit = a < lo || a > hi;
+    if (!hit) return a;
+    if (saturate) return a < lo ? lo : hi;
+    const uint64_t span = 1ull << width;
+    const uint64_t u = ((uint64_t)a + (1ull << (width - 1))) & (span - 1);
+    return (int64_t)u - (1ll << (width - 1));
+}
+
+// ExpLut.__call__ (ops/attention.py:153-159) for delta >= 0: clamp at
+// delta_max, t = floor(delta * log2e / 2^acc_frac), then
+// table[(t >> shift) & mask] >> integer part, zero past the last one.
+__device__ __forceinline__ int32_t exp_lut(const Geo &g, const int32_t *tab, int64_t delta) {
+    const int64_t d = delta < g.delta_max ? delta : g.delta_max;
+    const int64_t t = (d * g.log2e) >> g.acc_frac;
+    const int64_t u = t >> (g.acc_frac - g.exp_lut_bits);
+    const int64_t span = (int64_t)(g.prob_frac + 2) << g.exp_lut_bits;
+    if (u >= span) return 0;
+    return tab[u & ((1 << g.exp_lut_bits) - 1)] >> (int)(u >> g.exp_lut_bits);
+}
+
+// 2^62 / den by restoring division, 64 quotient bits.
+__device__ __forceinline__ uint64_t div_pow62(uint64_t den) {
+    uint64_t q = 0, rem = 0;
+    for (int i = 63; i >= 0; --i) {
+        rem = (rem << 1) | (i == 62 ? 1ull : 0ull);
+        if (rem >= den) {
+            rem -= den;
+            q |= 1ull << i;
+        }
+    }
+    return q;
+}
+
+// The normalised reciprocal (ops/attention.py:177-250): leading one capped
+// at L_WIDTH-1 = 47, l shifted into a 32-bit window, r = 2^62 // l_n, and the
+// total shift 62 - prob_frac + k.
+__device__ __forceinline__ void reciprocal(const Geo &g, int64_t l, int64_t &r, int &shift) {
+    int lead = 0;
+    if (l >= 2) {
+        lead = 63 - __clzll((unsigned long long)l);
+        if (lead > 47) lead = 47;
+    }
+    const int k = lead - 31;
+    const int64_t ln = k >= 0 ? (l >> k) : (int64_t)((uint64_t)l << (-k));
+    r = l > 0 ? (int64_t)div_pow62((uint64_t)(ln > 1 ? ln : 1)) : 0;
+    shift = 62 - g.prob_frac + k;
+}
+
+// Code `j` of a row held as 32-bit words, `kb` bits per code, LSB first
+// (ops/quantize.py:271-275).
+template <int KB>
+__device__ __forceinline__ uint32_t code_at(const uint32_t *w, int j, int kb_rt) {
+    const int kb = KB ? KB : kb_rt;
+    const int pos = j * kb, wi = pos >> 5, sh = pos & 31;
+    uint32_t val = w[wi] >> sh;
+    if (sh + kb > 32) val |= w[wi + 1] << (32 - sh);
+    return val & ((1u << kb) - 1u);
+}
+
+// Code `j` of a packed field starting at byte pointer `p`.
+__device__ __forceinline__ uint32_t code_at_bytes(const uint8_t *p, int j, int bits,
+                                                  int field_bytes) {
+    const int pos = j * bits, b = pos >> 3, sh = pos & 7;
+    uint32_t v = p[b];
+    if (b + 1 < field_bytes) v |= (uint32_t)p[b + 1] << 8;
+    return (v >> sh) & ((1u << bits) - 1u);
+}
+
+}  // namespace ins

@@ -1,0 +1,604 @@
+// Host side of the insitu_b200 C ABI: the cache handle, its paged pool and
+// page tables, argument checking, and the kernel launches.
+//
+// The host owns the cache metadata (lengths, page tables, the free-page
+// list), as the reference's CompressedCache owns its buffer and length
+// (cache/compressed.py:42-86). Kernels read device mirrors of it that every
+// mutating call refreshes with stream-ordered copies before its launch.
+
+#include <climits>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.cuh"
+#include "scan_chunked.cuh"
+
+using namespace ins;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string &msg) {
+    g_err = msg;
+    return code;
+}
+
+#define CK(call)                                                                       \
+    do {                                                                               \
+        cudaError_t e_ = (call);                                                       \
+        if (e_ != cudaSuccess)                                                         \
+            return fail(INS_ECUDA, std::string(#call " failed: ") + cudaGetErrorString(e_)); \
+    } while (0)
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+// A pinned host buffer and its device twin, grown on demand. Host writes wait
+// on the event of the last copy out of the buffer, so an enqueued copy never
+// reads a half-rewritten staging area.
+struct Staging {
+    void *h = nullptr;
+    void *d = nullptr;
+    size_t cap = 0;
+    cudaEvent_t done = nullptr;
+
+    int reserve(size_t bytes) {
+        if (!done) CK(cudaEventCreateWithFlags(&done, cudaEventDisableTiming));
+        CK(cudaEventSynchronize(done));
+        if (bytes <= cap) return INS_OK;
+        size_t want = cap ? cap : 4096;
+        while (want < bytes) want *= 2;
+        if (h) cudaFreeHost(h);
+        if (d) cudaFree(d);
+        h = d = nullptr;
+        cap = 0;
+        CK(cudaHostAlloc(&h, want, cudaHostAllocDefault));
+        CK(cudaMalloc(&d, want));
+        cap = want;
+        return INS_OK;
+    }
+    int upload(size_t bytes, cudaStream_t s) {
+        CK(cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, s));
+        CK(cudaEventRecord(done, s));
+        return INS_OK;
+    }
+    void release() {
+        if (done) cudaEventSynchronize(done), cudaEventDestroy(done);
+        if (h) cudaFreeHost(h);
+        if (d) cudaFree(d);
+        h = d = nullptr;
+        done = nullptr;
+        cap = 0;
+    }
+};
+
+}  // namespace
+
+struct ins_cache {
+    ins_config cfg;
+    Geo g;
+    int device = 0;
+    DevTables *d_tables = nullptr;
+    uint8_t *d_pool = nullptr;
+    int32_t *d_page_table = nullptr;   // [max_seqs, max_pages]
+    int32_t *d_seq_lens = nullptr;     // [max_seqs]
+    int32_t *d_status = nullptr;
+    // host mirrors (pinned, so their copies can be asynchronous)
+    int32_t *h_page_table = nullptr;
+    int32_t *h_seq_lens = nullptr;
+    cudaEvent_t mirror_done = nullptr;
+    std::vector<int32_t> free_pages;
+    Staging stage_a;                    // per-call index uploads
+    Staging stage_b;
+    ChunkScratch chunk;                 // scratch of the context-parallel scan
+};
+
+namespace {
+
+bool valid_bits(int b) { return b >= 1 && b <= 8; }
+
+int check_config(const ins_config *c) {
+    if (!c) return fail(INS_EINVAL, "config is NULL");
+    if (c->head_dim != D) return fail(INS_EINVAL, "this build supports head_dim 64 only");
+    if (c->n_kv_heads < 1 || c->n_kv_heads > 1024) return fail(INS_EINVAL, "n_kv_heads out of range");
+    if (!(c->kv_groups == 1 || c->kv_groups == 2 || c->kv_groups == 4 || c->kv_groups == 8))
+        return fail(INS_EINVAL, "kv_groups must be 1, 2, 4 or 8");
+    if (!valid_bits(c->key_bits) || !valid_bits(c->value_bits))
+        return fail(INS_EINVAL, "key_bits/value_bits outside 1..8");
+    if (c->norm_bits != 16) return fail(INS_EINVAL, "this build stores 16-bit norms only");
+    if (c->norm_frac < 0 || c->norm_frac >= c->norm_bits) return fail(INS_EINVAL, "norm_frac");
+    if (c->centroid_frac + c->norm_frac < c->qk_frac)
+        return fail(INS_EINVAL, "centroid_frac + norm_frac below qk_frac: the threshold "
+                                "comparison would truncate x (ops/quantize.py:150-156)");
+    if (c->acc_width < 2 || c->acc_width > 32 || c->score_width < 2 || c->score_width > 62)
+        return fail(INS_EINVAL, "acc_width/score_width");
+    if (c->exp_lut_bits < 1 || c->exp_lut_bits > 8 || c->acc_frac - c->exp_lut_bits < 0)
+        return fail(INS_EINVAL, "exp_lut_bits");
+    if (c->prob_frac < 1 || c->prob_frac > 16) return fail(INS_EINVAL, "prob_frac");
+    if (c->rot_rounds < 0 || c->rot_rounds > MAX_ROUNDS) return fail(INS_EINVAL, "rot_rounds 0..8");
+    if (c->page_tokens < 16 || c->page_tokens % 16 || c->page_tokens > 1024)
+        return fail(INS_EINVAL, "page_tokens must be a multiple of 16 in [16, 1024]");
+    if (c->max_seqs < 1 || c->max_pages_per_seq < 1 || c->n_pages < 1)
+        return fail(INS_EINVAL, "max_seqs, max_pages_per_seq and n_pages must be positive");
+    if (c->n_pages > INT32_MAX) return fail(INS_EINVAL, "n_pages above 2^31");
+    return INS_OK;
+}
+
+Geo make_geo(const ins_config &c) {
+    Geo g{};
+    g.n_kv = c.n_kv_heads;
+    g.H = c.kv_groups;
+    g.kb = c.key_bits;
+    g.vb = c.value_bits;
+    g.kbytes = D * c.key_bits / 8;
+    g.vbytes = D * c.value_bits / 8;
+    g.row_bytes = g.kbytes + g.vbytes + 2 * (c.norm_bits / 8);
+    g.P = c.page_tokens;
+    g.max_pages = c.max_pages_per_seq;
+    g.norm_bits = c.norm_bits;
+    g.norm_frac = c.norm_frac;
+    g.qk_frac = c.qk_frac;
+    g.centroid_frac = c.centroid_frac;
+    g.acc_frac = c.acc_frac;
+    g.acc_width = c.acc_width;
+    g.score_width = c.score_width;
+    g.prob_frac = c.prob_frac;
+    g.exp_lut_bits = c.exp_lut_bits;
+    g.saturate = c.saturate;
+    g.rounds = c.rot_rounds;
+    g.rot_shift = c.rot_shift;
+    g.rot_inv = c.rot_inv_sqrt_q15;
+    g.score_shift = c.qk_frac + c.centroid_frac + c.norm_frac - c.acc_frac;   // config.py:249-250
+    g.acc_shift = c.centroid_frac + c.norm_frac + c.prob_frac - c.acc_frac;   // config.py:252-254
+    g.enc_shift = c.centroid_frac + c.norm_frac - c.qk_frac;                  // ops/quantize.py:190
+    g.head_bytes = (int64_t)g.P * (g.kbytes + g.vbytes + 4);
+    g.page_bytes = g.head_bytes * g.n_kv;
+    return g;
+}
+
+int sync_mirrors(ins_cache *c) {
+    CK(cudaEventSynchronize(c->mirror_done));
+    return INS_OK;
+}
+
+// Copy the whole page table and length array to the device (a few hundred KB
+// at most; the same bytes a vLLM-style block manager ships per step).
+int push_mirrors(ins_cache *c, cudaStream_t s, int32_t seq_lo, int32_t seq_hi) {
+    const size_t row = (size_t)c->cfg.max_pages_per_seq;
+    CK(cudaMemcpyAsync(c->d_page_table + (size_t)seq_lo * row, c->h_page_table + (size_t)seq_lo * row,
+                       sizeof(int32_t) * row * (size_t)(seq_hi - seq_lo), cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(c->d_seq_lens + seq_lo, c->h_seq_lens + seq_lo,
+                       sizeof(int32_t) * (size_t)(seq_hi - seq_lo), cudaMemcpyHostToDevice, s));
+    CK(cudaEventRecord(c->mirror_done, s));
+    return INS_OK;
+}
+
+int64_t capacity_of(const ins_cache *c) {
+    return (int64_t)c->cfg.max_pages_per_seq * c->cfg.page_tokens;
+}
+
+// Reserve slots for n tokens appended to their sequences in order. On
+// failure nothing changes (the reference raises before it writes,
+// cache/base.py:67-73).
+int reserve_slots(ins_cache *c, int32_t n, const int32_t *seq_ids, int64_t *slots,
+                  int32_t *lo, int32_t *hi) {
+    const int P = c->cfg.page_tokens;
+    std::vector<int64_t> len_after;
+    std::vector<int32_t> touched;
+    int64_t need_pages = 0;
+    {
+        std::vector<int64_t> extra(c->cfg.max_seqs, 0);
+        for (int32_t i = 0; i < n; ++i) {
+            const int32_t s = seq_ids[i];
+            if (s < 0 || s >= c->cfg.max_seqs)
+                return fail(INS_EINVAL, "sequence id " + std::to_string(s) + " out of range");
+            extra[s] += 1;
+        }
+        for (int32_t s = 0; s < c->cfg.max_seqs; ++s) {
+            if (!extra[s]) continue;
+            const int64_t len = c->h_seq_lens[s], after = len + extra[s];
+            if (after > capacity_of(c))
+                return fail(INS_EBADLEN, "cache holds " + std::to_string(len) + " of " +
+                                             std::to_string(capacity_of(c)) +
+                                             " tokens for sequence " + std::to_string(s) +
+                                             "; cannot append " + std::to_string(extra[s]));
+            need_pages += (after + P - 1) / P - (len + P - 1) / P;
+        }
+        if (need_pages > (int64_t)c->free_pages.size())
+            return fail(INS_EBADLEN, "page pool exhausted: need " + std::to_string(need_pages) +
+                                         " pages, " + std::to_string(c->free_pages.size()) + " free");
+    }
+    int32_t smin = INT32_MAX, smax = -1;
+    const size_t row = (size_t)c->cfg.max_pages_per_seq;
+    for (int32_t i = 0; i < n; ++i) {
+        const int32_t s = seq_ids[i];
+        const int64_t pos = c->h_seq_lens[s];
+        int32_t &pg = c->h_page_table[(size_t)s * row + (size_t)(pos / P)];
+        if (pos % P == 0) {
+            pg = c->free_pages.back();
+            c->free_pages.pop_back();
+        }
+        slots[i] = (int64_t)pg * P + pos % P;
+        c->h_seq_lens[s] = (int32_t)(pos + 1);
+        smin = s < smin ? s : smin;
+        smax = s > smax ? s : smax;
+    }
+    *lo = smin;
+    *hi = smax + 1;
+    return INS_OK;
+}
+
+template <int H>
+int launch_scan_h(ins_cache *c, int32_t B, const int32_t *d_seq, const int64_t *d_T,
+                  const int64_t *h_T, const int32_t *q_rot, int64_t *out, ins_stats *stats,
+                  ins_softmax mode, cudaStream_t s) {
+    const Geo &g = c->g;
+    const int threads = H * 64;
+    const dim3 grid(B * g.n_kv);
+    if (mode == INS_SOFTMAX_TWO_PASS) {
+        const size_t smem = (size_t)H * g.P * 8 + (size_t)2 * H * g.P * 4 + (size_t)g.P * g.vbytes +
+                            (size_t)g.P * 4;
+        auto fn = (g.kb == 4 && g.vb == 2) ? k_scan_two_pass<H, 4, 2>
+                  : (g.kb == 3 && g.vb == 3) ? k_scan_two_pass<H, 3, 3>
+                                             : k_scan_two_pass<H, 0, 0>;
+        CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        fn<<<grid, threads, smem, s>>>(g, c->d_tables, d_seq, d_T, c->d_page_table,
+                                       c->d_pool, q_rot, out, stats);
+        CK(cudaGetLastError());
+        return INS_OK;
+    }
+    return launch_online(c->chunk, g, c->d_tables, B, d_seq, d_T, h_T, c->d_page_table,
+                         c->d_pool, q_rot, out, stats, c->d_status, H, s);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// launch_online picks the exact sequential kernel or the context-parallel
+// chunked scan; it is defined in scan_chunked.cuh and instantiated here.
+// ---------------------------------------------------------------------------
+
+extern "C" {
+
+int32_t ins_abi_version(void) { return 1; }
+
+const char *ins_last_error(void) { return g_err.c_str(); }
+
+int32_t ins_bytes_per_token(const ins_config *cfg) {
+    if (!cfg || cfg->head_dim <= 0) return -1;
+    const int32_t bits = cfg->head_dim * (cfg->key_bits + cfg->value_bits);
+    if (bits % 8 || (cfg->head_dim * cfg->key_bits) % 8 || cfg->norm_bits % 8) return -1;
+    return bits / 8 + 2 * (cfg->norm_bits / 8);
+}
+
+int ins_cache_create(const ins_config *cfg, const ins_tables *tb, int32_t device, ins_cache **out) {
+    if (!out) return fail(INS_EINVAL, "out is NULL");
+    *out = nullptr;
+    if (int rc = check_config(cfg)) return rc;
+    if (!tb || !tb->k_centroids || !tb->k_bounds || !tb->v_centroids || !tb->v_bounds ||
+        !tb->exp_table || (cfg->rot_rounds && !tb->signs))
+        return fail(INS_EINVAL, "tables incomplete");
+    int ndev = 0;
+    CK(cudaGetDeviceCount(&ndev));
+    if (device < 0 || device >= ndev) return fail(INS_EINVAL, "no such device");
+    DeviceGuard dg(device);
+
+    DevTables ht;
+    std::memset(&ht, 0, sizeof(ht));
+    const int nk = 1 << cfg->key_bits, nv = 1 << cfg->value_bits;
+    for (int i = 0; i < nk; ++i) {
+        ht.k_cent[i] = tb->k_centroids[i];
+        ht.k_cent_f64[i] = (double)tb->k_centroids[i];
+        if (tb->k_centroids[i] >= (1ll << 20) || tb->k_centroids[i] <= -(1ll << 20))
+            return fail(INS_EINVAL, "key centroid beyond 20 bits");
+    }
+    for (int i = 0; i + 1 < nk; ++i) ht.k_bound[i] = tb->k_bounds[i];
+    for (int i = 0; i < nv; ++i) ht.v_cent[i] = tb->v_centroids[i];
+    for (int i = 0; i + 1 < nv; ++i) ht.v_bound[i] = tb->v_bounds[i];
+    for (int i = 0; i < (1 << cfg->exp_lut_bits); ++i) ht.exp_tab[i] = (int32_t)tb->exp_table[i];
+    for (int r = 0; r < cfg->rot_rounds; ++r) {
+        uint64_t m = 0;
+        for (int j = 0; j < D; ++j) {
+            const int64_t s = tb->signs[r * D + j];
+            if (s != 1 && s != -1) return fail(INS_EINVAL, "signs must be +-1");
+            if (s < 0) m |= 1ull << j;
+        }
+        ht.sign_mask[r] = m;
+    }
+
+    ins_cache *c = new ins_cache();
+    c->cfg = *cfg;
+    c->g = make_geo(*cfg);
+    c->g.log2e = tb->log2e;
+    c->g.delta_max = tb->delta_max;
+    c->device = device;
+    auto cleanup = [&](int rc) {
+        ins_cache_destroy(c);
+        return rc;
+    };
+    const size_t pool_bytes = (size_t)cfg->n_pages * (size_t)c->g.page_bytes;
+    const size_t pt = (size_t)cfg->max_seqs * (size_t)cfg->max_pages_per_seq;
+    if (cudaMalloc(&c->d_tables, sizeof(DevTables)) != cudaSuccess ||
+        cudaMalloc(&c->d_pool, pool_bytes) != cudaSuccess ||
+        cudaMalloc(&c->d_page_table, sizeof(int32_t) * pt) != cudaSuccess ||
+        cudaMalloc(&c->d_seq_lens, sizeof(int32_t) * cfg->max_seqs) != cudaSuccess ||
+        cudaMalloc(&c->d_status, sizeof(int32_t)) != cudaSuccess ||
+        cudaHostAlloc(&c->h_page_table, sizeof(int32_t) * pt, cudaHostAllocDefault) != cudaSuccess ||
+        cudaHostAlloc(&c->h_seq_lens, sizeof(int32_t) * cfg->max_seqs, cudaHostAllocDefault) !=
+            cudaSuccess) {
+        cudaGetLastError();
+        return cleanup(fail(INS_ENOMEM, "allocation of " + std::to_string(pool_bytes) +
+                                            " B of cache pool (or its tables) failed"));
+    }
+    if (cudaEventCreateWithFlags(&c->mirror_done, cudaEventDisableTiming) != cudaSuccess)
+        return cleanup(fail(INS_ECUDA, "event creation failed"));
+    std::memset(c->h_page_table, 0xff, sizeof(int32_t) * pt);
+    std::memset(c->h_seq_lens, 0, sizeof(int32_t) * cfg->max_seqs);
+    c->free_pages.reserve((size_t)cfg->n_pages);
+    for (int64_t p = cfg->n_pages - 1; p >= 0; --p) c->free_pages.push_back((int32_t)p);
+    if (cudaMemcpy(c->d_tables, &ht, sizeof(ht), cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(c->d_page_table, c->h_page_table, sizeof(int32_t) * pt, cudaMemcpyHostToDevice) !=
+            cudaSuccess ||
+        cudaMemset(c->d_seq_lens, 0, sizeof(int32_t) * cfg->max_seqs) != cudaSuccess ||
+        cudaMemset(c->d_status, 0, sizeof(int32_t)) != cudaSuccess ||
+        cudaMemset(c->d_pool, 0, pool_bytes) != cudaSuccess)
+        return cleanup(fail(INS_ECUDA, "initial copies failed"));
+    if (cudaDeviceSynchronize() != cudaSuccess) return cleanup(fail(INS_ECUDA, "init sync failed"));
+    *out = c;
+    return INS_OK;
+}
+
+int ins_cache_destroy(ins_cache *c) {
+    if (!c) return INS_OK;
+    DeviceGuard dg(c->device);
+    cudaDeviceSynchronize();
+    c->stage_a.release();
+    c->stage_b.release();
+    c->chunk.release();
+    if (c->mirror_done) cudaEventDestroy(c->mirror_done);
+    cudaFree(c->d_tables);
+    cudaFree(c->d_pool);
+    cudaFree(c->d_page_table);
+    cudaFree(c->d_seq_lens);
+    cudaFree(c->d_status);
+    if (c->h_page_table) cudaFreeHost(c->h_page_table);
+    if (c->h_seq_lens) cudaFreeHost(c->h_seq_lens);
+    delete c;
+    return INS_OK;
+}
+
+int64_t ins_cache_length(const ins_cache *c, int32_t seq) {
+    if (!c || seq < 0 || seq >= c->cfg.max_seqs) return -1;
+    return c->h_seq_lens[seq];
+}
+
+int64_t ins_cache_capacity(const ins_cache *c) { return c ? capacity_of(c) : -1; }
+
+int ins_cache_reset(ins_cache *c, int32_t seq) {
+    if (!c) return fail(INS_EINVAL, "cache is NULL");
+    DeviceGuard dg(c->device);
+    if (int rc = sync_mirrors(c)) return rc;
+    const int32_t lo = seq < 0 ? 0 : seq, hi = seq < 0 ? c->cfg.max_seqs : seq + 1;
+    if (seq >= c->cfg.max_seqs) return fail(INS_EINVAL, "sequence id out of range");
+    const size_t row = (size_t)c->cfg.max_pages_per_seq;
+    for (int32_t s = lo; s < hi; ++s) {
+        for (size_t p = 0; p < row; ++p) {
+            int32_t &pg = c->h_page_table[(size_t)s * row + p];
+            if (pg >= 0) c->free_pages.push_back(pg);
+            pg = -1;
+        }
+        c->h_seq_lens[s] = 0;
+    }
+    if (int rc = push_mirrors(c, 0, lo, hi)) return rc;
+    CK(cudaStreamSynchronize(0));
+    return INS_OK;
+}
+
+int ins_ingress(ins_cache *c, int32_t n, const int32_t *seq_ids, const int32_t *q,
+                const int32_t *k, const int32_t *v, int32_t *q_rot, uint32_t flags,
+                void *stream) {
+    if (!c) return fail(INS_EINVAL, "cache is NULL");
+    if (n < 0 || (n > 0 && (!seq_ids || !k || !v))) return fail(INS_EINVAL, "ingress arguments");
+    if (q && !q_rot) return fail(INS_EINVAL, "q given without q_rot");
+    if (n == 0) return INS_OK;
+    auto aligned = [](const void *p) { return ((uintptr_t)p & 7u) == 0; };
+    if (!aligned(k) || !aligned(v) || (q && (!aligned(q) || !aligned(q_rot))))
+        return fail(INS_EINVAL, "q/k/v buffers must be 8-byte aligned");
+    DeviceGuard dg(c->device);
+    cudaStream_t s = (cudaStream_t)stream;
+    if (int rc = sync_mirrors(c)) return rc;
+    if (int rc = c->stage_a.reserve(sizeof(int64_t) * (size_t)n)) return rc;
+    int32_t lo, hi;
+    if (int rc = reserve_slots(c, n, seq_ids, (int64_t *)c->stage_a.h, &lo, &hi)) return rc;
+    if (int rc = c->stage_a.upload(sizeof(int64_t) * (size_t)n, s)) return rc;
+    if (int rc = push_mirrors(c, s, lo, hi)) return rc;
+    const int per_tok = (q ? c->g.n_kv * c->g.H : 0) + 2 * c->g.n_kv;
+    const int64_t warps = (int64_t)n * per_tok;
+    const int wpb = 8;
+    const int64_t blocks = (warps + wpb - 1) / wpb;
+    k_ingress<<<(unsigned)blocks, wpb * 32, 0, s>>>(c->g, c->d_tables, n,
+                                                    (const int64_t *)c->stage_a.d, q, k, v, q_rot,
+                                                    c->d_pool, flags, c->d_status);
+    CK(cudaGetLastError());
+    return INS_OK;
+}
+
+int ins_scan(ins_cache *c, int32_t B, const int32_t *seq_ids, const int64_t *lengths,
+             const int32_t *q_rot, int64_t *out, ins_stats *stats, ins_softmax mode,
+             void *stream) {
+    if (!c) return fail(INS_EINVAL, "cache is NULL");
+    if (B < 0 || (B > 0 && (!seq_ids || !q_rot || !out))) return fail(INS_EINVAL, "scan arguments");
+    if (mode != INS_SOFTMAX_ONLINE && mode != INS_SOFTMAX_TWO_PASS)
+        return fail(INS_EINVAL, "unknown softmax mode");
+    if (B == 0) return INS_OK;
+    DeviceGuard dg(c->device);
+    cudaStream_t s = (cudaStream_t)stream;
+    // staging: [T (B int64)][seq ids (B int32)]
+    const size_t bytes = sizeof(int64_t) * (size_t)B + sizeof(int32_t) * (size_t)B;
+    if (int rc = c->stage_b.reserve(bytes)) return rc;
+    int64_t *hT = (int64_t *)c->stage_b.h;
+    int32_t *hS = (int32_t *)(hT + B);
+    for (int32_t i = 0; i < B; ++i) {
+        const int32_t sq = seq_ids[i];
+        if (sq < 0 || sq >= c->cfg.max_seqs) return fail(INS_EINVAL, "sequence id out of range");
+        const int64_t len = c->h_seq_lens[sq];
+        int64_t T = len;
+        if (lengths) {
+            T = lengths[i];
+            if (T < 0 || T > len)
+                return fail(INS_EBADLEN, "scan length " + std::to_string(T) +
+                                             " outside the sequence's " + std::to_string(len) +
+                                             " cached tokens");
+        }
+        hT[i] = T;
+        hS[i] = sq;
+    }
+    if (int rc = c->stage_b.upload(bytes, s)) return rc;
+    const int64_t *d_T = (const int64_t *)c->stage_b.d;
+    const int32_t *d_seq = (const int32_t *)(d_T + B);
+    switch (c->g.H) {
+        case 1: return launch_scan_h<1>(c, B, d_seq, d_T, hT, q_rot, out, stats, mode, s);
+        case 2: return launch_scan_h<2>(c, B, d_seq, d_T, hT, q_rot, out, stats, mode, s);
+        case 4: return launch_scan_h<4>(c, B, d_seq, d_T, hT, q_rot, out, stats, mode, s);
+        case 8: return launch_scan_h<8>(c, B, d_seq, d_T, hT, q_rot, out, stats, mode, s);
+    }
+    return fail(INS_EINVAL, "kv_groups");
+}
+
+int ins_rotate(ins_cache *c, int64_t n, const int32_t *x, int32_t *y, void *stream) {
+    if (!c) return fail(INS_EINVAL, "cache is NULL");
+    if (n < 0 || (n > 0 && (!x || !y))) return fail(INS_EINVAL, "rotate arguments");
+    if (n == 0) return INS_OK;
+    if (((uintptr_t)x & 7u) || ((uintptr_t)y & 7u)) return fail(INS_EINVAL, "x/y must be 8-byte aligned");
+    DeviceGuard dg(c->device);
+    const int wpb = 8;
+    k_rotate<<<(unsigned)((n + wpb - 1) / wpb), wpb * 32, 0, (cudaStream_t)stream>>>(
+        c->g, c->d_tables, n, x, y, c->d_status);
+    CK(cudaGetLastError());
+    return INS_OK;
+}
+
+int ins_scores(ins_cache *c, int32_t seq, int32_t head, int64_t t0, int64_t n,
+               const int32_t *q_rot, int64_t *s_out, int64_t *ovf, void *stream) {
+    if (!c) return fail(INS_EINVAL, "cache is NULL");
+    if (seq < 0 || seq >= c->cfg.max_seqs || head < 0 || head >= c->g.n_kv)
+        return fail(INS_EINVAL, "sequence or head out of range");
+    if (t0 < 0 || n < 0 || t0 + n > c->h_seq_lens[seq])
+        return fail(INS_EBADLEN, "rows outside the sequence's length");
+    if (n > 0 && (!q_rot || !s_out)) return fail(INS_EINVAL, "scores arguments");
+    DeviceGuard dg(c->device);
+    cudaStream_t s = (cudaStream_t)stream;
+    if (ovf) CK(cudaMemsetAsync(ovf, 0, sizeof(int64_t), s));
+    if (n == 0) return INS_OK;
+    const int32_t *pt = c->d_page_table + (size_t)seq * c->cfg.max_pages_per_seq;
+    unsigned long long *o = (unsigned long long *)ovf;
+    const unsigned blocks = (unsigned)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+    const Geo &g = c->g;
+#define INS_SCORES(HH)                                                                    \
+    {                                                                                     \
+        auto fn = g.kb == 4 ? k_scores<HH, 4> : g.kb == 3 ? k_scores<HH, 3> : k_scores<HH, 0>; \
+        fn<<<blocks, 256, 0, s>>>(g, c->d_tables, pt, head, t0, n, c->d_pool, q_rot, s_out, o); \
+    }
+    switch (g.H) {
+        case 1: INS_SCORES(1) break;
+        case 2: INS_SCORES(2) break;
+        case 4: INS_SCORES(4) break;
+        case 8: INS_SCORES(8) break;
+    }
+#undef INS_SCORES
+    CK(cudaGetLastError());
+    return INS_OK;
+}
+
+int ins_cache_export(ins_cache *c, int32_t seq, int32_t head, int64_t t0, int64_t n, uint8_t *rows) {
+    if (!c) return fail(INS_EINVAL, "cache is NULL");
+    if (seq < 0 || seq >= c->cfg.max_seqs || head < 0 || head >= c->g.n_kv)
+        return fail(INS_EINVAL, "sequence or head out of range");
+    if (t0 < 0 || n < 0 || t0 + n > c->h_seq_lens[seq])
+        return fail(INS_EBADLEN, "rows outside the sequence's length");
+    if (n == 0) return INS_OK;
+    if (!rows) return fail(INS_EINVAL, "rows is NULL");
+    DeviceGuard dg(c->device);
+    if (int rc = sync_mirrors(c)) return rc;
+    const int P = c->cfg.page_tokens;
+    const size_t row = (size_t)c->cfg.max_pages_per_seq;
+    std::vector<int64_t> slots((size_t)n);
+    for (int64_t i = 0; i < n; ++i) {
+        const int64_t pos = t0 + i;
+        slots[(size_t)i] = (int64_t)c->h_page_table[(size_t)seq * row + (size_t)(pos / P)] * P + pos % P;
+    }
+    int64_t *d_slots = nullptr;
+    uint8_t *d_rows = nullptr;
+    CK(cudaMalloc(&d_slots, sizeof(int64_t) * (size_t)n));
+    if (cudaMalloc(&d_rows, (size_t)n * c->g.row_bytes) != cudaSuccess) {
+        cudaFree(d_slots);
+        return fail(INS_ENOMEM, "export buffer");
+    }
+    cudaMemcpy(d_slots, slots.data(), sizeof(int64_t) * (size_t)n, cudaMemcpyHostToDevice);
+    const int64_t total = n * c->g.row_bytes;
+    k_export_rows<<<(unsigned)((total + 255) / 256), 256>>>(c->g, c->d_pool, d_slots, n, head, d_rows);
+    cudaError_t e = cudaMemcpy(rows, d_rows, (size_t)total, cudaMemcpyDeviceToHost);
+    cudaFree(d_slots);
+    cudaFree(d_rows);
+    if (e != cudaSuccess) return fail(INS_ECUDA, std::string("export: ") + cudaGetErrorString(e));
+    return INS_OK;
+}
+
+int ins_cache_import(ins_cache *c, int32_t seq, int64_t n, const uint8_t *rows) {
+    if (!c) return fail(INS_EINVAL, "cache is NULL");
+    if (n < 0 || n > INT32_MAX) return fail(INS_EINVAL, "row count");
+    if (n == 0) return INS_OK;
+    if (!rows) return fail(INS_EINVAL, "rows is NULL");
+    DeviceGuard dg(c->device);
+    if (int rc = sync_mirrors(c)) return rc;
+    std::vector<int32_t> ids((size_t)n, seq);
+    std::vector<int64_t> slots((size_t)n);
+    int32_t lo, hi;
+    if (int rc = reserve_slots(c, (int32_t)n, ids.data(), slots.data(), &lo, &hi)) return rc;
+    if (int rc = push_mirrors(c, 0, lo, hi)) return rc;
+    const size_t bytes = (size_t)n * c->g.n_kv * c->g.row_bytes;
+    int64_t *d_slots = nullptr;
+    uint8_t *d_rows = nullptr;
+    CK(cudaMalloc(&d_slots, sizeof(int64_t) * (size_t)n));
+    if (cudaMalloc(&d_rows, bytes) != cudaSuccess) {
+        cudaFree(d_slots);
+        return fail(INS_ENOMEM, "import buffer");
+    }
+    cudaMemcpy(d_slots, slots.data(), sizeof(int64_t) * (size_t)n, cudaMemcpyHostToDevice);
+    cudaMemcpy(d_rows, rows, bytes, cudaMemcpyHostToDevice);
+    k_import_rows<<<(unsigned)((bytes + 255) / 256), 256>>>(c->g, c->d_pool, d_slots, n, d_rows);
+    cudaError_t e = cudaDeviceSynchronize();
+    cudaFree(d_slots);
+    cudaFree(d_rows);
+    if (e != cudaSuccess) return fail(INS_ECUDA, std::string("import: ") + cudaGetErrorString(e));
+    return INS_OK;
+}
+
+int ins_cache_status(ins_cache *c, void *stream) {
+    if (!c) return fail(INS_EINVAL, "cache is NULL");
+    DeviceGuard dg(c->device);
+    int32_t st = 0;
+    CK(cudaStreamSynchronize((cudaStream_t)stream));
+    CK(cudaMemcpy(&st, c->d_status, sizeof(st), cudaMemcpyDeviceToHost));
+    CK(cudaMemset(c->d_status, 0, sizeof(st)));
+    if (st & ST_TIMEOUT) return fail(INS_ETIMEOUT, "a bounded device wait gave up");
+    if (st & ST_RANGE) return fail(INS_ERANGE, "a value escaped its fixed-point format");
+    if (st & ST_INTERNAL) return fail(INS_EINVAL, "internal consistency check failed");
+    return INS_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,626 @@
+// Device kernels of the B200 compressed-KV attention path: ingress, the exact
+// sequential scan, the two-pass scan, and the row export / import used for
+// parity. The chunked (context-parallel) scan lives in scan_chunked.cuh.
+#pragma once
+
+#include "common.cuh"
+
+namespace ins {
+
+// ---------------------------------------------------------------------------
+// Ingress: one warp per 64-channel vector.
+//
+// Rotation.apply (ops/rotate.py:170-197): sign flip, the six butterfly stages
+// of fwht (numerics/fixed.py:202-226) in the same order, then the 1/sqrt(d)
+// floor shift. Lane l holds channels 2l and 2l+1, so stage h=1 is in-lane and
+// stages h=2..32 pair lane l with lane l ^ (h/2).
+//
+// For k and v the warp continues with _norm_wire (ops/quantize.py:164-181),
+// _encode_plane (183-196) and the LSB-first pack (237-252, 271-289), and
+// writes the codes and norms into the token's slot of the paged planes.
+// ---------------------------------------------------------------------------
+// One round structure of Rotation.apply for the two channels a lane holds.
+__device__ __forceinline__ void rotate_pair(const Geo &g, const DevTables *__restrict__ tb,
+                                            int lane, int64_t &x0, int64_t &x1) {
+    for (int rd = 0; rd < g.rounds; ++rd) {
+        const uint64_t m = tb->sign_mask[rd];
+        if ((m >> (2 * lane)) & 1ull) x0 = -x0;
+        if ((m >> (2 * lane + 1)) & 1ull) x1 = -x1;
+        const int64_t a = x0 + x1, b = x0 - x1;
+        x0 = a;
+        x1 = b;
+#pragma unroll
+        for (int hl = 1; hl < 32; hl <<= 1) {
+            const int64_t o0 = shfl_xor64(x0, hl), o1 = shfl_xor64(x1, hl);
+            const bool lo = (lane & hl) == 0;
+            x0 = lo ? x0 + o0 : o0 - x0;
+            x1 = lo ? x1 + o1 : o1 - x1;
+        }
+        if (g.rot_shift >= 0) {
+            x0 >>= g.rot_shift;
+            x1 >>= g.rot_shift;
+        } else {
+            x0 = (x0 * g.rot_inv) >> 15;
+            x1 = (x1 * g.rot_inv) >> 15;
+        }
+    }
+}
+
+// Rotation.apply alone, one warp per vector.
+__global__ void k_rotate(Geo g, const DevTables *__restrict__ tb, int64_t n,
+                         const int32_t *__restrict__ x, int32_t *__restrict__ y,
+                         int32_t *__restrict__ status) {
+    const int lane = threadIdx.x & 31;
+    const int64_t vec = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (vec >= n) return;
+    const int2 in = reinterpret_cast<const int2 *>(x + vec * D)[lane];
+    int64_t x0 = in.x, x1 = in.y;
+    rotate_pair(g, tb, lane, x0, x1);
+    const bool big = x0 < INT32_MIN || x0 > INT32_MAX || x1 < INT32_MIN || x1 > INT32_MAX;
+    if (__any_sync(FULL, big) && lane == 0) atomicOr(status, ST_RANGE);
+    reinterpret_cast<int2 *>(y + vec * D)[lane] = make_int2((int32_t)x0, (int32_t)x1);
+}
+
+__global__ void k_ingress(Geo g, const DevTables *__restrict__ tb, int32_t n,
+                          const int64_t *__restrict__ slots, const int32_t *__restrict__ q,
+                          const int32_t *__restrict__ k, const int32_t *__restrict__ v,
+                          int32_t *__restrict__ q_rot, uint8_t *__restrict__ pool,
+                          uint32_t flags, int32_t *__restrict__ status) {
+    __shared__ uint8_t codes_sm[8][D];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + wib;
+    const int Hq = q ? g.n_kv * g.H : 0;
+    const int per_tok = Hq + 2 * g.n_kv;
+    if (gw >= (int64_t)n * per_tok) return;
+    const int64_t tok = gw / per_tok;
+    const int r = (int)(gw % per_tok);
+    int kind, head;
+    const int32_t *src;
+    if (r < Hq) {
+        kind = 0;
+        head = r;
+        src = q + (tok * Hq + head) * D;
+    } else if (r < Hq + g.n_kv) {
+        kind = 1;
+        head = r - Hq;
+        src = k + (tok * g.n_kv + head) * D;
+    } else {
+        kind = 2;
+        head = r - Hq - g.n_kv;
+        src = v + (tok * g.n_kv + head) * D;
+    }
+    const int2 in = reinterpret_cast<const int2 *>(src)[lane];
+    int64_t x0 = in.x, x1 = in.y;
+    if (!(flags & INS_INGRESS_PREROTATED)) {
+        // The wire carries Q8.16 in 24-bit lanes (config.py:223-224); the RTL
+        // reports a lane outside it rather than saturating (rot_fwht.sv:64-67).
+        const int64_t wire = 1ll << 23;
+        const bool bad = x0 < -wire || x0 >= wire || x1 < -wire || x1 >= wire;
+        if (__any_sync(FULL, bad) && lane == 0) atomicOr(status, ST_RANGE);
+        rotate_pair(g, tb, lane, x0, x1);
+    }
+
+    if (kind == 0) {
+        const bool big = x0 < INT32_MIN || x0 > INT32_MAX || x1 < INT32_MIN || x1 > INT32_MAX;
+        if (__any_sync(FULL, big) && lane == 0) atomicOr(status, ST_RANGE);
+        reinterpret_cast<int2 *>(q_rot + (tok * Hq + head) * D)[lane] =
+            make_int2((int32_t)x0, (int32_t)x1);
+        return;
+    }
+
+    // _norm_wire: floor(sum x^2 / d), exact isqrt, round-half-even to
+    // Q(norm_frac), clamp to the signed norm_bits format. A rotated channel at
+    // or beyond 2^28 would overflow the reference's own int64 sum of squares
+    // (whose isqrt then refuses a negative operand), so it is reported.
+    {
+        const int64_t lim = 1ll << 28;
+        const bool big = x0 <= -lim || x0 >= lim || x1 <= -lim || x1 >= lim;
+        if (__any_sync(FULL, big) && lane == 0) atomicOr(status, ST_RANGE);
+    }
+    int64_t sq = x0 * x0 + x1 * x1;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += shfl_xor64(sq, o);
+    const int64_t ms = sq / D;
+    int64_t nrm = (int64_t)isqrt_u64((uint64_t)ms);
+    const int sh = g.qk_frac - g.norm_frac;
+    if (sh > 0) nrm = rshift_even(nrm, sh);
+    else if (sh < 0) nrm = (int64_t)((uint64_t)nrm << (-sh));
+    bool hit;
+    nrm = clamp_bits(nrm, g.norm_bits, hit);
+
+    // _encode_plane: code = #{ x << enc_shift > norm * boundary }, strict >.
+    const int bits = kind == 1 ? g.kb : g.vb;
+    const int64_t *bnd = kind == 1 ? tb->k_bound : tb->v_bound;
+    const int nb = (1 << bits) - 1;
+    const int64_t xs0 = x0 * (1ll << g.enc_shift), xs1 = x1 * (1ll << g.enc_shift);
+    int c0 = 0, c1 = 0;
+    for (int b = 0; b < nb; ++b) {
+        const int64_t thr = nrm * bnd[b];
+        c0 += xs0 > thr;
+        c1 += xs1 > thr;
+    }
+    codes_sm[wib][2 * lane] = (uint8_t)c0;
+    codes_sm[wib][2 * lane + 1] = (uint8_t)c1;
+    __syncwarp();
+
+    const int64_t slot = slots[tok];
+    const int64_t page = slot / g.P, t = slot % g.P;
+    uint8_t *region = pool + region_off(g, page, head);
+    const int field = D * bits / 8;
+    uint8_t *dst = kind == 1 ? region + t * g.kbytes : region + vplane_off(g) + t * g.vbytes;
+    for (int byte = lane; byte < field; byte += 32) {
+        uint32_t val = 0;
+        for (int bit = 0; bit < 8; ++bit) {
+            const int pos = byte * 8 + bit;
+            val |= ((uint32_t)(codes_sm[wib][pos / bits] >> (pos % bits)) & 1u) << bit;
+        }
+        dst[byte] = (uint8_t)val;
+    }
+    if (lane == 0) {
+        int16_t *np = reinterpret_cast<int16_t *>(region + nplane_off(g) + t * 4);
+        np[kind == 1 ? 0 : 1] = (int16_t)nrm;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Scores of one cached row against H query heads (ops/attention.py:333-359,
+// fused mode): dot = sum_j q[j] * centroid[code_j], then one multiply by the
+// signed norm and one floor shift by score_shift, then the 48-bit clamp.
+//
+// The dot runs as FP64 fused multiply-adds. Every operand is an integer below
+// 2^31 (q) or 2^17 (centroids) and, while |q| < 2^30, every partial sum is
+// below 2^53, so each FMA is exact and the double holds the same integer the
+// reference's int64 einsum does. Callers take the int64 path otherwise.
+// The product with the norm wraps at 64 bits as numpy's int64 does.
+// ---------------------------------------------------------------------------
+template <int H, int KB>
+__device__ __forceinline__ void row_scores_f64(const Geo &g, const uint8_t *__restrict__ krow,
+                                               int64_t knorm, const double *__restrict__ qd,
+                                               const double *__restrict__ kcd, int64_t *s,
+                                               int &ovf) {
+    uint32_t w[16];
+    const uint2 *src = reinterpret_cast<const uint2 *>(krow);
+    if (KB) {
+#pragma unroll
+        for (int i = 0; i < (KB ? KB : 1); ++i) {
+            const uint2 x = src[i];
+            w[2 * i] = x.x;
+            w[2 * i + 1] = x.y;
+        }
+    } else {
+        for (int i = 0; i < g.kb; ++i) {
+            const uint2 x = src[i];
+            w[2 * i] = x.x;
+            w[2 * i + 1] = x.y;
+        }
+    }
+    double dot[H];
+#pragma unroll
+    for (int h = 0; h < H; ++h) dot[h] = 0.0;
+#pragma unroll
+    for (int j = 0; j < D; ++j) {
+        const double c = kcd[code_at<KB>(w, j, g.kb)];
+#pragma unroll
+        for (int h = 0; h < H; ++h) dot[h] = fma(qd[h * D + j], c, dot[h]);
+    }
+#pragma unroll
+    for (int h = 0; h < H; ++h) {
+        const int64_t di = __double2ll_rn(dot[h]);
+        const int64_t prod = (int64_t)((uint64_t)di * (uint64_t)knorm);
+        bool hit;
+        s[h] = qclamp(prod >> g.score_shift, g.score_width, g.saturate, hit);
+        ovf += hit;
+    }
+}
+
+template <int H>
+__device__ __forceinline__ void row_scores_i64(const Geo &g, const uint8_t *__restrict__ krow,
+                                               int64_t knorm, const int32_t *__restrict__ qi,
+                                               const int64_t *__restrict__ kc, int64_t *s,
+                                               int &ovf) {
+    int64_t dot[H];
+#pragma unroll
+    for (int h = 0; h < H; ++h) dot[h] = 0;
+    for (int j = 0; j < D; ++j) {
+        const int64_t c = kc[code_at_bytes(krow, j, g.kb, g.kbytes)];
+#pragma unroll
+        for (int h = 0; h < H; ++h) dot[h] += (int64_t)qi[h * D + j] * c;
+    }
+#pragma unroll
+    for (int h = 0; h < H; ++h) {
+        const int64_t prod = (int64_t)((uint64_t)dot[h] * (uint64_t)knorm);
+        bool hit;
+        s[h] = qclamp(prod >> g.score_shift, g.score_width, g.saturate, hit);
+        ovf += hit;
+    }
+}
+
+// The smem layout shared by the per-(sequence, KV head) scan kernels.
+template <int H>
+struct SeqSmem {
+    double qd[H * D];
+    int32_t qi[H * D];
+    double kcd[256];
+    int64_t kc[256];
+    int64_t vc[256];
+    int32_t exp_tab[256];
+    int64_t m_state[H];
+    unsigned long long resc, sovf, aovf;
+    long long max_s, max_acc;
+    int exact64;
+};
+
+template <int H>
+__device__ void load_seq_smem(SeqSmem<H> &sm, const Geo &g, const DevTables *tb,
+                              const int32_t *qrow) {
+    for (int i = threadIdx.x; i < H * D; i += blockDim.x) {
+        const int32_t x = qrow[i];
+        sm.qi[i] = x;
+        sm.qd[i] = (double)x;
+    }
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+        sm.kcd[i] = tb->k_cent_f64[i];
+        sm.kc[i] = tb->k_cent[i];
+        sm.vc[i] = tb->v_cent[i];
+        sm.exp_tab[i] = tb->exp_tab[i];
+    }
+    if (threadIdx.x < H) sm.m_state[threadIdx.x] = -(1ll << (g.score_width - 1));
+    if (threadIdx.x == 0) {
+        sm.resc = sm.sovf = sm.aovf = 0;
+        sm.max_s = sm.max_acc = 0;
+        sm.exact64 = 0;
+    }
+    __syncthreads();
+    int big = 0;
+    for (int i = threadIdx.x; i < H * D; i += blockDim.x) {
+        const int32_t x = sm.qi[i];
+        big |= (x >= (1 << 30) || x <= -(1 << 30));
+    }
+    if (__syncthreads_or(big) && threadIdx.x == 0) sm.exact64 = 1;
+    __syncthreads();
+}
+
+// Scores for rows [0, n) of one page region into s_sm[h * P + t].
+template <int H, int KB>
+__device__ void tile_scores(const Geo &g, SeqSmem<H> &sm, const uint8_t *region, int n,
+                            int64_t *s_sm) {
+    const uint8_t *nplane = region + nplane_off(g);
+    int ovf = 0;
+    long long mx = 0;
+    for (int t = threadIdx.x; t < n; t += blockDim.x) {
+        const int64_t knorm = reinterpret_cast<const int16_t *>(nplane + t * 4)[0];
+        int64_t s[H];
+        if (!sm.exact64) row_scores_f64<H, KB>(g, region + (int64_t)t * g.kbytes, knorm, sm.qd,
+                                               sm.kcd, s, ovf);
+        else row_scores_i64<H>(g, region + (int64_t)t * g.kbytes, knorm, sm.qi, sm.kc, s, ovf);
+#pragma unroll
+        for (int h = 0; h < H; ++h) {
+            s_sm[h * g.P + t] = s[h];
+            const long long a = s[h] < 0 ? -s[h] : s[h];
+            mx = a > mx ? a : mx;
+        }
+    }
+    if (ovf) atomicAdd(&sm.sovf, (unsigned long long)ovf);
+    atomicMax(&sm.max_s, mx);
+}
+
+// The online recurrence's control for one tile, per head (ops/attention.py:
+// 480-496): given the running maximum before the tile, every token's running
+// maximum after it, whether it grew, the rescale factor exp(s - m_old) at a
+// growth, and p = exp(m - s). Warp h handles head h with a prefix-max scan.
+template <int H>
+__device__ void tile_online_control(const Geo &g, SeqSmem<H> &sm, const int64_t *s_sm, int n,
+                                    int32_t *p_sm, int32_t *f_sm, uint8_t *grew_sm) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp >= H) return;
+    const int h = warp;
+    const int64_t *s = s_sm + h * g.P;
+    const int per = (n + 31) / 32;
+    const int t0 = lane * per, t1 = min(n, t0 + per);
+    int64_t lmax = INT64_MIN;
+    for (int t = t0; t < t1; ++t) lmax = s[t] > lmax ? s[t] : lmax;
+    int64_t incl = lmax;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int64_t o = __shfl_up_sync(FULL, incl, off);
+        if (lane >= off) incl = o > incl ? o : incl;
+    }
+    int64_t excl = __shfl_up_sync(FULL, incl, 1);
+    const int64_t m_in = sm.m_state[h];
+    if (lane == 0) excl = INT64_MIN;
+    int64_t run = excl > m_in ? excl : m_in;
+    const int32_t unity = 1 << g.prob_frac;
+    int resc = 0;
+    for (int t = t0; t < t1; ++t) {
+        const int64_t st = s[t];
+        const bool grew = st > run;
+        int32_t f = unity;
+        if (grew) {
+            f = exp_lut(g, sm.exp_tab, st - run);
+            run = st;
+            ++resc;
+        }
+        p_sm[h * g.P + t] = exp_lut(g, sm.exp_tab, run - st);
+        f_sm[h * g.P + t] = f;
+        grew_sm[h * g.P + t] = grew;
+    }
+    const int64_t total = __shfl_sync(FULL, incl, 31);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) resc += __shfl_xor_sync(FULL, resc, o);
+    __syncwarp();
+    if (lane == 0) {
+        sm.m_state[h] = total > m_in ? total : m_in;
+        atomicAdd(&sm.resc, (unsigned long long)resc);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// The exact sequential scan: one CTA per (sequence, KV head), H*64 threads.
+//
+// attend_online (ops/attention.py:451-513) token by token, with the reference's
+// truncation pattern and its per-token 32-bit clamp: thread (h, j) owns
+// acc[h][j] and applies, in causal order, the rescale at every growth of the
+// running maximum and then the floor-shifted V term. Scores and the softmax
+// control of a page are computed in parallel first; only the accumulate is
+// sequential. Bit-exact under every input, saturation included.
+// ---------------------------------------------------------------------------
+template <int H, int KB, int VB>
+__global__ void __launch_bounds__(H * 64)
+    k_scan_seq(Geo g, const DevTables *__restrict__ tb, const int32_t *__restrict__ seq_ids,
+               const int64_t *__restrict__ lens, const int32_t *__restrict__ page_table,
+               const uint8_t *__restrict__ pool, const int32_t *__restrict__ q_rot,
+               int64_t *__restrict__ out, ins_stats *__restrict__ stats,
+               const int32_t *__restrict__ only) {
+    extern __shared__ __align__(16) uint8_t dyn[];
+    __shared__ SeqSmem<H> sm;
+    const int item = blockIdx.x;
+    if (only && !only[item]) return;
+    const int b = item / g.n_kv, kvh = item % g.n_kv;
+    const int seq = seq_ids[b];
+    const int64_t T = lens[b];
+    const int32_t *qrow = q_rot + ((int64_t)b * g.n_kv * H + (int64_t)kvh * H) * D;
+    load_seq_smem<H>(sm, g, tb, qrow);
+
+    int64_t *s_sm = reinterpret_cast<int64_t *>(dyn);
+    int32_t *p_sm = reinterpret_cast<int32_t *>(s_sm + H * g.P);
+    int32_t *f_sm = p_sm + H * g.P;
+    uint8_t *v_sm = reinterpret_cast<uint8_t *>(f_sm + H * g.P);
+    uint8_t *n_sm = v_sm + (int64_t)g.P * g.vbytes;
+    uint8_t *grew_sm = n_sm + (int64_t)g.P * 4;
+
+    const int h = threadIdx.x / D, j = threadIdx.x % D;
+    int64_t acc = 0, l = 0;
+    int aovf = 0;
+    const int vb = VB ? VB : g.vb;
+    const int vbytes = VB ? (D * VB / 8) : g.vbytes;
+
+    for (int64_t t0 = 0; t0 < T; t0 += g.P) {
+        const int n = (int)min((int64_t)g.P, T - t0);
+        const int64_t page = page_table[(int64_t)seq * g.max_pages + t0 / g.P];
+        const uint8_t *region = pool + region_off(g, page, kvh);
+        // stage the V plane and the norms of this page
+        {
+            const uint4 *vs = reinterpret_cast<const uint4 *>(region + vplane_off(g));
+            uint4 *vd = reinterpret_cast<uint4 *>(v_sm);
+            const int nv = g.P * g.vbytes / 16;
+            for (int i = threadIdx.x; i < nv; i += blockDim.x) vd[i] = vs[i];
+            const uint4 *ns = reinterpret_cast<const uint4 *>(region + nplane_off(g));
+            uint4 *nd = reinterpret_cast<uint4 *>(n_sm);
+            for (int i = threadIdx.x; i < g.P * 4 / 16; i += blockDim.x) nd[i] = ns[i];
+        }
+        tile_scores<H, KB>(g, sm, region, n, s_sm);
+        __syncthreads();
+        tile_online_control<H>(g, sm, s_sm, n, p_sm, f_sm, grew_sm);
+        __syncthreads();
+        const int32_t *ph = p_sm + h * g.P;
+        const int32_t *fh = f_sm + h * g.P;
+        const uint8_t *gh = grew_sm + h * g.P;
+        for (int t = 0; t < n; ++t) {
+            if (gh[t]) {
+                const int64_t f = fh[t];
+                acc = (acc * f) >> g.prob_frac;
+                l = (l * f) >> g.prob_frac;
+            }
+            const int64_t p = ph[t];
+            l += p;
+            const int64_t w = (int64_t)reinterpret_cast<const int16_t *>(n_sm + t * 4)[1] * p;
+            const uint32_t code = code_at_bytes(v_sm + t * vbytes, j, vb, vbytes);
+            const int64_t term = (w * sm.vc[code]) >> g.acc_shift;
+            bool hit;
+            acc = qclamp(acc + term, g.acc_width, g.saturate, hit);
+            aovf += hit;
+        }
+        __syncthreads();
+    }
+
+    int64_t r;
+    int shift;
+    reciprocal(g, l, r, shift);
+    out[((int64_t)b * g.n_kv * H + (int64_t)kvh * H + h) * D + j] = (acc * r) >> shift;
+    if (stats) {
+        if (aovf) atomicAdd(&sm.aovf, (unsigned long long)aovf);
+        atomicMax(&sm.max_acc, (long long)(acc < 0 ? -acc : acc));
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            ins_stats st;
+            st.n_tokens = T;
+            st.rescale_events = (int64_t)sm.resc;
+            st.score_overflows = (int64_t)sm.sovf;
+            st.acc_overflows = (int64_t)sm.aovf;
+            st.max_abs_score = sm.max_s;
+            st.max_abs_acc = sm.max_acc;
+            stats[item] = st;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// attend_two_pass (ops/attention.py:429-449): the global maximum first, then
+// one accumulation with no rescale and the clamp applied once at the end.
+// One CTA per (sequence, KV head); pass 1 reads the K plane for the maximum,
+// pass 2 reads K and V again. Order-free, hence exact.
+// ---------------------------------------------------------------------------
+template <int H, int KB, int VB>
+__global__ void __launch_bounds__(H * 64)
+    k_scan_two_pass(Geo g, const DevTables *__restrict__ tb, const int32_t *__restrict__ seq_ids,
+                    const int64_t *__restrict__ lens, const int32_t *__restrict__ page_table,
+                    const uint8_t *__restrict__ pool, const int32_t *__restrict__ q_rot,
+                    int64_t *__restrict__ out, ins_stats *__restrict__ stats) {
+    extern __shared__ __align__(16) uint8_t dyn[];
+    __shared__ SeqSmem<H> sm;
+    __shared__ long long hmax[H];
+    __shared__ unsigned long long lsum[H];
+    const int item = blockIdx.x;
+    const int b = item / g.n_kv, kvh = item % g.n_kv;
+    const int seq = seq_ids[b];
+    const int64_t T = lens[b];
+    const int32_t *qrow = q_rot + ((int64_t)b * g.n_kv * H + (int64_t)kvh * H) * D;
+    load_seq_smem<H>(sm, g, tb, qrow);
+    if (threadIdx.x < H) {
+        hmax[threadIdx.x] = LLONG_MIN;
+        lsum[threadIdx.x] = 0;
+    }
+    int64_t *s_sm = reinterpret_cast<int64_t *>(dyn);
+    int32_t *p_sm = reinterpret_cast<int32_t *>(s_sm + H * g.P);
+    uint8_t *v_sm = reinterpret_cast<uint8_t *>(p_sm + 2 * H * g.P);
+    uint8_t *n_sm = v_sm + (int64_t)g.P * g.vbytes;
+    __syncthreads();
+
+    // pass 1: the maximum of every head's scores
+    for (int64_t t0 = 0; t0 < T; t0 += g.P) {
+        const int n = (int)min((int64_t)g.P, T - t0);
+        const int64_t page = page_table[(int64_t)seq * g.max_pages + t0 / g.P];
+        const uint8_t *region = pool + region_off(g, page, kvh);
+        tile_scores<H, KB>(g, sm, region, n, s_sm);
+        __syncthreads();
+        for (int t = threadIdx.x; t < n; t += blockDim.x)
+            for (int hh = 0; hh < H; ++hh) atomicMax(&hmax[hh], (long long)s_sm[hh * g.P + t]);
+        __syncthreads();
+    }
+    const unsigned long long sovf = sm.sovf;
+    const long long maxs = sm.max_s;
+
+    const int h = threadIdx.x / D, j = threadIdx.x % D;
+    const int vb = VB ? VB : g.vb;
+    const int vbytes = VB ? (D * VB / 8) : g.vbytes;
+    int64_t acc = 0;
+    for (int64_t t0 = 0; t0 < T; t0 += g.P) {
+        const int n = (int)min((int64_t)g.P, T - t0);
+        const int64_t page = page_table[(int64_t)seq * g.max_pages + t0 / g.P];
+        const uint8_t *region = pool + region_off(g, page, kvh);
+        {
+            const uint4 *vs = reinterpret_cast<const uint4 *>(region + vplane_off(g));
+            uint4 *vd = reinterpret_cast<uint4 *>(v_sm);
+            for (int i = threadIdx.x; i < g.P * g.vbytes / 16; i += blockDim.x) vd[i] = vs[i];
+            const uint4 *ns = reinterpret_cast<const uint4 *>(region + nplane_off(g));
+            uint4 *nd = reinterpret_cast<uint4 *>(n_sm);
+            for (int i = threadIdx.x; i < g.P * 4 / 16; i += blockDim.x) nd[i] = ns[i];
+        }
+        tile_scores<H, KB>(g, sm, region, n, s_sm);
+        __syncthreads();
+        for (int t = threadIdx.x; t < n; t += blockDim.x)
+            for (int hh = 0; hh < H; ++hh) {
+                const int32_t p = exp_lut(g, sm.exp_tab, hmax[hh] - s_sm[hh * g.P + t]);
+                p_sm[hh * g.P + t] = p;
+                atomicAdd(&lsum[hh], (unsigned long long)p);
+            }
+        __syncthreads();
+        for (int t = 0; t < n; ++t) {
+            const int64_t p = p_sm[h * g.P + t];
+            const int64_t w = (int64_t)reinterpret_cast<const int16_t *>(n_sm + t * 4)[1] * p;
+            const uint32_t code = code_at_bytes(v_sm + t * vbytes, j, vb, vbytes);
+            acc += (w * sm.vc[code]) >> g.acc_shift;
+        }
+        __syncthreads();
+    }
+    bool hit;
+    acc = qclamp(acc, g.acc_width, g.saturate, hit);
+    const int64_t l = (int64_t)lsum[h];
+    int64_t r;
+    int shift;
+    reciprocal(g, l, r, shift);
+    out[((int64_t)b * g.n_kv * H + (int64_t)kvh * H + h) * D + j] = (acc * r) >> shift;
+    if (stats) {
+        if (hit) atomicAdd(&sm.aovf, 1ull);
+        atomicMax(&sm.max_acc, (long long)(acc < 0 ? -acc : acc));
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            ins_stats st;
+            st.n_tokens = T;
+            st.rescale_events = 0;
+            st.score_overflows = (int64_t)sovf;
+            st.acc_overflows = (int64_t)sm.aovf;
+            st.max_abs_score = maxs;
+            st.max_abs_acc = sm.max_acc;
+            stats[item] = st;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// CompressedAttention.scores for rows [t0, t0+n) of one sequence and KV head.
+// ---------------------------------------------------------------------------
+template <int H, int KB>
+__global__ void __launch_bounds__(256)
+    k_scores(Geo g, const DevTables *__restrict__ tb, const int32_t *__restrict__ pt_row,
+             int32_t kvh, int64_t t0, int64_t n, const uint8_t *__restrict__ pool,
+             const int32_t *__restrict__ q, int64_t *__restrict__ s_out,
+             unsigned long long *__restrict__ ovf_out) {
+    __shared__ SeqSmem<H> sm;
+    load_seq_smem<H>(sm, g, tb, q);
+    int ovf = 0;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = t0 + i;
+        const uint8_t *region = pool + region_off(g, pt_row[t / g.P], kvh);
+        const int64_t r = t % g.P;
+        const int64_t knorm =
+            reinterpret_cast<const int16_t *>(region + nplane_off(g) + r * 4)[0];
+        int64_t s[H];
+        if (!sm.exact64) row_scores_f64<H, KB>(g, region + r * g.kbytes, knorm, sm.qd, sm.kcd, s, ovf);
+        else row_scores_i64<H>(g, region + r * g.kbytes, knorm, sm.qi, sm.kc, s, ovf);
+#pragma unroll
+        for (int h = 0; h < H; ++h) s_out[h * n + i] = s[h];
+    }
+    if (ovf_out && ovf) atomicAdd(ovf_out, (unsigned long long)ovf);
+}
+
+// ---------------------------------------------------------------------------
+// Export / import between the paged planes and the reference's packed rows
+// (ops/quantize.py:237-264): [K codes][V codes][k_norm LE16][v_norm LE16].
+// One thread per (row, byte).
+// ---------------------------------------------------------------------------
+__global__ void k_export_rows(Geo g, const uint8_t *__restrict__ pool,
+                              const int64_t *__restrict__ slots, int64_t n, int32_t head,
+                              uint8_t *__restrict__ rows) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n * g.row_bytes) return;
+    const int64_t r = i / g.row_bytes;
+    const int c = (int)(i % g.row_bytes);
+    const int64_t slot = slots[r], page = slot / g.P, t = slot % g.P;
+    const uint8_t *region = pool + region_off(g, page, head);
+    uint8_t v;
+    if (c < g.kbytes) v = region[t * g.kbytes + c];
+    else if (c < g.kbytes + g.vbytes) v = region[vplane_off(g) + t * g.vbytes + (c - g.kbytes)];
+    else v = region[nplane_off(g) + t * 4 + (c - g.kbytes - g.vbytes)];
+    rows[i] = v;
+}
+
+__global__ void k_import_rows(Geo g, uint8_t *__restrict__ pool, const int64_t *__restrict__ slots,
+                              int64_t n, const uint8_t *__restrict__ rows) {
+    // rows: [n, n_kv, row_bytes]
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t per_tok = (int64_t)g.n_kv * g.row_bytes;
+    if (i >= n * per_tok) return;
+    const int64_t r = i / per_tok;
+    const int head = (int)((i % per_tok) / g.row_bytes);
+    const int c = (int)(i % g.row_bytes);
+    const int64_t slot = slots[r], page = slot / g.P, t = slot % g.P;
+    uint8_t *region = pool + region_off(g, page, head);
+    const uint8_t v = rows[i];
+    if (c < g.kbytes) region[t * g.kbytes + c] = v;
+    else if (c < g.kbytes + g.vbytes) region[vplane_off(g) + t * g.vbytes + (c - g.kbytes)] = v;
+    else region[nplane_off(g) + t * 4 + (c - g.kbytes - g.vbytes)] = v;
+}
+
+}  // namespace ins

@@ -1,0 +1,209 @@
+"""``PagedCache``: one C-ABI cache handle, driven with torch device tensors.
+
+torch is the plumbing here -- device memory, the current stream -- and nothing
+else. Every byte of compute runs in the CUDA kernels behind the C ABI.
+
+A ``PagedCache`` holds up to ``max_seqs`` sequences of one attention layer in
+a paged pool on one GPU. It is what the reference-shaped classes
+(``CompressedCache``, ``CompressedAttention``) and the batched decode step
+(``DecodeAttention``) are built on.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import math
+
+import numpy as np
+import torch
+
+from . import _lib
+from .config import FixedFormat, Geometry, QuantConfig
+from .tables import Tables
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device):
+    return C.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _require_cuda():
+    if not torch.cuda.is_available():
+        raise RuntimeError("insitu_b200 needs a CUDA device (sm_100a); there is no CPU path")
+
+
+class PagedCache:
+    """Paged compressed KV cache for ``max_seqs`` sequences, plus its kernels."""
+
+    def __init__(self, quant: QuantConfig, fmt: FixedFormat | None = None,
+                 geo: Geometry | None = None, *, max_seqs: int = 1, capacity: int = 4096,
+                 page_tokens: int = 256, n_pages: int | None = None,
+                 device: int | torch.device | None = None):
+        _require_cuda()
+        self.quant = quant
+        self.fmt = fmt or FixedFormat()
+        self.geo = geo or Geometry()
+        if self.geo.head_dim != 64:
+            raise ValueError("this build supports head_dim 64")
+        self.device = torch.device("cuda", torch.cuda.current_device() if device is None
+                                   else torch.device("cuda", device).index
+                                   if not isinstance(device, torch.device) else device.index)
+        self.tables = Tables.build(quant, self.fmt, self.geo.head_dim)
+        pages_per_seq = max(1, math.ceil(capacity / page_tokens))
+        if n_pages is None:
+            n_pages = max_seqs * pages_per_seq
+        t = self.tables
+        f = self.fmt
+        self.cfg = _lib.Config(
+            self.geo.head_dim, self.geo.n_kv_heads, self.geo.kv_groups, quant.key_bits,
+            quant.value_bits, quant.norm_bits, quant.norm_frac, f.qk_frac, f.centroid_frac,
+            f.acc_frac, f.acc_width, f.score_width, f.prob_frac, f.exp_lut_bits, int(f.saturate),
+            quant.rot_rounds, t.rot_shift, t.rot_inv_sqrt_q15, page_tokens, max_seqs,
+            pages_per_seq, 0, n_pages)
+        self._keep = [np.ascontiguousarray(a, dtype=np.int64) for a in (
+            t.signs.reshape(-1) if t.signs.size else np.zeros(1, np.int64), t.k_centroids,
+            t.k_bounds if t.k_bounds.size else np.zeros(1, np.int64), t.v_centroids,
+            t.v_bounds if t.v_bounds.size else np.zeros(1, np.int64), t.exp_table)]
+        p = lambda a: a.ctypes.data_as(C.POINTER(C.c_int64))
+        tb = _lib.Tables(*(p(a) for a in self._keep), t.log2e, t.delta_max)
+        self._L = _lib.lib()
+        h = C.c_void_p()
+        _lib.check(self._L.ins_cache_create(C.byref(self.cfg), C.byref(tb), self.device.index,
+                                            C.byref(h)))
+        self._h = h
+        self.max_seqs = max_seqs
+        self.page_tokens = page_tokens
+        self.row_bytes = self._L.ins_bytes_per_token(C.byref(self.cfg))
+        self.capacity = int(self._L.ins_cache_capacity(self._h))
+
+    # -- lifecycle -----------------------------------------------------------
+    def close(self) -> None:
+        if getattr(self, "_h", None) is not None and self._h.value:
+            torch.cuda.synchronize(self.device)
+            self._L.ins_cache_destroy(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def length(self, seq: int = 0) -> int:
+        return int(self._L.ins_cache_length(self._h, seq))
+
+    def reset(self, seq: int | None = None) -> None:
+        _lib.check(self._L.ins_cache_reset(self._h, -1 if seq is None else seq))
+
+    def status(self) -> None:
+        """Raise if a kernel latched an error (range, bounded-wait timeout)."""
+        _lib.check(self._L.ins_cache_status(self._h, _stream(self.device)))
+
+    # -- tensors -------------------------------------------------------------
+    def _dev_i32(self, x, shape_tail) -> torch.Tensor:
+        t = torch.as_tensor(x)
+        if t.dtype != torch.int32:
+            if t.dtype.is_floating_point:
+                raise TypeError("fixed-point input must be integer; convert with Q.from_float")
+            if t.numel() and (int(t.max()) >= 2 ** 31 or int(t.min()) < -2 ** 31):
+                raise _lib.RangeError(_lib.INS_ERANGE, "value does not fit int32")
+            t = t.to(torch.int32)
+        t = t.to(self.device).contiguous()
+        if tuple(t.shape[1:]) != tuple(shape_tail):
+            raise ValueError(f"expected (..., {shape_tail}), got {tuple(t.shape)}")
+        return t
+
+    # -- kernels -------------------------------------------------------------
+    def ingress(self, seq_ids, k, v, q=None, *, prerotated: bool = False):
+        """Rotate, quantise, pack and append one token per row (see ins_ingress).
+
+        ``k``, ``v``: (n, n_kv, d); ``q``: (n, n_kv*groups, d) or None.
+        Returns the rotated q (device int32) or None.
+        """
+        g = self.geo
+        k = self._dev_i32(k, (g.n_kv_heads, g.head_dim))
+        v = self._dev_i32(v, (g.n_kv_heads, g.head_dim))
+        n = k.shape[0]
+        if v.shape[0] != n:
+            raise ValueError("k and v carry different token counts")
+        ids = np.ascontiguousarray(np.broadcast_to(np.asarray(seq_ids, dtype=np.int32), (n,)))
+        q_rot = None
+        if q is not None:
+            q = self._dev_i32(q, (g.num_heads, g.head_dim))
+            if q.shape[0] != n:
+                raise ValueError("q carries a different token count")
+            q_rot = torch.empty_like(q)
+        flags = _lib.INS_INGRESS_PREROTATED if prerotated else 0
+        _lib.check(self._L.ins_ingress(self._h, n, ids.ctypes.data_as(C.c_void_p), _ptr(q),
+                                       _ptr(k), _ptr(v), _ptr(q_rot), flags,
+                                       _stream(self.device)))
+        return q_rot
+
+    def rotate(self, x) -> torch.Tensor:
+        """Rotation.apply on the device: (..., d) int32 in, int32 out."""
+        t = torch.as_tensor(x)
+        shape = t.shape
+        t = self._dev_i32(t.reshape(-1, self.geo.head_dim), (self.geo.head_dim,))
+        y = torch.empty_like(t)
+        _lib.check(self._L.ins_rotate(self._h, t.shape[0], _ptr(t), _ptr(y),
+                                      _stream(self.device)))
+        return y.reshape(shape)
+
+    def scores(self, seq: int, kv_head: int, q_rot, t0: int = 0, n: int | None = None):
+        """(s, overflows) for rows [t0, t0+n) of one sequence and KV head."""
+        g = self.geo
+        q = self._dev_i32(torch.as_tensor(q_rot).reshape(g.kv_groups, g.head_dim),
+                          (g.head_dim,))
+        if n is None:
+            n = self.length(seq) - t0
+        s = torch.empty((g.kv_groups, max(n, 0)), dtype=torch.int64, device=self.device)
+        ovf = torch.zeros(1, dtype=torch.int64, device=self.device)
+        _lib.check(self._L.ins_scores(self._h, seq, kv_head, t0, n, _ptr(q), _ptr(s), _ptr(ovf),
+                                      _stream(self.device)))
+        return s, ovf
+
+    def scan(self, seq_ids, q_rot, *, lengths=None, mode: str = "online", stats: bool = True,
+             out: torch.Tensor | None = None, stats_out: torch.Tensor | None = None):
+        """One decode step for B sequences: (out (B, Hq, d) int64, stats (B, n_kv, 6))."""
+        g = self.geo
+        q = self._dev_i32(q_rot, (g.num_heads, g.head_dim))
+        B = q.shape[0]
+        ids = np.ascontiguousarray(np.broadcast_to(np.asarray(seq_ids, dtype=np.int32), (B,)))
+        lens = None
+        if lengths is not None:
+            lens = np.ascontiguousarray(np.broadcast_to(np.asarray(lengths, dtype=np.int64), (B,)))
+        if out is None:
+            out = torch.empty((B, g.num_heads, g.head_dim), dtype=torch.int64, device=self.device)
+        st = None
+        if stats:
+            st = stats_out if stats_out is not None else torch.empty(
+                (B, g.n_kv_heads, len(_lib.STATS_FIELDS)), dtype=torch.int64, device=self.device)
+        m = {"online": _lib.INS_SOFTMAX_ONLINE, "two_pass": _lib.INS_SOFTMAX_TWO_PASS}[mode]
+        _lib.check(self._L.ins_scan(self._h, B, ids.ctypes.data_as(C.c_void_p),
+                                    None if lens is None else lens.ctypes.data_as(C.c_void_p),
+                                    _ptr(q), _ptr(out), _ptr(st), m, _stream(self.device)))
+        return out, st
+
+    # -- format conversion (blocking) --------------------------------------------
+    def export(self, seq: int, kv_head: int, t0: int = 0, n: int | None = None) -> np.ndarray:
+        """Rows [t0, t0+n) in the reference's packed format: (n, row_bytes) uint8."""
+        if n is None:
+            n = self.length(seq) - t0
+        rows = np.empty((max(n, 0), self.row_bytes), dtype=np.uint8)
+        torch.cuda.synchronize(self.device)
+        _lib.check(self._L.ins_cache_export(self._h, seq, kv_head, t0, n,
+                                            rows.ctypes.data_as(C.c_void_p)))
+        return rows
+
+    def import_rows(self, seq: int, rows) -> None:
+        """Append packed rows shaped (n, n_kv, row_bytes) -- a cache image."""
+        rows = np.ascontiguousarray(rows, dtype=np.uint8)
+        if rows.ndim != 3 or rows.shape[1:] != (self.geo.n_kv_heads, self.row_bytes):
+            raise ValueError(f"expected (n, {self.geo.n_kv_heads}, {self.row_bytes}) rows, "
+                             f"got {rows.shape}")
+        torch.cuda.synchronize(self.device)
+        _lib.check(self._L.ins_cache_import(self._h, seq, rows.shape[0],
+                                            rows.ctypes.data_as(C.c_void_p)))

@@ -1,0 +1,302 @@
+"""CUDA path vs the oracle and the reference's golden vectors, bit for bit.
+
+Every test here calls the hand-written sm_100a kernels through the C ABI
+(``insitu_b200.PagedCache`` -> ``libinsitu_b200.so``). Integer, byte and index
+results must be identical; there is no tolerance anywhere in this file.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import make_oracle
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+def _pc(kb=4, vb=2, n_kv=8, groups=4, max_seqs=1, capacity=4096, page_tokens=256, seed=0):
+    from insitu_b200 import FixedFormat, Geometry, PagedCache, QuantConfig
+    return PagedCache(QuantConfig(key_bits=kb, value_bits=vb, seed=seed), FixedFormat(),
+                      Geometry(n_kv, groups, 64), max_seqs=max_seqs, capacity=capacity,
+                      page_tokens=page_tokens)
+
+
+def _np(t):
+    return t.cpu().numpy()
+
+
+def _wire(rng, shape, scale=1.0):
+    x = np.rint(rng.standard_normal(shape) * scale * 65536.0).astype(np.int64)
+    return np.clip(x, -(1 << 23), (1 << 23) - 1).astype(np.int32)
+
+
+# -- ingress -----------------------------------------------------------------
+
+def test_rotation_kernel_matches_rot_vectors(tbvec):
+    pc = _pc(n_kv=1, groups=1)
+    for s in ("q", "k", "v"):
+        got = _np(pc.rotate(torch.from_numpy(tbvec[f"wire_{s}"].astype(np.int32))))
+        np.testing.assert_array_equal(got, tbvec[f"rot_{s}"])
+    got = _np(pc.rotate(torch.from_numpy(tbvec["rot_random_in"].astype(np.int32))))
+    np.testing.assert_array_equal(got, tbvec["rot_random_out"])
+    pc.status()
+
+
+def test_fused_ingress_matches_kv_rows_and_rot_q(tbvec):
+    pc = _pc()
+    q_rot = pc.ingress([0], tbvec["wire_k"][None], tbvec["wire_v"][None],
+                       tbvec["wire_q"][None])
+    pc.status()
+    np.testing.assert_array_equal(_np(q_rot)[0], tbvec["rot_q"])
+    rows = np.stack([pc.export(0, h) for h in range(8)], axis=1)[0]
+    np.testing.assert_array_equal(rows, tbvec["kv_rows"])
+
+
+def test_encoder_matches_enc_vectors_incl_boundary_ties(tbvec):
+    x = tbvec["enc_in"].astype(np.int32)                       # already rotated
+    n = x.shape[0]
+    pc = _pc(n_kv=1, groups=1, capacity=1024)
+    pc.ingress(np.zeros(n, np.int32), x[:, None, :], x[:, None, :], prerotated=True)
+    pc.status()
+    from insitu_b200 import KVQuantizer, QuantConfig
+    kv = KVQuantizer(64, QuantConfig(key_bits=4, value_bits=2)).unpack(pc.export(0, 0))
+    np.testing.assert_array_equal(kv.k_norm, tbvec["enc_norm"])
+    np.testing.assert_array_equal(kv.v_norm, tbvec["enc_norm"])
+    np.testing.assert_array_equal(kv.k_idx, tbvec["enc_idx_key"])
+    np.testing.assert_array_equal(kv.v_idx, tbvec["enc_idx_value"])
+
+
+# -- scan over the reference's own cache image ----------------------------------
+
+@pytest.fixture(scope="module")
+def tb_cache(tbvec):
+    pc = _pc()
+    pc.import_rows(0, tbvec["cache_rows"])
+    return pc
+
+
+def test_imported_image_exports_byte_identical(tb_cache, tbvec):
+    for h in range(8):
+        np.testing.assert_array_equal(tb_cache.export(0, h), tbvec["cache_rows"][:, h])
+
+
+def test_scores_kernel_matches_scores_hex(tb_cache, tbvec):
+    q = tbvec["rot_q"].astype(np.int32)
+    got = []
+    for h in range(8):
+        s, ovf = tb_cache.scores(0, h, torch.from_numpy(q[4 * h:4 * h + 4]))
+        got.append(_np(s))
+        assert int(ovf.item()) == 0
+    np.testing.assert_array_equal(np.concatenate(got), tbvec["scores"])
+
+
+def test_scores_signed_norm_edge_rows(tbvec):
+    pc = _pc(n_kv=1, groups=1)
+    rows = tbvec["score_edge_rows"][:, None, :]
+    pc.import_rows(0, rows)
+    s, _ = pc.scores(0, 0, torch.from_numpy(tbvec["rot_q"][:1].astype(np.int32)))
+    np.testing.assert_array_equal(_np(s)[0], tbvec["score_edge_gold"])
+
+
+def test_online_scan_matches_out_online(tb_cache, tbvec):
+    out, st = tb_cache.scan([0], torch.from_numpy(tbvec["rot_q"][None].astype(np.int32)))
+    tb_cache.status()
+    np.testing.assert_array_equal(_np(out).reshape(1, -1), tbvec["out_online"])
+    orc = make_oracle()
+    _, ost = orc.decode_layer(tbvec["rot_q"][None], [tbvec["cache_rows"]])
+    np.testing.assert_array_equal(_np(st), ost)
+
+
+def test_two_pass_scan_matches_out_hex(tb_cache, tbvec):
+    out, _ = tb_cache.scan([0], torch.from_numpy(tbvec["rot_q"][None].astype(np.int32)),
+                           mode="two_pass")
+    np.testing.assert_array_equal(_np(out).reshape(1, -1), tbvec["out_two_pass"])
+
+
+def test_stress_query_with_many_rescale_factors(tbvec, widths):
+    pc = _pc(n_kv=1, groups=4)
+    pc.import_rows(0, widths["stress_rows"][:, None, :])
+    out, st = pc.scan([0], torch.from_numpy(widths["stress_q_rot"][None].astype(np.int32)))
+    np.testing.assert_array_equal(_np(out)[0], widths["stress_online"])
+    np.testing.assert_array_equal(_np(st)[0, 0], widths["stress_online_stats"])
+
+
+def test_saturating_accumulator_clamps_exactly(widths):
+    pc = _pc(n_kv=1, groups=4)
+    pc.import_rows(0, widths["sat_rows"][:, None, :])
+    q = torch.from_numpy(widths["sat_q_rot"][None].astype(np.int32))
+    out, st = pc.scan([0], q)
+    np.testing.assert_array_equal(_np(out)[0], widths["sat_online"])
+    np.testing.assert_array_equal(_np(st)[0, 0], widths["sat_online_stats"])
+    assert _np(st)[0, 0, 3] > 0
+    out2, st2 = pc.scan([0], q, mode="two_pass")
+    np.testing.assert_array_equal(_np(out2)[0], widths["sat_two_pass"])
+    np.testing.assert_array_equal(_np(st2)[0, 0], widths["sat_two_pass_stats"])
+
+
+# -- every width the reference tests --------------------------------------------
+
+@pytest.mark.parametrize("kb,vb", [(4, 2), (3, 3), (3, 2), (4, 4), (6, 6), (1, 1)])
+def test_widths_end_to_end(widths, kb, vb):
+    t = f"k{kb}v{vb}"
+    g = lambda n: widths[f"{t}_{n}"]
+    pc = _pc(kb, vb, n_kv=1, groups=4)
+    T = g("k").shape[0]
+    pc.ingress(np.zeros(T, np.int32), g("k")[:, None, :].astype(np.int32),
+               g("v")[:, None, :].astype(np.int32))
+    pc.status()
+    np.testing.assert_array_equal(pc.export(0, 0), g("rows"))
+    q_rot = _np(pc.rotate(torch.from_numpy(g("q").astype(np.int32))))
+    np.testing.assert_array_equal(q_rot, g("q_rot"))
+    s, ovf = pc.scores(0, 0, torch.from_numpy(q_rot))
+    np.testing.assert_array_equal(_np(s), g("scores"))
+    out, st = pc.scan([0], torch.from_numpy(q_rot[None]))
+    np.testing.assert_array_equal(_np(out)[0], g("online"))
+    np.testing.assert_array_equal(_np(st)[0, 0], g("online_stats"))
+    out2, st2 = pc.scan([0], torch.from_numpy(q_rot[None]), mode="two_pass")
+    np.testing.assert_array_equal(_np(out2)[0], g("two_pass"))
+    np.testing.assert_array_equal(_np(st2)[0, 0], g("two_pass_stats"))
+
+
+# -- 512 sequential ingress steps, then bit-exact ----------------
+
+def test_config1_sequential_ingress_and_decode(config1):
+    pc = _pc(capacity=512)
+    wk, wv = config1["wire_k"], config1["wire_v"]
+    steps = list(config1["steps"])
+    for t in range(wk.shape[0]):
+        if t in steps:
+            i = steps.index(t)
+            q_rot = pc.ingress([0], wk[t:t + 1], wv[t:t + 1], config1["wire_q"][i:i + 1])
+            out, _ = pc.scan([0], q_rot)
+            np.testing.assert_array_equal(_np(out).reshape(-1), config1["out_online"][i],
+                                          err_msg=f"step {t}")
+        else:
+            pc.ingress([0], wk[t:t + 1], wv[t:t + 1])
+    pc.status()
+    rows = np.stack([pc.export(0, h) for h in range(8)], axis=1)
+    np.testing.assert_array_equal(rows, config1["cache"])
+
+
+# -- larger, ragged, batched: GPU vs oracle ------------------------------------------
+
+def test_batched_ragged_decode_matches_oracle():
+    rng = np.random.default_rng(11)
+    lens = [0, 1, 2, 255, 256, 257, 3000, 9001]
+    B = len(lens)
+    pc = _pc(max_seqs=B, capacity=9216)
+    orc = make_oracle()
+    caches = []
+    for b, T in enumerate(lens):
+        k = _wire(rng, (T, 8, 64))
+        v = _wire(rng, (T, 8, 64))
+        if T:
+            pc.ingress(np.full(T, b, np.int32), k, v)
+        caches.append(orc.ingress_rows(k, v, threads=8) if T else np.zeros((0, 8, 52), np.uint8))
+    pc.status()
+    for b, T in enumerate(lens):
+        if T:
+            for h in (0, 7):
+                np.testing.assert_array_equal(pc.export(b, h), caches[b][:, h])
+    q = _wire(rng, (B, 32, 64), 1.0 / 8.0)
+    q_rot = orc.rotate(q)
+    out, st = pc.scan(np.arange(B), torch.from_numpy(q_rot.astype(np.int32)))
+    want, wst = orc.decode_layer(q_rot, caches, threads=8)
+    np.testing.assert_array_equal(_np(out), want)
+    np.testing.assert_array_equal(_np(st), wst)
+    # a causal prefix of each sequence (kv.select(slice(0, ctx)))
+    pre = [max(0, T - 7) for T in lens]
+    out, _ = pc.scan(np.arange(B), torch.from_numpy(q_rot.astype(np.int32)), lengths=pre)
+    want, _ = orc.decode_layer(q_rot, [c[:p] for c, p in zip(caches, pre)], threads=8)
+    np.testing.assert_array_equal(_np(out), want)
+
+
+def test_long_single_sequence_matches_oracle():
+    rng = np.random.default_rng(12)
+    T = 40000
+    pc = _pc(capacity=T)
+    k, v = _wire(rng, (T, 8, 64)), _wire(rng, (T, 8, 64))
+    pc.ingress(np.zeros(T, np.int32), k, v)
+    q_rot = make_oracle().rotate(_wire(rng, (1, 32, 64), 1.0 / 8.0))
+    out, st = pc.scan([0], torch.from_numpy(q_rot.astype(np.int32)))
+    orc = make_oracle()
+    rows = orc.ingress_rows(k, v, threads=8)
+    want, wst = orc.decode_layer(q_rot, [rows], threads=8)
+    np.testing.assert_array_equal(_np(out), want)
+    np.testing.assert_array_equal(_np(st), wst)
+
+
+# -- error behaviour -------------------------------------------------------------
+
+def test_capacity_overflow_raises_and_changes_nothing():
+    from insitu_b200._lib import CapacityError
+    pc = _pc(capacity=256)
+    rng = np.random.default_rng(1)
+    pc.ingress(np.zeros(250, np.int32), _wire(rng, (250, 8, 64)), _wire(rng, (250, 8, 64)))
+    with pytest.raises(ValueError):
+        pc.ingress(np.zeros(10, np.int32), _wire(rng, (10, 8, 64)), _wire(rng, (10, 8, 64)))
+    with pytest.raises(CapacityError):
+        pc.ingress(np.zeros(7, np.int32), _wire(rng, (7, 8, 64)), _wire(rng, (7, 8, 64)))
+    assert pc.length(0) == 250
+    pc.ingress(np.zeros(6, np.int32), _wire(rng, (6, 8, 64)), _wire(rng, (6, 8, 64)))
+    assert pc.length(0) == 256
+
+
+def test_wire_value_outside_24_bits_is_reported():
+    from insitu_b200._lib import RangeError
+    pc = _pc(n_kv=1, groups=1)
+    k = np.zeros((1, 1, 64), np.int32)
+    k[0, 0, 5] = 1 << 23
+    pc.ingress([0], k, np.zeros_like(k))
+    with pytest.raises(RangeError):
+        pc.status()
+    pc.status()                     # cleared after reading
+
+
+def test_reset_returns_pages_and_empties_the_sequence():
+    pc = _pc(capacity=512, max_seqs=2)
+    rng = np.random.default_rng(3)
+    pc.ingress(np.zeros(300, np.int32), _wire(rng, (300, 8, 64)), _wire(rng, (300, 8, 64)))
+    pc.reset(0)
+    assert pc.length(0) == 0
+    out, st = pc.scan([0], torch.zeros((1, 32, 64), dtype=torch.int32))
+    assert not _np(out).any() and (_np(st)[..., 0] == 0).all()
+
+
+# -- the reference-shaped classes ------------------------------------------------
+
+def test_dropin_cache_and_attention_match_oracle(widths):
+    from insitu_b200 import CompressedAttention, CompressedCache, QuantConfig
+    g = lambda n: widths[f"k4v2_{n}"]
+    cache = CompressedCache(1, 64, 128, QuantConfig(key_bits=4, value_bits=2))
+    cache.append_rotated(g("k_rot")[:, None, :].astype(np.int32),
+                         g("v_rot")[:, None, :].astype(np.int32))
+    assert cache.length == g("k").shape[0]
+    np.testing.assert_array_equal(cache.buf[:, 0], g("rows"))
+    attn = CompressedAttention(cache.quantizer)
+    kv = cache.view(0)
+    out, st = attn.attend_online(g("q_rot"), kv)
+    np.testing.assert_array_equal(out, g("online"))
+    assert [st.n_tokens, st.rescale_events, st.score_overflows, st.acc_overflows,
+            st.max_abs_score, st.max_abs_acc] == g("online_stats").tolist()
+    out, _ = attn.attend_two_pass(g("q_rot"), kv)
+    np.testing.assert_array_equal(out, g("two_pass"))
+    s, ovf = attn.scores(g("q_rot"), kv)
+    np.testing.assert_array_equal(s, g("scores"))
+    # a causal prefix, and the host-array path
+    pre = kv.select(slice(0, 40))
+    host = cache.view_from_buffer(0).select(slice(0, 40))
+    a, _ = attn.attend_online(g("q_rot"), pre)
+    b, _ = attn.attend_online(g("q_rot"), host)
+    orc = make_oracle()
+    want, _ = orc.attend_online(g("q_rot"), g("k_idx")[:40], g("k_norm")[:40],
+                                g("v_idx")[:40], g("v_norm")[:40])
+    np.testing.assert_array_equal(a, want)
+    np.testing.assert_array_equal(b, want)
+    # KVQuantizer.encode on the device
+    kvq = cache.quantizer.encode(g("k_rot"), g("v_rot"))
+    np.testing.assert_array_equal(kvq.k_idx, g("k_idx"))
+    np.testing.assert_array_equal(kvq.v_norm, g("v_norm"))
