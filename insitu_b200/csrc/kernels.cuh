@@ -364,23 +364,22 @@ __device__ void tile_online_control(const Geo &g, SeqSmem<H> &sm, const int64_t 
 // control of a page are computed in parallel first; only the accumulate is
 // sequential. Bit-exact under every input, saturation included.
 // ---------------------------------------------------------------------------
-template <int H, int KB, int VB>
-__global__ void __launch_bounds__(H * 64)
-    k_scan_seq(Geo g, const DevTables *__restrict__ tb, const int32_t *__restrict__ seq_ids,
-               const int64_t *__restrict__ lens, const int32_t *__restrict__ page_table,
-               const uint8_t *__restrict__ pool, const int32_t *__restrict__ q_rot,
-               int64_t *__restrict__ out, ins_stats *__restrict__ stats,
-               const int32_t *__restrict__ only) {
-    extern __shared__ __align__(16) uint8_t dyn[];
-    __shared__ SeqSmem<H> sm;
-    const int item = blockIdx.x;
-    if (only && !only[item]) return;
-    const int b = item / g.n_kv, kvh = item % g.n_kv;
-    const int seq = seq_ids[b];
-    const int64_t T = lens[b];
-    const int32_t *qrow = q_rot + ((int64_t)b * g.n_kv * H + (int64_t)kvh * H) * D;
-    load_seq_smem<H>(sm, g, tb, qrow);
+// Smem bytes the sequential scan body needs beyond SeqSmem.
+template <int H>
+__host__ __device__ inline size_t seq_dyn_smem(const Geo &g) {
+    return (size_t)H * g.P * (8 + 4 + 4 + 1) + (size_t)g.P * g.vbytes + (size_t)g.P * 4;
+}
 
+// The sequential scan of one (sequence, KV head) item, run by a whole CTA
+// whose threads [0, H*64) own (head, channel) pairs. Writes the H*64 outputs
+// and, when st_out is given, the item's stats. `dyn` holds seq_dyn_smem bytes.
+template <int H, int KB, int VB>
+__device__ void seq_scan_item(const Geo &g, const DevTables *__restrict__ tb, int seq, int64_t T,
+                              int kvh, const int32_t *__restrict__ page_table,
+                              const uint8_t *__restrict__ pool, const int32_t *qrow,
+                              int64_t *out_row, ins_stats *st_out, SeqSmem<H> &sm,
+                              uint8_t *dyn) {
+    load_seq_smem<H>(sm, g, tb, qrow);
     int64_t *s_sm = reinterpret_cast<int64_t *>(dyn);
     int32_t *p_sm = reinterpret_cast<int32_t *>(s_sm + H * g.P);
     int32_t *f_sm = p_sm + H * g.P;
@@ -388,7 +387,8 @@ __global__ void __launch_bounds__(H * 64)
     uint8_t *n_sm = v_sm + (int64_t)g.P * g.vbytes;
     uint8_t *grew_sm = n_sm + (int64_t)g.P * 4;
 
-    const int h = threadIdx.x / D, j = threadIdx.x % D;
+    const bool owner = threadIdx.x < H * D;
+    const int h = owner ? threadIdx.x / D : 0, j = threadIdx.x % D;
     int64_t acc = 0, l = 0;
     int aovf = 0;
     const int vb = VB ? VB : g.vb;
@@ -398,7 +398,6 @@ __global__ void __launch_bounds__(H * 64)
         const int n = (int)min((int64_t)g.P, T - t0);
         const int64_t page = page_table[(int64_t)seq * g.max_pages + t0 / g.P];
         const uint8_t *region = pool + region_off(g, page, kvh);
-        // stage the V plane and the norms of this page
         {
             const uint4 *vs = reinterpret_cast<const uint4 *>(region + vplane_off(g));
             uint4 *vd = reinterpret_cast<uint4 *>(v_sm);
@@ -412,23 +411,26 @@ __global__ void __launch_bounds__(H * 64)
         __syncthreads();
         tile_online_control<H>(g, sm, s_sm, n, p_sm, f_sm, grew_sm);
         __syncthreads();
-        const int32_t *ph = p_sm + h * g.P;
-        const int32_t *fh = f_sm + h * g.P;
-        const uint8_t *gh = grew_sm + h * g.P;
-        for (int t = 0; t < n; ++t) {
-            if (gh[t]) {
-                const int64_t f = fh[t];
-                acc = (acc * f) >> g.prob_frac;
-                l = (l * f) >> g.prob_frac;
+        if (owner) {
+            const int32_t *ph = p_sm + h * g.P;
+            const int32_t *fh = f_sm + h * g.P;
+            const uint8_t *gh = grew_sm + h * g.P;
+            for (int t = 0; t < n; ++t) {
+                if (gh[t]) {
+                    const int64_t f = fh[t];
+                    acc = (acc * f) >> g.prob_frac;
+                    l = (l * f) >> g.prob_frac;
+                }
+                const int64_t p = ph[t];
+                l += p;
+                const int64_t w =
+                    (int64_t)reinterpret_cast<const int16_t *>(n_sm + t * 4)[1] * p;
+                const uint32_t code = code_at_bytes(v_sm + t * vbytes, j, vb, vbytes);
+                const int64_t term = (w * sm.vc[code]) >> g.acc_shift;
+                bool hit;
+                acc = qclamp(acc + term, g.acc_width, g.saturate, hit);
+                aovf += hit;
             }
-            const int64_t p = ph[t];
-            l += p;
-            const int64_t w = (int64_t)reinterpret_cast<const int16_t *>(n_sm + t * 4)[1] * p;
-            const uint32_t code = code_at_bytes(v_sm + t * vbytes, j, vb, vbytes);
-            const int64_t term = (w * sm.vc[code]) >> g.acc_shift;
-            bool hit;
-            acc = qclamp(acc + term, g.acc_width, g.saturate, hit);
-            aovf += hit;
         }
         __syncthreads();
     }
@@ -436,10 +438,10 @@ __global__ void __launch_bounds__(H * 64)
     int64_t r;
     int shift;
     reciprocal(g, l, r, shift);
-    out[((int64_t)b * g.n_kv * H + (int64_t)kvh * H + h) * D + j] = (acc * r) >> shift;
-    if (stats) {
+    if (owner) out_row[h * D + j] = (acc * r) >> shift;
+    if (st_out) {
         if (aovf) atomicAdd(&sm.aovf, (unsigned long long)aovf);
-        atomicMax(&sm.max_acc, (long long)(acc < 0 ? -acc : acc));
+        if (owner) atomicMax(&sm.max_acc, (long long)(acc < 0 ? -acc : acc));
         __syncthreads();
         if (threadIdx.x == 0) {
             ins_stats st;
@@ -449,9 +451,38 @@ __global__ void __launch_bounds__(H * 64)
             st.acc_overflows = (int64_t)sm.aovf;
             st.max_abs_score = sm.max_s;
             st.max_abs_acc = sm.max_acc;
-            stats[item] = st;
+            *st_out = st;
         }
     }
+    __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
+// The exact sequential scan: one CTA per (sequence, KV head), H*64 threads.
+//
+// attend_online (ops/attention.py:451-513) token by token, with the reference's
+// truncation pattern and its per-token 32-bit clamp: thread (h, j) owns
+// acc[h][j] and applies, in causal order, the rescale at every growth of the
+// running maximum and then the floor-shifted V term. Scores and the softmax
+// control of a page are computed in parallel first; only the accumulate is
+// sequential. Bit-exact under every input, saturation included. The chunked
+// scan falls back to this body for an item whose exactness it cannot prove.
+// ---------------------------------------------------------------------------
+template <int H, int KB, int VB>
+__global__ void __launch_bounds__(H * 64)
+    k_scan_seq(Geo g, const DevTables *__restrict__ tb, const int32_t *__restrict__ seq_ids,
+               const int64_t *__restrict__ lens, const int32_t *__restrict__ page_table,
+               const uint8_t *__restrict__ pool, const int32_t *__restrict__ q_rot,
+               int64_t *__restrict__ out, ins_stats *__restrict__ stats,
+               const int32_t *__restrict__ only) {
+    extern __shared__ __align__(16) uint8_t dyn[];
+    __shared__ SeqSmem<H> sm;
+    const int item = blockIdx.x;
+    if (only && !only[item]) return;
+    const int b = item / g.n_kv, kvh = item % g.n_kv;
+    const int64_t base = ((int64_t)b * g.n_kv * H + (int64_t)kvh * H) * D;
+    seq_scan_item<H, KB, VB>(g, tb, seq_ids[b], lens[b], kvh, page_table, pool, q_rot + base,
+                             out + base, stats ? stats + item : nullptr, sm, dyn);
 }
 
 // ---------------------------------------------------------------------------

@@ -300,3 +300,39 @@ def test_dropin_cache_and_attention_match_oracle(widths):
     kvq = cache.quantizer.encode(g("k_rot"), g("v_rot"))
     np.testing.assert_array_equal(kvq.k_idx, g("k_idx"))
     np.testing.assert_array_equal(kvq.v_norm, g("v_norm"))
+
+
+# -- the context-parallel scan's hard cases ------------------------------------------
+
+def _rising_keys(T, step, rng):
+    """Keys along one direction with a norm that grows every `step` tokens, so
+    the running maximum keeps moving across chunk boundaries."""
+    base = _wire(rng, (64,), 0.5).astype(np.int64)
+    scale = 1.0 + (np.arange(T) // step) * 0.01
+    k = np.clip(np.rint(base[None, :] * scale[:, None] / 8), -(1 << 23), (1 << 23) - 1)
+    k = k + rng.integers(-40, 40, size=(T, 64))
+    return np.clip(k, -(1 << 23), (1 << 23) - 1).astype(np.int32), base
+
+
+@pytest.mark.parametrize("T,step", [(5000, 97), (3000, 1)])
+def test_rescales_across_chunks_and_fallback(T, step):
+    rng = np.random.default_rng(T + step)
+    kk, base = _rising_keys(T, step, rng)
+    k = np.stack([kk] * 8, axis=1)
+    v = _wire(rng, (T, 8, 64))
+    pc = _pc(capacity=T)
+    pc.ingress(np.zeros(T, np.int32), k, v)
+    orc = make_oracle()
+    qr = orc.rotate(np.tile(base[None, None, :] // 4, (1, 32, 1)))
+    q_rot = torch.from_numpy(qr.astype(np.int32))
+    out, st = pc.scan([0], q_rot)
+    pc.status()
+    rows = orc.ingress_rows(k, v, threads=8)
+    want, wst = orc.decode_layer(qr, [rows], threads=8)
+    assert wst[0, :, 1].sum() > 20                      # many rescale events
+    np.testing.assert_array_equal(_np(out), want)
+    np.testing.assert_array_equal(_np(st), wst)
+    # repeatable: a second launch reuses the scratch and gives the same bits
+    out2, st2 = pc.scan([0], q_rot)
+    np.testing.assert_array_equal(_np(out2), want)
+    np.testing.assert_array_equal(_np(st2), wst)
