@@ -115,6 +115,17 @@ __device__ __forceinline__ int32_t exp_lut(const Geo &g, const int32_t *tab, int
     return tab[u & ((1 << g.exp_lut_bits) - 1)] >> (int)(u >> g.exp_lut_bits);
 }
 
+// exp_lut for a distance known to be non-negative, in 32-bit arithmetic:
+// after the clamp d <= delta_max < 2^32, and u = floor(d * log2e / 2^(2*acc_frac
+// - exp_lut_bits)) is the same nested floor exp_lut takes in two steps.
+__device__ __forceinline__ int32_t exp_lut32(const Geo &g, const int32_t *tab, int64_t delta) {
+    const uint32_t d = (uint32_t)(delta < g.delta_max ? delta : g.delta_max);
+    const uint64_t prod = (uint64_t)d * (uint64_t)(uint32_t)g.log2e;
+    const uint32_t u = (uint32_t)(prod >> (2 * g.acc_frac - g.exp_lut_bits));
+    const uint32_t span = (uint32_t)(g.prob_frac + 2) << g.exp_lut_bits;
+    return u >= span ? 0 : (tab[u & ((1u << g.exp_lut_bits) - 1u)] >> (u >> g.exp_lut_bits));
+}
+
 // 2^62 / den by restoring division, 64 quotient bits.
 __device__ __forceinline__ uint64_t div_pow62(uint64_t den) {
     uint64_t q = 0, rem = 0;

@@ -37,13 +37,20 @@ namespace ins {
 
 constexpr int HMAX = 8;
 constexpr int LB_SPIN_LIMIT = 1 << 22;   // ~0.4 s of polling at most
-constexpr int SEGMAX = 32;               // rescales of one head one chunk can hold
+constexpr int SEGMAX = 32;               // rescales one head's chunk can hold
+constexpr int GBLK = 32;                 // chunks folded per level-1 block
+#ifndef INS_JGROUP
+#define INS_JGROUP 8
+#endif
+#ifndef INS_SCORE_ROWS
+#define INS_SCORE_ROWS 2
+#endif
 
-struct SegEntry {          // one rescale segment of one head in one chunk
-    int32_t S[D];          // sum of terms from the rescale token to the segment end
+struct SegEntry {          // a rescale and the translation that follows it
+    int64_t S[D];          // sum of terms after the rescale (per channel)
     int64_t l;             // sum of p over the same tokens
-    int32_t f;             // the factor applied to acc and l before this segment
-    int32_t tok;
+    int32_t f;             // factor applied to acc and l at the rescale
+    int32_t pad;
 };
 
 struct ChunkRec {          // one (item, chunk)
@@ -54,8 +61,16 @@ struct ChunkRec {          // one (item, chunk)
     int32_t seg_base[HMAX];
 };
 
+struct BlockRec {          // GBLK consecutive chunks of one item, folded
+    int64_t Spre[HMAX][D]; // translation before the block's first rescale
+    int64_t Y[HMAX][D];    // max over the block of |local partial sum| (clamp proof)
+    int64_t lpre[HMAX];
+    int32_t nent[HMAX];
+    int32_t ent_base[HMAX];
+};
+
 struct ItemAcc {
-    unsigned long long done;
+    unsigned long long done_blocks;
     unsigned long long resc;
     unsigned long long sovf;
     long long maxs;
@@ -70,6 +85,7 @@ struct ChunkArgs {
     int32_t n_tiles;
     int32_t C;                    // rows per chunk
     int32_t max_chunks;
+    int32_t max_blocks;
     int32_t n_items;
     const int32_t *item_nchunks;
     const int32_t *seq_ids;
@@ -84,10 +100,13 @@ struct ChunkArgs {
     unsigned long long *lb_flag;  // [n_items * max_chunks]
     long long *lb_val;            // [n_items * max_chunks * 2 * HMAX]
     ChunkRec *recs;               // [n_items * max_chunks]
+    BlockRec *blks;               // [n_items * max_blocks]
+    unsigned int *blk_done;       // [n_items * max_blocks]
     SegEntry *segs;
     unsigned int *seg_top;
     int32_t seg_cap;
     ItemAcc *items;               // [n_items]
+    int32_t *redo;                // [n_items]: 1 = recompute with the sequential body
     unsigned long long *all_done;
     int32_t *status;
     unsigned long long epoch;
@@ -99,19 +118,20 @@ struct ChunkArgs {
 struct ChunkScratch {
     void *base = nullptr;
     size_t bytes = 0;
-    int32_t n_items = 0, max_chunks = 0, seg_cap = 0;
+    int32_t n_items = 0, max_chunks = 0, seg_cap = 0, tile_cap = 0;
     unsigned long long epoch = 0;
     unsigned long long claim_base = 0;
-    // carved views
     unsigned long long *claim = nullptr, *lb_flag = nullptr, *all_done = nullptr;
     long long *lb_val = nullptr;
     ChunkRec *recs = nullptr;
+    BlockRec *blks = nullptr;
+    unsigned int *blk_done = nullptr;
     SegEntry *segs = nullptr;
     unsigned int *seg_top = nullptr;
     ItemAcc *items = nullptr;
+    int32_t *redo = nullptr;
     int4 *tiles = nullptr;
     int32_t *item_nchunks = nullptr;
-    int32_t tile_cap = 0;
 
     void release() {
         if (base) cudaFree(base);
@@ -128,57 +148,63 @@ template <int H, int VB>
 struct ChunkLayout {
     static constexpr int NC = 1 << VB;                    // V codes
     static constexpr int SUB = VB <= 2 ? 256 : 128;       // tokens per term-table sub-tile
+    static constexpr int PS = SUB * H + 4;                // words per code plane (padded)
     static constexpr int VW = 2 * VB;                     // 32-bit words per V row
     int C;
-    size_t off_s, off_p, off_vt, off_vn, off_tab, off_grew, off_any, off_s0, total;
+    size_t off_s, off_p, off_vt, off_vn, off_tab, off_grew, off_pre, off_bmax, off_bcar, off_s0, total;
     __host__ __device__ explicit ChunkLayout(int C_) : C(C_) {
         size_t o = 0;
         off_s = o;    o += (size_t)H * C * 8;             // scores (int64)
         off_p = o;    o += (size_t)H * C * 4;             // p (int32)
         off_vt = o;   o += (size_t)VW * C * 4;            // V codes, word-major
         off_vn = o;   o += (size_t)C * 4;                 // v_norm (int32)
-        off_tab = o;  o += (size_t)SUB * NC * H * 4;      // terms [t][code][h]
-        off_grew = o; o += (size_t)H * (C / 32) * 4;      // rescale bitmask per head
-        off_any = o;  o += (size_t)(C / 32) * 4;          // any head
+        off_tab = o;  o += (size_t)NC * PS * 4;           // terms [code][t][h]
+        off_grew = o; o += (size_t)(H + 1) * (C / 32) * 4;  // rescale bits per head, + any
+        off_pre = o;  o += (size_t)H * (C / 32) * 4;      // rescales before each bit word
+        off_bmax = o; o += (size_t)H * (C / 32) * 8;      // max score of each 32-row block
+        off_bcar = o; o += (size_t)H * (C / 32) * 8;      // running max entering each block
         off_s0 = o;   o += (size_t)H * D * 4;             // segment-0 partials
         total = o;
     }
 };
 
 // Scores of R rows for one thread (register-blocked over rows), exact.
+// Channels are taken 32 at a time: 32 codes of KB bits are exactly KB words,
+// so every code extraction below is at a compile-time position.
 template <int H, int KB, int R>
 __device__ __forceinline__ void score_rows(const Geo &g, const uint8_t *const *krow,
                                            const int64_t *knorm, const bool *valid,
                                            const double *__restrict__ qd,
                                            const uint32_t *__restrict__ khi, int64_t (*s)[H],
                                            int &ovf) {
-    constexpr int NW = 2 * KB;                 // 32-bit words of K codes per row
-    uint32_t w[R][NW];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-        const uint2 *src = reinterpret_cast<const uint2 *>(krow[r]);
-#pragma unroll
-        for (int i = 0; i < KB; ++i) {
-            uint2 x = valid[r] ? src[i] : make_uint2(0u, 0u);
-            w[r][2 * i] = x.x;
-            w[r][2 * i + 1] = x.y;
-        }
-    }
     double acc[R][H];
 #pragma unroll
     for (int r = 0; r < R; ++r)
 #pragma unroll
         for (int h = 0; h < H; ++h) acc[r][h] = 0.0;
+#pragma unroll 1
+    for (int grp = 0; grp < D / 32; ++grp) {
+        uint32_t w[R][KB];
 #pragma unroll
-    for (int j = 0; j < D; ++j) {
-        double c[R];
+        for (int r = 0; r < R; ++r) {
+            const uint32_t *src = reinterpret_cast<const uint32_t *>(krow[r]) + grp * KB;
 #pragma unroll
-        for (int r = 0; r < R; ++r) c[r] = __hiloint2double((int)khi[code_at<KB>(w[r], j, KB)], 0);
+            for (int i = 0; i < KB; ++i) w[r][i] = valid[r] ? src[i] : 0u;
+        }
+        const double *qg = qd + grp * 32;
 #pragma unroll
-        for (int h = 0; h < H; ++h) {
-            const double qv = qd[h * D + j];
+        for (int jj = 0; jj < 32; ++jj) {
+            double c[R];
 #pragma unroll
-            for (int r = 0; r < R; ++r) acc[r][h] = fma(qv, c[r], acc[r][h]);
+            for (int r = 0; r < R; ++r)
+                c[r] = __hiloint2double((int)khi[code_at<KB>(w[r], jj, KB)], 0);
+#pragma unroll
+            for (int h = 0; h < H; ++h) {
+                const double qv = qg[h * D + jj];
+#pragma unroll
+                for (int r = 0; r < R; ++r) acc[r][h] = fma(qv, c[r], acc[r][h]);
+            }
+            if ((jj & (INS_JGROUP - 1)) == INS_JGROUP - 1) asm volatile("" ::: "memory");
         }
     }
 #pragma unroll
@@ -193,29 +219,187 @@ __device__ __forceinline__ void score_rows(const Geo &g, const uint8_t *const *k
         }
 }
 
-__device__ __forceinline__ int64_t ld_volatile(const long long *p) {
+__device__ __forceinline__ long long ld_volatile(const long long *p) {
     return *reinterpret_cast<const volatile long long *>(p);
 }
 __device__ __forceinline__ unsigned long long ld_volatile(const unsigned long long *p) {
     return *reinterpret_cast<const volatile unsigned long long *>(p);
 }
 
+template <class T>
+__device__ __forceinline__ T ldcg(const T *p) {
+    return __ldcg(p);
+}
+
+// Level 1: fold the chunks of block `blk` of `item` into a BlockRec.
+// Threads [0, H*64) own (head, channel) pairs.
+template <int H>
+__device__ void merge_block(const ChunkArgs &a, int item, int blk, int nchunks,
+                            int *base_sm /* [H] */) {
+    const int tid = threadIdx.x;
+    const bool own = tid < H * D;
+    const int h = own ? tid / D : 0, ch = tid % D;
+    const int c0 = blk * GBLK, c1 = min(nchunks, c0 + GBLK);
+    const ChunkRec *recs = a.recs + (int64_t)item * a.max_chunks;
+    // entries this head needs = rescales in the block's chunks
+    if (own && ch == 0) {
+        int need = 0;
+        for (int c = c0; c < c1; ++c) need += ldcg(&recs[c].nseg[h]);
+        unsigned b = 0;
+        if (need) b = atomicAdd(a.seg_top, (unsigned)need);
+        if (need && b + need > (unsigned)a.seg_cap) {
+            atomicExch(&a.items[item].fail, 1);
+            need = 0;
+        }
+        base_sm[h] = need ? (int)b : -1;
+    }
+    __syncthreads();
+    if (own) {
+        const int eb = base_sm[h];
+        int64_t loc = 0, Y = 0, curS = 0, curl = 0, Spre = 0, lpre = 0;
+        int ne = 0;
+        bool opened = false;
+        for (int cb = c0; cb < c1; cb += 8) {
+            int32_t S0[8], ns[8], sb[8];
+            int64_t Bk[8], l0[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int c = cb + u;
+                if (c < c1) {
+                    S0[u] = ldcg(&recs[c].S0[h][ch]);
+                    Bk[u] = ldcg(&recs[c].B[h]);
+                    l0[u] = ldcg(&recs[c].l0[h]);
+                    ns[u] = ldcg(&recs[c].nseg[h]);
+                    sb[u] = ldcg(&recs[c].seg_base[h]);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                if (cb + u >= c1) break;
+                const int64_t al = loc < 0 ? -loc : loc;
+                Y = max(Y, al + Bk[u]);
+                loc += S0[u];
+                curS += S0[u];
+                curl += l0[u];
+                for (int e = 0; e < ns[u]; ++e) {
+                    const SegEntry &se = a.segs[sb[u] + e];
+                    const int64_t f = ldcg(&se.f);
+                    const int64_t sS = ldcg(&se.S[ch]);
+                    const int64_t sl = ldcg(&se.l);
+                    if (eb >= 0) {
+                        if (!opened) {
+                            Spre = curS;
+                            lpre = curl;
+                            opened = true;
+                        } else {
+                            a.segs[eb + ne - 1].S[ch] = curS;
+                            if (ch == 0) a.segs[eb + ne - 1].l = curl;
+                        }
+                        if (ch == 0) a.segs[eb + ne].f = (int32_t)f;
+                        ++ne;
+                    }
+                    curS = sS;
+                    curl = sl;
+                    loc = ((loc * f) >> a.g.prob_frac) + sS;
+                }
+            }
+        }
+        if (!opened) {
+            Spre = curS;
+            lpre = curl;
+        } else if (eb >= 0) {
+            a.segs[eb + ne - 1].S[ch] = curS;
+            if (ch == 0) a.segs[eb + ne - 1].l = curl;
+        }
+        BlockRec &br = a.blks[(int64_t)item * a.max_blocks + blk];
+        br.Spre[h][ch] = Spre;
+        br.Y[h][ch] = Y;
+        if (ch == 0) {
+            br.lpre[h] = lpre;
+            br.nent[h] = eb >= 0 ? ne : 0;
+            br.ent_base[h] = eb >= 0 ? eb : 0;
+        }
+    }
+}
+
+// Level 2: fold the item's blocks; finalize or mark the item for the exact
+// sequential recomputation.
+template <int H>
+__device__ void merge_item(const ChunkArgs &a, int item, int nblocks, int64_t T,
+                           int64_t qbase, long long *maxs_sm) {
+    const int tid = threadIdx.x;
+    const bool own = tid < H * D;
+    const int h = own ? tid / D : 0, ch = tid % D;
+    const BlockRec *blks = a.blks + (int64_t)item * a.max_blocks;
+    int64_t acc = 0, l = 0;
+    bool bad = *reinterpret_cast<volatile int32_t *>(&a.items[item].fail) != 0;
+    if (own && !bad) {
+        for (int bb = 0; bb < nblocks; ++bb) {
+            const BlockRec &br = blks[bb];
+            const int64_t Y = ldcg(&br.Y[h][ch]);
+            const int64_t Sp = ldcg(&br.Spre[h][ch]);
+            const int64_t lp = ldcg(&br.lpre[h]);
+            const int ne = ldcg(&br.nent[h]);
+            const int eb = ldcg(&br.ent_base[h]);
+            const int64_t aa = acc < 0 ? -acc : acc;
+            if (aa + Y > INT32_MAX) bad = true;
+            acc += Sp;
+            l += lp;
+            for (int e = 0; e < ne; ++e) {
+                const SegEntry &se = a.segs[eb + e];
+                const int64_t f = ldcg(&se.f);
+                acc = ((acc * f) >> a.g.prob_frac) + ldcg(&se.S[ch]);
+                l = ((l * f) >> a.g.prob_frac) + ldcg(&se.l);
+            }
+        }
+    }
+    bad = __syncthreads_or(bad);
+    if (tid == 0) {
+        a.redo[item] = bad ? 1 : 0;
+        *maxs_sm = 0;
+    }
+    if (bad) return;
+    int64_t *out_row = a.out + qbase;
+    long long mx = 0;
+    if (own) {
+        int64_t r;
+        int shift;
+        reciprocal(a.g, l, r, shift);
+        out_row[h * D + ch] = (acc * r) >> shift;
+        mx = acc < 0 ? -acc : acc;
+    }
+    __syncthreads();
+    if (own) atomicMax(maxs_sm, mx);
+    __syncthreads();
+    if (tid == 0 && a.stats) {
+        const volatile ItemAcc &ia = a.items[item];
+        ins_stats st;
+        st.n_tokens = T;
+        st.rescale_events = (int64_t)ia.resc;
+        st.score_overflows = (int64_t)ia.sovf;
+        st.acc_overflows = 0;
+        st.max_abs_score = ia.maxs;
+        st.max_abs_acc = *maxs_sm;
+        a.stats[item] = st;
+    }
+}
+
 template <int H, int KB, int VB>
 __global__ void __launch_bounds__(H * 64 > 256 ? H * 64 : 256, H * 64 > 256 ? 1 : 2)
     k_scan_chunk(ChunkArgs a) {
     using L = ChunkLayout<H, VB>;
-    constexpr int NC = L::NC, SUB = L::SUB, VW = L::VW;
+    constexpr int NC = L::NC, SUB = L::SUB, VW = L::VW, PS = L::PS;
     constexpr int NT = H * 64 > 256 ? H * 64 : 256;
-    constexpr int R = 4;                             // rows per thread in the score phase
+    constexpr int R = INS_SCORE_ROWS;                // rows per thread in the score phase
     extern __shared__ __align__(16) uint8_t dyn[];
-    __shared__ SeqSmem<H> seqsm;                     // the fallback's own state
     __shared__ double qd[H * D];
     __shared__ uint32_t khi[256];
     __shared__ int32_t vcent[256];
     __shared__ int32_t exp_tab[256];
     __shared__ long long cmax[H], m_in_sm[H];
-    __shared__ int tile_sm, merge_sm, fail_sm;
-    __shared__ int nseg_sm[H], segbase_sm[H];
+    __shared__ int tile_sm, flag_sm, fail_sm;
+    __shared__ int nseg_sm[H], segbase_sm[H], base_sm[H];
+    __shared__ int32_t rl_f[H][SEGMAX];
     __shared__ unsigned long long lsum_sm[H][SEGMAX + 1];
     __shared__ long long bsum_sm[H];
     __shared__ unsigned long long resc_sm;
@@ -226,13 +410,17 @@ __global__ void __launch_bounds__(H * 64 > 256 ? H * 64 : 256, H * 64 > 256 ? 1 
     const Geo &g = a.g;
     const int tid = threadIdx.x;
     const L lay(a.C);
+    const int CW = a.C / 32;
     int64_t *s_sm = reinterpret_cast<int64_t *>(dyn + lay.off_s);
     int32_t *p_sm = reinterpret_cast<int32_t *>(dyn + lay.off_p);
     uint32_t *vt = reinterpret_cast<uint32_t *>(dyn + lay.off_vt);
     int32_t *vn_sm = reinterpret_cast<int32_t *>(dyn + lay.off_vn);
     int32_t *tab = reinterpret_cast<int32_t *>(dyn + lay.off_tab);
-    uint32_t *grew = reinterpret_cast<uint32_t *>(dyn + lay.off_grew);
-    uint32_t *anyg = reinterpret_cast<uint32_t *>(dyn + lay.off_any);
+    uint32_t *grew = reinterpret_cast<uint32_t *>(dyn + lay.off_grew);   // [H][CW], then any [CW]
+    uint32_t *anyg = grew + H * CW;
+    int32_t *gpre = reinterpret_cast<int32_t *>(dyn + lay.off_pre);     // [H][CW]
+    long long *bmax = reinterpret_cast<long long *>(dyn + lay.off_bmax);  // [H][CW]
+    long long *bcar = reinterpret_cast<long long *>(dyn + lay.off_bcar);  // [H][CW]
     int32_t *s0p = reinterpret_cast<int32_t *>(dyn + lay.off_s0);
 
     for (int i = tid; i < 256; i += NT) {
@@ -275,8 +463,7 @@ __global__ void __launch_bounds__(H * 64 > 256 ? H * 64 : 256, H * 64 > 256 ? 1 
             maxs_sm = 0;
             fail_sm = 0;
         }
-        for (int i = tid; i < H * (a.C / 32); i += NT) grew[i] = 0;
-        for (int i = tid; i < a.C / 32; i += NT) anyg[i] = 0;
+        for (int i = tid; i < (H + 1) * CW; i += NT) grew[i] = 0;
         for (int i = tid; i < H * D; i += NT) s0p[i] = 0;
         __syncthreads();
         bool big = false;
@@ -325,14 +512,22 @@ __global__ void __launch_bounds__(H * 64 > 256 ? H * 64 : 256, H * 64 > 256 ? 1 
                 score_rows<H, KB, R>(g, krow, knorm, valid, qd, khi, s, ovf);
 #pragma unroll
                 for (int r = 0; r < R; ++r) {
-                    if (!valid[r]) continue;
                     const int row = base + r * NT + tid;
 #pragma unroll
                     for (int h = 0; h < H; ++h) {
-                        s_sm[h * a.C + row] = s[r][h];
-                        hmax[h] = s[r][h] > hmax[h] ? s[r][h] : hmax[h];
-                        const long long ab = s[r][h] < 0 ? -s[r][h] : s[r][h];
-                        mx = ab > mx ? ab : mx;
+                        long long bm = valid[r] ? s[r][h] : LLONG_MIN;
+                        if (valid[r]) {
+                            s_sm[h * a.C + row] = s[r][h];
+                            const long long ab = s[r][h] < 0 ? -s[r][h] : s[r][h];
+                            mx = ab > mx ? ab : mx;
+                        }
+#pragma unroll
+                        for (int o = 16; o > 0; o >>= 1) {
+                            const long long w = __shfl_xor_sync(FULL, bm, o);
+                            bm = w > bm ? w : bm;
+                        }
+                        hmax[h] = bm > hmax[h] ? bm : hmax[h];
+                        if ((tid & 31) == 0 && row < a.C) bmax[h * CW + (row >> 5)] = bm;
                     }
                 }
             }
@@ -352,32 +547,54 @@ __global__ void __launch_bounds__(H * 64 > 256 ? H * 64 : 256, H * 64 > 256 ? 1 
             __threadfence();
             __syncwarp();
             if (lane == 0) atomicExch(&flags[c], (a.epoch << 2) | 1ull);
-            long long m_in = s_lo;
+            // Warp-parallel look-back: lane i inspects chunk p_hi - i. Every
+            // predecessor up to the nearest one that published an inclusive
+            // maximum contributes its (aggregate or inclusive) maximum.
+            long long m_in[H];
+#pragma unroll
+            for (int h = 0; h < H; ++h) m_in[h] = s_lo;
             bool timed_out = false;
-            for (int p = c - 1; p >= 0; --p) {
-                unsigned long long f = 0;
-                int it = 0;
-                for (; it < LB_SPIN_LIMIT; ++it) {
-                    f = ld_volatile(&flags[p]);
-                    if ((f >> 2) == a.epoch && (f & 3ull)) break;
-                    __nanosleep(64);
-                }
-                if (it == LB_SPIN_LIMIT) {
-                    timed_out = true;
-                    break;
+            for (int p_hi = c - 1; p_hi >= 0; p_hi -= 32) {
+                const int p = p_hi - lane;
+                int state = 2;                     // before chunk 0: inclusive of nothing
+                if (p >= 0) {
+                    unsigned long long f = 0;
+                    int it = 0;
+                    for (; it < LB_SPIN_LIMIT; ++it) {
+                        f = ld_volatile(&flags[p]);
+                        if ((f >> 2) == a.epoch && (f & 3ull)) break;
+                        __nanosleep(32);
+                    }
+                    if (it == LB_SPIN_LIMIT) {
+                        timed_out = true;
+                        f = (a.epoch << 2) | 2ull;  // stop here; the item is recomputed
+                    }
+                    state = (int)(f & 3ull);
                 }
                 __threadfence();
-                const bool incl = (f & 3ull) == 2ull;
-                if (lane < H) {
-                    const long long v = ld_volatile(&vals[(int64_t)p * 2 * HMAX + (incl ? HMAX : 0) + lane]);
-                    m_in = v > m_in ? v : m_in;
+                const uint32_t incl = __ballot_sync(FULL, state == 2);
+                const int stop = incl ? __ffs(incl) - 1 : 31;
+#pragma unroll
+                for (int h = 0; h < H; ++h) {
+                    long long v = s_lo;
+                    if (p >= 0 && lane <= stop)
+                        v = ld_volatile(&vals[(int64_t)p * 2 * HMAX + (state == 2 ? HMAX : 0) + h]);
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) {
+                        const long long w = __shfl_xor_sync(FULL, v, o);
+                        v = w > v ? w : v;
+                    }
+                    m_in[h] = v > m_in[h] ? v : m_in[h];
                 }
-                if (incl) break;
+                if (__any_sync(FULL, timed_out) || incl) break;
             }
-            if (lane < H) {
-                m_in_sm[lane] = m_in;
-                const long long inc = cmax[lane] > m_in ? cmax[lane] : m_in;
-                vals[(int64_t)c * 2 * HMAX + HMAX + lane] = inc;
+            timed_out = __any_sync(FULL, timed_out);
+            if (lane == 0) {
+#pragma unroll
+                for (int h = 0; h < H; ++h) {
+                    m_in_sm[h] = m_in[h];
+                    vals[(int64_t)c * 2 * HMAX + HMAX + h] = cmax[h] > m_in[h] ? cmax[h] : m_in[h];
+                }
             }
             __threadfence();
             __syncwarp();
@@ -391,80 +608,90 @@ __global__ void __launch_bounds__(H * 64 > 256 ? H * 64 : 256, H * 64 > 256 ? 1 
         }
         __syncthreads();
 
-        // ---- 3. the online control: running max, rescale points, p ---------------
+        // ---- 3. the online control, one warp per head -----------------------------
+        // Lane b holds 32-row block b. A prefix-max over the block maxima gives the
+        // running maximum entering every block. A block whose maximum does not
+        // exceed it has no rescale point and one running maximum for all its
+        // tokens (p is then computed in the term build). Only the rare blocks
+        // that can rescale are scanned token by token here: rescale points
+        // (ballot bits), factors exp(s - m_old), p, and their l per segment.
         if (tid < H * 32) {
             const int h = tid >> 5, lane = tid & 31;
-            const int64_t *s = s_sm + h * a.C;
-            const int per = (n + 31) / 32;
-            const int ta = lane * per, tb = min(n, ta + per);
-            int64_t lmax = LLONG_MIN;
-            for (int t = ta; t < tb; ++t) lmax = s[t] > lmax ? s[t] : lmax;
-            int64_t incl = lmax;
-#pragma unroll
-            for (int off = 1; off < 32; off <<= 1) {
-                const int64_t o = __shfl_up_sync(FULL, incl, off);
-                if (lane >= off) incl = o > incl ? o : incl;
-            }
-            int64_t excl = __shfl_up_sync(FULL, incl, 1);
+            const int nb = (n + 31) / 32;
             const int64_t m_in = m_in_sm[h];
-            if (lane == 0) excl = LLONG_MIN;
-            int64_t run = excl > m_in ? excl : m_in;
-            int cnt = 0;
-            unsigned long long lpart = 0;
-            for (int t = ta; t < tb; ++t) {
-                const int64_t st = s[t];
-                if (st > run) {
-                    run = st;
-                    ++cnt;
-                    atomicOr(&grew[h * (a.C / 32) + (t >> 5)], 1u << (t & 31));
-                    atomicOr(&anyg[t >> 5], 1u << (t & 31));
-                }
-                const int32_t pv = exp_lut(g, exp_tab, run - st);
-                p_sm[h * a.C + t] = pv;
-                lpart += (unsigned long long)pv;
-            }
-            // segment index of this lane's first token = rescales before it
-            int before = cnt;
+            int64_t x = lane < nb ? bmax[h * CW + lane] : LLONG_MIN;
 #pragma unroll
             for (int off = 1; off < 32; off <<= 1) {
-                const int o = __shfl_up_sync(FULL, before, off);
-                if (lane >= off) before += o;
+                const int64_t y = __shfl_up_sync(FULL, x, off);
+                if (lane >= off) x = y > x ? y : x;
             }
-            before -= cnt;
-            const int total = __shfl_sync(FULL, before + cnt, 31);
+            int64_t car = __shfl_up_sync(FULL, x, 1);
+            if (lane == 0) car = LLONG_MIN;
+            car = car > m_in ? car : m_in;
+            const bool scanb = lane < nb && bmax[h * CW + lane] > car;
+            if (lane < CW) {
+                bcar[h * CW + lane] = car;
+                grew[h * CW + lane] = 0u;
+            }
             __syncwarp();
-            if (cnt == 0) {
-                if (lpart && before <= SEGMAX) atomicAdd(&lsum_sm[h][before], lpart);
-            } else {
-                // a lane whose range holds a rescale splits its sum per segment
-                int seg = before;
-                int64_t rr = run;  // recompute the walk to split at rescale points
-                rr = excl > m_in ? excl : m_in;
-                unsigned long long acc = 0;
-                for (int t = ta; t < tb; ++t) {
-                    if (s[t] > rr) {
-                        if (seg <= SEGMAX && acc) atomicAdd(&lsum_sm[h][seg], acc);
-                        acc = 0;
-                        ++seg;
-                        rr = s[t];
-                    }
-                    acc += (unsigned long long)p_sm[h * a.C + t];
+            uint32_t todo = __ballot_sync(FULL, scanb);
+            int nres = 0;                              // rescales found in this head
+            int blkres = 0;                            // this lane's block's rescales
+            while (todo) {
+                const int bb = __ffs(todo) - 1;
+                todo &= todo - 1;
+                const int t = bb * 32 + lane;
+                const bool valid = t < n;
+                const int64_t st = valid ? s_sm[h * a.C + t] : LLONG_MIN;
+                const int64_t carry = __shfl_sync(FULL, car, bb);
+                int64_t y = st;
+#pragma unroll
+                for (int off = 1; off < 32; off <<= 1) {
+                    const int64_t z = __shfl_up_sync(FULL, y, off);
+                    if (lane >= off) y = z > y ? z : y;
                 }
-                if (seg <= SEGMAX && acc) atomicAdd(&lsum_sm[h][seg], acc);
+                const int64_t yprev = __shfl_up_sync(FULL, y, 1);
+                const int64_t Mprev = lane == 0 ? carry : (yprev > carry ? yprev : carry);
+                const int64_t Mt = y > carry ? y : carry;
+                const bool gr = valid && st > Mprev;
+                const uint32_t mask = __ballot_sync(FULL, gr);
+                if (lane == 0) grew[h * CW + bb] = mask;
+                if (valid) p_sm[h * a.C + t] = exp_lut32(g, exp_tab, Mt - st);
+                // the factor of every rescale point of this block, in order
+                const int k = nres + __popc(mask & ((1u << lane) - 1u));
+                if (gr && k < SEGMAX) rl_f[h][k] = exp_lut(g, exp_tab, st - Mprev);
+                if (lane == bb) blkres = __popc(mask);
+                nres += __popc(mask);
             }
+            // rescales before each block
+            int pre = blkres;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const int z = __shfl_up_sync(FULL, pre, off);
+                if (lane >= off) pre += z;
+            }
+            pre -= blkres;
+            if (lane < CW) gpre[h * CW + lane] = pre;
             if (lane == 0) {
-                nseg_sm[h] = total;
-                atomicAdd(&resc_sm, (unsigned long long)total);
+                nseg_sm[h] = nres;
+                atomicAdd(&resc_sm, (unsigned long long)nres);
             }
         }
         __syncthreads();
-
+        for (int i = tid; i < CW; i += NT) {
+            uint32_t m = 0;
+#pragma unroll
+            for (int h = 0; h < H; ++h) m |= grew[h * CW + i];
+            anyg[i] = m;
+        }
         // segment slots in the pool, zeroed for the atomic partial sums
         if (tid == 0) {
             int need = 0;
-            for (int h = 0; h < H; ++h) need += nseg_sm[h];
             bool ok = true;
-            for (int h = 0; h < H; ++h) ok &= nseg_sm[h] <= SEGMAX;
+            for (int h = 0; h < H; ++h) {
+                need += nseg_sm[h];
+                ok &= nseg_sm[h] <= SEGMAX;
+            }
             unsigned base = 0;
             if (need && ok) {
                 base = atomicAdd(a.seg_top, (unsigned)need);
@@ -477,7 +704,7 @@ __global__ void __launch_bounds__(H * 64 > 256 ? H * 64 : 256, H * 64 > 256 ? 1 
             int acc = 0;
             for (int h = 0; h < H; ++h) {
                 segbase_sm[h] = ok ? (int)base + acc : 0;
-                acc += nseg_sm[h];
+                acc += ok ? nseg_sm[h] : 0;
             }
         }
         __syncthreads();
@@ -487,6 +714,7 @@ __global__ void __launch_bounds__(H * 64 > 256 ? H * 64 : 256, H * 64 > 256 ? 1 
                 for (int k = 0; k < nseg_sm[h]; ++k) {
                     SegEntry &e = a.segs[segbase_sm[h] + k];
                     for (int i = tid; i < D; i += NT) e.S[i] = 0;
+                    if (tid == 0) e.f = rl_f[h][k];
                 }
         }
         __syncthreads();
@@ -497,50 +725,91 @@ __global__ void __launch_bounds__(H * 64 > 256 ? H * 64 : 256, H * 64 > 256 ? 1 
             constexpr int TG = NT / D;
             int32_t acc[H];
             int cur[H];
-#pragma unroll
-            for (int h = 0; h < H; ++h) acc[h] = 0;
             long long bnd[H];
 #pragma unroll
-            for (int h = 0; h < H; ++h) bnd[h] = 0;
-            // where this thread's channel sits in a V row
+            for (int h = 0; h < H; ++h) {
+                acc[h] = 0;
+                bnd[h] = 0;
+            }
             const int bit0 = ch * VB, w0 = bit0 >> 5, sh0 = bit0 & 31;
             const bool straddle = sh0 + VB > 32;
+            const uint32_t cmask = (1u << VB) - 1u;
+            int64_t cmax_v = 0;
+#pragma unroll
+            for (int k = 0; k < NC; ++k) {
+                const int64_t ab = vcent[k] < 0 ? -(int64_t)vcent[k] : vcent[k];
+                cmax_v = ab > cmax_v ? ab : cmax_v;
+            }
+            const uint32_t *vw = vt + w0 * a.C;
             for (int st = 0; st < n; st += SUB) {
                 const int ns = min(SUB, n - st);
-                // build the term table of this sub-tile: [t][code][h]
-                for (int tl = tid; tl < ns; tl += NT) {
-                    const int t = st + tl;
-                    const int64_t vnt = vn_sm[t];
+                // the term table of this sub-tile: [code][t][h], one token per thread
+                for (int tl0 = 0; tl0 < ns; tl0 += NT) {
+                    const int tl = tl0 + tid;
+                    const bool tv = tl < ns;
+                    const int t = st + (tv ? tl : 0);
+                    const int blkt = t >> 5;
+                    const int32_t vnt = tv ? vn_sm[t] : 0;
+                    int32_t term[NC][H];
 #pragma unroll
                     for (int h = 0; h < H; ++h) {
-                        const int64_t w = vnt * (int64_t)p_sm[h * a.C + t];
-                        int64_t mxk = 0;
+                        // p: from the scan for a block that rescales, else from its
+                        // single running maximum
+                        const uint32_t gw = grew[h * CW + blkt];
+                        const bool quiet = bmax[h * CW + blkt] <= bcar[h * CW + blkt];
+                        int32_t pv = 0;
+                        if (tv) pv = quiet ? exp_lut32(g, exp_tab, bcar[h * CW + blkt] - s_sm[h * a.C + t])
+                                           : p_sm[h * a.C + t];
+                        // l of the segment the token belongs to
+                        const int seg = gpre[h * CW + blkt] + __popc(gw & ((2u << (t & 31)) - 1u));
+                        const int seg0 = __shfl_sync(FULL, seg, 0);
+                        if (__all_sync(FULL, seg == seg0)) {
+                            unsigned sum = (unsigned)pv;
 #pragma unroll
-                        for (int k = 0; k < NC; ++k) {
-                            const int64_t term = (w * (int64_t)vcent[k]) >> g.acc_shift;
-                            tab[(tl * NC + k) * H + h] = (int32_t)term;
-                            const int64_t ab = term < 0 ? -term : term;
-                            mxk = ab > mxk ? ab : mxk;
+                            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(FULL, sum, o);
+                            if ((tid & 31) == 0 && sum && seg0 <= SEGMAX)
+                                atomicAdd(&lsum_sm[h][seg0], (unsigned long long)sum);
+                        } else if (tv && pv && seg <= SEGMAX) {
+                            atomicAdd(&lsum_sm[h][seg], (unsigned long long)pv);
                         }
-                        bnd[h] += mxk;
+                        const int32_t w = vnt * pv;                    // |w| <= 2^30
+#pragma unroll
+                        for (int k = 0; k < NC; ++k)
+                            term[k][h] = (int32_t)(((int64_t)w * (int64_t)vcent[k]) >> g.acc_shift);
+                        // |term| <= floor(|w| * max|c| / 2^acc_shift) + 1 for every code
+                        const int64_t aw = w < 0 ? -(int64_t)w : (int64_t)w;
+                        bnd[h] += ((aw * cmax_v) >> g.acc_shift) + 1;
+                    }
+#pragma unroll
+                    if (tv)
+#pragma unroll
+                    for (int k = 0; k < NC; ++k) {
+                        int32_t *dst = tab + k * PS + tl * H;
+                        if constexpr (H == 4) {
+                            *reinterpret_cast<int4 *>(dst) =
+                                make_int4(term[k][0], term[k][1], term[k][2], term[k][3]);
+                        } else if constexpr (H == 8) {
+                            reinterpret_cast<int4 *>(dst)[0] =
+                                make_int4(term[k][0], term[k][1], term[k][2], term[k][3]);
+                            reinterpret_cast<int4 *>(dst)[1] =
+                                make_int4(term[k][4], term[k][5], term[k][6], term[k][7]);
+                        } else {
+#pragma unroll
+                            for (int h = 0; h < H; ++h) dst[h] = term[k][h];
+                        }
                     }
                 }
                 __syncthreads();
-                // this thread's tokens of the sub-tile
                 const int per = (ns + TG - 1) / TG;
                 const int ta = st + tg * per, tb = min(st + ns, ta + per);
                 if (ta < tb) {
-                    // segment of each head at ta
 #pragma unroll
-                    for (int h = 0; h < H; ++h) {
-                        int k = 0;
-                        for (int wd = 0; wd < (ta >> 5); ++wd) k += __popc(grew[h * (a.C / 32) + wd]);
-                        k += __popc(grew[h * (a.C / 32) + (ta >> 5)] & ((1u << (ta & 31)) - 1u));
-                        cur[h] = k;
-                    }
+                    for (int h = 0; h < H; ++h)
+                        cur[h] = gpre[h * CW + (ta >> 5)] +
+                                 __popc(grew[h * CW + (ta >> 5)] & ((1u << (ta & 31)) - 1u));
+                    const int32_t *tab_t = tab - st * H;   // index with t directly
                     int t = ta;
                     while (t < tb) {
-                        // next token in [t, tb) where some head rescales
                         int nxt = tb;
                         for (int wd = t >> 5; wd <= ((tb - 1) >> 5); ++wd) {
                             uint32_t m = anyg[wd];
@@ -550,50 +819,68 @@ __global__ void __launch_bounds__(H * 64 > 256 ? H * 64 : 256, H * 64 > 256 ? 1 
                                 break;
                             }
                         }
-                        for (; t < nxt; ++t) {
-                            uint32_t wv = vt[w0 * a.C + t] >> sh0;
-                            if (straddle) wv |= vt[(w0 + 1) * a.C + t] << (32 - sh0);
-                            const int code = (int)(wv & ((1u << VB) - 1u));
-                            const int32_t *tt = tab + ((t - st) * NC + code) * H;
+                        auto one = [&](int tt) {
+                            uint32_t wv = vw[tt] >> sh0;
+                            if (straddle) wv |= vw[a.C + tt] << (32 - sh0);
+                            const int32_t *e = tab_t + (int)(wv & cmask) * PS + tt * H;
                             if constexpr (H == 4) {
-                                const int4 v4 = *reinterpret_cast<const int4 *>(tt);
+                                const int4 v4 = *reinterpret_cast<const int4 *>(e);
                                 acc[0] += v4.x;
                                 acc[1] += v4.y;
                                 acc[2] += v4.z;
                                 acc[3] += v4.w;
                             } else {
 #pragma unroll
-                                for (int h = 0; h < H; ++h) acc[h] += tt[h];
+                                for (int h = 0; h < H; ++h) acc[h] += e[h];
+                            }
+                        };
+                        for (; t < nxt && (t & 3); ++t) one(t);
+                        if constexpr (H == 4 && !(VB == 3)) {
+                            for (; t + 4 <= nxt; t += 4) {
+                                const uint4 w4 = *reinterpret_cast<const uint4 *>(vw + t);
+                                const int32_t *e0 = tab_t + (int)((w4.x >> sh0) & cmask) * PS + t * H;
+                                const int32_t *e1 = tab_t + (int)((w4.y >> sh0) & cmask) * PS + (t + 1) * H;
+                                const int32_t *e2 = tab_t + (int)((w4.z >> sh0) & cmask) * PS + (t + 2) * H;
+                                const int32_t *e3 = tab_t + (int)((w4.w >> sh0) & cmask) * PS + (t + 3) * H;
+                                const int4 a0 = *reinterpret_cast<const int4 *>(e0);
+                                const int4 a1 = *reinterpret_cast<const int4 *>(e1);
+                                const int4 a2 = *reinterpret_cast<const int4 *>(e2);
+                                const int4 a3 = *reinterpret_cast<const int4 *>(e3);
+                                acc[0] += a0.x + a1.x;
+                                acc[1] += a0.y + a1.y;
+                                acc[2] += a0.z + a1.z;
+                                acc[3] += a0.w + a1.w;
+                                acc[0] += a2.x + a3.x;
+                                acc[1] += a2.y + a3.y;
+                                acc[2] += a2.z + a3.z;
+                                acc[3] += a2.w + a3.w;
                             }
                         }
+                        for (; t < nxt; ++t) one(t);
                         if (t < tb) {
-                            // token t starts a new segment for the heads that grew
+                            // token t opens a new segment for the heads that grew
 #pragma unroll
                             for (int h = 0; h < H; ++h) {
-                                if ((grew[h * (a.C / 32) + (t >> 5)] >> (t & 31)) & 1u) {
+                                if ((grew[h * CW + (t >> 5)] >> (t & 31)) & 1u) {
                                     if (cur[h] == 0) atomicAdd(&s0p[h * D + ch], acc[h]);
                                     else if (seg_ok)
-                                        atomicAdd(&a.segs[segbase_sm[h] + cur[h] - 1].S[ch], acc[h]);
+                                        atomicAdd((unsigned long long *)&a.segs[segbase_sm[h] + cur[h] - 1].S[ch],
+                                                  (unsigned long long)(long long)acc[h]);
                                     acc[h] = 0;
                                     ++cur[h];
                                 }
                             }
-                            uint32_t wv = vt[w0 * a.C + t] >> sh0;
-                            if (straddle) wv |= vt[(w0 + 1) * a.C + t] << (32 - sh0);
-                            const int code = (int)(wv & ((1u << VB) - 1u));
-                            const int32_t *tt = tab + ((t - st) * NC + code) * H;
-#pragma unroll
-                            for (int h = 0; h < H; ++h) acc[h] += tt[h];
+                            one(t);
                             ++t;
                         }
                     }
-                    // flush to the segment each head ended the range in
 #pragma unroll
                     for (int h = 0; h < H; ++h) {
                         if (acc[h]) {
                             if (cur[h] == 0) atomicAdd(&s0p[h * D + ch], acc[h]);
                             else if (seg_ok)
-                                atomicAdd(&a.segs[segbase_sm[h] + cur[h] - 1].S[ch], acc[h]);
+                                atomicAdd((unsigned long long *)&a.segs[segbase_sm[h] + cur[h] - 1].S[ch],
+                                          (unsigned long long)(long long)acc[h]);
                         }
                         acc[h] = 0;
                     }
@@ -601,10 +888,18 @@ __global__ void __launch_bounds__(H * 64 > 256 ? H * 64 : 256, H * 64 > 256 ? 1 
                 __syncthreads();
             }
 #pragma unroll
-            for (int h = 0; h < H; ++h)
-                if (bnd[h]) atomicAdd((unsigned long long *)&bsum_sm[h], (unsigned long long)bnd[h]);
+            for (int h = 0; h < H; ++h) {
+                unsigned long long v = (unsigned long long)bnd[h];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
+                if ((tid & 31) == 0 && v) atomicAdd((unsigned long long *)&bsum_sm[h], v);
+            }
         }
         __syncthreads();
+        // l of the rescale segments, now that the build has summed p
+        if (seg_ok && tid < H)
+            for (int k = 0; k < nseg_sm[tid]; ++k)
+                a.segs[segbase_sm[tid] + k].l = (int64_t)lsum_sm[tid][k + 1];
 
         // ---- 5. the chunk record ------------------------------------------------
         {
@@ -616,25 +911,6 @@ __global__ void __launch_bounds__(H * 64 > 256 ? H * 64 : 256, H * 64 > 256 ? 1 
                 rec.B[h] = bsum_sm[h];
                 rec.nseg[h] = seg_ok ? nseg_sm[h] : 0;
                 rec.seg_base[h] = segbase_sm[h];
-                if (seg_ok) {
-                    // factors and l sums of the rescale segments
-                    const int64_t *s = s_sm + h * a.C;
-                    int64_t prev = m_in_sm[h];
-                    int k = 0;
-                    for (int wd = 0; wd < (n + 31) / 32 && k < nseg_sm[h]; ++wd) {
-                        uint32_t m = grew[h * (a.C / 32) + wd];
-                        while (m) {
-                            const int t = wd * 32 + __ffs(m) - 1;
-                            m &= m - 1;
-                            SegEntry &e = a.segs[segbase_sm[h] + k];
-                            e.f = exp_lut(g, exp_tab, s[t] - prev);
-                            e.tok = t;
-                            e.l = (int64_t)lsum_sm[h][k + 1];
-                            prev = s[t];
-                            ++k;
-                        }
-                    }
-                }
             }
             if (tid == 0) {
                 ItemAcc &ia = a.items[item];
@@ -646,94 +922,43 @@ __global__ void __launch_bounds__(H * 64 > 256 ? H * 64 : 256, H * 64 > 256 ? 1 
         __threadfence();
         __syncthreads();
 
-        // ---- 6. the last chunk of an item folds the item --------------------------
+        // ---- 6. fold: the last chunk of a block folds the block, the last block
+        //         of an item folds the item ---------------------------------------
+        const int nc = a.item_nchunks[item];
+        const int blk = c / GBLK;
+        const int nblk = (nc + GBLK - 1) / GBLK;
+        const int in_blk = min(nc, blk * GBLK + GBLK) - blk * GBLK;
         if (tid == 0) {
-            const unsigned long long old = atomicAdd(&a.items[item].done, 1ull);
-            merge_sm = old + 1 == (unsigned long long)a.item_nchunks[item];
+            const unsigned old = atomicAdd(&a.blk_done[(int64_t)item * a.max_blocks + blk], 1u);
+            flag_sm = old + 1 == (unsigned)in_blk;
         }
         __syncthreads();
-        if (merge_sm) {
+        if (flag_sm) {
             __threadfence();
-            const int nc = a.item_nchunks[item];
-            const int64_t T = a.T[b];
-            bool bad = *reinterpret_cast<volatile int32_t *>(&a.items[item].fail) != 0;
-            int64_t acc_k[(H * D + NT - 1) / NT];
-            int64_t l_k[(H * D + NT - 1) / NT];
-            constexpr int KK = (H * D + NT - 1) / NT;
-#pragma unroll
-            for (int k = 0; k < KK; ++k) acc_k[k] = l_k[k] = 0;
-            if (!bad) {
-                const ChunkRec *recs = a.recs + (int64_t)item * a.max_chunks;
-                for (int cc = 0; cc < nc; ++cc) {
-                    const ChunkRec &rec = recs[cc];
-#pragma unroll
-                    for (int k = 0; k < KK; ++k) {
-                        const int i = tid + k * NT;
-                        if (i >= H * D) continue;
-                        const int h = i / D, ch = i % D;
-                        const int64_t ab = acc_k[k] < 0 ? -acc_k[k] : acc_k[k];
-                        if (ab + *reinterpret_cast<const volatile int64_t *>(&rec.B[h]) > INT32_MAX) bad = true;
-                        acc_k[k] += *reinterpret_cast<const volatile int32_t *>(&rec.S0[h][ch]);
-                        l_k[k] += *reinterpret_cast<const volatile int64_t *>(&rec.l0[h]);
-                        const int ns = *reinterpret_cast<const volatile int32_t *>(&rec.nseg[h]);
-                        const int sb = *reinterpret_cast<const volatile int32_t *>(&rec.seg_base[h]);
-                        for (int e = 0; e < ns; ++e) {
-                            const SegEntry &se = a.segs[sb + e];
-                            const int64_t f = *reinterpret_cast<const volatile int32_t *>(&se.f);
-                            acc_k[k] = (acc_k[k] * f) >> g.prob_frac;
-                            l_k[k] = (l_k[k] * f) >> g.prob_frac;
-                            acc_k[k] += *reinterpret_cast<const volatile int32_t *>(&se.S[ch]);
-                            l_k[k] += *reinterpret_cast<const volatile int64_t *>(&se.l);
-                        }
-                    }
-                }
-            }
-            bad = __syncthreads_or(bad);
-            int64_t *out_row = a.out + qbase;
-            ins_stats *st_out = a.stats ? a.stats + item : nullptr;
-            if (bad) {
-                seq_scan_item<H, KB, VB>(g, a.tb, seq, T, kvh, a.page_table, a.pool,
-                                         a.q_rot + qbase, out_row, st_out, seqsm, dyn);
-            } else {
-                long long mx = 0;
-#pragma unroll
-                for (int k = 0; k < KK; ++k) {
-                    const int i = tid + k * NT;
-                    if (i >= H * D) continue;
-                    int64_t r;
-                    int shift;
-                    reciprocal(g, l_k[k], r, shift);
-                    out_row[i] = (acc_k[k] * r) >> shift;
-                    const long long ab = acc_k[k] < 0 ? -acc_k[k] : acc_k[k];
-                    mx = ab > mx ? ab : mx;
-                }
-                if (tid == 0) maxs_sm = 0;
-                __syncthreads();
-                atomicMax(&maxs_sm, mx);
-                __syncthreads();
-                if (tid == 0 && st_out) {
-                    const volatile ItemAcc &ia = a.items[item];
-                    ins_stats st;
-                    st.n_tokens = T;
-                    st.rescale_events = (int64_t)ia.resc;
-                    st.score_overflows = (int64_t)ia.sovf;
-                    st.acc_overflows = 0;
-                    st.max_abs_score = ia.maxs;
-                    st.max_abs_acc = maxs_sm;
-                    *st_out = st;
-                }
-            }
+            merge_block<H>(a, item, blk, nc, base_sm);
+            __threadfence();
             __syncthreads();
             if (tid == 0) {
-                ItemAcc &ia = a.items[item];
-                ia.done = 0;
-                ia.resc = 0;
-                ia.sovf = 0;
-                ia.maxs = 0;
-                ia.fail = 0;
+                a.blk_done[(int64_t)item * a.max_blocks + blk] = 0;
+                const unsigned long long old = atomicAdd(&a.items[item].done_blocks, 1ull);
+                flag_sm = old + 1 == (unsigned long long)nblk;
+            }
+            __syncthreads();
+            if (flag_sm) {
+                __threadfence();
+                merge_item<H>(a, item, nblk, a.T[b], qbase, &maxs_sm);
+                __syncthreads();
+                if (tid == 0) {
+                    ItemAcc &ia = a.items[item];
+                    ia.done_blocks = 0;
+                    ia.resc = 0;
+                    ia.sovf = 0;
+                    ia.maxs = 0;
+                    ia.fail = 0;
+                }
             }
         }
-        // ---- 7. the last tile of the launch resets the shared counters ------------
+        // ---- 7. the last tile of the launch resets the pool ----------------------
         if (tid == 0) {
             __threadfence();
             const unsigned long long d = atomicAdd(a.all_done, 1ull);
@@ -774,28 +999,19 @@ inline int chunk_rows(const Geo &g, size_t smem_cap) {
     return pages * g.P;
 }
 
-template <int H, int KB, int VB>
-inline int launch_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, int32_t B,
-                          const int32_t *d_seq, const int64_t *d_T, const int64_t *h_T,
-                          const int32_t *d_pt, const uint8_t *pool, const int32_t *q_rot,
-                          int64_t *out, ins_stats *stats, int32_t *d_status, cudaStream_t s) {
+// The tile list: every item's chunks, in (chunk, item) order so a chunk is
+// always claimed after all of its predecessors.
+inline void build_tiles(const Geo &g, int32_t B, const int64_t *h_T, int C, std::vector<int4> &tiles,
+                        std::vector<int32_t> &nc, int &max_nc) {
     const int n_items = B * g.n_kv;
-    const size_t smem_cap = 100 * 1024;
-    const int C = chunk_rows<H, VB>(g, smem_cap);
-    const ChunkLayout<H, VB> lay(C);
-    size_t dyn = lay.total;
-    const size_t seqdyn = seq_dyn_smem<H>(g);
-    if (seqdyn > dyn) dyn = seqdyn;
-    // tiles in (chunk, item) order, so a chunk is always claimed after its predecessors
-    int max_nc = 1;
-    std::vector<int> nc(n_items);
+    nc.assign(n_items, 1);
+    max_nc = 1;
     for (int it = 0; it < n_items; ++it) {
         const int64_t T = h_T[it / g.n_kv];
         nc[it] = T ? (int)((T + C - 1) / C) : 1;
         max_nc = nc[it] > max_nc ? nc[it] : max_nc;
     }
-    std::vector<int4> tiles;
-    tiles.reserve((size_t)n_items * 2);
+    tiles.clear();
     for (int cidx = 0; cidx < max_nc; ++cidx)
         for (int it = 0; it < n_items; ++it)
             if (cidx < nc[it]) {
@@ -803,60 +1019,87 @@ inline int launch_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, i
                 const int64_t t0 = (int64_t)cidx * C;
                 tiles.push_back(make_int4(it, cidx, (int)t0, (int)(T - t0 < C ? T - t0 : C)));
             }
-    const int n_tiles = (int)tiles.size();
-    // scratch
-    const int seg_cap = 64 * n_items * H + 4 * n_tiles;
-    const bool grow = !cs.base || n_items > cs.n_items || max_nc > cs.max_chunks ||
-                      seg_cap > cs.seg_cap || n_tiles > cs.tile_cap;
-    if (grow) {
-        cudaStreamSynchronize(s);
-        const int ni = n_items > cs.n_items ? n_items : cs.n_items;
-        const int mc = max_nc > cs.max_chunks ? max_nc : cs.max_chunks;
-        const int sc = seg_cap > cs.seg_cap ? seg_cap : cs.seg_cap;
-        const int tc = n_tiles > cs.tile_cap ? n_tiles : cs.tile_cap;
-        cs.release();
-        auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
-        size_t o = 0;
-        const size_t o_claim = o; o += al(8);
-        const size_t o_all = o; o += al(8);
-        const size_t o_top = o; o += al(8);
-        const size_t o_flag = o; o += al(sizeof(unsigned long long) * (size_t)ni * mc);
-        const size_t o_val = o; o += al(sizeof(long long) * (size_t)ni * mc * 2 * HMAX);
-        const size_t o_rec = o; o += al(sizeof(ChunkRec) * (size_t)ni * mc);
-        const size_t o_seg = o; o += al(sizeof(SegEntry) * (size_t)sc);
-        const size_t o_items = o; o += al(sizeof(ItemAcc) * (size_t)ni);
-        const size_t o_tiles = o; o += al(sizeof(int4) * (size_t)tc);
-        const size_t o_nc = o; o += al(sizeof(int32_t) * (size_t)ni);
-        if (cudaMalloc(&cs.base, o) != cudaSuccess) {
-            cudaGetLastError();
-            cs.base = nullptr;
-            return INS_ENOMEM;
-        }
-        if (cudaMemset(cs.base, 0, o) != cudaSuccess) return INS_ECUDA;
-        uint8_t *p = (uint8_t *)cs.base;
-        cs.bytes = o;
-        cs.claim = (unsigned long long *)(p + o_claim);
-        cs.all_done = (unsigned long long *)(p + o_all);
-        cs.seg_top = (unsigned int *)(p + o_top);
-        cs.lb_flag = (unsigned long long *)(p + o_flag);
-        cs.lb_val = (long long *)(p + o_val);
-        cs.recs = (ChunkRec *)(p + o_rec);
-        cs.segs = (SegEntry *)(p + o_seg);
-        cs.items = (ItemAcc *)(p + o_items);
-        cs.tiles = (int4 *)(p + o_tiles);
-        cs.item_nchunks = (int32_t *)(p + o_nc);
-        cs.n_items = ni;
-        cs.max_chunks = mc;
-        cs.seg_cap = sc;
-        cs.tile_cap = tc;
-        cs.claim_base = 0;
+}
+
+// Carve (or grow) the scratch for n_items items of up to max_nc chunks.
+inline int reserve_scratch(ChunkScratch &cs, int n_items, int max_nc, int n_tiles, int H,
+                           cudaStream_t s) {
+    const int seg_cap = 2 * (64 * n_items * H) + 4 * n_tiles;
+    if (cs.base && n_items <= cs.n_items && max_nc <= cs.max_chunks && seg_cap <= cs.seg_cap &&
+        n_tiles <= cs.tile_cap)
+        return INS_OK;
+    cudaStreamSynchronize(s);
+    const int ni = n_items > cs.n_items ? n_items : cs.n_items;
+    const int mc = max_nc > cs.max_chunks ? max_nc : cs.max_chunks;
+    const int sc = seg_cap > cs.seg_cap ? seg_cap : cs.seg_cap;
+    const int tc = n_tiles > cs.tile_cap ? n_tiles : cs.tile_cap;
+    const int mb = (mc + GBLK - 1) / GBLK;
+    cs.release();
+    auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
+    size_t o = 0;
+    const size_t o_claim = o; o += al(8);
+    const size_t o_all = o; o += al(8);
+    const size_t o_top = o; o += al(8);
+    const size_t o_flag = o; o += al(sizeof(unsigned long long) * (size_t)ni * mc);
+    const size_t o_val = o; o += al(sizeof(long long) * (size_t)ni * mc * 2 * HMAX);
+    const size_t o_rec = o; o += al(sizeof(ChunkRec) * (size_t)ni * mc);
+    const size_t o_blk = o; o += al(sizeof(BlockRec) * (size_t)ni * mb);
+    const size_t o_bd = o; o += al(sizeof(unsigned int) * (size_t)ni * mb);
+    const size_t o_seg = o; o += al(sizeof(SegEntry) * (size_t)sc);
+    const size_t o_items = o; o += al(sizeof(ItemAcc) * (size_t)ni);
+    const size_t o_redo = o; o += al(sizeof(int32_t) * (size_t)ni);
+    const size_t o_tiles = o; o += al(sizeof(int4) * (size_t)tc);
+    const size_t o_nc = o; o += al(sizeof(int32_t) * (size_t)ni);
+    if (cudaMalloc(&cs.base, o) != cudaSuccess) {
+        cudaGetLastError();
+        cs.base = nullptr;
+        return INS_ENOMEM;
     }
+    if (cudaMemset(cs.base, 0, o) != cudaSuccess) return INS_ECUDA;
+    uint8_t *p = (uint8_t *)cs.base;
+    cs.bytes = o;
+    cs.claim = (unsigned long long *)(p + o_claim);
+    cs.all_done = (unsigned long long *)(p + o_all);
+    cs.seg_top = (unsigned int *)(p + o_top);
+    cs.lb_flag = (unsigned long long *)(p + o_flag);
+    cs.lb_val = (long long *)(p + o_val);
+    cs.recs = (ChunkRec *)(p + o_rec);
+    cs.blks = (BlockRec *)(p + o_blk);
+    cs.blk_done = (unsigned int *)(p + o_bd);
+    cs.segs = (SegEntry *)(p + o_seg);
+    cs.items = (ItemAcc *)(p + o_items);
+    cs.redo = (int32_t *)(p + o_redo);
+    cs.tiles = (int4 *)(p + o_tiles);
+    cs.item_nchunks = (int32_t *)(p + o_nc);
+    cs.n_items = ni;
+    cs.max_chunks = mc;
+    cs.seg_cap = sc;
+    cs.tile_cap = tc;
+    cs.claim_base = 0;
+    return INS_OK;
+}
+
+template <int H, int KB, int VB>
+inline int launch_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, int32_t B,
+                          const int32_t *d_seq, const int64_t *d_T, const int64_t *h_T,
+                          const int32_t *d_pt, const uint8_t *pool, const int32_t *q_rot,
+                          int64_t *out, ins_stats *stats, int32_t *d_status, cudaStream_t s) {
+    const int n_items = B * g.n_kv;
+    const int C = chunk_rows<H, VB>(g, 100 * 1024);
+    const ChunkLayout<H, VB> lay(C);
+    std::vector<int4> tiles;
+    std::vector<int32_t> nc;
+    int max_nc = 1;
+    build_tiles(g, B, h_T, C, tiles, nc, max_nc);
+    const int n_tiles = (int)tiles.size();
+    if (int rc = reserve_scratch(cs, n_items, max_nc, n_tiles, H, s)) return rc;
     if (cudaMemcpyAsync(cs.tiles, tiles.data(), sizeof(int4) * tiles.size(), cudaMemcpyHostToDevice,
                         s) != cudaSuccess ||
         cudaMemcpyAsync(cs.item_nchunks, nc.data(), sizeof(int32_t) * nc.size(),
                         cudaMemcpyHostToDevice, s) != cudaSuccess)
         return INS_ECUDA;
     auto fn = k_scan_chunk<H, KB, VB>;
+    const size_t dyn = lay.total;
     if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) != cudaSuccess)
         return INS_ECUDA;
     constexpr int NT = H * 64 > 256 ? H * 64 : 256;
@@ -874,6 +1117,7 @@ inline int launch_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, i
     a.n_tiles = n_tiles;
     a.C = C;
     a.max_chunks = cs.max_chunks;
+    a.max_blocks = (cs.max_chunks + GBLK - 1) / GBLK;
     a.n_items = n_items;
     a.item_nchunks = cs.item_nchunks;
     a.seq_ids = d_seq;
@@ -888,17 +1132,25 @@ inline int launch_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, i
     a.lb_flag = cs.lb_flag;
     a.lb_val = cs.lb_val;
     a.recs = cs.recs;
+    a.blks = cs.blks;
+    a.blk_done = cs.blk_done;
     a.segs = cs.segs;
     a.seg_top = cs.seg_top;
     a.seg_cap = cs.seg_cap;
     a.items = cs.items;
+    a.redo = cs.redo;
     a.all_done = cs.all_done;
     a.status = d_status;
     a.epoch = ++cs.epoch;
     fn<<<grid, NT, dyn, s>>>(a);
     // every tile claim and every CTA's final failing claim bump the counter once
     cs.claim_base += (unsigned long long)n_tiles + (unsigned long long)grid;
-    return cudaGetLastError() == cudaSuccess ? INS_OK : INS_ECUDA;
+    if (cudaGetLastError() != cudaSuccess) return INS_ECUDA;
+    // items whose exactness the fold could not prove are recomputed in order
+    return launch_seq<H>(g, tb, B, d_seq, d_T, d_pt, pool, q_rot, out, stats, cs.redo, s) ==
+                   cudaSuccess
+               ? INS_OK
+               : INS_ECUDA;
 }
 
 inline int launch_online(ChunkScratch &cs, const Geo &g, const DevTables *tb, int32_t B,
