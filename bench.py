@@ -1,0 +1,425 @@
+#!/usr/bin/env python
+"""Benchmark: compressed-cache scan GB/s and µs per decode step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (BASELINE config 2 at its largest context): one Llama-3.2-1B-shaped
+attention layer below the seam -- 8 KV heads x head_dim 64, 4 query heads per
+KV head, 4-bit K / 2-bit V codebooks -- holding one sequence of 1,048,576
+cached tokens per GPU. A step is one decode step of the hot path: the ingress
+of one new token (rotate q/k/v, quantise, pack, append) followed by the
+online-softmax scan of every cached row for all 32 query heads.
+
+`value` is whole-job GB/s of algorithmic cache bytes (8 KV heads x T rows x
+52 B per step, plus the 8 rows written), summed over ranks and divided by the
+slowest rank's device time, inputs already in HBM. `e2e` is the same metric
+through DecodeAttention.step with the step's q/k/v copied from pinned host
+memory and the output read back every step. Multi-GPU runs are weak scaling:
+every rank owns its own sequence (batch sharding needs no exchange).
+
+`--impl reference` times the reference algorithm on the host cores: the
+oracle's C restatement of attend_online (the reference's own numpy model is
+Python and does not travel), on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "compressed-cache scan GB/s & µs/decode-step (vs HBM peak) at ctx 32K–1M, 1/2/4/8 GPU"
+ROW_BYTES = 52
+N_KV, GROUPS, D = 8, 4, 64
+
+
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--ctx", type=int, default=1 << 20, help="cached tokens per GPU")
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    return ap.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def traffic_per_row():
+    """DRAM bytes per scanned row of the scan kernel, from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "scan_chunk_traffic.txt")
+    try:
+        for ln in open(path):
+            if ln.startswith("dram_bytes_per_row:"):
+                return float(ln.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.lines: list[str] = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.device)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# the workload
+# ---------------------------------------------------------------------------
+
+def make_decoder(ctx: int, extra: int, device: int, seed: int):
+    import torch
+    from insitu_b200 import DecodeAttention, FixedFormat, Geometry, QuantConfig
+    dec = DecodeAttention(QuantConfig(key_bits=4, value_bits=2), FixedFormat(),
+                          Geometry(N_KV, GROUPS, D), max_seqs=1, capacity=ctx + extra,
+                          page_tokens=256, device=device)
+    gen = torch.Generator(device=f"cuda:{device}")
+    gen.manual_seed(seed)
+    chunk = 1 << 17
+    for lo in range(0, ctx, chunk):
+        n = min(chunk, ctx - lo)
+        kv = (torch.randn((2, n, N_KV, D), device=f"cuda:{device}", generator=gen) * 65536.0)
+        kv = kv.round_().clamp_(-(1 << 23), (1 << 23) - 1).to(torch.int32)
+        dec.prefill(0, kv[0], kv[1])
+        del kv
+    return dec, gen
+
+
+def step_inputs(gen, n: int, device: int):
+    import torch
+    dev = f"cuda:{device}"
+    wire = lambda shape, s: (torch.randn(shape, device=dev, generator=gen) * s * 65536.0).round_(
+    ).clamp_(-(1 << 23), (1 << 23) - 1).to(torch.int32)
+    return wire((n, 1, N_KV * GROUPS, D), 1 / 8), wire((n, 1, N_KV, D), 1.0), wire((n, 1, N_KV, D), 1.0)
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    device = local if world > 1 else 0
+    torch.cuda.set_device(device)
+    K, W = args.steps, args.warmup
+    ctx = args.ctx
+
+    dec, gen = make_decoder(ctx, K + W + 8, device, seed=1234 + rank)
+    q_all, k_all, v_all = step_inputs(gen, K + W, device)
+    pc = dec.pc
+    stream = torch.cuda.current_stream(device)
+
+    def barrier():
+        torch.cuda.synchronize(device)
+        if world > 1:
+            dist.barrier()
+
+    # warm-up
+    for i in range(W):
+        q_rot = pc.ingress([0], k_all[i], v_all[i], q_all[i])
+        out, st = pc.scan([0], q_rot)
+    pc.status()
+
+    # timed: device-resident inputs
+    T0 = pc.length(0)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
+    clocks = ClockSampler(device)
+    barrier()
+    clocks.start()
+    time.sleep(0.3)
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(K):
+        ev[i][0].record(stream)
+        q_rot = pc.ingress([0], k_all[W + i], v_all[W + i], q_all[W + i])
+        ev[i][1].record(stream)
+        out, st = pc.scan([0], q_rot)
+        ev[i][2].record(stream)
+    t_end.record(stream)
+    barrier()
+    clk = clocks.stop()
+    pc.status()
+    ms_local = t_start.elapsed_time(t_end)
+    scan_ms = [ev[i][1].elapsed_time(ev[i][2]) for i in range(K)]
+    ingress_ms = [ev[i][0].elapsed_time(ev[i][1]) for i in range(K)]
+    rows = sum(N_KV * (T0 + i + 1) for i in range(K))          # rows scanned, this rank
+    bytes_local = rows * ROW_BYTES + K * N_KV * ROW_BYTES         # + rows written by ingress
+
+    # e2e through the public API, host buffers in and out every step
+    qh = [q_all[i].cpu().pin_memory() for i in range(K)]
+    kh = [k_all[i].cpu().pin_memory() for i in range(K)]
+    vh = [v_all[i].cpu().pin_memory() for i in range(K)]
+    outh = torch.empty((1, N_KV * GROUPS, D), dtype=torch.int64).pin_memory()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    T1 = pc.length(0)
+    e0.record(stream)
+    for i in range(K):
+        q = qh[i].to(f"cuda:{device}", non_blocking=True)
+        k = kh[i].to(f"cuda:{device}", non_blocking=True)
+        v = vh[i].to(f"cuda:{device}", non_blocking=True)
+        out, st = dec.step(q, k, v)
+        outh.copy_(out, non_blocking=True)
+        stream.synchronize()
+    e1.record(stream)
+    barrier()
+    e2e_ms_local = e0.elapsed_time(e1)
+    e2e_rows = sum(N_KV * (T1 + i + 1) for i in range(K))
+    e2e_bytes_local = e2e_rows * ROW_BYTES + K * N_KV * ROW_BYTES
+    h2d = int(qh[0].numel() * 4 + kh[0].numel() * 4 + vh[0].numel() * 4)
+    d2h = int(outh.numel() * 8)
+
+    # max over ranks of time, sum of bytes
+    vals = torch.tensor([ms_local, e2e_ms_local, bytes_local, e2e_bytes_local,
+                         statistics.mean(scan_ms)], dtype=torch.float64, device=f"cuda:{device}")
+    if world > 1:
+        mx = vals.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = vals.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        ms, e2e_ms, scan_avg = float(mx[0]), float(mx[1]), float(mx[4])
+        tot_bytes, tot_e2e = float(sm[2]), float(sm[3])
+    else:
+        ms, e2e_ms, tot_bytes, tot_e2e, scan_avg = (float(x) for x in vals.cpu())
+
+    result = None
+    if rank == 0:
+        gbs = tot_bytes / (ms * 1e-3) / 1e9
+        peak, peak_kind = peaks()
+        T_mid = T0 + K // 2
+        scan_bytes = N_KV * T_mid * ROW_BYTES
+        achieved = scan_bytes / (scan_avg * 1e-3) / 1e9
+        tpr = traffic_per_row()
+        result = {
+            "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": round(ms / K, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int64",
+            "data": "synthetic: seeded N(0,1) k/v in Q8.16 (24-bit lanes) through the ingress "
+                    "kernel, q ~ N(0,1/64); random tokens, no checkpoint",
+            "config": {
+                "workload": "BASELINE config 2 at 1M: one Llama-3.2-1B-shaped layer below the "
+                            "seam (8 KV heads x d64, 4 q heads per KV head), 4b K / 2b V, one "
+                            f"sequence of {ctx} cached tokens per GPU; step = ingress of one "
+                            "token + online-softmax scan of all rows",
+                "context": ctx, "kv_heads": N_KV, "q_heads": N_KV * GROUPS, "head_dim": D,
+                "key_bits": 4, "value_bits": 2, "row_bytes": ROW_BYTES,
+                "parallelism": f"{world} sequence(s), one per GPU, no exchange",
+                "l2": f"inputs larger than L2: {N_KV * ctx * ROW_BYTES / 1e6:.0f} MB of cache "
+                      "per GPU vs 126 MB L2",
+            },
+            "rows_per_s": round(tot_bytes / ROW_BYTES / (ms * 1e-3), 1),
+            "us_per_step": round(ms / K * 1e3, 2),
+            "scan_us": round(scan_avg * 1e3, 2),
+            "ingress_us": round(statistics.mean(ingress_ms) * 1e3, 2),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_kind": peak_kind,
+                         "traffic": (round(tpr * N_KV * T_mid) if tpr else None),
+                         "kernel": "k_scan_chunk (+ its exact-fallback check launch)"},
+            "e2e": {"value": round(tot_e2e / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "us_per_step": round(e2e_ms / K * 1e3, 2)},
+            "gpu_launches": 3 * K,
+            "clocks": clk,
+        }
+    dec.close()
+    del q_all, k_all, v_all
+    torch.cuda.synchronize(device)
+
+    if rank == 0 and world == 1:
+        if not args.no_sweep:
+            result["sweep"] = sweep(device)
+        if not args.no_cpu:
+            result["cpu_baseline"] = cpu_baseline(device)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def sweep(device: int):
+    """GB/s and µs per step at the other contexts of config 2 (a few steps each)."""
+    import torch
+    res = {}
+    for ctx in (4096, 32768, 131072):
+        dec, gen = make_decoder(ctx, 16, device, seed=99)
+        q, k, v = step_inputs(gen, 8, device)
+        for i in range(3):
+            dec.step(q[i], k[i], v[i])
+        torch.cuda.synchronize(device)
+        # contexts below L2 are scanned from a cold L2: flush between steps
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{device}")
+        times, T = [], dec.pc.length(0)
+        for i in range(3, 8):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            dec.step(q[i], k[i], v[i])
+            e1.record()
+            torch.cuda.synchronize(device)
+            times.append(e0.elapsed_time(e1))
+        ms = statistics.median(times)
+        byts = N_KV * (T + 3) * ROW_BYTES
+        res[str(ctx)] = {"GB/s": round(byts / (ms * 1e-3) / 1e9, 2), "us_per_step": round(ms * 1e3, 2),
+                         "l2": "flushed between steps"}
+        dec.close()
+        del flush
+    return res
+
+
+def cpu_baseline(device: int, sample_tokens: int = 1 << 18):
+    """The oracle's attend_online over a sample of this GPU's own cache rows."""
+    import torch
+    import oracle  # noqa: F401  (timed CPU baseline only)
+    from tests.conftest import make_oracle
+    dec, gen = make_decoder(sample_tokens, 16, device, seed=7)
+    rows = np.stack([dec.pc.export(0, h) for h in range(N_KV)], axis=1)
+    q = step_inputs(gen, 1, device)[0][0].cpu().numpy().astype(np.int64)
+    dec.close()
+    orc = make_oracle()
+    qr = orc.rotate(q)
+    threads = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    orc.decode_layer(qr, [rows], threads=threads)
+    dt = time.perf_counter() - t0
+    return {"value": round(N_KV * sample_tokens * ROW_BYTES / dt / 1e9, 4), "unit": "GB/s",
+            "cores": min(threads, N_KV), "kind": "port",
+            "sample": f"attend_online (oracle C port) over {sample_tokens} cached tokens x 8 KV "
+                      f"heads x 4 q heads, one decode step, {dt:.2f} s on "
+                      f"{min(threads, N_KV)} host threads (one per KV head)"}
+
+
+# ---------------------------------------------------------------------------
+# the reference arm: the reference algorithm on the host cores
+# ---------------------------------------------------------------------------
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import oracle  # noqa: F401  (the reference arm times the oracle port)
+    from tests.conftest import make_oracle
+    orc = make_oracle()
+    rng = np.random.default_rng(1234)
+    T = 1 << 16                               # bounded sample of the 1M-token workload
+    k = np.clip(np.rint(rng.standard_normal((T, N_KV, D)) * 65536), -(1 << 23), (1 << 23) - 1)
+    v = np.clip(np.rint(rng.standard_normal((T, N_KV, D)) * 65536), -(1 << 23), (1 << 23) - 1)
+    threads = os.cpu_count() or 1
+    rows = orc.ingress_rows(k.astype(np.int64), v.astype(np.int64), threads=threads)
+    q = np.clip(np.rint(rng.standard_normal((args.warmup + args.steps, 1, 32, D)) * 8192),
+                -(1 << 23), (1 << 23) - 1).astype(np.int64)
+    for i in range(args.warmup):
+        orc.decode_layer(orc.rotate(q[i]), [rows], threads=threads)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        orc.decode_layer(orc.rotate(q[args.warmup + i]), [rows], threads=threads)
+    dt = time.perf_counter() - t0
+    gbs = args.steps * N_KV * T * ROW_BYTES / dt / 1e9
+    cores = min(threads, N_KV)
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 4), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int64",
+        "data": "synthetic: seeded N(0,1) k/v in Q8.16, q ~ N(0,1/64)",
+        "config": {"workload": "BASELINE config 2: one layer, 8 KV heads x d64, 4b K / 2b V, one "
+                               "sequence; each step a bounded sample of 65536 cached tokens",
+                   "context_sample": T, "parallelism": "host threads, one per KV head"},
+        "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": f"attend_online over {T} cached tokens x 8 KV heads per step"},
+        "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()
