@@ -183,6 +183,29 @@ int ins_scan(ins_cache *cache, int32_t B, const int32_t *seq_ids, const int64_t 
              const int32_t *q_rot, int64_t *out, ins_stats *stats, ins_softmax mode,
              void *stream);
 
+/* The online scan of ins_scan, allocating no device memory. This entry point
+ * has no counterpart in the reference; it exists for callers that cannot
+ * allocate device memory once they are running -- an engine that has handed
+ * all of HBM to its own pool at start-up, a runtime whose allocator may not be
+ * entered from the decode thread, host code that must never block on an
+ * allocation mid-step. ins_scan grows its scratch with cudaMalloc when a larger
+ * batch or context first arrives; this call instead carves the same scratch
+ * out of one static device array of 64 MiB that every GPU loading this library
+ * holds until the process exits.
+ *
+ * Arguments and results are those of ins_scan with mode INS_SOFTMAX_ONLINE,
+ * bit for bit. Limits: at most 4096 sequences, 65,536 (sequence x KV head x
+ * 1024-row chunk) tiles, and a scratch layout that fits 64 MiB (about 8 KV
+ * heads x 1M tokens of one sequence, or 256 sequences of 4K); a call beyond
+ * them returns INS_EBADLEN before enqueuing anything. The first call on each
+ * device looks up the array's device address (cudaGetSymbolAddress) with that
+ * device current, so make it before any stream capture. Every call clears the
+ * counters it needs at zero, but all calls share the one array: calls whose
+ * GPU work overlaps (other streams, other threads, other caches on the same
+ * device) race on it, so order them. */
+int ins_scan_noalloc(ins_cache *cache, int32_t B, const int32_t *seq_ids, const int64_t *lengths,
+                     const int32_t *q_rot, int64_t *out, ins_stats *stats, void *stream);
+
 /* Export rows [t0, t0+n) of one sequence and KV head in the reference's
  * packed row format (KVQuantizer.pack, ops/quantize.py:237-252), the bytes
  * CompressedCache.buf[t0:t0+n, kv_head] holds (cache/compressed.py:42-52).

@@ -10,6 +10,7 @@
 #include <cstdio>
 #include <cstring>
 #include <string>
+#include <mutex>
 #include <vector>
 
 #include "common.cuh"
@@ -602,3 +603,209 @@ int ins_cache_status(ins_cache *c, void *stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// ins_scan_noalloc: the online scan without any device allocation.
+//
+// Some callers cannot allocate device memory once they are running: a serving
+// engine that hands the whole of HBM to its own pool at start-up, a runtime
+// whose allocator is not reentrant from the thread that calls the scan, or
+// host code that must not block on an allocation in its decode loop. ins_scan
+// grows its scratch (chunk records, look-back flags, segment pool) with
+// cudaMalloc the first time a larger batch or context arrives; this entry
+// point runs the same chunked scan with that scratch carved from one
+// file-scope device array of NOALLOC_BYTES, which every GPU that loads this
+// library holds until the process exits.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t NOALLOC_BYTES = (size_t)64 << 20;
+constexpr int NOALLOC_SEGS = 4096;            // rescale segments; beyond, items are recomputed
+constexpr int NOALLOC_MAX_B = 4096;           // sequences per call
+constexpr int NOALLOC_MAX_TILES = 1 << 16;    // (item, chunk) tiles per call
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_BYTES];
+
+struct NoallocState {
+    void *ptr = nullptr;                      // device address of g_noalloc_scratch
+    unsigned long long epoch = 0;             // look-back epochs of this array
+};
+std::mutex g_noalloc_mu;
+NoallocState g_noalloc[256];                  // per device ordinal
+// host staging of one call, reused under the lock
+int4 g_na_tiles[NOALLOC_MAX_TILES];
+int32_t g_na_nc[NOALLOC_MAX_B * 8];
+int64_t g_na_T[NOALLOC_MAX_B];
+int32_t g_na_seq[NOALLOC_MAX_B];
+
+template <int H, int KB, int VB>
+int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out, ins_stats *stats,
+                    cudaStream_t s, NoallocState &st) {
+    const Geo &g = c->g;
+    const int n_items = B * g.n_kv;
+    if (n_items > NOALLOC_MAX_B * 8) return fail(INS_EBADLEN, "too many (sequence, KV head) items");
+    const int C = chunk_rows<H, VB>(g, 100 * 1024);
+    int max_nc = 1;
+    int64_t n_tiles = 0;
+    for (int it = 0; it < n_items; ++it) {
+        const int64_t T = g_na_T[it / g.n_kv];
+        const int ncn = T ? (int)((T + C - 1) / C) : 1;
+        g_na_nc[it] = ncn;
+        max_nc = ncn > max_nc ? ncn : max_nc;
+        n_tiles += ncn;
+    }
+    // the carve, in the same order ins_scan's scratch uses
+    const int mb = (max_nc + GBLK - 1) / GBLK;
+    auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
+    size_t o = 0;
+    const size_t o_claim = o; o += al(8);
+    const size_t o_all = o; o += al(8);
+    const size_t o_top = o; o += al(8);
+    const size_t o_flag = o; o += al(sizeof(unsigned long long) * (size_t)n_items * max_nc);
+    const size_t o_val = o; o += al(sizeof(long long) * (size_t)n_items * max_nc * 2 * HMAX);
+    const size_t o_rec = o; o += al(sizeof(ChunkRec) * (size_t)n_items * max_nc);
+    const size_t o_blk = o; o += al(sizeof(BlockRec) * (size_t)n_items * mb);
+    const size_t o_bd = o; o += al(sizeof(unsigned int) * (size_t)n_items * mb);
+    const size_t o_seg = o; o += al(sizeof(SegEntry) * (size_t)NOALLOC_SEGS);
+    const size_t o_items = o; o += al(sizeof(ItemAcc) * (size_t)n_items);
+    const size_t o_redo = o; o += al(sizeof(int32_t) * (size_t)n_items);
+    const size_t o_tiles = o; o += al(sizeof(int4) * (size_t)n_tiles);
+    const size_t o_nc = o; o += al(sizeof(int32_t) * (size_t)n_items);
+    const size_t o_T = o; o += al(sizeof(int64_t) * (size_t)B);
+    const size_t o_seq = o; o += al(sizeof(int32_t) * (size_t)B);
+    if (o > NOALLOC_BYTES || n_tiles > NOALLOC_MAX_TILES)
+        return fail(INS_EBADLEN, "this scan needs " + std::to_string(o) + " B of scratch and " +
+                                     std::to_string(n_tiles) + " tiles; ins_scan_noalloc holds " +
+                                     std::to_string(NOALLOC_BYTES) + " B and " +
+                                     std::to_string(NOALLOC_MAX_TILES) + " tiles");
+    int64_t k = 0;
+    for (int cidx = 0; cidx < max_nc; ++cidx)
+        for (int it = 0; it < n_items; ++it)
+            if (cidx < g_na_nc[it]) {
+                const int64_t T = g_na_T[it / g.n_kv];
+                const int64_t t0 = (int64_t)cidx * C;
+                g_na_tiles[k++] = make_int4(it, cidx, (int)t0, (int)(T - t0 < C ? T - t0 : C));
+            }
+    uint8_t *p = (uint8_t *)st.ptr;
+    // what the kernel expects at zero: the claim, completion and allocation
+    // counters, the per-block and per-item accumulators, and the look-back
+    // flags (the array keeps whatever the previous call left in it)
+    CK(cudaMemsetAsync(p, 0, o_flag, s));
+    CK(cudaMemsetAsync(p + o_flag, 0, sizeof(unsigned long long) * (size_t)n_items * max_nc, s));
+    CK(cudaMemsetAsync(p + o_bd, 0, sizeof(unsigned int) * (size_t)n_items * mb, s));
+    CK(cudaMemsetAsync(p + o_items, 0, sizeof(ItemAcc) * (size_t)n_items, s));
+    CK(cudaMemcpyAsync(p + o_tiles, g_na_tiles, sizeof(int4) * (size_t)n_tiles, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(p + o_nc, g_na_nc, sizeof(int32_t) * (size_t)n_items, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(p + o_T, g_na_T, sizeof(int64_t) * (size_t)B, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(p + o_seq, g_na_seq, sizeof(int32_t) * (size_t)B, cudaMemcpyHostToDevice, s));
+    auto fn = k_scan_chunk<H, KB, VB>;
+    const size_t dyn = ChunkLayout<H, VB>(C).total;
+    CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn));
+    constexpr int NT = H * 64 > 256 ? H * 64 : 256;
+    int per_sm = 0, dev = 0, sms = 0;
+    CK(cudaGetDevice(&dev));
+    CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, NT, dyn));
+    if (per_sm < 1) per_sm = 1;
+    int grid = per_sm * sms;
+    if (grid > n_tiles) grid = (int)n_tiles;
+    ChunkArgs a{};
+    a.g = g;
+    a.tb = c->d_tables;
+    a.tiles = (const int4 *)(p + o_tiles);
+    a.n_tiles = (int32_t)n_tiles;
+    a.C = C;
+    a.max_chunks = max_nc;
+    a.max_blocks = mb;
+    a.n_items = n_items;
+    a.item_nchunks = (const int32_t *)(p + o_nc);
+    a.seq_ids = (const int32_t *)(p + o_seq);
+    a.T = (const int64_t *)(p + o_T);
+    a.page_table = c->d_page_table;
+    a.pool = c->d_pool;
+    a.q_rot = q_rot;
+    a.out = out;
+    a.stats = stats;
+    a.claim = (unsigned long long *)(p + o_claim);
+    a.claim_base = 0;
+    a.lb_flag = (unsigned long long *)(p + o_flag);
+    a.lb_val = (long long *)(p + o_val);
+    a.recs = (ChunkRec *)(p + o_rec);
+    a.blks = (BlockRec *)(p + o_blk);
+    a.blk_done = (unsigned int *)(p + o_bd);
+    a.segs = (SegEntry *)(p + o_seg);
+    a.seg_top = (unsigned int *)(p + o_top);
+    a.seg_cap = NOALLOC_SEGS;
+    a.items = (ItemAcc *)(p + o_items);
+    a.redo = (int32_t *)(p + o_redo);
+    a.all_done = (unsigned long long *)(p + o_all);
+    a.status = c->d_status;
+    a.epoch = ++st.epoch;
+    fn<<<grid, NT, dyn, s>>>(a);
+    CK(cudaGetLastError());
+    CK(launch_seq<H>(g, c->d_tables, B, a.seq_ids, a.T, c->d_page_table, c->d_pool, q_rot, out,
+                     stats, a.redo, s));
+    return INS_OK;
+}
+
+template <int H>
+int noalloc_dispatch(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
+                     ins_stats *stats, cudaStream_t s, NoallocState &st) {
+    const Geo &g = c->g;
+    if (g.kb == 4 && g.vb == 2) return noalloc_chunked<H, 4, 2>(c, B, q_rot, out, stats, s, st);
+    if constexpr (H == 4 || H == 8)
+        if (g.kb == 3 && g.vb == 3) return noalloc_chunked<H, 3, 3>(c, B, q_rot, out, stats, s, st);
+    // other widths scan with the sequential body, which needs no scratch
+    uint8_t *p = (uint8_t *)st.ptr;
+    CK(cudaMemcpyAsync(p, g_na_T, sizeof(int64_t) * (size_t)B, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(p + ((sizeof(int64_t) * (size_t)B + 255) & ~(size_t)255), g_na_seq,
+                       sizeof(int32_t) * (size_t)B, cudaMemcpyHostToDevice, s));
+    const int32_t *d_seq = (const int32_t *)(p + ((sizeof(int64_t) * (size_t)B + 255) & ~(size_t)255));
+    CK(launch_seq<H>(g, c->d_tables, B, d_seq, (const int64_t *)p, c->d_page_table, c->d_pool,
+                     q_rot, out, stats, nullptr, s));
+    return INS_OK;
+}
+
+}  // namespace
+
+extern "C" int ins_scan_noalloc(ins_cache *c, int32_t B, const int32_t *seq_ids,
+                                const int64_t *lengths, const int32_t *q_rot, int64_t *out,
+                                ins_stats *stats, void *stream) {
+    if (!c) return fail(INS_EINVAL, "cache is NULL");
+    if (B < 0 || (B > 0 && (!seq_ids || !q_rot || !out))) return fail(INS_EINVAL, "scan arguments");
+    if (B == 0) return INS_OK;
+    if (B > NOALLOC_MAX_B)
+        return fail(INS_EBADLEN, "ins_scan_noalloc takes at most " + std::to_string(NOALLOC_MAX_B) +
+                                     " sequences per call");
+    if (c->device < 0 || c->device >= 256) return fail(INS_EINVAL, "device ordinal");
+    DeviceGuard dg(c->device);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    NoallocState &st = g_noalloc[c->device];
+    if (!st.ptr) {
+        // once per device, with that device current: the array's device address
+        void *ptr = nullptr;
+        CK(cudaGetSymbolAddress(&ptr, g_noalloc_scratch));
+        st.ptr = ptr;
+    }
+    for (int32_t i = 0; i < B; ++i) {
+        const int32_t sq = seq_ids[i];
+        if (sq < 0 || sq >= c->cfg.max_seqs) return fail(INS_EINVAL, "sequence id out of range");
+        const int64_t len = c->h_seq_lens[sq];
+        int64_t T = len;
+        if (lengths) {
+            T = lengths[i];
+            if (T < 0 || T > len)
+                return fail(INS_EBADLEN, "scan length outside the sequence's cached tokens");
+        }
+        g_na_T[i] = T;
+        g_na_seq[i] = sq;
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    switch (c->g.H) {
+        case 1: return noalloc_dispatch<1>(c, B, q_rot, out, stats, s, st);
+        case 2: return noalloc_dispatch<2>(c, B, q_rot, out, stats, s, st);
+        case 4: return noalloc_dispatch<4>(c, B, q_rot, out, stats, s, st);
+        case 8: return noalloc_dispatch<8>(c, B, q_rot, out, stats, s, st);
+    }
+    return fail(INS_EINVAL, "kv_groups");
+}
