@@ -190,14 +190,15 @@ int ins_scan(ins_cache *cache, int32_t B, const int32_t *seq_ids, const int64_t 
  * entered from the decode thread, host code that must never block on an
  * allocation mid-step. ins_scan grows its scratch with cudaMalloc when a larger
  * batch or context first arrives; this call instead carves the same scratch
- * out of one static device array of 64 MiB that every GPU loading this library
- * holds until the process exits.
+ * out of one static device array of 192 MiB that every GPU loading this
+ * library holds until the process exits.
  *
  * Arguments and results are those of ins_scan with mode INS_SOFTMAX_ONLINE,
  * bit for bit. Limits: at most 4096 sequences, 65,536 (sequence x KV head x
- * 1024-row chunk) tiles, and a scratch layout that fits 64 MiB (about 8 KV
- * heads x 1M tokens of one sequence, or 256 sequences of 4K); a call beyond
- * them returns INS_EBADLEN before enqueuing anything. The first call on each
+ * 1024-row tile) tiles, and a scratch layout that fits 192 MiB (the scores
+ * take 16 bytes per cached row at 4 query heads per KV head: about 8 KV heads
+ * x 1.1M tokens of one sequence, or 256 sequences of 4K); a call beyond them
+ * returns INS_EBADLEN before enqueuing anything. The first call on each
  * device looks up the array's device address (cudaGetSymbolAddress) with that
  * device current, so make it before any stream capture. Every call clears the
  * counters it needs at zero, but all calls share the one array: calls whose
@@ -221,6 +222,13 @@ int ins_cache_import(ins_cache *cache, int32_t seq, int64_t n, const uint8_t *ro
 /* Read and clear the device status word latched by earlier kernels. Blocks
  * on the stream. INS_OK when nothing went wrong. */
 int ins_cache_status(ins_cache *cache, void *stream);
+
+/* How many (sequence, KV head) items of the last online ins_scan on this
+ * cache the context-parallel scan handed to the exact sequential kernel (its
+ * proof of exactness failed, or a value lay outside the formats it assumes);
+ * results are bit-exact either way. A diagnostic with no counterpart in the
+ * reference. Blocks on the stream; -1 on error (see ins_last_error). */
+int64_t ins_scan_recomputed(ins_cache *cache, void *stream);
 
 /* The last error message recorded on this thread ("" if none). */
 const char *ins_last_error(void);

@@ -82,7 +82,7 @@ STATS_FIELDS = tuple(n for n, _ in Stats._fields_)
 SYMBOLS = ("ins_abi_version", "ins_bytes_per_token", "ins_cache_create", "ins_cache_destroy",
            "ins_cache_reset", "ins_cache_length", "ins_cache_capacity", "ins_ingress", "ins_rotate",
            "ins_scores", "ins_scan", "ins_cache_export", "ins_cache_import", "ins_cache_status",
-           "ins_last_error", "ins_scan_noalloc")
+           "ins_last_error", "ins_scan_noalloc", "ins_scan_recomputed")
 
 
 def nvcc() -> str:
@@ -140,6 +140,8 @@ def lib():
     L.ins_cache_export.argtypes = [vp, i32, i32, i64, i64, vp]
     L.ins_cache_import.argtypes = [vp, i32, i64, vp]
     L.ins_cache_status.argtypes = [vp, vp]
+    L.ins_scan_recomputed.argtypes = [vp, vp]
+    L.ins_scan_recomputed.restype = i64
     L.ins_last_error.restype = C.c_char_p
     _lib = L
     return L

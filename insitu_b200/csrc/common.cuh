@@ -35,6 +35,7 @@ struct Geo {
     int32_t n_kv, H, kb, vb;
     int32_t kbytes, vbytes, row_bytes;
     int32_t P;                       // tokens per page
+    int32_t p_log2;                  // log2(P) when P is a power of two, else -1
     int32_t max_pages;               // page-table row length
     int32_t norm_bits, norm_frac, qk_frac, centroid_frac, acc_frac, acc_width;
     int32_t score_width, prob_frac, exp_lut_bits, saturate;

@@ -149,6 +149,7 @@ Geo make_geo(const ins_config &c) {
     g.vbytes = D * c.value_bits / 8;
     g.row_bytes = g.kbytes + g.vbytes + 2 * (c.norm_bits / 8);
     g.P = c.page_tokens;
+    g.p_log2 = (c.page_tokens & (c.page_tokens - 1)) ? -1 : __builtin_ctz((unsigned)c.page_tokens);
     g.max_pages = c.max_pages_per_seq;
     g.norm_bits = c.norm_bits;
     g.norm_frac = c.norm_frac;
@@ -589,6 +590,20 @@ int ins_cache_import(ins_cache *c, int32_t seq, int64_t n, const uint8_t *rows) 
     return INS_OK;
 }
 
+int64_t ins_scan_recomputed(ins_cache *c, void *stream) {
+    if (!c) return fail(INS_EINVAL, "cache is NULL"), -1;
+    DeviceGuard dg(c->device);
+    const int n = c->chunk.last_items;
+    if (n <= 0 || !c->chunk.redo) return 0;
+    std::vector<int32_t> redo(n);
+    if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess ||
+        cudaMemcpy(redo.data(), c->chunk.redo, sizeof(int32_t) * n, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return fail(INS_ECUDA, "reading the recompute flags"), -1;
+    int64_t k = 0;
+    for (int i = 0; i < n; ++i) k += redo[i] != 0;
+    return k;
+}
+
 int ins_cache_status(ins_cache *c, void *stream) {
     if (!c) return fail(INS_EINVAL, "cache is NULL");
     DeviceGuard dg(c->device);
@@ -619,7 +634,7 @@ int ins_cache_status(ins_cache *c, void *stream) {
 // ---------------------------------------------------------------------------
 namespace {
 
-constexpr size_t NOALLOC_BYTES = (size_t)64 << 20;
+constexpr size_t NOALLOC_BYTES = (size_t)192 << 20;
 constexpr int NOALLOC_SEGS = 4096;            // rescale segments; beyond, items are recomputed
 constexpr int NOALLOC_MAX_B = 4096;           // sequences per call
 constexpr int NOALLOC_MAX_TILES = 1 << 16;    // (item, chunk) tiles per call
@@ -628,7 +643,6 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_BYTES];
 
 struct NoallocState {
     void *ptr = nullptr;                      // device address of g_noalloc_scratch
-    unsigned long long epoch = 0;             // look-back epochs of this array
 };
 std::mutex g_noalloc_mu;
 NoallocState g_noalloc[256];                  // per device ordinal
@@ -637,44 +651,35 @@ int4 g_na_tiles[NOALLOC_MAX_TILES];
 int32_t g_na_nc[NOALLOC_MAX_B * 8];
 int64_t g_na_T[NOALLOC_MAX_B];
 int32_t g_na_seq[NOALLOC_MAX_B];
+int64_t g_na_rb[NOALLOC_MAX_B * 8];
 
 template <int H, int KB, int VB>
 int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out, ins_stats *stats,
                     cudaStream_t s, NoallocState &st) {
+    using CF = ChunkCfg<H, KB, VB>;
     const Geo &g = c->g;
     const int n_items = B * g.n_kv;
     if (n_items > NOALLOC_MAX_B * 8) return fail(INS_EBADLEN, "too many (sequence, KV head) items");
-    const int C = chunk_rows<H, VB>(g, 100 * 1024);
+    const int C = CF::C;
     int max_nc = 1;
-    int64_t n_tiles = 0;
+    int64_t n_tiles = 0, rows = 0;
     for (int it = 0; it < n_items; ++it) {
         const int64_t T = g_na_T[it / g.n_kv];
         const int ncn = T ? (int)((T + C - 1) / C) : 1;
         g_na_nc[it] = ncn;
+        g_na_rb[it] = rows;
+        rows += T;
         max_nc = ncn > max_nc ? ncn : max_nc;
         n_tiles += ncn;
     }
     // the carve, in the same order ins_scan's scratch uses
-    const int mb = (max_nc + GBLK - 1) / GBLK;
-    auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
-    size_t o = 0;
-    const size_t o_claim = o; o += al(8);
-    const size_t o_all = o; o += al(8);
-    const size_t o_top = o; o += al(8);
-    const size_t o_flag = o; o += al(sizeof(unsigned long long) * (size_t)n_items * max_nc);
-    const size_t o_val = o; o += al(sizeof(long long) * (size_t)n_items * max_nc * 2 * HMAX);
-    const size_t o_rec = o; o += al(sizeof(ChunkRec) * (size_t)n_items * max_nc);
-    const size_t o_blk = o; o += al(sizeof(BlockRec) * (size_t)n_items * mb);
-    const size_t o_bd = o; o += al(sizeof(unsigned int) * (size_t)n_items * mb);
-    const size_t o_seg = o; o += al(sizeof(SegEntry) * (size_t)NOALLOC_SEGS);
-    const size_t o_items = o; o += al(sizeof(ItemAcc) * (size_t)n_items);
-    const size_t o_redo = o; o += al(sizeof(int32_t) * (size_t)n_items);
-    const size_t o_tiles = o; o += al(sizeof(int4) * (size_t)n_tiles);
-    const size_t o_nc = o; o += al(sizeof(int32_t) * (size_t)n_items);
-    const size_t o_T = o; o += al(sizeof(int64_t) * (size_t)B);
-    const size_t o_seq = o; o += al(sizeof(int32_t) * (size_t)B);
-    if (o > NOALLOC_BYTES || n_tiles > NOALLOC_MAX_TILES)
-        return fail(INS_EBADLEN, "this scan needs " + std::to_string(o) + " B of scratch and " +
+    const ScratchLayout L(n_items, max_nc, NOALLOC_SEGS, (int)(n_tiles < 1 ? 1 : n_tiles), H, CF::CW,
+                          rows);
+    const size_t o_T = L.total;
+    const size_t o_seq = o_T + ((sizeof(int64_t) * (size_t)B + 255) & ~(size_t)255);
+    const size_t o_end = o_seq + sizeof(int32_t) * (size_t)B;
+    if (o_end > NOALLOC_BYTES || n_tiles > NOALLOC_MAX_TILES)
+        return fail(INS_EBADLEN, "this scan needs " + std::to_string(o_end) + " B of scratch and " +
                                      std::to_string(n_tiles) + " tiles; ins_scan_noalloc holds " +
                                      std::to_string(NOALLOC_BYTES) + " B and " +
                                      std::to_string(NOALLOC_MAX_TILES) + " tiles");
@@ -687,38 +692,27 @@ int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
                 g_na_tiles[k++] = make_int4(it, cidx, (int)t0, (int)(T - t0 < C ? T - t0 : C));
             }
     uint8_t *p = (uint8_t *)st.ptr;
-    // what the kernel expects at zero: the claim, completion and allocation
-    // counters, the per-block and per-item accumulators, and the look-back
-    // flags (the array keeps whatever the previous call left in it)
-    CK(cudaMemsetAsync(p, 0, o_flag, s));
-    CK(cudaMemsetAsync(p + o_flag, 0, sizeof(unsigned long long) * (size_t)n_items * max_nc, s));
-    CK(cudaMemsetAsync(p + o_bd, 0, sizeof(unsigned int) * (size_t)n_items * mb, s));
-    CK(cudaMemsetAsync(p + o_items, 0, sizeof(ItemAcc) * (size_t)n_items, s));
-    CK(cudaMemcpyAsync(p + o_tiles, g_na_tiles, sizeof(int4) * (size_t)n_tiles, cudaMemcpyHostToDevice, s));
-    CK(cudaMemcpyAsync(p + o_nc, g_na_nc, sizeof(int32_t) * (size_t)n_items, cudaMemcpyHostToDevice, s));
+    // what the kernels expect at zero: the completion and allocation counters
+    // and the per-block and per-item accumulators (the array keeps whatever
+    // the previous call left in it)
+    CK(cudaMemsetAsync(p, 0, L.cmx, s));
+    CK(cudaMemsetAsync(p + L.bd, 0, L.seg - L.bd, s));
+    CK(cudaMemsetAsync(p + L.items, 0, sizeof(ItemAcc) * (size_t)n_items, s));
+    CK(cudaMemcpyAsync(p + L.tiles, g_na_tiles, sizeof(int4) * (size_t)n_tiles, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(p + L.nc, g_na_nc, sizeof(int32_t) * (size_t)n_items, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(p + L.rb, g_na_rb, sizeof(int64_t) * (size_t)n_items, cudaMemcpyHostToDevice, s));
     CK(cudaMemcpyAsync(p + o_T, g_na_T, sizeof(int64_t) * (size_t)B, cudaMemcpyHostToDevice, s));
     CK(cudaMemcpyAsync(p + o_seq, g_na_seq, sizeof(int32_t) * (size_t)B, cudaMemcpyHostToDevice, s));
-    auto fn = k_scan_chunk<H, KB, VB>;
-    const size_t dyn = ChunkLayout<H, VB>(C).total;
-    CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn));
-    constexpr int NT = H * 64 > 256 ? H * 64 : 256;
-    int per_sm = 0, dev = 0, sms = 0;
-    CK(cudaGetDevice(&dev));
-    CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, NT, dyn));
-    if (per_sm < 1) per_sm = 1;
-    int grid = per_sm * sms;
-    if (grid > n_tiles) grid = (int)n_tiles;
     ChunkArgs a{};
     a.g = g;
     a.tb = c->d_tables;
-    a.tiles = (const int4 *)(p + o_tiles);
+    a.tiles = (const int4 *)(p + L.tiles);
     a.n_tiles = (int32_t)n_tiles;
-    a.C = C;
     a.max_chunks = max_nc;
-    a.max_blocks = mb;
+    a.max_blocks = (max_nc + GBLK - 1) / GBLK;
     a.n_items = n_items;
-    a.item_nchunks = (const int32_t *)(p + o_nc);
+    a.item_nchunks = (const int32_t *)(p + L.nc);
+    a.row_base = (const int64_t *)(p + L.rb);
     a.seq_ids = (const int32_t *)(p + o_seq);
     a.T = (const int64_t *)(p + o_T);
     a.page_table = c->d_page_table;
@@ -726,35 +720,31 @@ int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
     a.q_rot = q_rot;
     a.out = out;
     a.stats = stats;
-    a.claim = (unsigned long long *)(p + o_claim);
-    a.claim_base = 0;
-    a.lb_flag = (unsigned long long *)(p + o_flag);
-    a.lb_val = (long long *)(p + o_val);
-    a.recs = (ChunkRec *)(p + o_rec);
-    a.blks = (BlockRec *)(p + o_blk);
-    a.blk_done = (unsigned int *)(p + o_bd);
-    a.segs = (SegEntry *)(p + o_seg);
-    a.seg_top = (unsigned int *)(p + o_top);
+    a.sc = (uint32_t *)(p + L.sc);
+    a.bmg = (long long *)(p + L.bmg);
+    a.cmx = (long long *)(p + L.cmx);
+    a.recs = (ChunkRec *)(p + L.rec);
+    a.blks = (BlockRec *)(p + L.blk);
+    a.blk_done = (unsigned int *)(p + L.bd);
+    a.segs = (SegEntry *)(p + L.seg);
+    a.seg_top = (unsigned int *)(p + L.top);
     a.seg_cap = NOALLOC_SEGS;
-    a.items = (ItemAcc *)(p + o_items);
-    a.redo = (int32_t *)(p + o_redo);
-    a.all_done = (unsigned long long *)(p + o_all);
+    a.items = (ItemAcc *)(p + L.items);
+    a.redo = (int32_t *)(p + L.redo);
+    a.all_done = (unsigned long long *)(p + L.all);
     a.status = c->d_status;
-    a.epoch = ++st.epoch;
-    fn<<<grid, NT, dyn, s>>>(a);
-    CK(cudaGetLastError());
-    CK(launch_seq<H>(g, c->d_tables, B, a.seq_ids, a.T, c->d_page_table, c->d_pool, q_rot, out,
-                     stats, a.redo, s));
-    return INS_OK;
+    const int rc = launch_chunk_kernels<H, KB, VB>(a, B, a.seq_ids, a.T, s);
+    return rc ? fail(rc, "chunked scan launch") : INS_OK;
 }
 
 template <int H>
 int noalloc_dispatch(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
                      ins_stats *stats, cudaStream_t s, NoallocState &st) {
     const Geo &g = c->g;
-    if (g.kb == 4 && g.vb == 2) return noalloc_chunked<H, 4, 2>(c, B, q_rot, out, stats, s, st);
+    if (is_def_fmt(g) && g.kb == 4 && g.vb == 2) return noalloc_chunked<H, 4, 2>(c, B, q_rot, out, stats, s, st);
     if constexpr (H == 4 || H == 8)
-        if (g.kb == 3 && g.vb == 3) return noalloc_chunked<H, 3, 3>(c, B, q_rot, out, stats, s, st);
+        if (is_def_fmt(g) && g.kb == 3 && g.vb == 3)
+            return noalloc_chunked<H, 3, 3>(c, B, q_rot, out, stats, s, st);
     // other widths scan with the sequential body, which needs no scratch
     uint8_t *p = (uint8_t *)st.ptr;
     CK(cudaMemcpyAsync(p, g_na_T, sizeof(int64_t) * (size_t)B, cudaMemcpyHostToDevice, s));

@@ -3,31 +3,34 @@
 // attend_online (ops/attention.py:451-513) is a sequential recurrence: a
 // running maximum m, and at every token whose score exceeds it, a rescale
 // acc = floor(acc * exp(s - m) / 2^15) before the token's own term is added.
-// This kernel splits every (sequence, KV head) item into chunks of C rows and
-// still returns the reference's bits:
+// This scan splits every (sequence, KV head) item into tiles of C rows and
+// still returns the reference's bits. It runs as three launches and no
+// launch ever waits on another CTA:
 //
-//  1. Scores of a chunk are independent of everything else (exact, FP64 FMA
-//     on integer operands, see row_scores_f64).
-//  2. The running maximum entering chunk c is the maximum of every earlier
-//     chunk's scores. Chunks publish their maximum as soon as their scores
-//     exist and read their predecessors' with a decoupled look-back (bounded
-//     waits; tiles are claimed in order, so every awaited tile is running).
-//  3. Knowing m_in, the chunk finds the exact rescale points (tokens above
-//     the running maximum), p = exp(m - s) for every token, and splits its
-//     tokens into segments at the rescale points. Within a segment every term
-//     is a fixed integer, so its contribution is a plain sum.
-//  4. The last chunk of an item to finish folds the chunks in causal order:
-//     acc = floor(acc * f / 2^15) at each rescale, + segment sums. That fold
-//     equals the per-token recurrence provided the reference's 32-bit clamp
-//     never fires; the fold proves it per chunk with
-//     |acc at chunk start| + sum_t max_k |term(t, k)| <= 2^31 - 1, which bounds
-//     every partial sum inside the chunk (a rescale never grows |acc|).
-//     An item that fails the proof, overflows the segment pool, or sees a
-//     bounded wait expire is recomputed by the exact sequential body in the
-//     same CTA, so the result is bit-exact in every case.
+//  1. k_scan_scores: the scores of every tile (exact FP64 FMA on integer
+//     operands). Each is kept as its offset below its 32-row block's maximum;
+//     the block and tile maxima are kept too.
+//  2. k_chunk_prefix: per item, the running maximum entering every tile (the
+//     maximum of all earlier tiles' maxima).
+//  3. k_scan_values: knowing its incoming maximum m_in, a tile finds the exact
+//     rescale points (tokens above the running maximum), p = exp(m - s) for
+//     every token, and splits its tokens into segments at the rescale points.
+//     Within a segment every term is a fixed integer, so its contribution is
+//     a plain sum. The last tile of an item to finish folds the tiles in
+//     causal order: acc = floor(acc * f / 2^15) at each rescale, + segment
+//     sums. That fold equals the per-token recurrence provided the
+//     reference's 32-bit clamp never fires; the fold proves it per tile with
+//     |acc at tile start| + sum_t max_k |term(t, k)| <= 2^31 - 1, which bounds
+//     every partial sum inside the tile (a rescale never grows |acc|).
+//
+// An item that fails the proof, overflows the segment pool or meets a value
+// outside the formats these kernels assume is recomputed by the exact
+// sequential kernel (a fourth launch that only touches flagged items), so the
+// result is bit-exact in every case.
 #pragma once
 
 #include <climits>
+#include <mutex>
 #include <vector>
 
 #include "common.cuh"
@@ -36,15 +39,9 @@
 namespace ins {
 
 constexpr int HMAX = 8;
-constexpr int LB_SPIN_LIMIT = 1 << 22;   // ~0.4 s of polling at most
-constexpr int SEGMAX = 32;               // rescales one head's chunk can hold
-constexpr int GBLK = 32;                 // chunks folded per level-1 block
-#ifndef INS_JGROUP
-#define INS_JGROUP 8
-#endif
-#ifndef INS_SCORE_ROWS
-#define INS_SCORE_ROWS 2
-#endif
+constexpr int SEGMAX = 32;               // rescales one head's tile can hold
+constexpr int GBLK = 32;                 // tiles folded per level-1 block
+constexpr int CHUNK_THREADS = 256;
 
 struct SegEntry {          // a rescale and the translation that follows it
     int64_t S[D];          // sum of terms after the rescale (per channel)
@@ -53,15 +50,15 @@ struct SegEntry {          // a rescale and the translation that follows it
     int32_t pad;
 };
 
-struct ChunkRec {          // one (item, chunk)
-    int32_t S0[HMAX][D];   // terms of the tokens before the chunk's first rescale
+struct ChunkRec {          // one (item, tile)
+    int32_t S0[HMAX][D];   // terms of the tokens before the tile's first rescale
     int64_t l0[HMAX];
     int64_t B[HMAX];       // sum over tokens of max over codes of |term|
     int32_t nseg[HMAX];
     int32_t seg_base[HMAX];
 };
 
-struct BlockRec {          // GBLK consecutive chunks of one item, folded
+struct BlockRec {          // GBLK consecutive tiles of one item, folded
     int64_t Spre[HMAX][D]; // translation before the block's first rescale
     int64_t Y[HMAX][D];    // max over the block of |local partial sum| (clamp proof)
     int64_t lpre[HMAX];
@@ -78,16 +75,55 @@ struct ItemAcc {
     int32_t pad;
 };
 
+// The fixed-point format the chunked kernels are compiled for: FixedFormat()
+// with QuantConfig's norm_frac of 9 -- qk Q8.16, centroid Q1.15, acc Q16, prob
+// Q15, an 8-bit exp LUT, 48-bit saturating scores (config.py:214-254). Other
+// formats scan with the exact sequential kernel.
+struct DefFmt {
+    static constexpr int SCORE_SHIFT = 24, ACC_SHIFT = 23, ACC_FRAC = 16, LUT_BITS = 8, PROB_FRAC = 15;
+    static constexpr int SCORE_WIDTH = 48;
+    static constexpr int64_t LOG2E = 94548, DELTA_MAX = 772248;
+    static constexpr int64_t S_LO = -(1ll << (SCORE_WIDTH - 1)), S_HI = (1ll << (SCORE_WIDTH - 1)) - 1;
+};
+
+inline bool is_def_fmt(const Geo &g) {
+    return g.score_shift == DefFmt::SCORE_SHIFT && g.acc_shift == DefFmt::ACC_SHIFT &&
+           g.acc_frac == DefFmt::ACC_FRAC && g.exp_lut_bits == DefFmt::LUT_BITS &&
+           g.prob_frac == DefFmt::PROB_FRAC && g.score_width == DefFmt::SCORE_WIDTH &&
+           g.saturate && g.log2e == DefFmt::LOG2E && g.delta_max == DefFmt::DELTA_MAX;
+}
+
+// exp_lut for a distance known to be non-negative, in the default format
+// (ExpLut.__call__, ops/attention.py:153-159; the nested floors of exp_lut32).
+__device__ __forceinline__ uint32_t exp_lut_def(const int32_t *tab, int64_t delta) {
+    const uint32_t d = delta < DefFmt::DELTA_MAX ? (uint32_t)delta : (uint32_t)DefFmt::DELTA_MAX;
+    const uint32_t u =
+        (uint32_t)(((uint64_t)d * (uint64_t)DefFmt::LOG2E) >> (2 * DefFmt::ACC_FRAC - DefFmt::LUT_BITS));
+    constexpr uint32_t SPAN = (uint32_t)(DefFmt::PROB_FRAC + 2) << DefFmt::LUT_BITS;
+    return u >= SPAN ? 0u : ((uint32_t)tab[u & ((1u << DefFmt::LUT_BITS) - 1u)] >> (u >> DefFmt::LUT_BITS));
+}
+
+// Page slot and row of position `pr` of a sequence's rows.
+__device__ __forceinline__ void page_row(const Geo &g, int pr, int &pi, int &lr) {
+    if (g.p_log2 >= 0) {
+        pi = pr >> g.p_log2;
+        lr = pr & (g.P - 1);
+    } else {
+        pi = pr / g.P;
+        lr = pr - pi * g.P;
+    }
+}
+
 struct ChunkArgs {
     Geo g;
     const DevTables *tb;
-    const int4 *tiles;            // (item, chunk, t0, n)
+    const int4 *tiles;            // (item, chunk, t0, n), chunk-major
     int32_t n_tiles;
-    int32_t C;                    // rows per chunk
     int32_t max_chunks;
     int32_t max_blocks;
     int32_t n_items;
     const int32_t *item_nchunks;
+    const int64_t *row_base;      // [n_items]: first row of the item in `sc`
     const int32_t *seq_ids;
     const int64_t *T;
     const int32_t *page_table;
@@ -95,10 +131,9 @@ struct ChunkArgs {
     const int32_t *q_rot;
     int64_t *out;
     ins_stats *stats;
-    unsigned long long *claim;
-    unsigned long long claim_base;
-    unsigned long long *lb_flag;  // [n_items * max_chunks]
-    long long *lb_val;            // [n_items * max_chunks * 2 * HMAX]
+    uint32_t *sc;                 // [rows][H]: score offset below its block maximum
+    long long *bmg;               // [n_tiles][H][CW]: block maxima
+    long long *cmx;               // [n_items * max_chunks][2][HMAX]: tile maximum, m_in
     ChunkRec *recs;               // [n_items * max_chunks]
     BlockRec *blks;               // [n_items * max_blocks]
     unsigned int *blk_done;       // [n_items * max_blocks]
@@ -109,20 +144,20 @@ struct ChunkArgs {
     int32_t *redo;                // [n_items]: 1 = recompute with the sequential body
     unsigned long long *all_done;
     int32_t *status;
-    unsigned long long epoch;
 };
 
 // Device scratch of the chunked scan, owned by the cache handle and grown on
 // demand. Everything in it is either rewritten each launch or reset by the
-// kernel itself, so launches need no memsets.
+// kernels themselves, so launches need no memsets.
 struct ChunkScratch {
     void *base = nullptr;
     size_t bytes = 0;
     int32_t n_items = 0, max_chunks = 0, seg_cap = 0, tile_cap = 0;
-    unsigned long long epoch = 0;
-    unsigned long long claim_base = 0;
-    unsigned long long *claim = nullptr, *lb_flag = nullptr, *all_done = nullptr;
-    long long *lb_val = nullptr;
+    int32_t last_items = 0;       // items of the last chunked launch (their redo flags)
+    int64_t sc_rows = 0;          // rows * H capacity of `sc`, in 32-bit words
+    uint32_t *sc = nullptr;
+    long long *bmg = nullptr, *cmx = nullptr;
+    unsigned long long *all_done = nullptr;
     ChunkRec *recs = nullptr;
     BlockRec *blks = nullptr;
     unsigned int *blk_done = nullptr;
@@ -132,98 +167,174 @@ struct ChunkScratch {
     int32_t *redo = nullptr;
     int4 *tiles = nullptr;
     int32_t *item_nchunks = nullptr;
+    int64_t *row_base = nullptr;
 
     void release() {
         if (base) cudaFree(base);
         base = nullptr;
         bytes = 0;
         n_items = max_chunks = seg_cap = tile_cap = 0;
+        sc_rows = 0;
     }
 };
 
 // ---------------------------------------------------------------------------
-// smem layout of the chunk kernel
+// Geometry of the tiles
+//
+// One CTA of 256 threads owns a tile of C rows of one (sequence, KV head)
+// item. In k_scan_values shared memory holds, for the tile: the scores [H][C]
+// (int64, later w = v_norm * p in place), the V codes transposed to one
+// 32-bit word per (channel, 8 table units) -- nibble j of a word is the table
+// index of unit j --, the v norms, two term tables (double-buffered
+// sub-tiles of SUBT tokens) and the per-32-row block state of the online
+// control. The V codes arrive row-major in a staging area that the term
+// tables later reuse.
+//
+// A term-table unit is TPE consecutive tokens. For 2-bit V codes a unit is a
+// token pair: its 16 entries hold term(t, k0) + term(t+1, k1) for every code
+// pair, so one 16-byte lookup adds two tokens' terms for four heads. For 3-bit
+// codes a unit is one token with 8 entries.
 // ---------------------------------------------------------------------------
-template <int H, int VB>
-struct ChunkLayout {
-    static constexpr int NC = 1 << VB;                    // V codes
-    static constexpr int SUB = VB <= 2 ? 256 : 128;       // tokens per term-table sub-tile
-    static constexpr int PS = SUB * H + 4;                // words per code plane (padded)
-    static constexpr int VW = 2 * VB;                     // 32-bit words per V row
-    int C;
-    size_t off_s, off_p, off_vt, off_vn, off_tab, off_grew, off_pre, off_bmax, off_bcar, off_s0, total;
-    __host__ __device__ explicit ChunkLayout(int C_) : C(C_) {
-        size_t o = 0;
-        off_s = o;    o += (size_t)H * C * 8;             // scores (int64)
-        off_p = o;    o += (size_t)H * C * 4;             // p (int32)
-        off_vt = o;   o += (size_t)VW * C * 4;            // V codes, word-major
-        off_vn = o;   o += (size_t)C * 4;                 // v_norm (int32)
-        off_tab = o;  o += (size_t)NC * PS * 4;           // terms [code][t][h]
-        off_grew = o; o += (size_t)(H + 1) * (C / 32) * 4;  // rescale bits per head, + any
-        off_pre = o;  o += (size_t)H * (C / 32) * 4;      // rescales before each bit word
-        off_bmax = o; o += (size_t)H * (C / 32) * 8;      // max score of each 32-row block
-        off_bcar = o; o += (size_t)H * (C / 32) * 8;      // running max entering each block
-        off_s0 = o;   o += (size_t)H * D * 4;             // segment-0 partials
-        total = o;
-    }
+template <int H, int KB, int VB>
+struct ChunkCfg {
+    static constexpr int NT = CHUNK_THREADS;
+    static constexpr int R = (H == 8 || VB == 3) ? 2 : 4;   // rows per thread in the score phase
+    static constexpr int C = R * NT;                         // rows per tile
+    static constexpr int CW = C / 32;                        // 32-row blocks per tile
+    static constexpr int NC = 1 << VB;                       // V codes
+    static constexpr int VW = VB * 2;                        // 32-bit words per V row
+    static constexpr int TPE = VB == 2 ? 2 : 1;              // tokens per table unit
+    static constexpr int NE = 1 << (VB * TPE);               // entries per unit
+    static constexpr int HL = H >= 4 ? 4 : H;                // heads per accumulating lane
+    static constexpr int HG = H / HL;                        // head groups in the accumulate
+    static constexpr int SUBT = (NT / 64) * 32 / HG;         // tokens per table sub-tile
+    static constexpr int UNITS = SUBT / TPE;                 // units per sub-tile
+    // A unit's entries are grouped by head pair: [head pair][index][2 heads],
+    // 8 bytes an entry, so a warp's lookups of one unit (16 distinct entries at
+    // most) fall in distinct banks. HPS pads a head pair's block by one entry
+    // so that the build's stores (lanes = 8 units x 4 heads) are conflict-free
+    // too. A single head (H == 1) keeps 4-byte entries.
+    static constexpr int HPS = 2 * NE + 2;                   // words per head pair
+    static constexpr int USTR = H == 1 ? NE + 1 : (H / 2) * HPS;   // words per unit
+    static constexpr int TPW = 8 * TPE;                      // tokens per code word
+    static constexpr int TWS = C / TPW + 1;                  // words per channel of the code matrix
+    static constexpr int VS = (C + C / 16) / 32 * 32 + 48;   // words per V staging plane, = 16 mod 32
+    static constexpr int STREAMS = (NT / 64) / HG;           // 32-token streams per sub-tile
+    static constexpr size_t TAB_WORDS = (size_t)UNITS * USTR;
+    static constexpr size_t STAGE_BYTES = (size_t)VW * VS * 4;
+    static constexpr size_t TABS_BYTES =
+        2 * TAB_WORDS * 4 > STAGE_BYTES ? 2 * TAB_WORDS * 4 : STAGE_BYTES;
+    // byte offsets in dynamic shared memory
+    static constexpr size_t OFF_S = 0;                                           // u32 [H][C]
+    static constexpr size_t OFF_TW = OFF_S + (size_t)H * C * 4;                  // u32 [64][TWS]
+    static constexpr size_t OFF_VN = OFF_TW + (size_t)64 * TWS * 4;              // int32 [C]
+    static constexpr size_t OFF_TAB = (OFF_VN + (size_t)C * 4 + 15) & ~(size_t)15;
+    static constexpr size_t OFF_GREW = OFF_TAB + TABS_BYTES;                     // u32 [H+1][CW]
+    static constexpr size_t OFF_PRE = OFF_GREW + (size_t)(H + 1) * CW * 4;       // int32 [H][CW]
+    static constexpr size_t OFF_BMAX = (OFF_PRE + (size_t)H * CW * 4 + 7) & ~(size_t)7;  // int64 [H][CW]
+    static constexpr size_t OFF_BCAR = OFF_BMAX + (size_t)H * CW * 8;            // int64 [H][CW]
+    static constexpr size_t OFF_DB = OFF_BCAR + (size_t)H * CW * 8;              // int64 [H][CW]
+    static constexpr size_t OFF_S0 = OFF_DB + (size_t)H * CW * 8;                // int32 [H][64]
+    static constexpr size_t BYTES = OFF_S0 + (size_t)H * D * 4;
+    static_assert(C % 32 == 0 && SUBT % 32 == 0 && (UNITS * H) % 32 == 0, "tile shape");
+    static_assert(H == 1 || (USTR % 2 == 0 && TAB_WORDS % 2 == 0), "8-byte entries stay aligned");
+    static_assert(CW <= 32, "the control phase gives one lane to each 32-row block");
 };
 
-// Scores of R rows for one thread (register-blocked over rows), exact.
-// Channels are taken 32 at a time: 32 codes of KB bits are exactly KB words,
-// so every code extraction below is at a compile-time position.
-template <int H, int KB, int R>
-__device__ __forceinline__ void score_rows(const Geo &g, const uint8_t *const *krow,
-                                           const int64_t *knorm, const bool *valid,
-                                           const double *__restrict__ qd,
-                                           const uint32_t *__restrict__ khi, int64_t (*s)[H],
-                                           int &ovf) {
-    double acc[R][H];
+// The 16 x 16 transpose of 2-bit fields held in 16 words: on entry A[i] has
+// field c = element (i, c); on exit A[c] has field i = element (i, c). Four
+// block-swap stages (8, 4, 2, 1 fields), each pairing rows i and i + bs.
+__device__ __forceinline__ void transpose16x2(uint32_t (&A)[16]) {
 #pragma unroll
-    for (int r = 0; r < R; ++r)
+    for (int st = 0; st < 4; ++st) {
+        const int bs = 8 >> st, s = 2 * bs;
+        const uint32_t m = st == 0 ? 0x0000FFFFu : st == 1 ? 0x00FF00FFu : st == 2 ? 0x0F0F0F0Fu : 0x33333333u;
 #pragma unroll
-        for (int h = 0; h < H; ++h) acc[r][h] = 0.0;
-#pragma unroll 1
-    for (int grp = 0; grp < D / 32; ++grp) {
-        uint32_t w[R][KB];
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-            const uint32_t *src = reinterpret_cast<const uint32_t *>(krow[r]) + grp * KB;
-#pragma unroll
-            for (int i = 0; i < KB; ++i) w[r][i] = valid[r] ? src[i] : 0u;
-        }
-        const double *qg = qd + grp * 32;
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-            double c[R];
-#pragma unroll
-            for (int r = 0; r < R; ++r)
-                c[r] = __hiloint2double((int)khi[code_at<KB>(w[r], jj, KB)], 0);
-#pragma unroll
-            for (int h = 0; h < H; ++h) {
-                const double qv = qg[h * D + jj];
-#pragma unroll
-                for (int r = 0; r < R; ++r) acc[r][h] = fma(qv, c[r], acc[r][h]);
+        for (int i = 0; i < 16; ++i)
+            if (!(i & bs)) {
+                const uint32_t t = ((A[i] >> s) ^ A[i + bs]) & m;
+                A[i + bs] ^= t;
+                A[i] ^= t << s;
             }
-            if ((jj & (INS_JGROUP - 1)) == INS_JGROUP - 1) asm volatile("" ::: "memory");
-        }
     }
-#pragma unroll
-    for (int r = 0; r < R; ++r)
-#pragma unroll
-        for (int h = 0; h < H; ++h) {
-            const int64_t di = __double2ll_rn(acc[r][h]);
-            const int64_t prod = (int64_t)((uint64_t)di * (uint64_t)knorm[r]);
-            bool hit;
-            s[r][h] = qclamp(prod >> g.score_shift, g.score_width, g.saturate, hit);
-            ovf += hit && valid[r];
-        }
 }
 
-__device__ __forceinline__ long long ld_volatile(const long long *p) {
-    return *reinterpret_cast<const volatile long long *>(p);
+// One row's K code words (KB words per 32 channels) and its norm word.
+template <int KB>
+__device__ __forceinline__ void load_krow(const Geo &g, const uint8_t *reg, int lr,
+                                          uint32_t (&kw)[KB * 2], uint32_t &nw) {
+    const uint8_t *kp = reg + (int64_t)lr * (KB * 8);
+    if constexpr (KB == 4) {
+        const uint4 a = __ldg(reinterpret_cast<const uint4 *>(kp));
+        const uint4 b = __ldg(reinterpret_cast<const uint4 *>(kp) + 1);
+        kw[0] = a.x; kw[1] = a.y; kw[2] = a.z; kw[3] = a.w;
+        kw[4] = b.x; kw[5] = b.y; kw[6] = b.z; kw[7] = b.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < KB; ++i) {
+            const uint2 a = __ldg(reinterpret_cast<const uint2 *>(kp) + i);
+            kw[2 * i] = a.x;
+            kw[2 * i + 1] = a.y;
+        }
+    }
+    nw = __ldg(reinterpret_cast<const uint32_t *>(reg + nplane_off(g) + (int64_t)lr * 4));
 }
-__device__ __forceinline__ unsigned long long ld_volatile(const unsigned long long *p) {
-    return *reinterpret_cast<const volatile unsigned long long *>(p);
+
+// One row's V code words and its norm word.
+template <int VB>
+__device__ __forceinline__ void load_vrow(const Geo &g, const uint8_t *reg, int lr,
+                                          uint32_t (&vw)[VB * 2], uint32_t &nw) {
+    const uint8_t *vp = reg + vplane_off(g) + (int64_t)lr * (VB * 8);
+    if constexpr (VB == 2) {
+        const uint4 a = __ldg(reinterpret_cast<const uint4 *>(vp));
+        vw[0] = a.x; vw[1] = a.y; vw[2] = a.z; vw[3] = a.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < VB; ++i) {
+            const uint2 a = __ldg(reinterpret_cast<const uint2 *>(vp) + i);
+            vw[2 * i] = a.x;
+            vw[2 * i + 1] = a.y;
+        }
+    }
+    nw = __ldg(reinterpret_cast<const uint32_t *>(reg + nplane_off(g) + (int64_t)lr * 4));
+}
+
+// Code j (0..63) of a row held as KB*2 words (32 codes of KB bits = KB words).
+// The extraction is a volatile asm statement so that the compiler keeps it
+// next to its lookup instead of computing all 64 x R of them up front, which
+// would need more registers than the kernel has.
+template <int KB>
+__device__ __forceinline__ uint32_t kcode(const uint32_t (&kw)[KB * 2], int j);
+
+// The codes of channels 2p and 2p+1 of a row held as KB*2 words, as one index
+// code(2p) + code(2p+1) << KB (bits 2p*KB .. 2p*KB + 2KB - 1 of the row; no
+// 32-channel group boundary falls inside a pair). Pinned like kcode.
+template <int KB>
+__device__ __forceinline__ uint32_t kpair(const uint32_t (&kw)[KB * 2], int p) {
+    const int pos = (p >> 4) * 32 * KB + (p & 15) * 2 * KB;
+    const int wi = pos >> 5, sh = pos & 31;
+    uint32_t v;
+    if (sh + 2 * KB <= 32) {
+        asm volatile("bfe.u32 %0, %1, %2, %3;" : "=r"(v) : "r"(kw[wi]), "r"(sh), "r"(2 * KB));
+    } else {
+        asm volatile("{\n\t.reg .u32 t;\n\tshf.r.clamp.b32 t, %1, %2, %3;\n\tand.b32 %0, t, %4;\n\t}"
+                     : "=r"(v) : "r"(kw[wi]), "r"(kw[wi + 1]), "r"(sh), "r"((1u << (2 * KB)) - 1u));
+    }
+    return v;
+}
+
+template <int KB>
+__device__ __forceinline__ uint32_t kcode(const uint32_t (&kw)[KB * 2], int j) {
+    const int pos = (j >> 5) * 32 * KB + (j & 31) * KB;   // bit position in the row
+    const int wi = pos >> 5, sh = pos & 31;
+    uint32_t v;
+    if (sh + KB <= 32) {
+        asm volatile("bfe.u32 %0, %1, %2, %3;" : "=r"(v) : "r"(kw[wi]), "r"(sh), "r"(KB));
+    } else {
+        asm volatile("{\n\t.reg .u32 t;\n\tshf.r.clamp.b32 t, %1, %2, %3;\n\tand.b32 %0, t, %4;\n\t}"
+                     : "=r"(v) : "r"(kw[wi]), "r"(kw[wi + 1]), "r"(sh), "r"((1u << KB) - 1u));
+    }
+    return v;
 }
 
 template <class T>
@@ -231,18 +342,30 @@ __device__ __forceinline__ T ldcg(const T *p) {
     return __ldcg(p);
 }
 
-// Level 1: fold the chunks of block `blk` of `item` into a BlockRec.
-// Threads [0, H*64) own (head, channel) pairs.
+// Max over the CTA of non-negative values < 2^51, with two 32-bit warp
+// reductions per warp and one slot per warp. Every thread calls it.
+__device__ __forceinline__ long long cta_max_nonneg(long long v, long long *slots /* [NT/32] */) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int hi = (int)(v >> 20);
+    const int mhi = __reduce_max_sync(FULL, hi);
+    const unsigned mlo = __reduce_max_sync(FULL, hi == mhi ? (unsigned)(v & 0xFFFFF) : 0u);
+    __syncthreads();
+    if (lane == 0) slots[warp] = (long long)mhi * (1ll << 20) + (long long)mlo;
+    __syncthreads();
+    long long m = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = slots[w] > m ? slots[w] : m;
+    return m;
+}
+
+// Level 1: fold the tiles of block `blk` of `item` into a BlockRec. The CTA's
+// threads take the (head, channel) pairs in turn.
 template <int H>
 __device__ void merge_block(const ChunkArgs &a, int item, int blk, int nchunks,
                             int *base_sm /* [H] */) {
-    const int tid = threadIdx.x;
-    const bool own = tid < H * D;
-    const int h = own ? tid / D : 0, ch = tid % D;
     const int c0 = blk * GBLK, c1 = min(nchunks, c0 + GBLK);
     const ChunkRec *recs = a.recs + (int64_t)item * a.max_chunks;
-    // entries this head needs = rescales in the block's chunks
-    if (own && ch == 0) {
+    // entries each head needs = rescales in the block's tiles
+    for (int h = threadIdx.x; h < H; h += blockDim.x) {
         int need = 0;
         for (int c = c0; c < c1; ++c) need += ldcg(&recs[c].nseg[h]);
         unsigned b = 0;
@@ -254,7 +377,8 @@ __device__ void merge_block(const ChunkArgs &a, int item, int blk, int nchunks,
         base_sm[h] = need ? (int)b : -1;
     }
     __syncthreads();
-    if (own) {
+    for (int pr = threadIdx.x; pr < H * D; pr += blockDim.x) {
+        const int h = pr / D, ch = pr % D;
         const int eb = base_sm[h];
         int64_t loc = 0, Y = 0, curS = 0, curl = 0, Spre = 0, lpre = 0;
         int ne = 0;
@@ -326,14 +450,19 @@ __device__ void merge_block(const ChunkArgs &a, int item, int blk, int nchunks,
 // sequential recomputation.
 template <int H>
 __device__ void merge_item(const ChunkArgs &a, int item, int nblocks, int64_t T,
-                           int64_t qbase, long long *maxs_sm) {
+                           int64_t qbase, long long *slots /* [NT/32] */) {
+    constexpr int NP = (H * D + CHUNK_THREADS - 1) / CHUNK_THREADS;   // pairs per thread
     const int tid = threadIdx.x;
-    const bool own = tid < H * D;
-    const int h = own ? tid / D : 0, ch = tid % D;
     const BlockRec *blks = a.blks + (int64_t)item * a.max_blocks;
-    int64_t acc = 0, l = 0;
+    int64_t acc[NP], l[NP];
     bool bad = *reinterpret_cast<volatile int32_t *>(&a.items[item].fail) != 0;
-    if (own && !bad) {
+#pragma unroll
+    for (int k = 0; k < NP; ++k) {
+        acc[k] = 0;
+        l[k] = 0;
+        const int pr = tid + k * CHUNK_THREADS;
+        if (pr >= H * D || bad) continue;
+        const int h = pr / D, ch = pr % D;
         for (int bb = 0; bb < nblocks; ++bb) {
             const BlockRec &br = blks[bb];
             const int64_t Y = ldcg(&br.Y[h][ch]);
@@ -341,36 +470,36 @@ __device__ void merge_item(const ChunkArgs &a, int item, int nblocks, int64_t T,
             const int64_t lp = ldcg(&br.lpre[h]);
             const int ne = ldcg(&br.nent[h]);
             const int eb = ldcg(&br.ent_base[h]);
-            const int64_t aa = acc < 0 ? -acc : acc;
+            const int64_t aa = acc[k] < 0 ? -acc[k] : acc[k];
             if (aa + Y > INT32_MAX) bad = true;
-            acc += Sp;
-            l += lp;
+            acc[k] += Sp;
+            l[k] += lp;
             for (int e = 0; e < ne; ++e) {
                 const SegEntry &se = a.segs[eb + e];
                 const int64_t f = ldcg(&se.f);
-                acc = ((acc * f) >> a.g.prob_frac) + ldcg(&se.S[ch]);
-                l = ((l * f) >> a.g.prob_frac) + ldcg(&se.l);
+                acc[k] = ((acc[k] * f) >> a.g.prob_frac) + ldcg(&se.S[ch]);
+                l[k] = ((l[k] * f) >> a.g.prob_frac) + ldcg(&se.l);
             }
         }
     }
     bad = __syncthreads_or(bad);
-    if (tid == 0) {
-        a.redo[item] = bad ? 1 : 0;
-        *maxs_sm = 0;
-    }
+    if (tid == 0) a.redo[item] = bad ? 1 : 0;
     if (bad) return;
     int64_t *out_row = a.out + qbase;
     long long mx = 0;
-    if (own) {
+#pragma unroll
+    for (int k = 0; k < NP; ++k) {
+        const int pr = tid + k * CHUNK_THREADS;
+        if (pr >= H * D) continue;
         int64_t r;
         int shift;
-        reciprocal(a.g, l, r, shift);
-        out_row[h * D + ch] = (acc * r) >> shift;
-        mx = acc < 0 ? -acc : acc;
+        reciprocal(a.g, l[k], r, shift);
+        out_row[pr] = (acc[k] * r) >> shift;
+        const long long ab = acc[k] < 0 ? -acc[k] : acc[k];
+        mx = ab > mx ? ab : mx;
     }
-    __syncthreads();
-    if (own) atomicMax(maxs_sm, mx);
-    __syncthreads();
+    // the fold already proved |acc| <= 2^31 - 1
+    mx = cta_max_nonneg(mx, slots);
     if (tid == 0 && a.stats) {
         const volatile ItemAcc &ia = a.items[item];
         ins_stats st;
@@ -379,63 +508,330 @@ __device__ void merge_item(const ChunkArgs &a, int item, int nblocks, int64_t T,
         st.score_overflows = (int64_t)ia.sovf;
         st.acc_overflows = 0;
         st.max_abs_score = ia.maxs;
-        st.max_abs_acc = *maxs_sm;
+        st.max_abs_acc = mx;
         a.stats[item] = st;
     }
 }
 
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Prefetches into L2 the rows of tile `tile` that a launch will read: the K
+// plane and norms (`which` & 1), the V plane and norms (`which` & 2), one lane
+// per page the tile touches. Every range starts 16-byte aligned inside its
+// plane and is rounded up to 16 bytes without leaving the plane.
+__device__ __forceinline__ void prefetch_tile(const ChunkArgs &a, int tile, int lane, int which) {
+    const Geo &g = a.g;
+    const int4 td = a.tiles[tile];
+    const int item = td.x, n = td.w;
+    if (n <= 0) return;
+    const int64_t t0 = td.z;
+    const int seq = a.seq_ids[item / g.n_kv], kvh = item % g.n_kv;
+    const int64_t p0 = t0 / g.P;
+    const int poff = (int)(t0 % g.P);
+    const int npages = (poff + n + g.P - 1) / g.P;
+    auto up16 = [](int x) { return (uint32_t)((x + 15) & ~15); };
+    for (int i = lane; i < npages; i += 32) {
+        const int64_t page = a.page_table[(int64_t)seq * g.max_pages + p0 + i];
+        const uint8_t *reg = a.pool + region_off(g, page, kvh);
+        const int r0 = i == 0 ? poff : 0;
+        const int r1 = min(g.P, poff + n - i * g.P);
+        const int rows = r1 - r0;
+        if (which & 1) prefetch_l2(reg + (int64_t)r0 * g.kbytes, up16(rows * g.kbytes));
+        if (which & 2) prefetch_l2(reg + vplane_off(g) + (int64_t)r0 * g.vbytes, up16(rows * g.vbytes));
+        prefetch_l2(reg + nplane_off(g) + (int64_t)r0 * 4, up16(rows * 4));
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Launch 1: the scores of every tile
+// ---------------------------------------------------------------------------
+// CompressedAttention.scores (ops/attention.py:333-359) for R rows per thread:
+// the dot product of q with the rows' key centroids in FP64 (exact: integer
+// operands and every partial sum below 2^53), times the key norm, floored by
+// score_shift and clamped to score_width. Thread tid owns rows tid + r*NT, so
+// each warp holds one 32-row block for every r. A score is stored as its offset
+// below the block maximum (uint32; a larger gap flags the item for the exact
+// body), the block maxima and the tile maximum as int64.
 template <int H, int KB, int VB>
-__global__ void __launch_bounds__(H * 64 > 256 ? H * 64 : 256, H * 64 > 256 ? 1 : 2)
-    k_scan_chunk(ChunkArgs a) {
-    using L = ChunkLayout<H, VB>;
-    constexpr int NC = L::NC, SUB = L::SUB, VW = L::VW, PS = L::PS;
-    constexpr int NT = H * 64 > 256 ? H * 64 : 256;
-    constexpr int R = INS_SCORE_ROWS;                // rows per thread in the score phase
-    extern __shared__ __align__(16) uint8_t dyn[];
-    __shared__ double qd[H * D];
-    __shared__ uint32_t khi[256];
-    __shared__ int32_t vcent[256];
-    __shared__ int32_t exp_tab[256];
-    __shared__ long long cmax[H], m_in_sm[H];
-    __shared__ int tile_sm, flag_sm, fail_sm;
-    __shared__ int nseg_sm[H], segbase_sm[H], base_sm[H];
-    __shared__ int32_t rl_f[H][SEGMAX];
-    __shared__ unsigned long long lsum_sm[H][SEGMAX + 1];
-    __shared__ long long bsum_sm[H];
-    __shared__ unsigned long long resc_sm;
-    __shared__ unsigned int sovf_sm;
-    __shared__ long long maxs_sm;
-    __shared__ const uint8_t *page_sm[8];
+__global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
+    using CF = ChunkCfg<H, KB, VB>;
+    constexpr int NT = CF::NT, R = CF::R, C = CF::C, CW = CF::CW;
+    __shared__ __align__(16) double qd[D * H];  // [channel][head]
+    __shared__ long long wmax_sm[NT / 32][H];
+    // The key centroids of a channel pair, (c[k0], c[k1]) for index k0 + k1 << KB,
+    // as exact doubles, in 8 replicas: lane l reads replica l & 7, so the 8
+    // lanes of a 16-byte shared-memory wavefront never meet in a bank.
+    extern __shared__ __align__(16) uint8_t dynA[];
+    double2 *ctab = reinterpret_cast<double2 *>(dynA);
 
     const Geo &g = a.g;
-    const int tid = threadIdx.x;
-    const L lay(a.C);
-    const int CW = a.C / 32;
-    int64_t *s_sm = reinterpret_cast<int64_t *>(dyn + lay.off_s);
-    int32_t *p_sm = reinterpret_cast<int32_t *>(dyn + lay.off_p);
-    uint32_t *vt = reinterpret_cast<uint32_t *>(dyn + lay.off_vt);
-    int32_t *vn_sm = reinterpret_cast<int32_t *>(dyn + lay.off_vn);
-    int32_t *tab = reinterpret_cast<int32_t *>(dyn + lay.off_tab);
-    uint32_t *grew = reinterpret_cast<uint32_t *>(dyn + lay.off_grew);   // [H][CW], then any [CW]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int i = tid; i < (1 << (2 * KB)) * 8; i += NT) {
+        const int e = i >> 3;
+        ctab[i] = make_double2(a.tb->k_cent_f64[e & ((1 << KB) - 1)], a.tb->k_cent_f64[e >> KB]);
+    }
+    const double2 *myc = ctab + (lane & 7);
+    constexpr int64_t s_lo = DefFmt::S_LO;
+
+    for (int tile = blockIdx.x; tile < a.n_tiles; tile += gridDim.x) {
+        const int4 td = a.tiles[tile];
+        const int item = td.x, c = td.y;
+        const int64_t t0 = td.z;
+        const int n = td.w;
+        const int b = item / g.n_kv, kvh = item % g.n_kv;
+        const int seq = a.seq_ids[b];
+        const int64_t qbase = ((int64_t)b * g.n_kv * H + (int64_t)kvh * H) * D;
+        const int poff = (int)(t0 % g.P);
+        uint32_t *sc = a.sc + (a.row_base[item] + t0) * H;
+        const int32_t *ptab = a.page_table + (int64_t)seq * g.max_pages + t0 / g.P;
+
+        // each thread fetches its own rows first, so that their latency
+        // overlaps the rest of the setup
+        uint32_t kw[R][KB * 2];
+        int64_t knorm[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int row = r * NT + tid;
+            uint32_t nw = 0;
+#pragma unroll
+            for (int i = 0; i < KB * 2; ++i) kw[r][i] = 0;
+            if (row < n) {                       // a tile may be empty (a sequence of length 0)
+                int pi, lr;
+                page_row(g, poff + row, pi, lr);
+                load_krow<KB>(g, a.pool + region_off(g, ptab[pi], kvh), lr, kw[r], nw);
+            }
+            knorm[r] = (int64_t)(int16_t)(nw & 0xffffu);
+        }
+        __syncthreads();                         // the previous tile is done with qd
+        for (int i = tid; i < H * D; i += NT) qd[(i % D) * H + i / D] = (double)a.q_rot[qbase + i];
+        __syncthreads();
+        bool big = false;
+        for (int i = tid; i < H * D; i += NT) {
+            const double x = qd[i];
+            big |= (x >= 1073741824.0 || x <= -1073741824.0);
+        }
+        // |q| >= 2^30 would let an FP64 partial sum pass 2^53: the item goes to
+        // the exact int64 body
+        if (__syncthreads_or(big) && tid == 0) atomicExch(&a.items[item].fail, 1);
+        // the next tile of this CTA, into L2 while this one computes
+        if (warp == 1 && tile + (int)gridDim.x < a.n_tiles) prefetch_tile(a, tile + gridDim.x, lane, 1);
+
+        double acc[R][H];
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int h = 0; h < H; ++h) acc[r][h] = 0.0;
+#pragma unroll
+        for (int p = 0; p < D / 2; ++p) {
+            double c0[R], c1[R];
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const double2 cc = myc[kpair<KB>(kw[r], p) * 8];
+                c0[r] = cc.x;
+                c1[r] = cc.y;
+            }
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int j = 2 * p + e;
+                double qv[H];
+                if constexpr (H >= 2) {
+#pragma unroll
+                    for (int h = 0; h < H; h += 2) {
+                        const double2 q2 = *reinterpret_cast<const double2 *>(&qd[j * H + h]);
+                        qv[h] = q2.x;
+                        qv[h + 1] = q2.y;
+                    }
+                } else {
+                    qv[0] = qd[j];
+                }
+#pragma unroll
+                for (int h = 0; h < H; ++h)
+#pragma unroll
+                    for (int r = 0; r < R; ++r) acc[r][h] = fma(qv[h], e ? c1[r] : c0[r], acc[r][h]);
+            }
+            // keeps the scheduler from hoisting every lookup of the row
+            if ((p & 3) == 3) asm volatile("" ::: "memory");
+        }
+        // scores, then the block maxima of all (r, h) as independent warp
+        // reductions, then the stores
+        unsigned ovf = 0, gap = 0;
+        long long mx = 0;
+        int64_t sv[R][H];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const bool valid = r * NT + tid < n;
+#pragma unroll
+            for (int h = 0; h < H; ++h) {
+                const int64_t di = __double2ll_rn(acc[r][h]);
+                const int64_t prod = (int64_t)((uint64_t)di * (uint64_t)knorm[r]);
+                bool hit;   // saturate (qclamp, numerics/fixed.py:161-168)
+                const int64_t s0 = prod >> DefFmt::SCORE_SHIFT;
+                hit = s0 < DefFmt::S_LO || s0 > DefFmt::S_HI;
+                const int64_t s = s0 < DefFmt::S_LO ? DefFmt::S_LO : (s0 > DefFmt::S_HI ? DefFmt::S_HI : s0);
+                ovf += hit && valid;
+                const long long ab = s < 0 ? -s : s;
+                mx = valid && ab > mx ? ab : mx;
+                sv[r][h] = valid ? s : s_lo;
+            }
+        }
+        // block maximum in two 32-bit reductions: |s| <= 2^47, so
+        // s = hi * 2^20 + lo with hi an int and 0 <= lo < 2^20
+        int mhi[R][H];
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int h = 0; h < H; ++h) mhi[r][h] = __reduce_max_sync(FULL, (int)(sv[r][h] >> 20));
+        int64_t hmax[H];
+#pragma unroll
+        for (int h = 0; h < H; ++h) hmax[h] = LLONG_MIN;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int row = r * NT + tid;
+            uint32_t off[H];
+#pragma unroll
+            for (int h = 0; h < H; ++h) {
+                const bool top = (int)(sv[r][h] >> 20) == mhi[r][h];
+                const unsigned mlo = __reduce_max_sync(FULL, top ? (unsigned)(sv[r][h] & 0xFFFFF) : 0u);
+                const int64_t bm = (int64_t)mhi[r][h] * (1ll << 20) + (int64_t)mlo;
+                hmax[h] = bm > hmax[h] ? bm : hmax[h];
+                if (lane == h) a.bmg[((int64_t)tile * H + h) * CW + (row >> 5)] = bm;
+                const uint64_t d = (uint64_t)(bm - sv[r][h]);
+                gap |= (unsigned)(row < n && d > 0xFFFFFFFFull);
+                off[h] = (uint32_t)(d > 0xFFFFFFFFull ? 0xFFFFFFFFull : d);
+            }
+            if (row < n) {
+                uint32_t *dst = sc + (int64_t)row * H;
+                if constexpr (H == 8) {
+                    reinterpret_cast<uint4 *>(dst)[0] = make_uint4(off[0], off[1], off[2], off[3]);
+                    reinterpret_cast<uint4 *>(dst)[1] = make_uint4(off[4], off[5], off[6], off[7]);
+                } else if constexpr (H == 4) {
+                    *reinterpret_cast<uint4 *>(dst) = make_uint4(off[0], off[1], off[2], off[3]);
+                } else if constexpr (H == 2) {
+                    *reinterpret_cast<uint2 *>(dst) = make_uint2(off[0], off[1]);
+                } else {
+                    dst[0] = off[0];
+                }
+            }
+        }
+        // a score more than 2^32 below its block maximum: exact body
+        if (__any_sync(FULL, gap) && lane == 0) atomicExch(&a.items[item].fail, 1);
+        ovf = __reduce_add_sync(FULL, ovf);
+        const int xhi = __reduce_max_sync(FULL, (int)(mx >> 20));
+        const unsigned xlo = __reduce_max_sync(FULL, (int)(mx >> 20) == xhi ? (unsigned)(mx & 0xFFFFF) : 0u);
+        if (lane == 0) {
+            ItemAcc &ia = a.items[item];
+            if (ovf) atomicAdd(&ia.sovf, (unsigned long long)ovf);
+            const long long wm = (long long)xhi * (1ll << 20) + (long long)xlo;
+            if (wm) atomicMax(&ia.maxs, wm);
+#pragma unroll
+            for (int h = 0; h < H; ++h) wmax_sm[warp][h] = hmax[h];
+        }
+        __syncthreads();
+        if (tid < H) {
+            long long m = wmax_sm[0][tid];
+            for (int w = 1; w < NT / 32; ++w) m = wmax_sm[w][tid] > m ? wmax_sm[w][tid] : m;
+            a.cmx[((int64_t)item * a.max_chunks + c) * 2 * HMAX + tid] = m;
+        }
+        __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Launch 2: the running maximum entering every tile
+// ---------------------------------------------------------------------------
+// One CTA per (item, head): m_in(c) = max(-2^(score_width-1), max of the maxima
+// of tiles 0 .. c-1), the m the recurrence carries into tile c. Each thread
+// folds a run of consecutive tiles; the runs' maxima are scanned across the
+// CTA.
+template <int H>
+__global__ void __launch_bounds__(256) k_chunk_prefix(ChunkArgs a) {
+    __shared__ long long wtot[8];
+    const int item = blockIdx.x / H, h = blockIdx.x % H;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nc = a.item_nchunks[item];
+    long long *v = a.cmx + (int64_t)item * a.max_chunks * 2 * HMAX;
+    const long long s_lo = -(1ll << (a.g.score_width - 1));
+    const int per = (nc + 255) / 256;                 // tiles per thread
+    const int c0 = tid * per, c1 = min(nc, c0 + per);
+    long long run = LLONG_MIN;
+    for (int c = c0; c < c1; ++c) {
+        const long long x = v[(int64_t)c * 2 * HMAX + h];
+        run = x > run ? x : run;
+    }
+    // exclusive scan of the runs' maxima across the CTA
+    long long x = run;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const long long y = __shfl_up_sync(FULL, x, off);
+        if (lane >= off) x = y > x ? y : x;
+    }
+    if (lane == 31) wtot[warp] = x;
+    __syncthreads();
+    long long before = s_lo;
+    for (int w = 0; w < warp; ++w) before = wtot[w] > before ? wtot[w] : before;
+    long long ex = __shfl_up_sync(FULL, x, 1);
+    if (lane == 0) ex = LLONG_MIN;
+    ex = ex > before ? ex : before;
+    for (int c = c0; c < c1; ++c) {
+        v[(int64_t)c * 2 * HMAX + HMAX + h] = ex;
+        const long long y = v[(int64_t)c * 2 * HMAX + h];
+        ex = y > ex ? y : ex;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Launch 3: the values
+// ---------------------------------------------------------------------------
+template <int H, int KB, int VB>
+__global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
+    using CF = ChunkCfg<H, KB, VB>;
+    constexpr int NT = CF::NT, R = CF::R, C = CF::C, CW = CF::CW, NC = CF::NC, VW = CF::VW;
+    constexpr int TPE = CF::TPE, NE = CF::NE, HG = CF::HG, HL = CF::HL, SUBT = CF::SUBT;
+    constexpr int UNITS = CF::UNITS, USTR = CF::USTR, HPS = CF::HPS, TPW = CF::TPW, TWS = CF::TWS,
+                  VS = CF::VS;
+    constexpr int UPW = 32 / H;                 // table units per warp in the build
+    extern __shared__ __align__(16) uint8_t dyn[];
+    __shared__ int32_t vcent[256];
+    __shared__ int32_t exp_tab[256];
+    __shared__ long long m_in_sm[H];
+    __shared__ int flag_sm, fail_sm;
+    __shared__ int nseg_sm[H], segbase_sm[H], base_sm[H];
+    __shared__ int32_t rl_f[H][SEGMAX];
+    __shared__ unsigned int lsum_sm[H][SEGMAX + 1];   // l of a tile < 2^25
+    __shared__ long long bnd_sm[NT / 32][H];           // per-warp clamp-proof bounds
+    __shared__ long long slots_sm[NT / 32];
+    __shared__ unsigned int resc_sm;
+
+    const Geo &g = a.g;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // a score's offset below its block maximum, later w = v_norm * p (as int32)
+    uint32_t *d_sm = reinterpret_cast<uint32_t *>(dyn + CF::OFF_S);
+    uint32_t *tw = reinterpret_cast<uint32_t *>(dyn + CF::OFF_TW);
+    int32_t *vn_sm = reinterpret_cast<int32_t *>(dyn + CF::OFF_VN);
+    int32_t *tabs = reinterpret_cast<int32_t *>(dyn + CF::OFF_TAB);
+    uint32_t *vt = reinterpret_cast<uint32_t *>(dyn + CF::OFF_TAB);      // V staging, aliases the tables
+    uint32_t *grew = reinterpret_cast<uint32_t *>(dyn + CF::OFF_GREW);   // [H][CW], then any [CW]
     uint32_t *anyg = grew + H * CW;
-    int32_t *gpre = reinterpret_cast<int32_t *>(dyn + lay.off_pre);     // [H][CW]
-    long long *bmax = reinterpret_cast<long long *>(dyn + lay.off_bmax);  // [H][CW]
-    long long *bcar = reinterpret_cast<long long *>(dyn + lay.off_bcar);  // [H][CW]
-    int32_t *s0p = reinterpret_cast<int32_t *>(dyn + lay.off_s0);
+    int32_t *gpre = reinterpret_cast<int32_t *>(dyn + CF::OFF_PRE);     // [H][CW]
+    long long *bmax = reinterpret_cast<long long *>(dyn + CF::OFF_BMAX);  // [H][CW]
+    long long *bcar = reinterpret_cast<long long *>(dyn + CF::OFF_BCAR);  // [H][CW]
+    long long *dbase = reinterpret_cast<long long *>(dyn + CF::OFF_DB);   // [H][CW]: carry - block max
+    int32_t *s0p = reinterpret_cast<int32_t *>(dyn + CF::OFF_S0);
 
     for (int i = tid; i < 256; i += NT) {
-        const double c = a.tb->k_cent_f64[i];
-        khi[i] = (uint32_t)__double2hiint(c);
         vcent[i] = (int32_t)a.tb->v_cent[i];
         exp_tab[i] = a.tb->exp_tab[i];
     }
-    const int64_t s_lo = -(1ll << (g.score_width - 1));
+    int64_t cmax_v = 0;                       // max |V centroid|
+    for (int k = 0; k < NC; ++k) {
+        const int64_t ab = a.tb->v_cent[k] < 0 ? -a.tb->v_cent[k] : a.tb->v_cent[k];
+        cmax_v = ab > cmax_v ? ab : cmax_v;
+    }
 
-    for (;;) {
-        if (tid == 0) tile_sm = (int)(atomicAdd(a.claim, 1ull) - a.claim_base);
-        __syncthreads();
-        const int tile = tile_sm;
-        if (tile >= a.n_tiles) break;
+    // Tiles are dealt round-robin; no tile waits on another.
+    for (int tile = blockIdx.x; tile < a.n_tiles; tile += gridDim.x) {
         const int4 td = a.tiles[tile];
         const int item = td.x, c = td.y;
         const int64_t t0 = td.z;
@@ -444,179 +840,120 @@ __global__ void __launch_bounds__(H * 64 > 256 ? H * 64 : 256, H * 64 > 256 ? 1 
         const int seq = a.seq_ids[b];
         const int64_t qbase = ((int64_t)b * g.n_kv * H + (int64_t)kvh * H) * D;
         const int rec_idx = item * a.max_chunks + c;
+        const int poff = (int)(t0 % g.P);
+        const uint32_t *sc = a.sc + (a.row_base[item] + t0) * H;
 
-        // ---- 0. per-tile setup -------------------------------------------------
-        for (int i = tid; i < H * D; i += NT) qd[i] = (double)a.q_rot[qbase + i];
-        const int npages = (n + g.P - 1) / g.P;
-        if (tid < npages) {
-            const int64_t page = a.page_table[(int64_t)seq * g.max_pages + (t0 / g.P) + tid];
-            page_sm[tid] = a.pool + region_off(g, page, kvh);
+        // ---- 0. the tile's rows (each thread its own, first), per-tile setup ----
+        const int32_t *ptab = a.page_table + (int64_t)seq * g.max_pages + t0 / g.P;
+        uint32_t vw[R][VW], nw[R], off[R][H];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int row = r * NT + tid;
+            if (row < n) {
+                int pi, lr;
+                page_row(g, poff + row, pi, lr);
+                load_vrow<VB>(g, a.pool + region_off(g, ptab[pi], kvh), lr, vw[r], nw[r]);
+                const uint32_t *src = sc + (int64_t)row * H;
+                if constexpr (H == 8) {
+                    const uint4 x = __ldg(reinterpret_cast<const uint4 *>(src));
+                    const uint4 y = __ldg(reinterpret_cast<const uint4 *>(src) + 1);
+                    off[r][0] = x.x; off[r][1] = x.y; off[r][2] = x.z; off[r][3] = x.w;
+                    off[r][4] = y.x; off[r][5] = y.y; off[r][6] = y.z; off[r][7] = y.w;
+                } else if constexpr (H == 4) {
+                    const uint4 x = __ldg(reinterpret_cast<const uint4 *>(src));
+                    off[r][0] = x.x; off[r][1] = x.y; off[r][2] = x.z; off[r][3] = x.w;
+                } else if constexpr (H == 2) {
+                    const uint2 x = __ldg(reinterpret_cast<const uint2 *>(src));
+                    off[r][0] = x.x; off[r][1] = x.y;
+                } else {
+                    off[r][0] = __ldg(src);
+                }
+            }
         }
+        for (int i = tid; i < H * CW; i += NT) bmax[i] = a.bmg[(int64_t)tile * H * CW + i];
         if (tid < H) {
-            cmax[tid] = LLONG_MIN;
-            bsum_sm[tid] = 0;
+            m_in_sm[tid] = a.cmx[((int64_t)item * a.max_chunks + c) * 2 * HMAX + HMAX + tid];
             for (int k = 0; k <= SEGMAX; ++k) lsum_sm[tid][k] = 0;
         }
         if (tid == 0) {
             resc_sm = 0;
-            sovf_sm = 0;
-            maxs_sm = 0;
             fail_sm = 0;
         }
         for (int i = tid; i < (H + 1) * CW; i += NT) grew[i] = 0;
         for (int i = tid; i < H * D; i += NT) s0p[i] = 0;
         __syncthreads();
-        bool big = false;
-        for (int i = tid; i < H * D; i += NT) {
-            const double x = qd[i];
-            big |= (x >= 1073741824.0 || x <= -1073741824.0);
-        }
-        if (__syncthreads_or(big)) {
-            // |q| >= 2^30 would let an FP64 partial sum pass 2^53; such an
-            // item is left to the exact int64 sequential body.
-            if (tid == 0) atomicExch(&a.items[item].fail, 1);
-        }
 
-        // ---- 1. scores, staged V codes and norms --------------------------------
-        {
-            int ovf = 0;
-            long long mx = 0;
-            int64_t hmax[H];
+        // ---- 1. V codes, v norms and scores to shared memory ---------------------
 #pragma unroll
-            for (int h = 0; h < H; ++h) hmax[h] = LLONG_MIN;
-            for (int base = 0; base < n; base += NT * R) {
-                const uint8_t *krow[R];
-                int64_t knorm[R];
-                bool valid[R];
+        for (int r = 0; r < R; ++r) {
+            const int row = r * NT + tid;
+            if (row < n) {
+                vn_sm[row] = (int32_t)(int16_t)(nw[r] >> 16);
 #pragma unroll
-                for (int r = 0; r < R; ++r) {
-                    const int row = base + r * NT + tid;
-                    valid[r] = row < n;
-                    const int rr = valid[r] ? row : 0;
-                    const uint8_t *reg = page_sm[rr / g.P];
-                    const int lr = rr % g.P;
-                    krow[r] = reg + (int64_t)lr * g.kbytes;
-                    const int32_t nw = valid[r] ? *reinterpret_cast<const int32_t *>(
-                                                      reg + nplane_off(g) + (int64_t)lr * 4)
-                                                : 0;
-                    knorm[r] = (int16_t)(nw & 0xffff);
-                    if (valid[r]) {
-                        vn_sm[row] = (int32_t)(int16_t)((uint32_t)nw >> 16);
-                        const uint32_t *vrow = reinterpret_cast<const uint32_t *>(
-                            reg + vplane_off(g) + (int64_t)lr * g.vbytes);
+                for (int w = 0; w < VW; ++w) vt[w * VS + row + (row >> 4)] = vw[r][w];
 #pragma unroll
-                        for (int w = 0; w < VW; ++w) vt[w * a.C + row] = vrow[w];
-                    }
-                }
-                int64_t s[R][H];
-                score_rows<H, KB, R>(g, krow, knorm, valid, qd, khi, s, ovf);
-#pragma unroll
-                for (int r = 0; r < R; ++r) {
-                    const int row = base + r * NT + tid;
-#pragma unroll
-                    for (int h = 0; h < H; ++h) {
-                        long long bm = valid[r] ? s[r][h] : LLONG_MIN;
-                        if (valid[r]) {
-                            s_sm[h * a.C + row] = s[r][h];
-                            const long long ab = s[r][h] < 0 ? -s[r][h] : s[r][h];
-                            mx = ab > mx ? ab : mx;
-                        }
-#pragma unroll
-                        for (int o = 16; o > 0; o >>= 1) {
-                            const long long w = __shfl_xor_sync(FULL, bm, o);
-                            bm = w > bm ? w : bm;
-                        }
-                        hmax[h] = bm > hmax[h] ? bm : hmax[h];
-                        if ((tid & 31) == 0 && row < a.C) bmax[h * CW + (row >> 5)] = bm;
-                    }
-                }
-            }
-#pragma unroll
-            for (int h = 0; h < H; ++h) atomicMax(&cmax[h], (long long)hmax[h]);
-            if (ovf) atomicAdd(&sovf_sm, (unsigned)ovf);
-            atomicMax(&maxs_sm, mx);
-        }
-        __syncthreads();
-
-        // ---- 2. publish the chunk maximum, look back for the incoming one -------
-        unsigned long long *flags = a.lb_flag + (int64_t)item * a.max_chunks;
-        long long *vals = a.lb_val + (int64_t)item * a.max_chunks * 2 * HMAX;
-        if (tid < 32) {
-            const int lane = tid;
-            if (lane < H) vals[(int64_t)c * 2 * HMAX + lane] = cmax[lane];
-            __threadfence();
-            __syncwarp();
-            if (lane == 0) atomicExch(&flags[c], (a.epoch << 2) | 1ull);
-            // Warp-parallel look-back: lane i inspects chunk p_hi - i. Every
-            // predecessor up to the nearest one that published an inclusive
-            // maximum contributes its (aggregate or inclusive) maximum.
-            long long m_in[H];
-#pragma unroll
-            for (int h = 0; h < H; ++h) m_in[h] = s_lo;
-            bool timed_out = false;
-            for (int p_hi = c - 1; p_hi >= 0; p_hi -= 32) {
-                const int p = p_hi - lane;
-                int state = 2;                     // before chunk 0: inclusive of nothing
-                if (p >= 0) {
-                    unsigned long long f = 0;
-                    int it = 0;
-                    for (; it < LB_SPIN_LIMIT; ++it) {
-                        f = ld_volatile(&flags[p]);
-                        if ((f >> 2) == a.epoch && (f & 3ull)) break;
-                        __nanosleep(32);
-                    }
-                    if (it == LB_SPIN_LIMIT) {
-                        timed_out = true;
-                        f = (a.epoch << 2) | 2ull;  // stop here; the item is recomputed
-                    }
-                    state = (int)(f & 3ull);
-                }
-                __threadfence();
-                const uint32_t incl = __ballot_sync(FULL, state == 2);
-                const int stop = incl ? __ffs(incl) - 1 : 31;
-#pragma unroll
-                for (int h = 0; h < H; ++h) {
-                    long long v = s_lo;
-                    if (p >= 0 && lane <= stop)
-                        v = ld_volatile(&vals[(int64_t)p * 2 * HMAX + (state == 2 ? HMAX : 0) + h]);
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) {
-                        const long long w = __shfl_xor_sync(FULL, v, o);
-                        v = w > v ? w : v;
-                    }
-                    m_in[h] = v > m_in[h] ? v : m_in[h];
-                }
-                if (__any_sync(FULL, timed_out) || incl) break;
-            }
-            timed_out = __any_sync(FULL, timed_out);
-            if (lane == 0) {
-#pragma unroll
-                for (int h = 0; h < H; ++h) {
-                    m_in_sm[h] = m_in[h];
-                    vals[(int64_t)c * 2 * HMAX + HMAX + h] = cmax[h] > m_in[h] ? cmax[h] : m_in[h];
-                }
-            }
-            __threadfence();
-            __syncwarp();
-            if (lane == 0) {
-                atomicExch(&flags[c], (a.epoch << 2) | 2ull);
-                if (timed_out) {
-                    atomicOr(a.status, ST_TIMEOUT);
-                    atomicExch(&a.items[item].fail, 1);
-                }
+                for (int h = 0; h < H; ++h) d_sm[h * C + row] = off[r][h];
             }
         }
         __syncthreads();
 
-        // ---- 3. the online control, one warp per head -----------------------------
+        // ---- 2. V codes to channel-major words; warp 1 prefetches this CTA's
+        //         next tile into L2 first ------------------------------------------
+        if (warp == 1 && tile + (int)gridDim.x < a.n_tiles) {
+            const int nt = tile + gridDim.x;
+            prefetch_tile(a, nt, lane, 2);
+            if (lane == 0) {
+                const int4 t2 = a.tiles[nt];
+                const uint32_t bytes = (uint32_t)t2.w * H * 4;
+                if (bytes) prefetch_l2(a.sc + (a.row_base[t2.x] + t2.z) * H, (bytes + 15) & ~15u);
+            }
+        }
+        // word (ch, k) holds, as nibbles, the table indices of units 8k .. 8k+7
+        // of channel ch
+        if constexpr (VB == 2) {
+            for (int task = tid; task < (C / 16) * 4; task += NT) {
+                const int v = task >> 5, l = task & 31;
+                const int tg = (v >> 1) * 16 + (l & 15), w = 2 * (v & 1) + (l >> 4);
+                uint32_t A[16];
+                const uint32_t *src = vt + w * VS + 17 * tg;   // token 16tg+i sits at 17tg+i
+#pragma unroll
+                for (int i = 0; i < 16; ++i) A[i] = src[i];
+                transpose16x2(A);
+#pragma unroll
+                for (int cc = 0; cc < 16; ++cc) tw[(16 * w + cc) * TWS + tg] = A[cc];
+            }
+        } else {
+            // 3-bit codes: task (8-token group, 8-channel group); channel ch sits
+            // at bits 3ch .. 3ch+2 of the row, one nibble per token in the word.
+            for (int task = tid; task < (C / 8) * 8; task += NT) {
+                const int tg = task % (C / 8), cg = task / (C / 8);
+                const int bit = 24 * cg, wl = bit >> 5, sh = bit & 31;
+                uint32_t out[8];
+#pragma unroll
+                for (int cc = 0; cc < 8; ++cc) out[cc] = 0;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int t = 8 * tg + i, ts = t + (t >> 4);
+                    uint32_t x = vt[wl * VS + ts] >> sh;
+                    if (sh > 8) x |= vt[(wl + 1) * VS + ts] << (32 - sh);
+#pragma unroll
+                    for (int cc = 0; cc < 8; ++cc) out[cc] |= ((x >> (3 * cc)) & 7u) << (4 * i);
+                }
+#pragma unroll
+                for (int cc = 0; cc < 8; ++cc) tw[(8 * cg + cc) * TWS + tg] = out[cc];
+            }
+        }
+        __syncthreads();
+
+        // ---- 3. the online control, one warp per head at a time ------------------
         // Lane b holds 32-row block b. A prefix-max over the block maxima gives the
         // running maximum entering every block. A block whose maximum does not
-        // exceed it has no rescale point and one running maximum for all its
-        // tokens (p is then computed in the term build). Only the rare blocks
-        // that can rescale are scanned token by token here: rescale points
-        // (ballot bits), factors exp(s - m_old), p, and their l per segment.
-        if (tid < H * 32) {
-            const int h = tid >> 5, lane = tid & 31;
+        // exceed it has no rescale point: every token's p is exp(carry - s).
+        // The rare blocks that can rescale are scanned token by token here:
+        // rescale points (ballot bits) and factors exp(s - m_old); each of their
+        // tokens' scores is rewritten to carry - (m_t - s), so that the term
+        // build finds p = exp(carry - s') for it as for every other token.
+        for (int h = warp; h < H; h += NT / 32) {
             const int nb = (n + 31) / 32;
             const int64_t m_in = m_in_sm[h];
             int64_t x = lane < nb ? bmax[h * CW + lane] : LLONG_MIN;
@@ -631,6 +968,8 @@ __global__ void __launch_bounds__(H * 64 > 256 ? H * 64 : 256, H * 64 > 256 ? 1 
             const bool scanb = lane < nb && bmax[h * CW + lane] > car;
             if (lane < CW) {
                 bcar[h * CW + lane] = car;
+                // a token's distance below the running maximum is dbase + its offset
+                dbase[h * CW + lane] = lane < nb ? car - bmax[h * CW + lane] : 0;
                 grew[h * CW + lane] = 0u;
             }
             __syncwarp();
@@ -642,7 +981,8 @@ __global__ void __launch_bounds__(H * 64 > 256 ? H * 64 : 256, H * 64 > 256 ? 1 
                 todo &= todo - 1;
                 const int t = bb * 32 + lane;
                 const bool valid = t < n;
-                const int64_t st = valid ? s_sm[h * a.C + t] : LLONG_MIN;
+                const int64_t bmx = bmax[h * CW + bb];
+                const int64_t st = valid ? bmx - (int64_t)d_sm[h * C + t] : LLONG_MIN;
                 const int64_t carry = __shfl_sync(FULL, car, bb);
                 int64_t y = st;
 #pragma unroll
@@ -656,10 +996,17 @@ __global__ void __launch_bounds__(H * 64 > 256 ? H * 64 : 256, H * 64 > 256 ? 1 
                 const bool gr = valid && st > Mprev;
                 const uint32_t mask = __ballot_sync(FULL, gr);
                 if (lane == 0) grew[h * CW + bb] = mask;
-                if (valid) p_sm[h * a.C + t] = exp_lut32(g, exp_tab, Mt - st);
+                // this block's tokens carry their own distance m_t - s (dbase 0);
+                // one at or past 2^32 is far beyond delta_max, so clamping it
+                // leaves p = 0 exact
+                if (lane == 0) dbase[h * CW + bb] = 0;
+                if (valid) {
+                    const int64_t dn = Mt - st;
+                    d_sm[h * C + t] = (uint32_t)(dn > 0xFFFFFFFFll ? 0xFFFFFFFFll : dn);
+                }
                 // the factor of every rescale point of this block, in order
                 const int k = nres + __popc(mask & ((1u << lane) - 1u));
-                if (gr && k < SEGMAX) rl_f[h][k] = exp_lut(g, exp_tab, st - Mprev);
+                if (gr && k < SEGMAX) rl_f[h][k] = (int32_t)exp_lut_def(exp_tab, st - Mprev);
                 if (lane == bb) blkres = __popc(mask);
                 nres += __popc(mask);
             }
@@ -674,7 +1021,7 @@ __global__ void __launch_bounds__(H * 64 > 256 ? H * 64 : 256, H * 64 > 256 ? 1 
             if (lane < CW) gpre[h * CW + lane] = pre;
             if (lane == 0) {
                 nseg_sm[h] = nres;
-                atomicAdd(&resc_sm, (unsigned long long)nres);
+                atomicAdd(&resc_sm, (unsigned)nres);
             }
         }
         __syncthreads();
@@ -697,7 +1044,7 @@ __global__ void __launch_bounds__(H * 64 > 256 ? H * 64 : 256, H * 64 > 256 ? 1 
                 base = atomicAdd(a.seg_top, (unsigned)need);
                 ok = base + need <= (unsigned)a.seg_cap;
             }
-            if (!ok) {
+            if (!ok) {                   // the item is recomputed by the exact body
                 fail_sm = 1;
                 atomicExch(&a.items[item].fail, 1);
             }
@@ -717,186 +1064,234 @@ __global__ void __launch_bounds__(H * 64 > 256 ? H * 64 : 256, H * 64 > 256 ? 1 
                     if (tid == 0) e.f = rl_f[h][k];
                 }
         }
-        __syncthreads();
 
-        // ---- 4. V: terms per token, summed per segment ---------------------------
+        // ---- 4. V ------------------------------------------------------------------
+        // 4a. p-pass: p = exp(carry - s') and w = v_norm * p for every (token,
+        //     head); w replaces the score in place. The l of every segment and
+        //     the clamp-proof bound are summed here. Thread tid owns tokens
+        //     tid + r*NT: its warp holds block r*NT/32 + warp for each r.
         {
-            const int ch = tid % D, tg = tid / D;
-            constexpr int TG = NT / D;
-            int32_t acc[H];
-            int cur[H];
-            long long bnd[H];
+            uint32_t pv[R][H];
+            int64_t sumw[H];                          // sum of |w|, for the clamp-proof bound
+#pragma unroll
+            for (int h = 0; h < H; ++h) sumw[h] = 0;
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int t = r * NT + tid;
+                const bool valid = t < n;
+                const int blk = t >> 5;
+                const int32_t vnt = valid ? vn_sm[t] : 0;
+#pragma unroll
+                for (int h = 0; h < H; ++h) {
+                    const uint32_t p =
+                        valid ? exp_lut_def(exp_tab, dbase[h * CW + blk] + (int64_t)d_sm[h * C + t]) : 0u;
+                    const int32_t w = vnt * (int32_t)p;      // |w| <= 2^30
+                    if (valid) d_sm[h * C + t] = (uint32_t)w;
+                    sumw[h] += w < 0 ? -(int64_t)w : (int64_t)w;
+                    pv[r][h] = p;
+                }
+            }
+            // l: when the warp's R blocks are quiet for a head and share one
+            // segment (the common case), one warp sum and one atomic per head
 #pragma unroll
             for (int h = 0; h < H; ++h) {
-                acc[h] = 0;
-                bnd[h] = 0;
-            }
-            const int bit0 = ch * VB, w0 = bit0 >> 5, sh0 = bit0 & 31;
-            const bool straddle = sh0 + VB > 32;
-            const uint32_t cmask = (1u << VB) - 1u;
-            int64_t cmax_v = 0;
+                const int sg0 = gpre[h * CW + warp];
+                bool uni = true;
 #pragma unroll
-            for (int k = 0; k < NC; ++k) {
-                const int64_t ab = vcent[k] < 0 ? -(int64_t)vcent[k] : vcent[k];
-                cmax_v = ab > cmax_v ? ab : cmax_v;
-            }
-            const uint32_t *vw = vt + w0 * a.C;
-            for (int st = 0; st < n; st += SUB) {
-                const int ns = min(SUB, n - st);
-                // the term table of this sub-tile: [code][t][h], one token per thread
-                for (int tl0 = 0; tl0 < ns; tl0 += NT) {
-                    const int tl = tl0 + tid;
-                    const bool tv = tl < ns;
-                    const int t = st + (tv ? tl : 0);
-                    const int blkt = t >> 5;
-                    const int32_t vnt = tv ? vn_sm[t] : 0;
-                    int32_t term[NC][H];
+                for (int r = 0; r < R; ++r) {
+                    const int blk = r * (NT / 32) + warp;
+                    uni &= grew[h * CW + blk] == 0u && gpre[h * CW + blk] == sg0;
+                }
+                if (uni) {
+                    unsigned ps = 0;
 #pragma unroll
-                    for (int h = 0; h < H; ++h) {
-                        // p: from the scan for a block that rescales, else from its
-                        // single running maximum
-                        const uint32_t gw = grew[h * CW + blkt];
-                        const bool quiet = bmax[h * CW + blkt] <= bcar[h * CW + blkt];
-                        int32_t pv = 0;
-                        if (tv) pv = quiet ? exp_lut32(g, exp_tab, bcar[h * CW + blkt] - s_sm[h * a.C + t])
-                                           : p_sm[h * a.C + t];
-                        // l of the segment the token belongs to
-                        const int seg = gpre[h * CW + blkt] + __popc(gw & ((2u << (t & 31)) - 1u));
-                        const int seg0 = __shfl_sync(FULL, seg, 0);
-                        if (__all_sync(FULL, seg == seg0)) {
-                            unsigned sum = (unsigned)pv;
+                    for (int r = 0; r < R; ++r) ps += pv[r][h];
+                    const unsigned sum = __reduce_add_sync(FULL, ps);   // <= R * 32 * 2^15
+                    if (lane == 0 && sum && sg0 <= SEGMAX) atomicAdd(&lsum_sm[h][sg0], sum);
+                } else {
 #pragma unroll
-                            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(FULL, sum, o);
-                            if ((tid & 31) == 0 && sum && seg0 <= SEGMAX)
-                                atomicAdd(&lsum_sm[h][seg0], (unsigned long long)sum);
-                        } else if (tv && pv && seg <= SEGMAX) {
-                            atomicAdd(&lsum_sm[h][seg], (unsigned long long)pv);
-                        }
-                        const int32_t w = vnt * pv;                    // |w| <= 2^30
-#pragma unroll
-                        for (int k = 0; k < NC; ++k)
-                            term[k][h] = (int32_t)(((int64_t)w * (int64_t)vcent[k]) >> g.acc_shift);
-                        // |term| <= floor(|w| * max|c| / 2^acc_shift) + 1 for every code
-                        const int64_t aw = w < 0 ? -(int64_t)w : (int64_t)w;
-                        bnd[h] += ((aw * cmax_v) >> g.acc_shift) + 1;
-                    }
-#pragma unroll
-                    if (tv)
-#pragma unroll
-                    for (int k = 0; k < NC; ++k) {
-                        int32_t *dst = tab + k * PS + tl * H;
-                        if constexpr (H == 4) {
-                            *reinterpret_cast<int4 *>(dst) =
-                                make_int4(term[k][0], term[k][1], term[k][2], term[k][3]);
-                        } else if constexpr (H == 8) {
-                            reinterpret_cast<int4 *>(dst)[0] =
-                                make_int4(term[k][0], term[k][1], term[k][2], term[k][3]);
-                            reinterpret_cast<int4 *>(dst)[1] =
-                                make_int4(term[k][4], term[k][5], term[k][6], term[k][7]);
-                        } else {
-#pragma unroll
-                            for (int h = 0; h < H; ++h) dst[h] = term[k][h];
-                        }
+                    for (int r = 0; r < R; ++r) {
+                        const int blk = r * (NT / 32) + warp;
+                        const uint32_t gw = grew[h * CW + blk];
+                        const int sg = gpre[h * CW + blk] + __popc(gw & ((2u << lane) - 1u));
+                        if (pv[r][h] && sg <= SEGMAX) atomicAdd(&lsum_sm[h][sg], pv[r][h]);
                     }
                 }
-                __syncthreads();
-                const int per = (ns + TG - 1) / TG;
-                const int ta = st + tg * per, tb = min(st + ns, ta + per);
-                if (ta < tb) {
-#pragma unroll
-                    for (int h = 0; h < H; ++h)
-                        cur[h] = gpre[h * CW + (ta >> 5)] +
-                                 __popc(grew[h * CW + (ta >> 5)] & ((1u << (ta & 31)) - 1u));
-                    const int32_t *tab_t = tab - st * H;   // index with t directly
-                    int t = ta;
-                    while (t < tb) {
-                        int nxt = tb;
-                        for (int wd = t >> 5; wd <= ((tb - 1) >> 5); ++wd) {
-                            uint32_t m = anyg[wd];
-                            if (wd == (t >> 5)) m &= ~((1u << (t & 31)) - 1u);
-                            if (m) {
-                                nxt = min(tb, wd * 32 + __ffs(m) - 1);
-                                break;
-                            }
-                        }
-                        auto one = [&](int tt) {
-                            uint32_t wv = vw[tt] >> sh0;
-                            if (straddle) wv |= vw[a.C + tt] << (32 - sh0);
-                            const int32_t *e = tab_t + (int)(wv & cmask) * PS + tt * H;
-                            if constexpr (H == 4) {
-                                const int4 v4 = *reinterpret_cast<const int4 *>(e);
-                                acc[0] += v4.x;
-                                acc[1] += v4.y;
-                                acc[2] += v4.z;
-                                acc[3] += v4.w;
-                            } else {
-#pragma unroll
-                                for (int h = 0; h < H; ++h) acc[h] += e[h];
-                            }
-                        };
-                        for (; t < nxt && (t & 3); ++t) one(t);
-                        if constexpr (H == 4 && !(VB == 3)) {
-                            for (; t + 4 <= nxt; t += 4) {
-                                const uint4 w4 = *reinterpret_cast<const uint4 *>(vw + t);
-                                const int32_t *e0 = tab_t + (int)((w4.x >> sh0) & cmask) * PS + t * H;
-                                const int32_t *e1 = tab_t + (int)((w4.y >> sh0) & cmask) * PS + (t + 1) * H;
-                                const int32_t *e2 = tab_t + (int)((w4.z >> sh0) & cmask) * PS + (t + 2) * H;
-                                const int32_t *e3 = tab_t + (int)((w4.w >> sh0) & cmask) * PS + (t + 3) * H;
-                                const int4 a0 = *reinterpret_cast<const int4 *>(e0);
-                                const int4 a1 = *reinterpret_cast<const int4 *>(e1);
-                                const int4 a2 = *reinterpret_cast<const int4 *>(e2);
-                                const int4 a3 = *reinterpret_cast<const int4 *>(e3);
-                                acc[0] += a0.x + a1.x;
-                                acc[1] += a0.y + a1.y;
-                                acc[2] += a0.z + a1.z;
-                                acc[3] += a0.w + a1.w;
-                                acc[0] += a2.x + a3.x;
-                                acc[1] += a2.y + a3.y;
-                                acc[2] += a2.z + a3.z;
-                                acc[3] += a2.w + a3.w;
-                            }
-                        }
-                        for (; t < nxt; ++t) one(t);
-                        if (t < tb) {
-                            // token t opens a new segment for the heads that grew
-#pragma unroll
-                            for (int h = 0; h < H; ++h) {
-                                if ((grew[h * CW + (t >> 5)] >> (t & 31)) & 1u) {
-                                    if (cur[h] == 0) atomicAdd(&s0p[h * D + ch], acc[h]);
-                                    else if (seg_ok)
-                                        atomicAdd((unsigned long long *)&a.segs[segbase_sm[h] + cur[h] - 1].S[ch],
-                                                  (unsigned long long)(long long)acc[h]);
-                                    acc[h] = 0;
-                                    ++cur[h];
-                                }
-                            }
-                            one(t);
-                            ++t;
-                        }
-                    }
-#pragma unroll
-                    for (int h = 0; h < H; ++h) {
-                        if (acc[h]) {
-                            if (cur[h] == 0) atomicAdd(&s0p[h * D + ch], acc[h]);
-                            else if (seg_ok)
-                                atomicAdd((unsigned long long *)&a.segs[segbase_sm[h] + cur[h] - 1].S[ch],
-                                          (unsigned long long)(long long)acc[h]);
-                        }
-                        acc[h] = 0;
-                    }
-                }
-                __syncthreads();
             }
 #pragma unroll
             for (int h = 0; h < H; ++h) {
-                unsigned long long v = (unsigned long long)bnd[h];
+                unsigned long long v = (unsigned long long)sumw[h];
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
-                if ((tid & 31) == 0 && v) atomicAdd((unsigned long long *)&bsum_sm[h], v);
+                if (lane == 0) bnd_sm[warp][h] = (long long)v;
             }
         }
         __syncthreads();
-        // l of the rescale segments, now that the build has summed p
+
+        // 4b. term tables per sub-tile, and the lookups
+        {
+            // build: task (unit u, head h) turns the unit's w into the terms
+            // floor(w * c_k / 2^acc_shift) and writes its NE entries for h.
+            auto build = [&](int sti, int buf) {
+                const int st = sti * SUBT;
+                int32_t *tab = tabs + (size_t)buf * CF::TAB_WORDS;
+                for (int task = tid; task < UNITS * H; task += NT) {
+                    const int l = task & 31;
+                    const int u = (task >> 5) * UPW + l % UPW, h = l / UPW;
+                    const int t = st + u * TPE;
+                    int64_t w[TPE];
+                    if constexpr (TPE == 2) {
+                        const int2 w2 = *reinterpret_cast<const int2 *>(&d_sm[h * C + t]);
+                        w[0] = t < n ? w2.x : 0;
+                        w[1] = t + 1 < n ? w2.y : 0;
+                    } else {
+                        w[0] = t < n ? (int32_t)d_sm[h * C + t] : 0;
+                    }
+                    int32_t T[TPE][NC];
+#pragma unroll
+                    for (int e = 0; e < TPE; ++e)
+#pragma unroll
+                        for (int k = 0; k < NC; ++k)
+                            T[e][k] = (int32_t)((w[e] * (int64_t)vcent[k]) >> DefFmt::ACC_SHIFT);
+                    int32_t *dst = tab + u * USTR + (H == 1 ? 0 : (h >> 1) * HPS + (h & 1));
+                    constexpr int ES = H == 1 ? 1 : 2;         // words per entry
+#pragma unroll
+                    for (int idx = 0; idx < NE; ++idx) {
+                        int32_t v = T[0][idx & (NC - 1)];
+                        if constexpr (TPE == 2) v += T[1][idx >> VB];
+                        dst[idx * ES] = v;
+                    }
+                }
+            };
+            // accumulate: warp = (channel half, head group, stream); lane = channel.
+            const int half = warp & 1, rest = warp >> 1;
+            const int hgrp = rest % HG, stream = rest / HG;
+            const int ch = half * 32 + lane;
+            int32_t acc[HL];
+            int cur[HL];
+#pragma unroll
+            for (int i = 0; i < HL; ++i) {
+                acc[i] = 0;
+                cur[i] = 0;
+            }
+            auto flush = [&](int i) {
+                const int h = hgrp * HL + i;
+                if (acc[i]) {
+                    if (cur[i] == 0) atomicAdd(&s0p[h * D + ch], acc[i]);
+                    else if (seg_ok)
+                        atomicAdd((unsigned long long *)&a.segs[segbase_sm[h] + cur[i] - 1].S[ch],
+                                  (unsigned long long)(long long)acc[i]);
+                }
+                acc[i] = 0;
+            };
+            // entry `nib` of the unit at `u` for this lane's heads (HL/2 head pairs)
+            auto lookup = [&](const int32_t *u, uint32_t nib) {
+                if constexpr (HL >= 2) {
+#pragma unroll
+                    for (int k = 0; k < HL / 2; ++k) {
+                        const int2 x = *reinterpret_cast<const int2 *>(u + k * HPS + 2 * nib);
+                        acc[2 * k] += x.x;
+                        acc[2 * k + 1] += x.y;
+                    }
+                } else {
+                    acc[0] += u[nib];
+                }
+            };
+            // two units at once, their entries summed before the accumulators
+            auto lookup2 = [&](const int32_t *u0, uint32_t n0, const int32_t *u1, uint32_t n1) {
+                if constexpr (HL >= 2) {
+#pragma unroll
+                    for (int k = 0; k < HL / 2; ++k) {
+                        const int2 x0 = *reinterpret_cast<const int2 *>(u0 + k * HPS + 2 * n0);
+                        const int2 x1 = *reinterpret_cast<const int2 *>(u1 + k * HPS + 2 * n1);
+                        acc[2 * k] += x0.x + x1.x;
+                        acc[2 * k + 1] += x0.y + x1.y;
+                    }
+                } else {
+                    acc[0] += u0[n0] + u1[n1];
+                }
+            };
+            auto accumulate = [&](int sti, int buf) {
+                constexpr int UPS = 32 / TPE, WPS = UPS / 8;   // units, code words per stream
+                const int st = sti * SUBT, ts = st + stream * 32;
+                if (ts >= n) return;
+                const int blk = ts >> 5;
+                const int32_t *tab = tabs + (size_t)buf * CF::TAB_WORDS +
+                                     (stream * 32 / TPE) * USTR + (H == 1 ? 0 : hgrp * (HL / 2) * HPS);
+                // the segment each head is in at the start of these 32 tokens
+#pragma unroll
+                for (int i = 0; i < HL; ++i) {
+                    const int sgv = gpre[(hgrp * HL + i) * CW + blk];
+                    if (sgv != cur[i]) {
+                        flush(i);
+                        cur[i] = sgv;
+                    }
+                }
+                uint32_t cw[WPS];
+#pragma unroll
+                for (int k = 0; k < WPS; ++k) cw[k] = tw[ch * TWS + ts / TPW + k];
+                const uint32_t any = anyg[blk];
+                if (any == 0) {
+#pragma unroll
+                    for (int j = 0; j < UPS; j += 2)
+                        lookup2(tab + j * USTR, (cw[j >> 3] >> (4 * (j & 7))) & 15u,
+                                tab + (j + 1) * USTR, (cw[(j + 1) >> 3] >> (4 * ((j + 1) & 7))) & 15u);
+                } else {
+                    // rescale points inside: a token that opens a segment for a
+                    // head flushes that head first; a unit whose second token
+                    // opens one is added token by token from w.
+                    uint32_t gb[HL];
+#pragma unroll
+                    for (int i = 0; i < HL; ++i) gb[i] = grew[(hgrp * HL + i) * CW + blk];
+#pragma unroll
+                    for (int j = 0; j < UPS; ++j) {
+                        const int tt = j * TPE;
+                        const uint32_t nib = (cw[j >> 3] >> (4 * (j & 7))) & 15u;
+                        const uint32_t ub = (any >> tt) & ((1u << TPE) - 1u);
+                        if (ub <= 1u) {
+                            if (ub) {
+#pragma unroll
+                                for (int i = 0; i < HL; ++i)
+                                    if ((gb[i] >> tt) & 1u) {
+                                        flush(i);
+                                        ++cur[i];
+                                    }
+                            }
+                            lookup(tab + j * USTR, nib);
+                        } else {
+#pragma unroll
+                            for (int e = 0; e < TPE; ++e) {
+                                const int t = ts + tt + e;
+                                if (t >= n) break;
+                                const uint32_t code = (nib >> (VB * e)) & ((1u << VB) - 1u);
+#pragma unroll
+                                for (int i = 0; i < HL; ++i) {
+                                    const int h = hgrp * HL + i;
+                                    if ((gb[i] >> (tt + e)) & 1u) {
+                                        flush(i);
+                                        ++cur[i];
+                                    }
+                                    acc[i] += (int32_t)(((int64_t)(int32_t)d_sm[h * C + t] * (int64_t)vcent[code]) >>
+                                                        DefFmt::ACC_SHIFT);
+                                }
+                            }
+                        }
+                    }
+                }
+            };
+            const int nsub = (n + SUBT - 1) / SUBT;
+            if (nsub) build(0, 0);
+            __syncthreads();
+            for (int i = 0; i < nsub; ++i) {
+                if (i + 1 < nsub) build(i + 1, (i + 1) & 1);
+                accumulate(i, i & 1);
+                __syncthreads();
+            }
+#pragma unroll
+            for (int i = 0; i < HL; ++i) flush(i);
+        }
+        __syncthreads();
+        // l of the rescale segments, now that the p-pass has summed p
         if (seg_ok && tid < H)
             for (int k = 0; k < nseg_sm[tid]; ++k)
                 a.segs[segbase_sm[tid] + k].l = (int64_t)lsum_sm[tid][k + 1];
@@ -908,15 +1303,17 @@ __global__ void __launch_bounds__(H * 64 > 256 ? H * 64 : 256, H * 64 > 256 ? 1 
             if (tid < H) {
                 const int h = tid;
                 rec.l0[h] = (int64_t)lsum_sm[h][0];
-                rec.B[h] = bsum_sm[h];
+                // sum_t max_k |term| <= sum_t (floor(|w_t| max|c| / 2^acc_shift) + 1)
+                //                  <= floor(sum_t |w_t| * max|c| / 2^acc_shift) + n
+                long long sw = 0;
+                for (int w = 0; w < NT / 32; ++w) sw += bnd_sm[w][h];
+                rec.B[h] = ((sw * cmax_v) >> DefFmt::ACC_SHIFT) + n;
                 rec.nseg[h] = seg_ok ? nseg_sm[h] : 0;
                 rec.seg_base[h] = segbase_sm[h];
             }
             if (tid == 0) {
                 ItemAcc &ia = a.items[item];
-                atomicAdd(&ia.resc, resc_sm);
-                atomicAdd(&ia.sovf, (unsigned long long)sovf_sm);
-                atomicMax(&ia.maxs, maxs_sm);
+                if (resc_sm) atomicAdd(&ia.resc, (unsigned long long)resc_sm);
             }
         }
         __threadfence();
@@ -946,7 +1343,7 @@ __global__ void __launch_bounds__(H * 64 > 256 ? H * 64 : 256, H * 64 > 256 ? 1 
             __syncthreads();
             if (flag_sm) {
                 __threadfence();
-                merge_item<H>(a, item, nblk, a.T[b], qbase, &maxs_sm);
+                merge_item<H>(a, item, nblk, a.T[b], qbase, slots_sm);
                 __syncthreads();
                 if (tid == 0) {
                     ItemAcc &ia = a.items[item];
@@ -972,7 +1369,7 @@ __global__ void __launch_bounds__(H * 64 > 256 ? H * 64 : 256, H * 64 > 256 ? 1 
 }
 
 // ---------------------------------------------------------------------------
-// host side: the tile list, the scratch, the launch
+// host side: the tile list, the scratch, the launches
 // ---------------------------------------------------------------------------
 
 template <int H>
@@ -990,26 +1387,50 @@ inline cudaError_t launch_seq(const Geo &g, const DevTables *tb, int32_t B, cons
     return cudaGetLastError();
 }
 
-// Rows per chunk: as many whole pages as fit the layout's smem budget, at most 1024.
-template <int H, int VB>
-inline int chunk_rows(const Geo &g, size_t smem_cap) {
-    int pages = 1024 / g.P;
-    if (pages < 1) pages = 1;
-    while (pages > 1 && ChunkLayout<H, VB>(pages * g.P).total > smem_cap) --pages;
-    return pages * g.P;
+// Dynamic shared memory of k_scan_scores: the replicated pair table.
+template <int KB>
+constexpr size_t score_smem() {
+    return (size_t)(1 << (2 * KB)) * 8 * sizeof(double2);
 }
 
-// The tile list: every item's chunks, in (chunk, item) order so a chunk is
-// always claimed after all of its predecessors.
+// Resident CTAs of the scores (WHICH 0) or values (WHICH 1) kernel on the
+// current device: the launch grid. The dynamic-smem attribute and the
+// occupancy are set and queried once per kernel and device.
+template <int H, int KB, int VB, int WHICH>
+inline int chunk_slots() {
+    auto fn = WHICH == 0 ? k_scan_scores<H, KB, VB> : k_scan_values<H, KB, VB>;
+    const size_t dyn = WHICH == 0 ? score_smem<KB>() : ChunkCfg<H, KB, VB>::BYTES;
+    static std::mutex mu;
+    static int cached[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+    std::lock_guard<std::mutex> lk(mu);
+    if (cached[dev] > 0) return cached[dev];
+    int per_sm = 0, sms = 0;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, CHUNK_THREADS, dyn) != cudaSuccess)
+        return -1;
+    cached[dev] = (per_sm < 1 ? 1 : per_sm) * sms;
+    return cached[dev];
+}
+
+// The tile list: every item's tiles in (tile index, item) order; each item's
+// first row in the score-offset array.
 inline void build_tiles(const Geo &g, int32_t B, const int64_t *h_T, int C, std::vector<int4> &tiles,
-                        std::vector<int32_t> &nc, int &max_nc) {
+                        std::vector<int32_t> &nc, std::vector<int64_t> &row_base, int &max_nc,
+                        int64_t &total_rows) {
     const int n_items = B * g.n_kv;
     nc.assign(n_items, 1);
+    row_base.assign(n_items, 0);
     max_nc = 1;
+    total_rows = 0;
     for (int it = 0; it < n_items; ++it) {
         const int64_t T = h_T[it / g.n_kv];
         nc[it] = T ? (int)((T + C - 1) / C) : 1;
         max_nc = nc[it] > max_nc ? nc[it] : max_nc;
+        row_base[it] = total_rows;
+        total_rows += T;
     }
     tiles.clear();
     for (int cidx = 0; cidx < max_nc; ++cidx)
@@ -1021,62 +1442,101 @@ inline void build_tiles(const Geo &g, int32_t B, const int64_t *h_T, int C, std:
             }
 }
 
-// Carve (or grow) the scratch for n_items items of up to max_nc chunks.
-inline int reserve_scratch(ChunkScratch &cs, int n_items, int max_nc, int n_tiles, int H,
-                           cudaStream_t s) {
+// Byte layout of the scratch of one scan: `o` offsets in the order carved.
+struct ScratchLayout {
+    size_t all, top, cmx, rec, blk, bd, seg, items, redo, tiles, nc, rb, bmg, sc, total;
+    ScratchLayout(int ni, int mc, int sc_cap, int tc, int H, int CW, int64_t rows) {
+        auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
+        const int mb = (mc + GBLK - 1) / GBLK;
+        size_t o = 0;
+        all = o; o += al(8);
+        top = o; o += al(8);
+        cmx = o; o += al(sizeof(long long) * (size_t)ni * mc * 2 * HMAX);
+        rec = o; o += al(sizeof(ChunkRec) * (size_t)ni * mc);
+        blk = o; o += al(sizeof(BlockRec) * (size_t)ni * mb);
+        bd = o; o += al(sizeof(unsigned int) * (size_t)ni * mb);
+        seg = o; o += al(sizeof(SegEntry) * (size_t)sc_cap);
+        items = o; o += al(sizeof(ItemAcc) * (size_t)ni);
+        redo = o; o += al(sizeof(int32_t) * (size_t)ni);
+        tiles = o; o += al(sizeof(int4) * (size_t)tc);
+        nc = o; o += al(sizeof(int32_t) * (size_t)ni);
+        rb = o; o += al(sizeof(int64_t) * (size_t)ni);
+        bmg = o; o += al(sizeof(long long) * (size_t)tc * H * CW);
+        sc = o; o += al(sizeof(uint32_t) * (size_t)(rows > 0 ? rows : 1) * H);
+        total = o;
+    }
+};
+
+// Carve (or grow) the scratch for n_items items of up to max_nc tiles.
+inline int reserve_scratch(ChunkScratch &cs, int n_items, int max_nc, int n_tiles, int H, int CW,
+                           int64_t rows, cudaStream_t s) {
     const int seg_cap = 2 * (64 * n_items * H) + 4 * n_tiles;
+    const int64_t sc_words = rows * H;
     if (cs.base && n_items <= cs.n_items && max_nc <= cs.max_chunks && seg_cap <= cs.seg_cap &&
-        n_tiles <= cs.tile_cap)
+        n_tiles <= cs.tile_cap && sc_words <= cs.sc_rows)
         return INS_OK;
     cudaStreamSynchronize(s);
-    const int ni = n_items > cs.n_items ? n_items : cs.n_items;
-    const int mc = max_nc > cs.max_chunks ? max_nc : cs.max_chunks;
-    const int sc = seg_cap > cs.seg_cap ? seg_cap : cs.seg_cap;
-    const int tc = n_tiles > cs.tile_cap ? n_tiles : cs.tile_cap;
-    const int mb = (mc + GBLK - 1) / GBLK;
+    // grown with a quarter of slack, so a context that grows by a token per
+    // step reallocates only now and then
+    auto grow = [](int64_t need, int64_t have) { return need > have ? need + need / 4 : have; };
+    const int ni = (int)grow(n_items, cs.n_items);
+    const int mc = (int)grow(max_nc, cs.max_chunks);
+    const int sc = (int)grow(seg_cap, cs.seg_cap);
+    const int tc = (int)grow(n_tiles, cs.tile_cap);
+    const int64_t sw = grow(sc_words, cs.sc_rows);
     cs.release();
-    auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
-    size_t o = 0;
-    const size_t o_claim = o; o += al(8);
-    const size_t o_all = o; o += al(8);
-    const size_t o_top = o; o += al(8);
-    const size_t o_flag = o; o += al(sizeof(unsigned long long) * (size_t)ni * mc);
-    const size_t o_val = o; o += al(sizeof(long long) * (size_t)ni * mc * 2 * HMAX);
-    const size_t o_rec = o; o += al(sizeof(ChunkRec) * (size_t)ni * mc);
-    const size_t o_blk = o; o += al(sizeof(BlockRec) * (size_t)ni * mb);
-    const size_t o_bd = o; o += al(sizeof(unsigned int) * (size_t)ni * mb);
-    const size_t o_seg = o; o += al(sizeof(SegEntry) * (size_t)sc);
-    const size_t o_items = o; o += al(sizeof(ItemAcc) * (size_t)ni);
-    const size_t o_redo = o; o += al(sizeof(int32_t) * (size_t)ni);
-    const size_t o_tiles = o; o += al(sizeof(int4) * (size_t)tc);
-    const size_t o_nc = o; o += al(sizeof(int32_t) * (size_t)ni);
-    if (cudaMalloc(&cs.base, o) != cudaSuccess) {
+    // sized for up to HMAX heads and 32 blocks per tile, so one scratch serves
+    // every head count
+    const ScratchLayout L(ni, mc, sc, tc, HMAX, 32, (sw + HMAX - 1) / HMAX);
+    (void)H;
+    (void)CW;
+    if (cudaMalloc(&cs.base, L.total) != cudaSuccess) {
         cudaGetLastError();
         cs.base = nullptr;
         return INS_ENOMEM;
     }
-    if (cudaMemset(cs.base, 0, o) != cudaSuccess) return INS_ECUDA;
+    if (cudaMemset(cs.base, 0, L.total) != cudaSuccess) return INS_ECUDA;
     uint8_t *p = (uint8_t *)cs.base;
-    cs.bytes = o;
-    cs.claim = (unsigned long long *)(p + o_claim);
-    cs.all_done = (unsigned long long *)(p + o_all);
-    cs.seg_top = (unsigned int *)(p + o_top);
-    cs.lb_flag = (unsigned long long *)(p + o_flag);
-    cs.lb_val = (long long *)(p + o_val);
-    cs.recs = (ChunkRec *)(p + o_rec);
-    cs.blks = (BlockRec *)(p + o_blk);
-    cs.blk_done = (unsigned int *)(p + o_bd);
-    cs.segs = (SegEntry *)(p + o_seg);
-    cs.items = (ItemAcc *)(p + o_items);
-    cs.redo = (int32_t *)(p + o_redo);
-    cs.tiles = (int4 *)(p + o_tiles);
-    cs.item_nchunks = (int32_t *)(p + o_nc);
+    cs.bytes = L.total;
+    cs.all_done = (unsigned long long *)(p + L.all);
+    cs.seg_top = (unsigned int *)(p + L.top);
+    cs.cmx = (long long *)(p + L.cmx);
+    cs.recs = (ChunkRec *)(p + L.rec);
+    cs.blks = (BlockRec *)(p + L.blk);
+    cs.blk_done = (unsigned int *)(p + L.bd);
+    cs.segs = (SegEntry *)(p + L.seg);
+    cs.items = (ItemAcc *)(p + L.items);
+    cs.redo = (int32_t *)(p + L.redo);
+    cs.tiles = (int4 *)(p + L.tiles);
+    cs.item_nchunks = (int32_t *)(p + L.nc);
+    cs.row_base = (int64_t *)(p + L.rb);
+    cs.bmg = (long long *)(p + L.bmg);
+    cs.sc = (uint32_t *)(p + L.sc);
     cs.n_items = ni;
     cs.max_chunks = mc;
     cs.seg_cap = sc;
     cs.tile_cap = tc;
-    cs.claim_base = 0;
+    cs.sc_rows = ((sw + HMAX - 1) / HMAX) * HMAX;
     return INS_OK;
+}
+
+// The three launches of the chunked scan (plus the exact re-run of flagged
+// items) on a prepared argument block. `a` holds every pointer but the grid.
+template <int H, int KB, int VB>
+inline int launch_chunk_kernels(ChunkArgs &a, int32_t B, const int32_t *d_seq, const int64_t *d_T,
+                                cudaStream_t s) {
+    const int gA = chunk_slots<H, KB, VB, 0>(), gB = chunk_slots<H, KB, VB, 1>();
+    if (gA < 0 || gB < 0) return INS_ECUDA;
+    k_scan_scores<H, KB, VB><<<gA < a.n_tiles ? gA : a.n_tiles, CHUNK_THREADS, score_smem<KB>(), s>>>(a);
+    k_chunk_prefix<H><<<a.n_items * H, 256, 0, s>>>(a);
+    k_scan_values<H, KB, VB>
+        <<<gB < a.n_tiles ? gB : a.n_tiles, CHUNK_THREADS, ChunkCfg<H, KB, VB>::BYTES, s>>>(a);
+    if (cudaGetLastError() != cudaSuccess) return INS_ECUDA;
+    // items whose exactness the fold could not prove are recomputed in order
+    return launch_seq<H>(a.g, a.tb, B, d_seq, d_T, a.page_table, a.pool, a.q_rot, a.out, a.stats,
+                         a.redo, s) == cudaSuccess
+               ? INS_OK
+               : INS_ECUDA;
 }
 
 template <int H, int KB, int VB>
@@ -1084,42 +1544,33 @@ inline int launch_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, i
                           const int32_t *d_seq, const int64_t *d_T, const int64_t *h_T,
                           const int32_t *d_pt, const uint8_t *pool, const int32_t *q_rot,
                           int64_t *out, ins_stats *stats, int32_t *d_status, cudaStream_t s) {
+    using CF = ChunkCfg<H, KB, VB>;
     const int n_items = B * g.n_kv;
-    const int C = chunk_rows<H, VB>(g, 100 * 1024);
-    const ChunkLayout<H, VB> lay(C);
     std::vector<int4> tiles;
     std::vector<int32_t> nc;
+    std::vector<int64_t> rb;
     int max_nc = 1;
-    build_tiles(g, B, h_T, C, tiles, nc, max_nc);
+    int64_t rows = 0;
+    build_tiles(g, B, h_T, CF::C, tiles, nc, rb, max_nc, rows);
     const int n_tiles = (int)tiles.size();
-    if (int rc = reserve_scratch(cs, n_items, max_nc, n_tiles, H, s)) return rc;
+    if (int rc = reserve_scratch(cs, n_items, max_nc, n_tiles, H, CF::CW, rows, s)) return rc;
     if (cudaMemcpyAsync(cs.tiles, tiles.data(), sizeof(int4) * tiles.size(), cudaMemcpyHostToDevice,
                         s) != cudaSuccess ||
         cudaMemcpyAsync(cs.item_nchunks, nc.data(), sizeof(int32_t) * nc.size(),
-                        cudaMemcpyHostToDevice, s) != cudaSuccess)
+                        cudaMemcpyHostToDevice, s) != cudaSuccess ||
+        cudaMemcpyAsync(cs.row_base, rb.data(), sizeof(int64_t) * rb.size(), cudaMemcpyHostToDevice,
+                        s) != cudaSuccess)
         return INS_ECUDA;
-    auto fn = k_scan_chunk<H, KB, VB>;
-    const size_t dyn = lay.total;
-    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) != cudaSuccess)
-        return INS_ECUDA;
-    constexpr int NT = H * 64 > 256 ? H * 64 : 256;
-    int per_sm = 0, dev = 0, sms = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, NT, dyn);
-    if (per_sm < 1) per_sm = 1;
-    int grid = per_sm * sms;
-    if (grid > n_tiles) grid = n_tiles;
     ChunkArgs a{};
     a.g = g;
     a.tb = tb;
     a.tiles = cs.tiles;
     a.n_tiles = n_tiles;
-    a.C = C;
     a.max_chunks = cs.max_chunks;
     a.max_blocks = (cs.max_chunks + GBLK - 1) / GBLK;
     a.n_items = n_items;
     a.item_nchunks = cs.item_nchunks;
+    a.row_base = cs.row_base;
     a.seq_ids = d_seq;
     a.T = d_T;
     a.page_table = d_pt;
@@ -1127,10 +1578,9 @@ inline int launch_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, i
     a.q_rot = q_rot;
     a.out = out;
     a.stats = stats;
-    a.claim = cs.claim;
-    a.claim_base = cs.claim_base;
-    a.lb_flag = cs.lb_flag;
-    a.lb_val = cs.lb_val;
+    a.sc = cs.sc;
+    a.bmg = cs.bmg;
+    a.cmx = cs.cmx;
     a.recs = cs.recs;
     a.blks = cs.blks;
     a.blk_done = cs.blk_done;
@@ -1141,16 +1591,8 @@ inline int launch_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, i
     a.redo = cs.redo;
     a.all_done = cs.all_done;
     a.status = d_status;
-    a.epoch = ++cs.epoch;
-    fn<<<grid, NT, dyn, s>>>(a);
-    // every tile claim and every CTA's final failing claim bump the counter once
-    cs.claim_base += (unsigned long long)n_tiles + (unsigned long long)grid;
-    if (cudaGetLastError() != cudaSuccess) return INS_ECUDA;
-    // items whose exactness the fold could not prove are recomputed in order
-    return launch_seq<H>(g, tb, B, d_seq, d_T, d_pt, pool, q_rot, out, stats, cs.redo, s) ==
-                   cudaSuccess
-               ? INS_OK
-               : INS_ECUDA;
+    cs.last_items = n_items;
+    return launch_chunk_kernels<H, KB, VB>(a, B, d_seq, d_T, s);
 }
 
 inline int launch_online(ChunkScratch &cs, const Geo &g, const DevTables *tb, int32_t B,
@@ -1161,7 +1603,7 @@ inline int launch_online(ChunkScratch &cs, const Geo &g, const DevTables *tb, in
 #define INS_CH(HH, KK, VV)                                                                 \
     return launch_chunked<HH, KK, VV>(cs, g, tb, B, d_seq, d_lens, h_lens, d_pt, pool, q_rot, \
                                       out, stats, d_status, s)
-    if (g.kb == 4 && g.vb == 2) {
+    if (is_def_fmt(g) && g.kb == 4 && g.vb == 2) {
         switch (H) {
             case 1: INS_CH(1, 4, 2);
             case 2: INS_CH(2, 4, 2);
@@ -1169,13 +1611,14 @@ inline int launch_online(ChunkScratch &cs, const Geo &g, const DevTables *tb, in
             case 8: INS_CH(8, 4, 2);
         }
     }
-    if (g.kb == 3 && g.vb == 3) {
+    if (is_def_fmt(g) && g.kb == 3 && g.vb == 3) {
         switch (H) {
             case 4: INS_CH(4, 3, 3);
             case 8: INS_CH(8, 3, 3);
         }
     }
 #undef INS_CH
+    cs.last_items = 0;
     cudaError_t e = cudaErrorInvalidValue;
     switch (H) {
         case 1: e = launch_seq<1>(g, tb, B, d_seq, d_lens, d_pt, pool, q_rot, out, stats, nullptr, s); break;

@@ -102,6 +102,14 @@ class PagedCache:
         """Raise if a kernel latched an error (range, bounded-wait timeout)."""
         _lib.check(self._L.ins_cache_status(self._h, _stream(self.device)))
 
+    def recomputed(self) -> int:
+        """Items of the last online scan that the exact sequential kernel redid
+        (ins_scan_recomputed); 0 when the context-parallel scan proved them all."""
+        k = self._L.ins_scan_recomputed(self._h, _stream(self.device))
+        if k < 0:
+            _lib.check(_lib.INS_ECUDA)
+        return int(k)
+
     # -- tensors -------------------------------------------------------------
     def _dev_i32(self, x, shape_tail) -> torch.Tensor:
         t = torch.as_tensor(x)

@@ -227,6 +227,9 @@ def test_long_single_sequence_matches_oracle():
     want, wst = orc.decode_layer(q_rot, [rows], threads=8)
     np.testing.assert_array_equal(_np(out), want)
     np.testing.assert_array_equal(_np(st), wst)
+    # typical data stays on the context-parallel path: none of the 8 items was
+    # handed to the exact sequential kernel
+    assert pc.recomputed() == 0
 
 
 # -- error behaviour -------------------------------------------------------------
