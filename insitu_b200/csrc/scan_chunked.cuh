@@ -30,6 +30,7 @@
 #pragma once
 
 #include <climits>
+#include <cstring>
 #include <mutex>
 #include <vector>
 
@@ -146,6 +147,48 @@ struct ChunkArgs {
     int32_t *status;
 };
 
+// Pinned host buffers for the per-call uploads (the tile list), used in turn:
+// a buffer is rewritten only after the copy that read it four calls ago has
+// run, so the host never waits for the stream to drain (a copy from pageable
+// memory would).
+struct PinnedRing {
+    static constexpr int N = 4;
+    void *h[N] = {};
+    size_t cap[N] = {};
+    cudaEvent_t ev[N] = {};
+    int next = 0;
+
+    void *take(size_t bytes, int &slot) {
+        slot = next;
+        next = (next + 1) % N;
+        if (!ev[slot]) {
+            if (cudaEventCreateWithFlags(&ev[slot], cudaEventDisableTiming) != cudaSuccess) return nullptr;
+        } else if (cudaEventSynchronize(ev[slot]) != cudaSuccess) {
+            return nullptr;
+        }
+        if (cap[slot] < bytes) {
+            if (h[slot]) cudaFreeHost(h[slot]);
+            h[slot] = nullptr;
+            cap[slot] = 0;
+            size_t want = 4096;
+            while (want < bytes) want *= 2;
+            if (cudaHostAlloc(&h[slot], want, cudaHostAllocDefault) != cudaSuccess) return nullptr;
+            cap[slot] = want;
+        }
+        return h[slot];
+    }
+    int done(int slot, cudaStream_t s) { return cudaEventRecord(ev[slot], s) == cudaSuccess ? 0 : -1; }
+    void release() {
+        for (int i = 0; i < N; ++i) {
+            if (ev[i]) cudaEventSynchronize(ev[i]), cudaEventDestroy(ev[i]);
+            if (h[i]) cudaFreeHost(h[i]);
+            ev[i] = nullptr;
+            h[i] = nullptr;
+            cap[i] = 0;
+        }
+    }
+};
+
 // Device scratch of the chunked scan, owned by the cache handle and grown on
 // demand. Everything in it is either rewritten each launch or reset by the
 // kernels themselves, so launches need no memsets.
@@ -168,8 +211,10 @@ struct ChunkScratch {
     int4 *tiles = nullptr;
     int32_t *item_nchunks = nullptr;
     int64_t *row_base = nullptr;
+    PinnedRing up;                // host side of the tile-list uploads
 
     void release() {
+        up.release();
         if (base) cudaFree(base);
         base = nullptr;
         bytes = 0;
@@ -1554,13 +1599,21 @@ inline int launch_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, i
     build_tiles(g, B, h_T, CF::C, tiles, nc, rb, max_nc, rows);
     const int n_tiles = (int)tiles.size();
     if (int rc = reserve_scratch(cs, n_items, max_nc, n_tiles, H, CF::CW, rows, s)) return rc;
-    if (cudaMemcpyAsync(cs.tiles, tiles.data(), sizeof(int4) * tiles.size(), cudaMemcpyHostToDevice,
-                        s) != cudaSuccess ||
-        cudaMemcpyAsync(cs.item_nchunks, nc.data(), sizeof(int32_t) * nc.size(),
-                        cudaMemcpyHostToDevice, s) != cudaSuccess ||
-        cudaMemcpyAsync(cs.row_base, rb.data(), sizeof(int64_t) * rb.size(), cudaMemcpyHostToDevice,
-                        s) != cudaSuccess)
-        return INS_ECUDA;
+    {
+        const size_t bt = sizeof(int4) * tiles.size(), bn = sizeof(int32_t) * nc.size(),
+                     br = sizeof(int64_t) * rb.size();
+        int slot = 0;
+        uint8_t *h = (uint8_t *)cs.up.take(bt + br + bn, slot);
+        if (!h) return INS_ECUDA;
+        memcpy(h, tiles.data(), bt);
+        memcpy(h + bt, rb.data(), br);
+        memcpy(h + bt + br, nc.data(), bn);
+        if (cudaMemcpyAsync(cs.tiles, h, bt, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+            cudaMemcpyAsync(cs.row_base, h + bt, br, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+            cudaMemcpyAsync(cs.item_nchunks, h + bt + br, bn, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+            cs.up.done(slot, s))
+            return INS_ECUDA;
+    }
     ChunkArgs a{};
     a.g = g;
     a.tb = tb;
