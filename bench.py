@@ -68,7 +68,7 @@ def peaks():
 
 def traffic_per_row():
     """DRAM bytes per scanned row of the scan kernel, from the committed ncu summary."""
-    path = os.path.join(ROOT, "profiles", "scan_chunk_traffic.txt")
+    path = os.path.join(ROOT, "profiles", "scan_ctx1m_traffic.txt")
     try:
         for ln in open(path):
             if ln.startswith("dram_bytes_per_row:"):
