@@ -230,6 +230,33 @@ int ins_cache_status(ins_cache *cache, void *stream);
  * reference. Blocks on the stream; -1 on error (see ins_last_error). */
 int64_t ins_scan_recomputed(ins_cache *cache, void *stream);
 
+/* Context split (one sequence's cached tokens held by several shards -- GPUs
+ * or caches -- each a causal range; SURVEY e2 / BASELINE config 5). No
+ * reference function does this; the reference scans one sequence in one
+ * process (ops/attention.py:451-513), and the merged result is that scan's
+ * output bit for bit whenever the merge can prove the 32-bit accumulator
+ * clamp never fires (otherwise it latches INS_ERANGE, read by
+ * ins_cache_status). Online softmax only; needs the context-parallel scan
+ * (4b/2b or 3b/3b codes, the default fixed-point format).
+ *
+ * 1. ins_scan_maxima: scores this shard's items and writes each item's
+ *    maximum score per query head to `maxima` (device int64
+ *    [B][n_kv][kv_groups]). Keeps the scores for step 2.
+ * 2. The caller exchanges the maxima; shard r's m_in is the maximum over
+ *    shards before it (-2^47 for the first), same layout.
+ * 3. ins_scan_part, with the arguments of step 1: writes one composite per
+ *    item to `part` (device, ins_part_bytes(B) bytes).
+ * 4. The caller gathers the shards' parts, in causal order, into one device
+ *    buffer; ins_merge_parts folds them and writes `out` and `stats` as
+ *    ins_scan would for the whole sequences. */
+int64_t ins_part_bytes(ins_cache *cache, int32_t B);
+int ins_scan_maxima(ins_cache *cache, int32_t B, const int32_t *seq_ids, const int64_t *lengths,
+                    const int32_t *q_rot, int64_t *maxima, void *stream);
+int ins_scan_part(ins_cache *cache, int32_t B, const int32_t *seq_ids, const int64_t *lengths,
+                  const int32_t *q_rot, const int64_t *m_in, void *part, void *stream);
+int ins_merge_parts(ins_cache *cache, int32_t B, int32_t n_parts, const void *parts, int64_t *out,
+                    ins_stats *stats, void *stream);
+
 /* The last error message recorded on this thread ("" if none). */
 const char *ins_last_error(void);
 

@@ -82,7 +82,8 @@ STATS_FIELDS = tuple(n for n, _ in Stats._fields_)
 SYMBOLS = ("ins_abi_version", "ins_bytes_per_token", "ins_cache_create", "ins_cache_destroy",
            "ins_cache_reset", "ins_cache_length", "ins_cache_capacity", "ins_ingress", "ins_rotate",
            "ins_scores", "ins_scan", "ins_cache_export", "ins_cache_import", "ins_cache_status",
-           "ins_last_error", "ins_scan_noalloc", "ins_scan_recomputed")
+           "ins_last_error", "ins_scan_noalloc", "ins_scan_recomputed", "ins_part_bytes",
+           "ins_scan_maxima", "ins_scan_part", "ins_merge_parts")
 
 
 def nvcc() -> str:
@@ -142,6 +143,11 @@ def lib():
     L.ins_cache_status.argtypes = [vp, vp]
     L.ins_scan_recomputed.argtypes = [vp, vp]
     L.ins_scan_recomputed.restype = i64
+    L.ins_part_bytes.argtypes = [vp, i32]
+    L.ins_part_bytes.restype = i64
+    L.ins_scan_maxima.argtypes = [vp, i32, vp, vp, vp, vp, vp]
+    L.ins_scan_part.argtypes = [vp, i32, vp, vp, vp, vp, vp, vp]
+    L.ins_merge_parts.argtypes = [vp, i32, i32, vp, vp, vp, vp]
     L.ins_last_error.restype = C.c_char_p
     _lib = L
     return L

@@ -106,6 +106,16 @@ struct ins_cache {
     Staging stage_a;                    // per-call index uploads
     Staging stage_b;
     ChunkScratch chunk;                 // scratch of the context-parallel scan
+    uint64_t gen = 0;                   // bumped by every call that rewrites `chunk`
+    struct {                            // context split: phase 1 waiting for phase 2
+        bool armed = false;
+        uint64_t gen = 0;
+        int32_t B = 0;
+        std::vector<int32_t> seq;
+        std::vector<int64_t> T;
+        const int32_t *q_rot = nullptr;
+        ChunkArgs a{};
+    } split;
 };
 
 namespace {
@@ -472,6 +482,7 @@ int ins_scan(ins_cache *c, int32_t B, const int32_t *seq_ids, const int64_t *len
     if (int rc = c->stage_b.upload(bytes, s)) return rc;
     const int64_t *d_T = (const int64_t *)c->stage_b.d;
     const int32_t *d_seq = (const int32_t *)(d_T + B);
+    ++c->gen;
     switch (c->g.H) {
         case 1: return launch_scan_h<1>(c, B, d_seq, d_T, hT, q_rot, out, stats, mode, s);
         case 2: return launch_scan_h<2>(c, B, d_seq, d_T, hT, q_rot, out, stats, mode, s);
@@ -614,6 +625,175 @@ int ins_cache_status(ins_cache *c, void *stream) {
     if (st & ST_TIMEOUT) return fail(INS_ETIMEOUT, "a bounded device wait gave up");
     if (st & ST_RANGE) return fail(INS_ERANGE, "a value escaped its fixed-point format");
     if (st & ST_INTERNAL) return fail(INS_EINVAL, "internal consistency check failed");
+    if (st & ST_SPLIT)
+        return fail(INS_ERANGE, "a context-split merge could not prove its result exact (a shard held "
+                                "more rescales of one head than its composite can carry, or the 32-bit "
+                                "accumulator could have clamped); those items' outputs were not written");
+    return INS_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Context split: one sequence's tokens held by several shards (GPUs), each a
+// causal range. Phase 1 gives each shard's per-item maxima; the caller
+// exchanges them; phase 2, knowing the running maximum entering the shard,
+// writes one composite per item; the caller gathers the composites and
+// ins_merge_parts folds them in causal order.
+// ---------------------------------------------------------------------------
+namespace {
+
+// Stage T and sequence ids of a scan call (the checks of ins_scan).
+int stage_scan_args(ins_cache *c, int32_t B, const int32_t *seq_ids, const int64_t *lengths,
+                    cudaStream_t s, std::vector<int32_t> *seq_out, std::vector<int64_t> *T_out,
+                    const int64_t **d_T, const int32_t **d_seq) {
+    const size_t bytes = sizeof(int64_t) * (size_t)B + sizeof(int32_t) * (size_t)B;
+    if (int rc = c->stage_b.reserve(bytes)) return rc;
+    int64_t *hT = (int64_t *)c->stage_b.h;
+    int32_t *hS = (int32_t *)(hT + B);
+    for (int32_t i = 0; i < B; ++i) {
+        const int32_t sq = seq_ids[i];
+        if (sq < 0 || sq >= c->cfg.max_seqs) return fail(INS_EINVAL, "sequence id out of range");
+        const int64_t len = c->h_seq_lens[sq];
+        int64_t T = len;
+        if (lengths) {
+            T = lengths[i];
+            if (T < 0 || T > len)
+                return fail(INS_EBADLEN, "scan length " + std::to_string(T) + " outside the sequence's " +
+                                             std::to_string(len) + " cached tokens");
+        }
+        hT[i] = T;
+        hS[i] = sq;
+    }
+    if (seq_out) seq_out->assign(hS, hS + B);
+    if (T_out) T_out->assign(hT, hT + B);
+    if (int rc = c->stage_b.upload(bytes, s)) return rc;
+    *d_T = (const int64_t *)c->stage_b.d;
+    *d_seq = (const int32_t *)(*d_T + B);
+    return INS_OK;
+}
+
+template <int H, int KB, int VB>
+int split_maxima_t(ins_cache *c, int32_t B, const int32_t *d_seq, const int64_t *d_T, const int64_t *h_T,
+                   const int32_t *q_rot, int64_t *maxima, cudaStream_t s) {
+    ChunkArgs a;
+    if (int rc = prepare_chunked<H, KB, VB>(c->chunk, c->g, c->d_tables, B, d_seq, d_T, h_T,
+                                            c->d_page_table, c->d_pool, q_rot, nullptr, nullptr,
+                                            c->d_status, a, s))
+        return fail(rc, "context-split scan scratch");
+    a.maxima = (long long *)maxima;
+    if (int rc = launch_split_maxima<H, KB, VB>(a, s)) return fail(rc, "context-split scores launch");
+    c->split.a = a;
+    return INS_OK;
+}
+
+template <int H, int KB, int VB>
+int split_part_t(ins_cache *c, const int64_t *m_in, void *part, cudaStream_t s) {
+    ChunkArgs a = c->split.a;
+    a.m_init = (const long long *)m_in;
+    a.parts = (PartRec *)part;
+    if (int rc = launch_split_part<H, KB, VB>(a, s)) return fail(rc, "context-split values launch");
+    return INS_OK;
+}
+
+int split_maxima(ins_cache *c, int variant, int32_t B, const int32_t *d_seq, const int64_t *d_T,
+                 const int64_t *h_T, const int32_t *q_rot, int64_t *maxima, cudaStream_t s) {
+#define CALL(HH, KK, VV) split_maxima_t<HH, KK, VV>(c, B, d_seq, d_T, h_T, q_rot, maxima, s)
+    switch (variant) {
+        case 142: return CALL(1, 4, 2);
+        case 242: return CALL(2, 4, 2);
+        case 442: return CALL(4, 4, 2);
+        case 842: return CALL(8, 4, 2);
+        case 433: return CALL(4, 3, 3);
+        case 833: return CALL(8, 3, 3);
+    }
+#undef CALL
+    return fail(INS_EINVAL, "no context-parallel scan for this cache");
+}
+
+int split_part(ins_cache *c, int variant, const int64_t *m_in, void *part, cudaStream_t s) {
+#define CALL(HH, KK, VV) split_part_t<HH, KK, VV>(c, m_in, part, s)
+    switch (variant) {
+        case 142: return CALL(1, 4, 2);
+        case 242: return CALL(2, 4, 2);
+        case 442: return CALL(4, 4, 2);
+        case 842: return CALL(8, 4, 2);
+        case 433: return CALL(4, 3, 3);
+        case 833: return CALL(8, 3, 3);
+    }
+#undef CALL
+    return fail(INS_EINVAL, "no context-parallel scan for this cache");
+}
+}  // namespace
+
+extern "C" {
+
+int64_t ins_part_bytes(ins_cache *c, int32_t B) {
+    if (!c || B < 0) return fail(INS_EINVAL, "part size arguments"), -1;
+    return (int64_t)B * c->g.n_kv * (int64_t)sizeof(PartRec);
+}
+
+int ins_scan_maxima(ins_cache *c, int32_t B, const int32_t *seq_ids, const int64_t *lengths,
+                    const int32_t *q_rot, int64_t *maxima, void *stream) {
+    if (!c) return fail(INS_EINVAL, "cache is NULL");
+    if (B <= 0 || !seq_ids || !q_rot || !maxima) return fail(INS_EINVAL, "scan_maxima arguments");
+    const int variant = chunk_variant(c->g, c->g.H);
+    if (!variant)
+        return fail(INS_EINVAL, "the context split needs the context-parallel scan (4b/2b or 3b/3b "
+                                "codes, the default fixed-point format)");
+    DeviceGuard dg(c->device);
+    cudaStream_t s = (cudaStream_t)stream;
+    c->split.armed = false;
+    const int64_t *d_T;
+    const int32_t *d_seq;
+    if (int rc = stage_scan_args(c, B, seq_ids, lengths, s, &c->split.seq, &c->split.T, &d_T, &d_seq))
+        return rc;
+    ++c->gen;
+    if (int rc = split_maxima(c, variant, B, d_seq, d_T, c->split.T.data(), q_rot, maxima, s)) return rc;
+    c->split.armed = true;
+    c->split.gen = c->gen;
+    c->split.B = B;
+    c->split.q_rot = q_rot;
+    return INS_OK;
+}
+
+int ins_scan_part(ins_cache *c, int32_t B, const int32_t *seq_ids, const int64_t *lengths,
+                  const int32_t *q_rot, const int64_t *m_in, void *part, void *stream) {
+    if (!c) return fail(INS_EINVAL, "cache is NULL");
+    if (B <= 0 || !seq_ids || !q_rot || !m_in || !part) return fail(INS_EINVAL, "scan_part arguments");
+    if (((uintptr_t)part & 7u) || ((uintptr_t)m_in & 7u)) return fail(INS_EINVAL, "part/m_in must be 8-byte aligned");
+    auto &sp = c->split;
+    bool same = sp.armed && sp.gen == c->gen && sp.B == B && sp.q_rot == q_rot;
+    for (int32_t i = 0; same && i < B; ++i) {
+        const int32_t sq = seq_ids[i];
+        const int64_t T = lengths ? lengths[i] : (sq >= 0 && sq < c->cfg.max_seqs ? c->h_seq_lens[sq] : -1);
+        same = sq == sp.seq[i] && T == sp.T[i];
+    }
+    if (!same)
+        return fail(INS_EINVAL, "ins_scan_part must follow ins_scan_maxima on this cache with the same "
+                                "sequences, lengths and q_rot, with no scan in between");
+    DeviceGuard dg(c->device);
+    sp.armed = false;
+    return split_part(c, chunk_variant(c->g, c->g.H), m_in, part, (cudaStream_t)stream);
+}
+
+int ins_merge_parts(ins_cache *c, int32_t B, int32_t n_parts, const void *parts, int64_t *out,
+                    ins_stats *stats, void *stream) {
+    if (!c) return fail(INS_EINVAL, "cache is NULL");
+    if (B <= 0 || n_parts <= 0 || !parts || !out) return fail(INS_EINVAL, "merge_parts arguments");
+    if ((uintptr_t)parts & 7u) return fail(INS_EINVAL, "parts must be 8-byte aligned");
+    DeviceGuard dg(c->device);
+    cudaStream_t s = (cudaStream_t)stream;
+    const int n_items = B * c->g.n_kv;
+    const PartRec *p = (const PartRec *)parts;
+    switch (c->g.H) {
+        case 1: k_merge_parts<1><<<n_items, CHUNK_THREADS, 0, s>>>(c->g, p, n_items, n_parts, out, stats, c->d_status); break;
+        case 2: k_merge_parts<2><<<n_items, CHUNK_THREADS, 0, s>>>(c->g, p, n_items, n_parts, out, stats, c->d_status); break;
+        case 4: k_merge_parts<4><<<n_items, CHUNK_THREADS, 0, s>>>(c->g, p, n_items, n_parts, out, stats, c->d_status); break;
+        case 8: k_merge_parts<8><<<n_items, CHUNK_THREADS, 0, s>>>(c->g, p, n_items, n_parts, out, stats, c->d_status); break;
+        default: return fail(INS_EINVAL, "kv_groups");
+    }
+    CK(cudaGetLastError());
     return INS_OK;
 }
 

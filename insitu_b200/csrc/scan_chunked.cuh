@@ -115,6 +115,31 @@ __device__ __forceinline__ void page_row(const Geo &g, int pr, int &pi, int &lr)
     }
 }
 
+// One item's contribution from one context shard (a rank holding a causal
+// range of a sequence): its tiles folded into one composite -- the sums before
+// its first rescale, every rescale (factor, following sums) in order, the
+// clamp-proof bound Y -- and its share of the statistics. Folding the shards'
+// records in causal order is the recurrence over the whole sequence.
+constexpr int PART_MAXE = 64;            // rescales one head's shard can hold
+
+struct PartEntry {
+    int32_t S[D];          // within a shard |S| <= Y, which the merge needs below 2^31
+    int64_t l;
+    int32_t f;
+    int32_t pad;
+};
+
+struct PartRec {
+    int64_t Spre[HMAX][D];
+    int64_t Y[HMAX][D];
+    int64_t lpre[HMAX];
+    int32_t nent[HMAX];
+    int32_t fail;                          // the shard could not build an exact composite
+    int32_t pad;
+    int64_t n_tokens, resc, sovf, maxs;
+    PartEntry ent[HMAX][PART_MAXE];
+};
+
 struct ChunkArgs {
     Geo g;
     const DevTables *tb;
@@ -145,6 +170,9 @@ struct ChunkArgs {
     int32_t *redo;                // [n_items]: 1 = recompute with the sequential body
     unsigned long long *all_done;
     int32_t *status;
+    const long long *m_init;      // [n_items][H] running maximum entering the first tile, or null
+    long long *maxima;            // [n_items][H] k_chunk_prefix writes each item's maximum, or null
+    PartRec *parts;               // [n_items] composites instead of finalized outputs, or null
 };
 
 // Pinned host buffers for the per-call uploads (the tile list), used in turn:
@@ -558,6 +586,152 @@ __device__ void merge_item(const ChunkArgs &a, int item, int nblocks, int64_t T,
     }
 }
 
+// A context shard's item: fold its blocks into the item's PartRec instead of
+// finalizing. The same translation-and-rescale fold as merge_block, over the
+// item's blocks; Y composes as max(Y, |partial at block start| + Y_block).
+template <int H>
+__device__ void fold_part(const ChunkArgs &a, int item, int nblocks, int64_t T, long long *slots) {
+    PartRec &pr = a.parts[item];
+    const BlockRec *blks = a.blks + (int64_t)item * a.max_blocks;
+    bool over = false;
+    for (int pi = threadIdx.x; pi < H * D; pi += blockDim.x) {
+        const int h = pi / D, ch = pi % D;
+        int64_t loc = 0, Y = 0, curS = 0, curl = 0, Spre = 0, lpre = 0;
+        int ne = 0;
+        bool opened = false;
+        for (int bb = 0; bb < nblocks; ++bb) {
+            const BlockRec &br = blks[bb];
+            const int64_t Yb = ldcg(&br.Y[h][ch]);
+            const int64_t Sp = ldcg(&br.Spre[h][ch]);
+            const int64_t lp = ldcg(&br.lpre[h]);
+            const int nb_e = ldcg(&br.nent[h]);
+            const int eb = ldcg(&br.ent_base[h]);
+            const int64_t al = loc < 0 ? -loc : loc;
+            Y = max(Y, al + Yb);
+            loc += Sp;
+            curS += Sp;
+            curl += lp;
+            for (int e = 0; e < nb_e; ++e) {
+                const SegEntry &se = a.segs[eb + e];
+                const int64_t f = ldcg(&se.f);
+                if (!opened) {
+                    Spre = curS;
+                    lpre = curl;
+                    opened = true;
+                } else if (ne - 1 < PART_MAXE) {
+                    over |= curS < INT32_MIN || curS > INT32_MAX;
+                    pr.ent[h][ne - 1].S[ch] = (int32_t)curS;
+                    if (ch == 0) pr.ent[h][ne - 1].l = curl;
+                }
+                if (ne < PART_MAXE && ch == 0) pr.ent[h][ne].f = (int32_t)f;
+                ++ne;
+                curS = ldcg(&se.S[ch]);
+                curl = ldcg(&se.l);
+                loc = ((loc * f) >> a.g.prob_frac) + curS;
+            }
+        }
+        if (!opened) {
+            Spre = curS;
+            lpre = curl;
+        } else if (ne - 1 < PART_MAXE) {
+            over |= curS < INT32_MIN || curS > INT32_MAX;
+            pr.ent[h][ne - 1].S[ch] = (int32_t)curS;
+            if (ch == 0) pr.ent[h][ne - 1].l = curl;
+        }
+        over |= ne > PART_MAXE;
+        pr.Spre[h][ch] = Spre;
+        pr.Y[h][ch] = Y;
+        if (ch == 0) {
+            pr.lpre[h] = lpre;
+            pr.nent[h] = ne < PART_MAXE ? ne : PART_MAXE;
+        }
+    }
+    const bool bad = __syncthreads_or(over) ||
+                     *reinterpret_cast<volatile int32_t *>(&a.items[item].fail) != 0;
+    (void)slots;
+    if (threadIdx.x == 0) {
+        const volatile ItemAcc &ia = a.items[item];
+        pr.fail = bad ? 1 : 0;
+        pr.n_tokens = T;
+        pr.resc = (int64_t)ia.resc;
+        pr.sovf = (int64_t)ia.sovf;
+        pr.maxs = ia.maxs;
+        a.redo[item] = 0;            // a shard's item is not re-run here
+    }
+}
+
+// The context-split merge: one CTA per item folds the shards' composites in
+// causal order (the first shard holds the first tokens) and finalizes. The
+// fold is the recurrence over the whole sequence provided the 32-bit clamp
+// never fires; each shard proves that with |acc at its start| + Y <= 2^31 - 1.
+// A shard without an exact composite (more than PART_MAXE rescales of one
+// head, or a flagged item), or a failed proof, latches ST_SPLIT and leaves the
+// item's outputs unwritten.
+template <int H>
+__global__ void __launch_bounds__(CHUNK_THREADS) k_merge_parts(Geo g, const PartRec *parts, int n_items,
+                                                               int n_parts, int64_t *out, ins_stats *stats,
+                                                               int32_t *status) {
+    constexpr int NP = (H * D + CHUNK_THREADS - 1) / CHUNK_THREADS;
+    __shared__ long long slots[CHUNK_THREADS / 32];
+    const int item = blockIdx.x, tid = threadIdx.x;
+    int64_t acc[NP], l[NP];
+    bool bad = false;
+#pragma unroll
+    for (int k = 0; k < NP; ++k) {
+        acc[k] = 0;
+        l[k] = 0;
+        const int pi = tid + k * CHUNK_THREADS;
+        if (pi >= H * D) continue;
+        const int h = pi / D, ch = pi % D;
+        for (int r = 0; r < n_parts; ++r) {
+            const PartRec &pr = parts[(int64_t)r * n_items + item];
+            bad |= pr.fail != 0;
+            const int64_t aa = acc[k] < 0 ? -acc[k] : acc[k];
+            if (aa + pr.Y[h][ch] > INT32_MAX) bad = true;
+            acc[k] += pr.Spre[h][ch];
+            l[k] += pr.lpre[h];
+            const int ne = pr.nent[h];
+            for (int e = 0; e < ne; ++e) {
+                const int64_t f = pr.ent[h][e].f;
+                acc[k] = ((acc[k] * f) >> g.prob_frac) + pr.ent[h][e].S[ch];
+                l[k] = ((l[k] * f) >> g.prob_frac) + pr.ent[h][e].l;
+            }
+        }
+    }
+    bad = __syncthreads_or(bad);
+    if (bad) {
+        if (tid == 0) atomicOr(status, ST_SPLIT);
+        return;
+    }
+    int64_t *out_row = out + (int64_t)item * H * D;
+    long long mx = 0;
+#pragma unroll
+    for (int k = 0; k < NP; ++k) {
+        const int pi = tid + k * CHUNK_THREADS;
+        if (pi >= H * D) continue;
+        int64_t r;
+        int shift;
+        reciprocal(g, l[k], r, shift);
+        out_row[pi] = (acc[k] * r) >> shift;
+        const long long ab = acc[k] < 0 ? -acc[k] : acc[k];
+        mx = ab > mx ? ab : mx;
+    }
+    mx = cta_max_nonneg(mx, slots);
+    if (tid == 0 && stats) {
+        ins_stats st{};
+        for (int r = 0; r < n_parts; ++r) {
+            const PartRec &pr = parts[(int64_t)r * n_items + item];
+            st.n_tokens += pr.n_tokens;
+            st.rescale_events += pr.resc;
+            st.score_overflows += pr.sovf;
+            st.max_abs_score = pr.maxs > st.max_abs_score ? pr.maxs : st.max_abs_score;
+        }
+        st.acc_overflows = 0;
+        st.max_abs_acc = mx;
+        stats[item] = st;
+    }
+}
+
 __device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
@@ -798,6 +972,8 @@ __global__ void __launch_bounds__(256) k_chunk_prefix(ChunkArgs a) {
     const int nc = a.item_nchunks[item];
     long long *v = a.cmx + (int64_t)item * a.max_chunks * 2 * HMAX;
     const long long s_lo = -(1ll << (a.g.score_width - 1));
+    const long long seed = a.m_init ? (a.m_init[(int64_t)item * H + h] > s_lo ? a.m_init[(int64_t)item * H + h] : s_lo)
+                                    : s_lo;
     const int per = (nc + 255) / 256;                 // tiles per thread
     const int c0 = tid * per, c1 = min(nc, c0 + per);
     long long run = LLONG_MIN;
@@ -814,7 +990,7 @@ __global__ void __launch_bounds__(256) k_chunk_prefix(ChunkArgs a) {
     }
     if (lane == 31) wtot[warp] = x;
     __syncthreads();
-    long long before = s_lo;
+    long long before = seed;
     for (int w = 0; w < warp; ++w) before = wtot[w] > before ? wtot[w] : before;
     long long ex = __shfl_up_sync(FULL, x, 1);
     if (lane == 0) ex = LLONG_MIN;
@@ -823,6 +999,12 @@ __global__ void __launch_bounds__(256) k_chunk_prefix(ChunkArgs a) {
         v[(int64_t)c * 2 * HMAX + HMAX + h] = ex;
         const long long y = v[(int64_t)c * 2 * HMAX + h];
         ex = y > ex ? y : ex;
+    }
+    // the item's own maximum (with no seed), for a context-split exchange
+    if (a.maxima && c1 == nc && c0 < c1) {
+        long long m = LLONG_MIN;
+        for (int w = 0; w < 8; ++w) m = wtot[w] > m ? wtot[w] : m;
+        a.maxima[(int64_t)item * H + h] = m > s_lo ? m : s_lo;
     }
 }
 
@@ -1388,7 +1570,8 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
             __syncthreads();
             if (flag_sm) {
                 __threadfence();
-                merge_item<H>(a, item, nblk, a.T[b], qbase, slots_sm);
+                if (a.parts) fold_part<H>(a, item, nblk, a.T[b], slots_sm);
+                else merge_item<H>(a, item, nblk, a.T[b], qbase, slots_sm);
                 __syncthreads();
                 if (tid == 0) {
                     ItemAcc &ia = a.items[item];
@@ -1584,11 +1767,14 @@ inline int launch_chunk_kernels(ChunkArgs &a, int32_t B, const int32_t *d_seq, c
                : INS_ECUDA;
 }
 
+// The tile list, the scratch and the argument block of one chunked scan; no
+// launch.
 template <int H, int KB, int VB>
-inline int launch_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, int32_t B,
-                          const int32_t *d_seq, const int64_t *d_T, const int64_t *h_T,
-                          const int32_t *d_pt, const uint8_t *pool, const int32_t *q_rot,
-                          int64_t *out, ins_stats *stats, int32_t *d_status, cudaStream_t s) {
+inline int prepare_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, int32_t B,
+                           const int32_t *d_seq, const int64_t *d_T, const int64_t *h_T,
+                           const int32_t *d_pt, const uint8_t *pool, const int32_t *q_rot,
+                           int64_t *out, ins_stats *stats, int32_t *d_status, ChunkArgs &a,
+                           cudaStream_t s) {
     using CF = ChunkCfg<H, KB, VB>;
     const int n_items = B * g.n_kv;
     std::vector<int4> tiles;
@@ -1614,7 +1800,7 @@ inline int launch_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, i
             cs.up.done(slot, s))
             return INS_ECUDA;
     }
-    ChunkArgs a{};
+    a = ChunkArgs{};
     a.g = g;
     a.tb = tb;
     a.tiles = cs.tiles;
@@ -1645,7 +1831,55 @@ inline int launch_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, i
     a.all_done = cs.all_done;
     a.status = d_status;
     cs.last_items = n_items;
+    return INS_OK;
+}
+
+template <int H, int KB, int VB>
+inline int launch_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, int32_t B,
+                          const int32_t *d_seq, const int64_t *d_T, const int64_t *h_T,
+                          const int32_t *d_pt, const uint8_t *pool, const int32_t *q_rot,
+                          int64_t *out, ins_stats *stats, int32_t *d_status, cudaStream_t s) {
+    ChunkArgs a;
+    if (int rc = prepare_chunked<H, KB, VB>(cs, g, tb, B, d_seq, d_T, h_T, d_pt, pool, q_rot, out, stats,
+                                            d_status, a, s))
+        return rc;
     return launch_chunk_kernels<H, KB, VB>(a, B, d_seq, d_T, s);
+}
+
+// Context split, phase 1: the scores of this shard and each item's maximum
+// (a.maxima), leaving the scores in the scratch for phase 2.
+template <int H, int KB, int VB>
+inline int launch_split_maxima(ChunkArgs &a, cudaStream_t s) {
+    const int gA = chunk_slots<H, KB, VB, 0>();
+    if (gA < 0) return INS_ECUDA;
+    ChunkArgs m = a;
+    m.m_init = nullptr;
+    m.parts = nullptr;
+    k_scan_scores<H, KB, VB><<<gA < m.n_tiles ? gA : m.n_tiles, CHUNK_THREADS, score_smem<KB>(), s>>>(m);
+    k_chunk_prefix<H><<<m.n_items * H, 256, 0, s>>>(m);
+    return cudaGetLastError() == cudaSuccess ? INS_OK : INS_ECUDA;
+}
+
+// Context split, phase 2: with the running maximum entering the shard
+// (a.m_init), the values and one composite per item (a.parts).
+template <int H, int KB, int VB>
+inline int launch_split_part(ChunkArgs &a, cudaStream_t s) {
+    const int gB = chunk_slots<H, KB, VB, 1>();
+    if (gB < 0) return INS_ECUDA;
+    ChunkArgs m = a;
+    m.maxima = nullptr;
+    k_chunk_prefix<H><<<m.n_items * H, 256, 0, s>>>(m);
+    k_scan_values<H, KB, VB>
+        <<<gB < m.n_tiles ? gB : m.n_tiles, CHUNK_THREADS, ChunkCfg<H, KB, VB>::BYTES, s>>>(m);
+    return cudaGetLastError() == cudaSuccess ? INS_OK : INS_ECUDA;
+}
+
+// Which chunked instantiation serves a cache: 0 none, else (H, KB, VB) packed.
+inline int chunk_variant(const Geo &g, int H) {
+    if (!is_def_fmt(g)) return 0;
+    if (g.kb == 4 && g.vb == 2 && (H == 1 || H == 2 || H == 4 || H == 8)) return H * 100 + 42;
+    if (g.kb == 3 && g.vb == 3 && (H == 4 || H == 8)) return H * 100 + 33;
+    return 0;
 }
 
 inline int launch_online(ChunkScratch &cs, const Geo &g, const DevTables *tb, int32_t B,

@@ -195,6 +195,71 @@ class PagedCache:
                                     _ptr(q), _ptr(out), _ptr(st), m, _stream(self.device)))
         return out, st
 
+    # -- context split (one sequence across shards) -------------------------------
+    S_LO = -(1 << 47)   # the running maximum before any token (score_width 48)
+
+    def _split_args(self, seq_ids, q_rot, lengths):
+        g = self.geo
+        q = self._dev_i32(q_rot, (g.num_heads, g.head_dim))
+        B = q.shape[0]
+        ids = np.ascontiguousarray(np.broadcast_to(np.asarray(seq_ids, dtype=np.int32), (B,)))
+        lens = None
+        if lengths is not None:
+            lens = np.ascontiguousarray(np.broadcast_to(np.asarray(lengths, dtype=np.int64), (B,)))
+        return q, B, ids, lens
+
+    def scan_maxima(self, seq_ids, q_rot, *, lengths=None) -> torch.Tensor:
+        """Phase 1 of a context split (ins_scan_maxima): this shard's maximum
+        score per (sequence, KV head, query head), (B, n_kv, groups) int64."""
+        q, B, ids, lens = self._split_args(seq_ids, q_rot, lengths)
+        mx = torch.empty((B, self.geo.n_kv_heads, self.geo.kv_groups), dtype=torch.int64,
+                         device=self.device)
+        _lib.check(self._L.ins_scan_maxima(self._h, B, ids.ctypes.data_as(C.c_void_p),
+                                           None if lens is None else lens.ctypes.data_as(C.c_void_p),
+                                           _ptr(q), _ptr(mx), _stream(self.device)))
+        self._split_q = q          # the same q_rot buffer must reach phase 2
+        return mx
+
+    def scan_part(self, seq_ids, m_in, *, lengths=None) -> torch.Tensor:
+        """Phase 2 (ins_scan_part): this shard's composites given the running
+        maximum entering it (``m_in`` shaped like scan_maxima's result); one
+        uint8 buffer of part_bytes(B) bytes."""
+        q = getattr(self, "_split_q", None)
+        if q is None:
+            raise RuntimeError("scan_part needs scan_maxima first")
+        _, B, ids, lens = self._split_args(seq_ids, q, lengths)
+        m = torch.as_tensor(m_in, dtype=torch.int64).to(self.device).contiguous()
+        if m.numel() != B * self.geo.n_kv_heads * self.geo.kv_groups:
+            raise ValueError("m_in must hold one value per (sequence, KV head, query head)")
+        part = torch.empty(self.part_bytes(B), dtype=torch.uint8, device=self.device)
+        _lib.check(self._L.ins_scan_part(self._h, B, ids.ctypes.data_as(C.c_void_p),
+                                         None if lens is None else lens.ctypes.data_as(C.c_void_p),
+                                         _ptr(q), _ptr(m), _ptr(part), _stream(self.device)))
+        self._split_q = None
+        return part
+
+    def part_bytes(self, B: int) -> int:
+        n = self._L.ins_part_bytes(self._h, int(B))
+        if n < 0:
+            _lib.check(_lib.INS_EINVAL)
+        return int(n)
+
+    def merge_parts(self, parts: torch.Tensor, B: int, *, stats: bool = True):
+        """Fold the shards' composites (``parts``: (n_parts, part_bytes(B)) uint8
+        on this device, in causal order) into outputs and stats, as
+        ``scan`` returns them for the whole sequences."""
+        g = self.geo
+        p = torch.as_tensor(parts).to(self.device).contiguous()
+        n_parts = p.shape[0]
+        if p.dtype != torch.uint8 or p.numel() != n_parts * self.part_bytes(B):
+            raise ValueError("parts must be (n_parts, part_bytes(B)) uint8")
+        out = torch.empty((B, g.num_heads, g.head_dim), dtype=torch.int64, device=self.device)
+        st = torch.empty((B, g.n_kv_heads, len(_lib.STATS_FIELDS)), dtype=torch.int64,
+                         device=self.device) if stats else None
+        _lib.check(self._L.ins_merge_parts(self._h, B, n_parts, _ptr(p), _ptr(out), _ptr(st),
+                                           _stream(self.device)))
+        return out, st
+
     # -- format conversion (blocking) --------------------------------------------
     def export(self, seq: int, kv_head: int, t0: int = 0, n: int | None = None) -> np.ndarray:
         """Rows [t0, t0+n) in the reference's packed format: (n, row_bytes) uint8."""
