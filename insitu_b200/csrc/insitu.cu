@@ -872,11 +872,9 @@ int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
                 g_na_tiles[k++] = make_int4(it, cidx, (int)t0, (int)(T - t0 < C ? T - t0 : C));
             }
     uint8_t *p = (uint8_t *)st.ptr;
-    // what the kernels expect at zero: the completion and allocation counters
-    // and the per-block and per-item accumulators (the array keeps whatever
-    // the previous call left in it)
-    CK(cudaMemsetAsync(p, 0, L.cmx, s));
-    CK(cudaMemsetAsync(p + L.bd, 0, L.seg - L.bd, s));
+    // what the kernels expect at zero: the per-item accumulators (the array
+    // keeps whatever the previous call left in it; the segment counter is
+    // cleared by the launch itself)
     CK(cudaMemsetAsync(p + L.items, 0, sizeof(ItemAcc) * (size_t)n_items, s));
     CK(cudaMemcpyAsync(p + L.tiles, g_na_tiles, sizeof(int4) * (size_t)n_tiles, cudaMemcpyHostToDevice, s));
     CK(cudaMemcpyAsync(p + L.nc, g_na_nc, sizeof(int32_t) * (size_t)n_items, cudaMemcpyHostToDevice, s));
@@ -905,13 +903,11 @@ int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
     a.cmx = (long long *)(p + L.cmx);
     a.recs = (ChunkRec *)(p + L.rec);
     a.blks = (BlockRec *)(p + L.blk);
-    a.blk_done = (unsigned int *)(p + L.bd);
     a.segs = (SegEntry *)(p + L.seg);
     a.seg_top = (unsigned int *)(p + L.top);
     a.seg_cap = NOALLOC_SEGS;
     a.items = (ItemAcc *)(p + L.items);
     a.redo = (int32_t *)(p + L.redo);
-    a.all_done = (unsigned long long *)(p + L.all);
     a.status = c->d_status;
     const int rc = launch_chunk_kernels<H, KB, VB>(a, B, a.seq_ids, a.T, s);
     return rc ? fail(rc, "chunked scan launch") : INS_OK;

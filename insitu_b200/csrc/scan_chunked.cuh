@@ -162,13 +162,11 @@ struct ChunkArgs {
     long long *cmx;               // [n_items * max_chunks][2][HMAX]: tile maximum, m_in
     ChunkRec *recs;               // [n_items * max_chunks]
     BlockRec *blks;               // [n_items * max_blocks]
-    unsigned int *blk_done;       // [n_items * max_blocks]
     SegEntry *segs;
     unsigned int *seg_top;
     int32_t seg_cap;
     ItemAcc *items;               // [n_items]
     int32_t *redo;                // [n_items]: 1 = recompute with the sequential body
-    unsigned long long *all_done;
     int32_t *status;
     const long long *m_init;      // [n_items][H] running maximum entering the first tile, or null
     long long *maxima;            // [n_items][H] k_chunk_prefix writes each item's maximum, or null
@@ -228,10 +226,8 @@ struct ChunkScratch {
     int64_t sc_rows = 0;          // rows * H capacity of `sc`, in 32-bit words
     uint32_t *sc = nullptr;
     long long *bmg = nullptr, *cmx = nullptr;
-    unsigned long long *all_done = nullptr;
     ChunkRec *recs = nullptr;
     BlockRec *blks = nullptr;
-    unsigned int *blk_done = nullptr;
     SegEntry *segs = nullptr;
     unsigned int *seg_top = nullptr;
     ItemAcc *items = nullptr;
@@ -1023,8 +1019,8 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
     __shared__ int32_t vcent[256];
     __shared__ int32_t exp_tab[256];
     __shared__ long long m_in_sm[H];
-    __shared__ int flag_sm, fail_sm;
-    __shared__ int nseg_sm[H], segbase_sm[H], base_sm[H];
+    __shared__ int fail_sm;
+    __shared__ int nseg_sm[H], segbase_sm[H];
     __shared__ int32_t rl_f[H][SEGMAX];
     __shared__ unsigned int lsum_sm[H][SEGMAX + 1];   // l of a tile < 2^25
     __shared__ long long bnd_sm[NT / 32][H];           // per-warp clamp-proof bounds
@@ -1543,56 +1539,42 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
                 if (resc_sm) atomicAdd(&ia.resc, (unsigned long long)resc_sm);
             }
         }
-        __threadfence();
-        __syncthreads();
+        __syncthreads();                 // the next tile reuses shared memory
+    }
+}
 
-        // ---- 6. fold: the last chunk of a block folds the block, the last block
-        //         of an item folds the item ---------------------------------------
-        const int nc = a.item_nchunks[item];
-        const int blk = c / GBLK;
-        const int nblk = (nc + GBLK - 1) / GBLK;
-        const int in_blk = min(nc, blk * GBLK + GBLK) - blk * GBLK;
-        if (tid == 0) {
-            const unsigned old = atomicAdd(&a.blk_done[(int64_t)item * a.max_blocks + blk], 1u);
-            flag_sm = old + 1 == (unsigned)in_blk;
-        }
-        __syncthreads();
-        if (flag_sm) {
-            __threadfence();
-            merge_block<H>(a, item, blk, nc, base_sm);
-            __threadfence();
-            __syncthreads();
-            if (tid == 0) {
-                a.blk_done[(int64_t)item * a.max_blocks + blk] = 0;
-                const unsigned long long old = atomicAdd(&a.items[item].done_blocks, 1ull);
-                flag_sm = old + 1 == (unsigned long long)nblk;
-            }
-            __syncthreads();
-            if (flag_sm) {
-                __threadfence();
-                if (a.parts) fold_part<H>(a, item, nblk, a.T[b], slots_sm);
-                else merge_item<H>(a, item, nblk, a.T[b], qbase, slots_sm);
-                __syncthreads();
-                if (tid == 0) {
-                    ItemAcc &ia = a.items[item];
-                    ia.done_blocks = 0;
-                    ia.resc = 0;
-                    ia.sovf = 0;
-                    ia.maxs = 0;
-                    ia.fail = 0;
-                }
-            }
-        }
-        // ---- 7. the last tile of the launch resets the pool ----------------------
-        if (tid == 0) {
-            __threadfence();
-            const unsigned long long d = atomicAdd(a.all_done, 1ull);
-            if (d + 1 == (unsigned long long)a.n_tiles) {
-                *a.seg_top = 0;
-                *a.all_done = 0;
-            }
-        }
-        __syncthreads();
+// ---------------------------------------------------------------------------
+// Launches 4 and 5: the fold, after every tile's record is written (the
+// stream orders it; no fence or counter is needed)
+// ---------------------------------------------------------------------------
+// Level 1: one CTA per (item, block of GBLK tiles).
+template <int H>
+__global__ void __launch_bounds__(CHUNK_THREADS) k_fold_blocks(ChunkArgs a) {
+    __shared__ int base_sm[H];
+    const int item = blockIdx.x / a.max_blocks, blk = blockIdx.x % a.max_blocks;
+    const int nc = a.item_nchunks[item];
+    if (blk * GBLK >= nc) return;
+    merge_block<H>(a, item, blk, nc, base_sm);
+}
+
+// Level 2: one CTA per item folds its blocks and finalizes (or, for a context
+// shard, writes its composite), then clears the item's accumulators.
+template <int H>
+__global__ void __launch_bounds__(CHUNK_THREADS) k_fold_items(ChunkArgs a) {
+    __shared__ long long slots[CHUNK_THREADS / 32];
+    const int item = blockIdx.x;
+    const int nc = a.item_nchunks[item], nblk = (nc + GBLK - 1) / GBLK;
+    const int b = item / a.g.n_kv;
+    if (a.parts) fold_part<H>(a, item, nblk, a.T[b], slots);
+    else merge_item<H>(a, item, nblk, a.T[b], (int64_t)item * H * D, slots);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        ItemAcc &ia = a.items[item];
+        ia.done_blocks = 0;
+        ia.resc = 0;
+        ia.sovf = 0;
+        ia.maxs = 0;
+        ia.fail = 0;
     }
 }
 
@@ -1672,17 +1654,15 @@ inline void build_tiles(const Geo &g, int32_t B, const int64_t *h_T, int C, std:
 
 // Byte layout of the scratch of one scan: `o` offsets in the order carved.
 struct ScratchLayout {
-    size_t all, top, cmx, rec, blk, bd, seg, items, redo, tiles, nc, rb, bmg, sc, total;
+    size_t top, cmx, rec, blk, seg, items, redo, tiles, nc, rb, bmg, sc, total;
     ScratchLayout(int ni, int mc, int sc_cap, int tc, int H, int CW, int64_t rows) {
         auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
         const int mb = (mc + GBLK - 1) / GBLK;
         size_t o = 0;
-        all = o; o += al(8);
         top = o; o += al(8);
         cmx = o; o += al(sizeof(long long) * (size_t)ni * mc * 2 * HMAX);
         rec = o; o += al(sizeof(ChunkRec) * (size_t)ni * mc);
         blk = o; o += al(sizeof(BlockRec) * (size_t)ni * mb);
-        bd = o; o += al(sizeof(unsigned int) * (size_t)ni * mb);
         seg = o; o += al(sizeof(SegEntry) * (size_t)sc_cap);
         items = o; o += al(sizeof(ItemAcc) * (size_t)ni);
         redo = o; o += al(sizeof(int32_t) * (size_t)ni);
@@ -1726,12 +1706,10 @@ inline int reserve_scratch(ChunkScratch &cs, int n_items, int max_nc, int n_tile
     if (cudaMemset(cs.base, 0, L.total) != cudaSuccess) return INS_ECUDA;
     uint8_t *p = (uint8_t *)cs.base;
     cs.bytes = L.total;
-    cs.all_done = (unsigned long long *)(p + L.all);
     cs.seg_top = (unsigned int *)(p + L.top);
     cs.cmx = (long long *)(p + L.cmx);
     cs.recs = (ChunkRec *)(p + L.rec);
     cs.blks = (BlockRec *)(p + L.blk);
-    cs.blk_done = (unsigned int *)(p + L.bd);
     cs.segs = (SegEntry *)(p + L.seg);
     cs.items = (ItemAcc *)(p + L.items);
     cs.redo = (int32_t *)(p + L.redo);
@@ -1755,10 +1733,13 @@ inline int launch_chunk_kernels(ChunkArgs &a, int32_t B, const int32_t *d_seq, c
                                 cudaStream_t s) {
     const int gA = chunk_slots<H, KB, VB, 0>(), gB = chunk_slots<H, KB, VB, 1>();
     if (gA < 0 || gB < 0) return INS_ECUDA;
+    if (cudaMemsetAsync(a.seg_top, 0, sizeof(unsigned int), s) != cudaSuccess) return INS_ECUDA;
     k_scan_scores<H, KB, VB><<<gA < a.n_tiles ? gA : a.n_tiles, CHUNK_THREADS, score_smem<KB>(), s>>>(a);
     k_chunk_prefix<H><<<a.n_items * H, 256, 0, s>>>(a);
     k_scan_values<H, KB, VB>
         <<<gB < a.n_tiles ? gB : a.n_tiles, CHUNK_THREADS, ChunkCfg<H, KB, VB>::BYTES, s>>>(a);
+    k_fold_blocks<H><<<a.n_items * a.max_blocks, CHUNK_THREADS, 0, s>>>(a);
+    k_fold_items<H><<<a.n_items, CHUNK_THREADS, 0, s>>>(a);
     if (cudaGetLastError() != cudaSuccess) return INS_ECUDA;
     // items whose exactness the fold could not prove are recomputed in order
     return launch_seq<H>(a.g, a.tb, B, d_seq, d_T, a.page_table, a.pool, a.q_rot, a.out, a.stats,
@@ -1822,13 +1803,11 @@ inline int prepare_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, 
     a.cmx = cs.cmx;
     a.recs = cs.recs;
     a.blks = cs.blks;
-    a.blk_done = cs.blk_done;
     a.segs = cs.segs;
     a.seg_top = cs.seg_top;
     a.seg_cap = cs.seg_cap;
     a.items = cs.items;
     a.redo = cs.redo;
-    a.all_done = cs.all_done;
     a.status = d_status;
     cs.last_items = n_items;
     return INS_OK;
@@ -1868,9 +1847,12 @@ inline int launch_split_part(ChunkArgs &a, cudaStream_t s) {
     if (gB < 0) return INS_ECUDA;
     ChunkArgs m = a;
     m.maxima = nullptr;
+    if (cudaMemsetAsync(m.seg_top, 0, sizeof(unsigned int), s) != cudaSuccess) return INS_ECUDA;
     k_chunk_prefix<H><<<m.n_items * H, 256, 0, s>>>(m);
     k_scan_values<H, KB, VB>
         <<<gB < m.n_tiles ? gB : m.n_tiles, CHUNK_THREADS, ChunkCfg<H, KB, VB>::BYTES, s>>>(m);
+    k_fold_blocks<H><<<m.n_items * m.max_blocks, CHUNK_THREADS, 0, s>>>(m);
+    k_fold_items<H><<<m.n_items, CHUNK_THREADS, 0, s>>>(m);
     return cudaGetLastError() == cudaSuccess ? INS_OK : INS_ECUDA;
 }
 
