@@ -96,7 +96,6 @@ struct ins_cache {
     DevTables *d_tables = nullptr;
     uint8_t *d_pool = nullptr;
     int32_t *d_page_table = nullptr;   // [max_seqs, max_pages]
-    int32_t *d_seq_lens = nullptr;     // [max_seqs]
     int32_t *d_status = nullptr;
     // host mirrors (pinned, so their copies can be asynchronous)
     int32_t *h_page_table = nullptr;
@@ -146,6 +145,8 @@ int check_config(const ins_config *c) {
     if (c->max_seqs < 1 || c->max_pages_per_seq < 1 || c->n_pages < 1)
         return fail(INS_EINVAL, "max_seqs, max_pages_per_seq and n_pages must be positive");
     if (c->n_pages > INT32_MAX) return fail(INS_EINVAL, "n_pages above 2^31");
+    if ((int64_t)c->max_seqs * c->max_pages_per_seq > INT32_MAX)
+        return fail(INS_EINVAL, "max_seqs x max_pages_per_seq above 2^31 page-table entries");
     return INS_OK;
 }
 
@@ -187,14 +188,12 @@ int sync_mirrors(ins_cache *c) {
     return INS_OK;
 }
 
-// Copy the whole page table and length array to the device (a few hundred KB
-// at most; the same bytes a vLLM-style block manager ships per step).
+// Copy the page-table rows of sequences seq_lo .. seq_hi-1 to the device
+// (after a reset or an import; ingress ships only the entries it adds).
 int push_mirrors(ins_cache *c, cudaStream_t s, int32_t seq_lo, int32_t seq_hi) {
     const size_t row = (size_t)c->cfg.max_pages_per_seq;
     CK(cudaMemcpyAsync(c->d_page_table + (size_t)seq_lo * row, c->h_page_table + (size_t)seq_lo * row,
                        sizeof(int32_t) * row * (size_t)(seq_hi - seq_lo), cudaMemcpyHostToDevice, s));
-    CK(cudaMemcpyAsync(c->d_seq_lens + seq_lo, c->h_seq_lens + seq_lo,
-                       sizeof(int32_t) * (size_t)(seq_hi - seq_lo), cudaMemcpyHostToDevice, s));
     CK(cudaEventRecord(c->mirror_done, s));
     return INS_OK;
 }
@@ -207,7 +206,7 @@ int64_t capacity_of(const ins_cache *c) {
 // failure nothing changes (the reference raises before it writes,
 // cache/base.py:67-73).
 int reserve_slots(ins_cache *c, int32_t n, const int32_t *seq_ids, int64_t *slots,
-                  int32_t *lo, int32_t *hi) {
+                  int32_t *lo, int32_t *hi, int2 *pt_new = nullptr, int32_t *n_new = nullptr) {
     const int P = c->cfg.page_tokens;
     std::vector<int64_t> len_after;
     std::vector<int32_t> touched;
@@ -236,13 +235,16 @@ int reserve_slots(ins_cache *c, int32_t n, const int32_t *seq_ids, int64_t *slot
     }
     int32_t smin = INT32_MAX, smax = -1;
     const size_t row = (size_t)c->cfg.max_pages_per_seq;
+    if (n_new) *n_new = 0;
     for (int32_t i = 0; i < n; ++i) {
         const int32_t s = seq_ids[i];
         const int64_t pos = c->h_seq_lens[s];
-        int32_t &pg = c->h_page_table[(size_t)s * row + (size_t)(pos / P)];
+        const size_t at = (size_t)s * row + (size_t)(pos / P);
+        int32_t &pg = c->h_page_table[at];
         if (pos % P == 0) {
             pg = c->free_pages.back();
             c->free_pages.pop_back();
+            if (pt_new) pt_new[(*n_new)++] = make_int2((int32_t)at, pg);
         }
         slots[i] = (int64_t)pg * P + pos % P;
         c->h_seq_lens[s] = (int32_t)(pos + 1);
@@ -347,7 +349,6 @@ int ins_cache_create(const ins_config *cfg, const ins_tables *tb, int32_t device
     if (cudaMalloc(&c->d_tables, sizeof(DevTables)) != cudaSuccess ||
         cudaMalloc(&c->d_pool, pool_bytes) != cudaSuccess ||
         cudaMalloc(&c->d_page_table, sizeof(int32_t) * pt) != cudaSuccess ||
-        cudaMalloc(&c->d_seq_lens, sizeof(int32_t) * cfg->max_seqs) != cudaSuccess ||
         cudaMalloc(&c->d_status, sizeof(int32_t)) != cudaSuccess ||
         cudaHostAlloc(&c->h_page_table, sizeof(int32_t) * pt, cudaHostAllocDefault) != cudaSuccess ||
         cudaHostAlloc(&c->h_seq_lens, sizeof(int32_t) * cfg->max_seqs, cudaHostAllocDefault) !=
@@ -365,7 +366,6 @@ int ins_cache_create(const ins_config *cfg, const ins_tables *tb, int32_t device
     if (cudaMemcpy(c->d_tables, &ht, sizeof(ht), cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMemcpy(c->d_page_table, c->h_page_table, sizeof(int32_t) * pt, cudaMemcpyHostToDevice) !=
             cudaSuccess ||
-        cudaMemset(c->d_seq_lens, 0, sizeof(int32_t) * cfg->max_seqs) != cudaSuccess ||
         cudaMemset(c->d_status, 0, sizeof(int32_t)) != cudaSuccess ||
         cudaMemset(c->d_pool, 0, pool_bytes) != cudaSuccess)
         return cleanup(fail(INS_ECUDA, "initial copies failed"));
@@ -385,7 +385,6 @@ int ins_cache_destroy(ins_cache *c) {
     cudaFree(c->d_tables);
     cudaFree(c->d_pool);
     cudaFree(c->d_page_table);
-    cudaFree(c->d_seq_lens);
     cudaFree(c->d_status);
     if (c->h_page_table) cudaFreeHost(c->h_page_table);
     if (c->h_seq_lens) cudaFreeHost(c->h_seq_lens);
@@ -433,18 +432,23 @@ int ins_ingress(ins_cache *c, int32_t n, const int32_t *seq_ids, const int32_t *
     DeviceGuard dg(c->device);
     cudaStream_t s = (cudaStream_t)stream;
     if (int rc = sync_mirrors(c)) return rc;
-    if (int rc = c->stage_a.reserve(sizeof(int64_t) * (size_t)n)) return rc;
-    int32_t lo, hi;
-    if (int rc = reserve_slots(c, n, seq_ids, (int64_t *)c->stage_a.h, &lo, &hi)) return rc;
-    if (int rc = c->stage_a.upload(sizeof(int64_t) * (size_t)n, s)) return rc;
-    if (int rc = push_mirrors(c, s, lo, hi)) return rc;
+    // staging: [slot of every token (n int64)][pages opened: (page-table index, page) (<= n int2)]
+    if (int rc = c->stage_a.reserve(sizeof(int64_t) * (size_t)n + sizeof(int2) * (size_t)n)) return rc;
+    int32_t lo, hi, n_new = 0;
+    int64_t *h_slots = (int64_t *)c->stage_a.h;
+    int2 *h_new = (int2 *)(h_slots + n);
+    if (int rc = reserve_slots(c, n, seq_ids, h_slots, &lo, &hi, h_new, &n_new)) return rc;
+    if (int rc = c->stage_a.upload(sizeof(int64_t) * (size_t)n + sizeof(int2) * (size_t)n_new, s))
+        return rc;
     const int per_tok = (q ? c->g.n_kv * c->g.H : 0) + 2 * c->g.n_kv;
     const int64_t warps = (int64_t)n * per_tok;
     const int wpb = 8;
     const int64_t blocks = (warps + wpb - 1) / wpb;
     k_ingress<<<(unsigned)blocks, wpb * 32, 0, s>>>(c->g, c->d_tables, n,
                                                     (const int64_t *)c->stage_a.d, q, k, v, q_rot,
-                                                    c->d_pool, flags, c->d_status);
+                                                    c->d_pool, flags, c->d_status,
+                                                    (const int2 *)((const int64_t *)c->stage_a.d + n), n_new,
+                                                    c->d_page_table);
     CK(cudaGetLastError());
     return INS_OK;
 }
@@ -817,7 +821,6 @@ namespace {
 constexpr size_t NOALLOC_BYTES = (size_t)192 << 20;
 constexpr int NOALLOC_SEGS = 4096;            // rescale segments; beyond, items are recomputed
 constexpr int NOALLOC_MAX_B = 4096;           // sequences per call
-constexpr int NOALLOC_MAX_TILES = 1 << 16;    // (item, chunk) tiles per call
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_BYTES];
 
@@ -827,11 +830,10 @@ struct NoallocState {
 std::mutex g_noalloc_mu;
 NoallocState g_noalloc[256];                  // per device ordinal
 // host staging of one call, reused under the lock
-int4 g_na_tiles[NOALLOC_MAX_TILES];
-int32_t g_na_nc[NOALLOC_MAX_B * 8];
 int64_t g_na_T[NOALLOC_MAX_B];
 int32_t g_na_seq[NOALLOC_MAX_B];
-int64_t g_na_rb[NOALLOC_MAX_B * 8];
+TilePlan g_na_plan;
+std::vector<uint8_t> g_na_desc;
 
 template <int H, int KB, int VB>
 int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out, ins_stats *stats,
@@ -840,57 +842,41 @@ int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
     const Geo &g = c->g;
     const int n_items = B * g.n_kv;
     if (n_items > NOALLOC_MAX_B * 8) return fail(INS_EBADLEN, "too many (sequence, KV head) items");
-    const int C = CF::C;
-    int max_nc = 1;
-    int64_t n_tiles = 0, rows = 0;
-    for (int it = 0; it < n_items; ++it) {
-        const int64_t T = g_na_T[it / g.n_kv];
-        const int ncn = T ? (int)((T + C - 1) / C) : 1;
-        g_na_nc[it] = ncn;
-        g_na_rb[it] = rows;
-        rows += T;
-        max_nc = ncn > max_nc ? ncn : max_nc;
-        n_tiles += ncn;
-    }
+    TilePlan &tp = g_na_plan;
+    tp.build(g, B, g_na_T, CF::C);
+    const int64_t n_tiles = tp.n_tiles;
     // the carve, in the same order ins_scan's scratch uses
-    const ScratchLayout L(n_items, max_nc, NOALLOC_SEGS, (int)(n_tiles < 1 ? 1 : n_tiles), H, CF::CW,
-                          rows);
+    const ScratchLayout L(n_items, tp.max_nc, NOALLOC_SEGS, (int)(n_tiles < 1 ? 1 : n_tiles), H, CF::CW,
+                          tp.rows);
     const size_t o_T = L.total;
     const size_t o_seq = o_T + ((sizeof(int64_t) * (size_t)B + 255) & ~(size_t)255);
     const size_t o_end = o_seq + sizeof(int32_t) * (size_t)B;
-    if (o_end > NOALLOC_BYTES || n_tiles > NOALLOC_MAX_TILES)
-        return fail(INS_EBADLEN, "this scan needs " + std::to_string(o_end) + " B of scratch and " +
-                                     std::to_string(n_tiles) + " tiles; ins_scan_noalloc holds " +
-                                     std::to_string(NOALLOC_BYTES) + " B and " +
-                                     std::to_string(NOALLOC_MAX_TILES) + " tiles");
-    int64_t k = 0;
-    for (int cidx = 0; cidx < max_nc; ++cidx)
-        for (int it = 0; it < n_items; ++it)
-            if (cidx < g_na_nc[it]) {
-                const int64_t T = g_na_T[it / g.n_kv];
-                const int64_t t0 = (int64_t)cidx * C;
-                g_na_tiles[k++] = make_int4(it, cidx, (int)t0, (int)(T - t0 < C ? T - t0 : C));
-            }
+    if (o_end > NOALLOC_BYTES || n_tiles > INT32_MAX / 2)
+        return fail(INS_EBADLEN, "this scan needs " + std::to_string(o_end) + " B of scratch; "
+                                 "ins_scan_noalloc holds " + std::to_string(NOALLOC_BYTES) + " B");
+    const TileDesc TD(n_items);
+    g_na_desc.assign(TD.total, 0);
+    tp.write(g_na_desc.data(), TD);
     uint8_t *p = (uint8_t *)st.ptr;
     // what the kernels expect at zero: the per-item accumulators (the array
     // keeps whatever the previous call left in it; the segment counter is
     // cleared by the launch itself)
     CK(cudaMemsetAsync(p + L.items, 0, sizeof(ItemAcc) * (size_t)n_items, s));
-    CK(cudaMemcpyAsync(p + L.tiles, g_na_tiles, sizeof(int4) * (size_t)n_tiles, cudaMemcpyHostToDevice, s));
-    CK(cudaMemcpyAsync(p + L.nc, g_na_nc, sizeof(int32_t) * (size_t)n_items, cudaMemcpyHostToDevice, s));
-    CK(cudaMemcpyAsync(p + L.rb, g_na_rb, sizeof(int64_t) * (size_t)n_items, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(p + L.desc, g_na_desc.data(), g_na_desc.size(), cudaMemcpyHostToDevice, s));
     CK(cudaMemcpyAsync(p + o_T, g_na_T, sizeof(int64_t) * (size_t)B, cudaMemcpyHostToDevice, s));
     CK(cudaMemcpyAsync(p + o_seq, g_na_seq, sizeof(int32_t) * (size_t)B, cudaMemcpyHostToDevice, s));
     ChunkArgs a{};
     a.g = g;
     a.tb = c->d_tables;
-    a.tiles = (const int4 *)(p + L.tiles);
+    a.runs = (const int4 *)(p + L.desc + TD.runs);
+    a.n_runs = (int32_t)tp.runs.size();
+    a.order = (const int32_t *)(p + L.desc + TD.ord);
+    a.tile_rows = CF::C;
     a.n_tiles = (int32_t)n_tiles;
-    a.max_chunks = max_nc;
-    a.max_blocks = (max_nc + GBLK - 1) / GBLK;
+    a.max_chunks = tp.max_nc;
+    a.max_blocks = (tp.max_nc + GBLK - 1) / GBLK;
     a.n_items = n_items;
-    a.item_nchunks = (const int32_t *)(p + L.nc);
-    a.row_base = (const int64_t *)(p + L.rb);
+    a.row_base = (const int64_t *)(p + L.desc + TD.rb);
     a.seq_ids = (const int32_t *)(p + o_seq);
     a.T = (const int64_t *)(p + o_T);
     a.page_table = c->d_page_table;

@@ -65,9 +65,17 @@ __global__ void k_ingress(Geo g, const DevTables *__restrict__ tb, int32_t n,
                           const int64_t *__restrict__ slots, const int32_t *__restrict__ q,
                           const int32_t *__restrict__ k, const int32_t *__restrict__ v,
                           int32_t *__restrict__ q_rot, uint8_t *__restrict__ pool,
-                          uint32_t flags, int32_t *__restrict__ status) {
+                          uint32_t flags, int32_t *__restrict__ status,
+                          const int2 *__restrict__ pt_new, int32_t n_new,
+                          int32_t *__restrict__ page_table) {
     __shared__ uint8_t codes_sm[8][D];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    // the pages these tokens opened, (page-table index, page): the scans that
+    // follow on the stream read them (nothing in this launch does)
+    {
+        const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+        if (t < n_new) page_table[pt_new[t].x] = pt_new[t].y;
+    }
     const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + wib;
     const int Hq = q ? g.n_kv * g.H : 0;
     const int per_tok = Hq + 2 * g.n_kv;

@@ -29,6 +29,7 @@
 // result is bit-exact in every case.
 #pragma once
 
+#include <algorithm>
 #include <climits>
 #include <cstring>
 #include <mutex>
@@ -143,12 +144,19 @@ struct PartRec {
 struct ChunkArgs {
     Geo g;
     const DevTables *tb;
-    const int4 *tiles;            // (item, chunk, t0, n), chunk-major
+    // The tiles, chunk-major: every item's chunk 0, then every item's chunk
+    // 1, ... (items with fewer chunks drop out). `order` lists the items by
+    // chunk count, most first; run r covers the chunks from runs[r].x on, in
+    // which the first runs[r].z items of `order` have a tile each, and its
+    // first tile is tile runs[r].y.
+    const int4 *runs;
+    int32_t n_runs;
+    const int32_t *order;
+    int32_t tile_rows;            // rows per tile (the last tile of an item may hold fewer)
     int32_t n_tiles;
     int32_t max_chunks;
     int32_t max_blocks;
     int32_t n_items;
-    const int32_t *item_nchunks;
     const int64_t *row_base;      // [n_items]: first row of the item in `sc`
     const int32_t *seq_ids;
     const int64_t *T;
@@ -173,18 +181,61 @@ struct ChunkArgs {
     PartRec *parts;               // [n_items] composites instead of finalized outputs, or null
 };
 
-// Pinned host buffers for the per-call uploads (the tile list), used in turn:
+// Chunks of an item: one per tile_rows rows, and one (empty) for an empty item.
+__device__ __forceinline__ int item_chunks(const ChunkArgs &a, int item) {
+    const int64_t T = a.T[item / a.g.n_kv];
+    return T ? (int)((T + a.tile_rows - 1) / a.tile_rows) : 1;
+}
+
+// Tile `tile` of the plan as (item, chunk, first row, rows). With one run all
+// items have the same chunk count and `order` is the identity, so the common
+// case reads nothing but T.
+__device__ __forceinline__ int4 tile_at(const ChunkArgs &a, int tile) {
+    int4 r;
+    int item;
+    if (a.n_runs == 1) {
+        r = a.runs[0];
+        item = (tile - r.y) % r.z;
+    } else {
+        int lo = 0, hi = a.n_runs - 1;              // the last run starting at or before `tile`
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (a.runs[mid].y <= tile) lo = mid;
+            else hi = mid - 1;
+        }
+        r = a.runs[lo];
+        item = a.order[(tile - r.y) % r.z];
+    }
+    const int c = r.x + (tile - r.y) / r.z;
+    const int64_t T = a.T[item / a.g.n_kv], t0 = (int64_t)c * a.tile_rows;
+    const int64_t n = T - t0 < a.tile_rows ? T - t0 : a.tile_rows;
+    return make_int4(item, c, (int)t0, (int)(n > 0 ? n : 0));
+}
+
+// Pinned host buffers for the per-call uploads (the tile plan), used in turn:
 // a buffer is rewritten only after the copy that read it four calls ago has
 // run, so the host never waits for the stream to drain (a copy from pageable
-// memory would).
+// memory would). The slots live in one allocation that grows for all of them
+// at once, so a warmed-up ring never allocates again.
 struct PinnedRing {
     static constexpr int N = 4;
-    void *h[N] = {};
-    size_t cap[N] = {};
+    uint8_t *base = nullptr;
+    size_t slot_bytes = 0;
     cudaEvent_t ev[N] = {};
     int next = 0;
 
     void *take(size_t bytes, int &slot) {
+        if (bytes > slot_bytes) {
+            for (int i = 0; i < N; ++i)
+                if (ev[i] && cudaEventSynchronize(ev[i]) != cudaSuccess) return nullptr;
+            if (base) cudaFreeHost(base);
+            base = nullptr;
+            slot_bytes = 0;
+            size_t want = 4096;
+            while (want < bytes) want *= 2;
+            if (cudaHostAlloc((void **)&base, want * N, cudaHostAllocDefault) != cudaSuccess) return nullptr;
+            slot_bytes = want;
+        }
         slot = next;
         next = (next + 1) % N;
         if (!ev[slot]) {
@@ -192,26 +243,80 @@ struct PinnedRing {
         } else if (cudaEventSynchronize(ev[slot]) != cudaSuccess) {
             return nullptr;
         }
-        if (cap[slot] < bytes) {
-            if (h[slot]) cudaFreeHost(h[slot]);
-            h[slot] = nullptr;
-            cap[slot] = 0;
-            size_t want = 4096;
-            while (want < bytes) want *= 2;
-            if (cudaHostAlloc(&h[slot], want, cudaHostAllocDefault) != cudaSuccess) return nullptr;
-            cap[slot] = want;
-        }
-        return h[slot];
+        return base + (size_t)slot * slot_bytes;
     }
     int done(int slot, cudaStream_t s) { return cudaEventRecord(ev[slot], s) == cudaSuccess ? 0 : -1; }
     void release() {
         for (int i = 0; i < N; ++i) {
             if (ev[i]) cudaEventSynchronize(ev[i]), cudaEventDestroy(ev[i]);
-            if (h[i]) cudaFreeHost(h[i]);
             ev[i] = nullptr;
-            h[i] = nullptr;
-            cap[i] = 0;
         }
+        if (base) cudaFreeHost(base);
+        base = nullptr;
+        slot_bytes = 0;
+    }
+};
+
+// Device layout of the tile plan of `ni` items: the runs, each item's first
+// row in the score-offset array, the item order (see ChunkArgs::runs).
+struct TileDesc {
+    size_t runs, rb, ord, total;
+    explicit TileDesc(int ni) {
+        auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
+        runs = 0;
+        rb = al(sizeof(int4) * (size_t)(ni + 1));
+        ord = rb + al(sizeof(int64_t) * (size_t)ni);
+        total = ord + sizeof(int32_t) * (size_t)ni;
+    }
+};
+
+// The tile plan of one scan, built on the host: items in chunk-count order
+// and the runs of chunk levels that the same items reach. A batch of equal
+// lengths is one run; B distinct lengths give at most B runs.
+struct TilePlan {
+    std::vector<int32_t> nc, order;
+    std::vector<int64_t> rb;
+    std::vector<int4> runs;
+    int max_nc = 1;
+    int64_t n_tiles = 0, rows = 0;
+
+    void build(const Geo &g, int32_t B, const int64_t *h_T, int C) {
+        const int ni = B * g.n_kv;
+        nc.resize(ni);
+        rb.resize(ni);
+        order.resize(ni);
+        rows = 0;
+        max_nc = 1;
+        bool uniform = true;
+        for (int it = 0; it < ni; ++it) {
+            const int64_t T = h_T[it / g.n_kv];
+            nc[it] = T ? (int)((T + C - 1) / C) : 1;
+            rb[it] = rows;
+            rows += T;
+            max_nc = nc[it] > max_nc ? nc[it] : max_nc;
+            uniform = uniform && nc[it] == nc[0];
+            order[it] = it;
+        }
+        if (!uniform)
+            std::stable_sort(order.begin(), order.end(), [&](int x, int y) { return nc[x] > nc[y]; });
+        runs.clear();
+        n_tiles = 0;
+        int c = 0, k = ni;
+        while (k > 0) {
+            const int cend = nc[order[k - 1]];        // chunks c .. cend-1 hold the first k items
+            if (cend > c) {
+                runs.push_back(make_int4(c, (int)n_tiles, k, 0));
+                n_tiles += (int64_t)k * (cend - c);
+                c = cend;
+            }
+            while (k > 0 && nc[order[k - 1]] == cend) --k;
+        }
+    }
+    // the plan in TileDesc layout at host address h
+    void write(uint8_t *h, const TileDesc &L) const {
+        memcpy(h + L.runs, runs.data(), sizeof(int4) * runs.size());
+        memcpy(h + L.rb, rb.data(), sizeof(int64_t) * rb.size());
+        memcpy(h + L.ord, order.data(), sizeof(int32_t) * order.size());
     }
 };
 
@@ -232,10 +337,9 @@ struct ChunkScratch {
     unsigned int *seg_top = nullptr;
     ItemAcc *items = nullptr;
     int32_t *redo = nullptr;
-    int4 *tiles = nullptr;
-    int32_t *item_nchunks = nullptr;
-    int64_t *row_base = nullptr;
-    PinnedRing up;                // host side of the tile-list uploads
+    uint8_t *desc = nullptr;      // the tile plan (TileDesc layout), uploaded per call
+    PinnedRing up;                // host side of the tile-plan uploads
+    TilePlan plan;                // the last call's plan (its vectors keep their capacity)
 
     void release() {
         up.release();
@@ -738,7 +842,7 @@ __device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
 // plane and is rounded up to 16 bytes without leaving the plane.
 __device__ __forceinline__ void prefetch_tile(const ChunkArgs &a, int tile, int lane, int which) {
     const Geo &g = a.g;
-    const int4 td = a.tiles[tile];
+    const int4 td = tile_at(a, tile);
     const int item = td.x, n = td.w;
     if (n <= 0) return;
     const int64_t t0 = td.z;
@@ -772,7 +876,7 @@ __device__ __forceinline__ void prefetch_tile(const ChunkArgs &a, int tile, int 
 template <int H, int KB, int VB>
 __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
     using CF = ChunkCfg<H, KB, VB>;
-    constexpr int NT = CF::NT, R = CF::R, C = CF::C, CW = CF::CW;
+    constexpr int NT = CF::NT, R = CF::R, CW = CF::CW;
     __shared__ __align__(16) double qd[D * H];  // [channel][head]
     __shared__ long long wmax_sm[NT / 32][H];
     // The key centroids of a channel pair, (c[k0], c[k1]) for index k0 + k1 << KB,
@@ -791,7 +895,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
     constexpr int64_t s_lo = DefFmt::S_LO;
 
     for (int tile = blockIdx.x; tile < a.n_tiles; tile += gridDim.x) {
-        const int4 td = a.tiles[tile];
+        const int4 td = tile_at(a, tile);
         const int item = td.x, c = td.y;
         const int64_t t0 = td.z;
         const int n = td.w;
@@ -965,7 +1069,10 @@ __global__ void __launch_bounds__(256) k_chunk_prefix(ChunkArgs a) {
     __shared__ long long wtot[8];
     const int item = blockIdx.x / H, h = blockIdx.x % H;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int nc = a.item_nchunks[item];
+    // the segment pool of the values launch starts empty (no launch before it
+    // allocates from it)
+    if (blockIdx.x == 0 && tid == 0) *a.seg_top = 0;
+    const int nc = item_chunks(a, item);
     long long *v = a.cmx + (int64_t)item * a.max_chunks * 2 * HMAX;
     const long long s_lo = -(1ll << (a.g.score_width - 1));
     const long long seed = a.m_init ? (a.m_init[(int64_t)item * H + h] > s_lo ? a.m_init[(int64_t)item * H + h] : s_lo)
@@ -1024,7 +1131,6 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
     __shared__ int32_t rl_f[H][SEGMAX];
     __shared__ unsigned int lsum_sm[H][SEGMAX + 1];   // l of a tile < 2^25
     __shared__ long long bnd_sm[NT / 32][H];           // per-warp clamp-proof bounds
-    __shared__ long long slots_sm[NT / 32];
     __shared__ unsigned int resc_sm;
 
     const Geo &g = a.g;
@@ -1055,13 +1161,12 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
 
     // Tiles are dealt round-robin; no tile waits on another.
     for (int tile = blockIdx.x; tile < a.n_tiles; tile += gridDim.x) {
-        const int4 td = a.tiles[tile];
+        const int4 td = tile_at(a, tile);
         const int item = td.x, c = td.y;
         const int64_t t0 = td.z;
         const int n = td.w;
         const int b = item / g.n_kv, kvh = item % g.n_kv;
         const int seq = a.seq_ids[b];
-        const int64_t qbase = ((int64_t)b * g.n_kv * H + (int64_t)kvh * H) * D;
         const int rec_idx = item * a.max_chunks + c;
         const int poff = (int)(t0 % g.P);
         const uint32_t *sc = a.sc + (a.row_base[item] + t0) * H;
@@ -1126,7 +1231,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
             const int nt = tile + gridDim.x;
             prefetch_tile(a, nt, lane, 2);
             if (lane == 0) {
-                const int4 t2 = a.tiles[nt];
+                const int4 t2 = tile_at(a, nt);
                 const uint32_t bytes = (uint32_t)t2.w * H * 4;
                 if (bytes) prefetch_l2(a.sc + (a.row_base[t2.x] + t2.z) * H, (bytes + 15) & ~15u);
             }
@@ -1552,7 +1657,7 @@ template <int H>
 __global__ void __launch_bounds__(CHUNK_THREADS) k_fold_blocks(ChunkArgs a) {
     __shared__ int base_sm[H];
     const int item = blockIdx.x / a.max_blocks, blk = blockIdx.x % a.max_blocks;
-    const int nc = a.item_nchunks[item];
+    const int nc = item_chunks(a, item);
     if (blk * GBLK >= nc) return;
     merge_block<H>(a, item, blk, nc, base_sm);
 }
@@ -1563,7 +1668,7 @@ template <int H>
 __global__ void __launch_bounds__(CHUNK_THREADS) k_fold_items(ChunkArgs a) {
     __shared__ long long slots[CHUNK_THREADS / 32];
     const int item = blockIdx.x;
-    const int nc = a.item_nchunks[item], nblk = (nc + GBLK - 1) / GBLK;
+    const int nc = item_chunks(a, item), nblk = (nc + GBLK - 1) / GBLK;
     const int b = item / a.g.n_kv;
     if (a.parts) fold_part<H>(a, item, nblk, a.T[b], slots);
     else merge_item<H>(a, item, nblk, a.T[b], (int64_t)item * H * D, slots);
@@ -1625,36 +1730,9 @@ inline int chunk_slots() {
     return cached[dev];
 }
 
-// The tile list: every item's tiles in (tile index, item) order; each item's
-// first row in the score-offset array.
-inline void build_tiles(const Geo &g, int32_t B, const int64_t *h_T, int C, std::vector<int4> &tiles,
-                        std::vector<int32_t> &nc, std::vector<int64_t> &row_base, int &max_nc,
-                        int64_t &total_rows) {
-    const int n_items = B * g.n_kv;
-    nc.assign(n_items, 1);
-    row_base.assign(n_items, 0);
-    max_nc = 1;
-    total_rows = 0;
-    for (int it = 0; it < n_items; ++it) {
-        const int64_t T = h_T[it / g.n_kv];
-        nc[it] = T ? (int)((T + C - 1) / C) : 1;
-        max_nc = nc[it] > max_nc ? nc[it] : max_nc;
-        row_base[it] = total_rows;
-        total_rows += T;
-    }
-    tiles.clear();
-    for (int cidx = 0; cidx < max_nc; ++cidx)
-        for (int it = 0; it < n_items; ++it)
-            if (cidx < nc[it]) {
-                const int64_t T = h_T[it / g.n_kv];
-                const int64_t t0 = (int64_t)cidx * C;
-                tiles.push_back(make_int4(it, cidx, (int)t0, (int)(T - t0 < C ? T - t0 : C)));
-            }
-}
-
 // Byte layout of the scratch of one scan: `o` offsets in the order carved.
 struct ScratchLayout {
-    size_t top, cmx, rec, blk, seg, items, redo, tiles, nc, rb, bmg, sc, total;
+    size_t top, cmx, rec, blk, seg, items, redo, desc, bmg, sc, total;
     ScratchLayout(int ni, int mc, int sc_cap, int tc, int H, int CW, int64_t rows) {
         auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
         const int mb = (mc + GBLK - 1) / GBLK;
@@ -1666,9 +1744,7 @@ struct ScratchLayout {
         seg = o; o += al(sizeof(SegEntry) * (size_t)sc_cap);
         items = o; o += al(sizeof(ItemAcc) * (size_t)ni);
         redo = o; o += al(sizeof(int32_t) * (size_t)ni);
-        tiles = o; o += al(sizeof(int4) * (size_t)tc);
-        nc = o; o += al(sizeof(int32_t) * (size_t)ni);
-        rb = o; o += al(sizeof(int64_t) * (size_t)ni);
+        desc = o; o += al(TileDesc(ni).total);
         bmg = o; o += al(sizeof(long long) * (size_t)tc * H * CW);
         sc = o; o += al(sizeof(uint32_t) * (size_t)(rows > 0 ? rows : 1) * H);
         total = o;
@@ -1713,9 +1789,7 @@ inline int reserve_scratch(ChunkScratch &cs, int n_items, int max_nc, int n_tile
     cs.segs = (SegEntry *)(p + L.seg);
     cs.items = (ItemAcc *)(p + L.items);
     cs.redo = (int32_t *)(p + L.redo);
-    cs.tiles = (int4 *)(p + L.tiles);
-    cs.item_nchunks = (int32_t *)(p + L.nc);
-    cs.row_base = (int64_t *)(p + L.rb);
+    cs.desc = p + L.desc;
     cs.bmg = (long long *)(p + L.bmg);
     cs.sc = (uint32_t *)(p + L.sc);
     cs.n_items = ni;
@@ -1733,7 +1807,6 @@ inline int launch_chunk_kernels(ChunkArgs &a, int32_t B, const int32_t *d_seq, c
                                 cudaStream_t s) {
     const int gA = chunk_slots<H, KB, VB, 0>(), gB = chunk_slots<H, KB, VB, 1>();
     if (gA < 0 || gB < 0) return INS_ECUDA;
-    if (cudaMemsetAsync(a.seg_top, 0, sizeof(unsigned int), s) != cudaSuccess) return INS_ECUDA;
     k_scan_scores<H, KB, VB><<<gA < a.n_tiles ? gA : a.n_tiles, CHUNK_THREADS, score_smem<KB>(), s>>>(a);
     k_chunk_prefix<H><<<a.n_items * H, 256, 0, s>>>(a);
     k_scan_values<H, KB, VB>
@@ -1758,39 +1831,33 @@ inline int prepare_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, 
                            cudaStream_t s) {
     using CF = ChunkCfg<H, KB, VB>;
     const int n_items = B * g.n_kv;
-    std::vector<int4> tiles;
-    std::vector<int32_t> nc;
-    std::vector<int64_t> rb;
-    int max_nc = 1;
-    int64_t rows = 0;
-    build_tiles(g, B, h_T, CF::C, tiles, nc, rb, max_nc, rows);
-    const int n_tiles = (int)tiles.size();
-    if (int rc = reserve_scratch(cs, n_items, max_nc, n_tiles, H, CF::CW, rows, s)) return rc;
+    TilePlan &tp = cs.plan;
+    tp.build(g, B, h_T, CF::C);
+    if (tp.n_tiles > INT32_MAX / 2) return INS_EBADLEN;
+    const int n_tiles = (int)tp.n_tiles;
+    if (int rc = reserve_scratch(cs, n_items, tp.max_nc, n_tiles, H, CF::CW, tp.rows, s)) return rc;
+    const TileDesc L(n_items);
     {
-        const size_t bt = sizeof(int4) * tiles.size(), bn = sizeof(int32_t) * nc.size(),
-                     br = sizeof(int64_t) * rb.size();
         int slot = 0;
-        uint8_t *h = (uint8_t *)cs.up.take(bt + br + bn, slot);
+        uint8_t *h = (uint8_t *)cs.up.take(L.total, slot);
         if (!h) return INS_ECUDA;
-        memcpy(h, tiles.data(), bt);
-        memcpy(h + bt, rb.data(), br);
-        memcpy(h + bt + br, nc.data(), bn);
-        if (cudaMemcpyAsync(cs.tiles, h, bt, cudaMemcpyHostToDevice, s) != cudaSuccess ||
-            cudaMemcpyAsync(cs.row_base, h + bt, br, cudaMemcpyHostToDevice, s) != cudaSuccess ||
-            cudaMemcpyAsync(cs.item_nchunks, h + bt + br, bn, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+        tp.write(h, L);
+        if (cudaMemcpyAsync(cs.desc, h, L.total, cudaMemcpyHostToDevice, s) != cudaSuccess ||
             cs.up.done(slot, s))
             return INS_ECUDA;
     }
     a = ChunkArgs{};
     a.g = g;
     a.tb = tb;
-    a.tiles = cs.tiles;
+    a.runs = (const int4 *)(cs.desc + L.runs);
+    a.n_runs = (int32_t)tp.runs.size();
+    a.order = (const int32_t *)(cs.desc + L.ord);
+    a.tile_rows = CF::C;
     a.n_tiles = n_tiles;
     a.max_chunks = cs.max_chunks;
     a.max_blocks = (cs.max_chunks + GBLK - 1) / GBLK;
     a.n_items = n_items;
-    a.item_nchunks = cs.item_nchunks;
-    a.row_base = cs.row_base;
+    a.row_base = (const int64_t *)(cs.desc + L.rb);
     a.seq_ids = d_seq;
     a.T = d_T;
     a.page_table = d_pt;
@@ -1847,7 +1914,6 @@ inline int launch_split_part(ChunkArgs &a, cudaStream_t s) {
     if (gB < 0) return INS_ECUDA;
     ChunkArgs m = a;
     m.maxima = nullptr;
-    if (cudaMemsetAsync(m.seg_top, 0, sizeof(unsigned int), s) != cudaSuccess) return INS_ECUDA;
     k_chunk_prefix<H><<<m.n_items * H, 256, 0, s>>>(m);
     k_scan_values<H, KB, VB>
         <<<gB < m.n_tiles ? gB : m.n_tiles, CHUNK_THREADS, ChunkCfg<H, KB, VB>::BYTES, s>>>(m);
