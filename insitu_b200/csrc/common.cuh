@@ -43,6 +43,10 @@ struct Geo {
     int32_t score_shift, acc_shift, enc_shift;
     int64_t head_bytes, page_bytes;
     int64_t log2e, delta_max;
+    // |q| below q_lim keeps every FP64 partial sum of a dot product under
+    // 2^53: min(2^30, floor(2^47 / max |key centroid|)), so that 64 products
+    // of at most 2^47 each sum exactly; larger queries take the int64 path
+    int64_t q_lim;
 };
 
 // Byte offsets of one (page, head) region's three planes: K codes (P rows of

@@ -339,6 +339,15 @@ int ins_cache_create(const ins_config *cfg, const ins_tables *tb, int32_t device
     c->g = make_geo(*cfg);
     c->g.log2e = tb->log2e;
     c->g.delta_max = tb->delta_max;
+    {
+        int64_t cmax = 1;
+        for (int i = 0; i < nk; ++i) {
+            const int64_t x = tb->k_centroids[i] < 0 ? -tb->k_centroids[i] : tb->k_centroids[i];
+            cmax = x > cmax ? x : cmax;
+        }
+        const int64_t lim = (1ll << 47) / cmax;
+        c->g.q_lim = lim < (1ll << 30) ? lim : (1ll << 30);
+    }
     c->device = device;
     auto cleanup = [&](int rc) {
         ins_cache_destroy(c);

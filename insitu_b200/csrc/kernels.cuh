@@ -175,10 +175,11 @@ __global__ void k_ingress(Geo g, const DevTables *__restrict__ tb, int32_t n,
 // fused mode): dot = sum_j q[j] * centroid[code_j], then one multiply by the
 // signed norm and one floor shift by score_shift, then the 48-bit clamp.
 //
-// The dot runs as FP64 fused multiply-adds. Every operand is an integer below
-// 2^31 (q) or 2^17 (centroids) and, while |q| < 2^30, every partial sum is
-// below 2^53, so each FMA is exact and the double holds the same integer the
-// reference's int64 einsum does. Callers take the int64 path otherwise.
+// The dot runs as FP64 fused multiply-adds. Every operand is an integer and,
+// while |q| < Geo::q_lim, each product is below 2^47 and every partial sum of
+// the 64 below 2^53, so each FMA is exact and the double holds the same
+// integer the reference's int64 einsum does. Callers take the int64 path
+// otherwise.
 // The product with the norm wraps at 64 bits as numpy's int64 does.
 // ---------------------------------------------------------------------------
 template <int H, int KB>
@@ -282,7 +283,7 @@ __device__ void load_seq_smem(SeqSmem<H> &sm, const Geo &g, const DevTables *tb,
     int big = 0;
     for (int i = threadIdx.x; i < H * D; i += blockDim.x) {
         const int32_t x = sm.qi[i];
-        big |= (x >= (1 << 30) || x <= -(1 << 30));
+        big |= (x >= g.q_lim || x <= -g.q_lim);
     }
     if (__syncthreads_or(big) && threadIdx.x == 0) sm.exact64 = 1;
     __syncthreads();

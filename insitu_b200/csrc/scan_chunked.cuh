@@ -927,12 +927,13 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
         for (int i = tid; i < H * D; i += NT) qd[(i % D) * H + i / D] = (double)a.q_rot[qbase + i];
         __syncthreads();
         bool big = false;
+        const double qlim = (double)g.q_lim;
         for (int i = tid; i < H * D; i += NT) {
             const double x = qd[i];
-            big |= (x >= 1073741824.0 || x <= -1073741824.0);
+            big |= (x >= qlim || x <= -qlim);
         }
-        // |q| >= 2^30 would let an FP64 partial sum pass 2^53: the item goes to
-        // the exact int64 body
+        // |q| >= q_lim could let an FP64 partial sum pass 2^53: the item goes
+        // to the exact int64 body
         if (__syncthreads_or(big) && tid == 0) atomicExch(&a.items[item].fail, 1);
         // the next tile of this CTA, into L2 while this one computes
         if (warp == 1 && tile + (int)gridDim.x < a.n_tiles) prefetch_tile(a, tile + gridDim.x, lane, 1);

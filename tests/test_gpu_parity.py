@@ -232,6 +232,42 @@ def test_long_single_sequence_matches_oracle():
     assert pc.recomputed() == 0
 
 
+def test_queries_at_the_edge_of_the_fp64_range():
+    """Scores run as exact FP64 dot products while |q| < 2^30 (for the default
+    codebooks, whose key centroids stay below 2^17). KV head 0 sits just inside
+    that range (FP64); KV heads 1 and 3 reach it and are handed to the int64
+    body. Both give the oracle's bits."""
+    rng = np.random.default_rng(21)
+    T = 3000
+    pc = _pc(capacity=T)
+    k, v = _wire(rng, (T, 8, 64)), _wire(rng, (T, 8, 64))
+    pc.ingress(np.zeros(T, np.int32), k, v)
+    orc = make_oracle()
+    rows = orc.ingress_rows(k, v, threads=8)
+    q = rng.integers(-(1 << 20), 1 << 20, size=(1, 32, 64)).astype(np.int64)
+    q[0, 0:4, 5] = (1 << 30) - 1
+    q[0, 0:4, 6] = -((1 << 30) - 1)
+    q[0, 4:8, 9] = -(1 << 30)
+    q[0, 13, 40] = (1 << 30) + 12345
+    out, st = pc.scan([0], torch.from_numpy(q.astype(np.int32)))
+    pc.status()
+    want, wst = orc.decode_layer(q, [rows], threads=8)
+    np.testing.assert_array_equal(_np(out), want)
+    np.testing.assert_array_equal(_np(st), wst)
+    # the two items past the limit went to the int64 body (head 0 may join
+    # them for its score spread, which passes 2^32 below the block maxima)
+    assert pc.recomputed() >= 2
+    # ins_scores on both paths: head 0 in FP64, head 3 in int64
+    from insitu_b200 import KVQuantizer, QuantConfig
+    kvq = KVQuantizer(64, QuantConfig(key_bits=4, value_bits=2))
+    for h in (0, 3):
+        kv = kvq.unpack(rows[:, h])
+        s, ovf = pc.scores(0, h, torch.from_numpy(q[0, 4 * h:4 * h + 4].astype(np.int32)))
+        ws, wovf = orc.scores(q[0, 4 * h:4 * h + 4], kv.k_idx, kv.k_norm)
+        np.testing.assert_array_equal(_np(s), ws)
+        assert int(_np(ovf)[0]) == wovf
+
+
 # -- error behaviour -------------------------------------------------------------
 
 def test_capacity_overflow_raises_and_changes_nothing():
