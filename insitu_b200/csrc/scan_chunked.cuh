@@ -414,6 +414,21 @@ struct ChunkCfg {
     static_assert(CW <= 32, "the control phase gives one lane to each 32-row block");
 };
 
+// Shared memory of k_scan_scores: the replicated pair table, then two tile
+// buffers (the tile's K rows, then their norm words) that bulk copies fill one
+// tile ahead of the arithmetic.
+template <int H, int KB, int VB>
+struct ScoreCfg {
+    static constexpr int C = ChunkCfg<H, KB, VB>::C;
+    static constexpr size_t CTAB = (size_t)(1 << (2 * KB)) * 8 * 16;
+    static constexpr size_t KPL = (size_t)C * KB * 8;              // K rows of a tile
+    static constexpr size_t BUF = KPL + (size_t)C * 4;             // + their norm words
+    static constexpr size_t BYTES = CTAB + 2 * BUF;
+    static constexpr int PGMAX = C / 16 + 1;                       // pages a tile touches (P >= 16)
+    static constexpr int PPL = (PGMAX + 31) / 32;                  // of them per lane
+    static_assert(CTAB % 16 == 0 && KPL % 16 == 0 && BUF % 16 == 0, "bulk copies need 16-byte alignment");
+};
+
 // The 16 x 16 transpose of 2-bit fields held in 16 words: on entry A[i] has
 // field c = element (i, c); on exit A[c] has field i = element (i, c). Four
 // block-swap stages (8, 4, 2, 1 fields), each pairing rows i and i + bs.
@@ -832,6 +847,41 @@ __global__ void __launch_bounds__(CHUNK_THREADS) k_merge_parts(Geo g, const Part
     }
 }
 
+// ---------------------------------------------------------------------------
+// Bulk copies into shared memory (the TMA engine, no tensor map: plain 1-D
+// ranges, 16-byte aligned, sizes a multiple of 16) completing on an mbarrier.
+// No multicast: every copy lands in the issuing CTA's own shared memory.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("{ .reg .b64 st; mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1; }"
+                 ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+// Waits for phase `parity` of the barrier to complete; gives up (false) after
+// a bounded number of polls, each of which the hardware may suspend briefly.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    const uint32_t addr = smem_addr(bar);
+    for (int it = 0; it < (1 << 22); ++it) {
+        uint32_t done;
+        asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                     : "=r"(done) : "r"(addr), "r"(parity) : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)) : "memory");
+}
+
 __device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
@@ -883,7 +933,14 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
     // as exact doubles, in 8 replicas: lane l reads replica l & 7, so the 8
     // lanes of a 16-byte shared-memory wavefront never meet in a bank.
     extern __shared__ __align__(16) uint8_t dynA[];
+    using SC = ScoreCfg<H, KB, VB>;
     double2 *ctab = reinterpret_cast<double2 *>(dynA);
+    // The staging of the tiles: descriptors and page ids two tiles ahead (in
+    // rings of 3 and 2), the rows one tile ahead (buffers j & 1).
+    __shared__ int4 tdesc_sm[3];
+    __shared__ long long trb_sm[3];
+    __shared__ int32_t pages_sm[2][SC::PGMAX];
+    __shared__ __align__(8) uint64_t full_bar[2];
 
     const Geo &g = a.g;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -893,50 +950,153 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
     }
     const double2 *myc = ctab + (lane & 7);
     constexpr int64_t s_lo = DefFmt::S_LO;
+    const int G = gridDim.x;
+    const int ntl = (a.n_tiles - (int)blockIdx.x + G - 1) / G;   // this CTA's tiles: blockIdx.x + j*G
+    auto up16 = [](int x) { return (uint32_t)((x + 15) & ~15); };
 
-    for (int tile = blockIdx.x; tile < a.n_tiles; tile += gridDim.x) {
-        const int4 td = tile_at(a, tile);
+    // Warp 1 looks up local tile j: resolve_load starts the loads, and
+    // resolve_store, a tile of arithmetic later, writes what they returned.
+    int4 rtd = make_int4(0, 0, 0, 0);
+    long long rrb = 0;
+    int32_t rpg[SC::PPL];
+    auto resolve_load = [&](int j) {
+        rtd = tile_at(a, (int)blockIdx.x + j * G);
+        rrb = a.row_base[rtd.x];
+        const int seq = a.seq_ids[rtd.x / g.n_kv];
+        const int poff = (int)(rtd.z % g.P);
+        const int npg = rtd.w ? (poff + rtd.w + g.P - 1) / g.P : 0;
+        const int32_t *pt = a.page_table + (int64_t)seq * g.max_pages + rtd.z / g.P;
+#pragma unroll
+        for (int k = 0; k < SC::PPL; ++k) {
+            const int i = lane + 32 * k;
+            rpg[k] = i < npg ? __ldg(pt + i) : 0;
+        }
+    };
+    auto resolve_store = [&](int j) {
+#pragma unroll
+        for (int k = 0; k < SC::PPL; ++k) {
+            const int i = lane + 32 * k;
+            if (i < SC::PGMAX) pages_sm[j & 1][i] = rpg[k];
+        }
+        if (lane == 0) {
+            tdesc_sm[j % 3] = rtd;
+            trb_sm[j % 3] = rrb;
+        }
+    };
+    // Warp 0 starts the bulk copies of local tile j's K rows and norm words
+    // into buffer j & 1, one lane per page. Page boundaries fall on multiples
+    // of 16 rows of a tile (tiles start at multiples of C, pages hold a
+    // multiple of 16 rows), so every range starts 16-byte aligned; a range
+    // rounded up to 16 bytes stays inside its plane and its buffer.
+    auto issue = [&](int j) {
+        const int4 td = tdesc_sm[j % 3];
+        const int n = td.w, kvh = td.x % g.n_kv;
+        const int poff = (int)(td.z % g.P);
+        const int npg = n ? (poff + n + g.P - 1) / g.P : 0;
+        uint8_t *bk = dynA + SC::CTAB + (size_t)(j & 1) * SC::BUF;
+        uint8_t *bn = bk + SC::KPL;
+        uint32_t bytes = 0;
+        for (int i = lane; i < npg; i += 32) {
+            const int r0 = i == 0 ? poff : 0, r1 = min(g.P, poff + n - i * g.P);
+            bytes += up16((r1 - r0) * KB * 8) + up16((r1 - r0) * 4);
+        }
+        bytes = __reduce_add_sync(FULL, bytes);
+        if (lane == 0) mbar_arrive_tx(&full_bar[j & 1], bytes);
+        __syncwarp();
+        for (int i = lane; i < npg; i += 32) {
+            const int r0 = i == 0 ? poff : 0, r1 = min(g.P, poff + n - i * g.P);
+            const int row = i * g.P - poff + r0;              // the page's first row in the tile
+            const uint8_t *reg = a.pool + region_off(g, pages_sm[j & 1][i], kvh);
+            bulk_g2s(bk + (size_t)row * (KB * 8), reg + (int64_t)r0 * (KB * 8), up16((r1 - r0) * KB * 8),
+                     &full_bar[j & 1]);
+            bulk_g2s(bn + (size_t)row * 4, reg + nplane_off(g) + (int64_t)r0 * 4, up16((r1 - r0) * 4),
+                     &full_bar[j & 1]);
+        }
+    };
+
+    if (tid == 0) {
+        mbar_init(&full_bar[0], 1);
+        mbar_init(&full_bar[1], 1);
+        mbar_fence_init();
+    }
+    if (warp == 1) {
+        resolve_load(0);
+        resolve_store(0);
+        if (ntl > 1) {
+            resolve_load(1);
+            resolve_store(1);
+        }
+    }
+    __syncthreads();
+    if (warp == 0 && ntl > 0) issue(0);
+    int prev_item = -1;
+
+    for (int li = 0; li < ntl; ++li) {
+        const int tile = (int)blockIdx.x + li * G;
+        // buffer (li + 1) & 1 was released by the barrier that ended tile li - 1
+        if (warp == 0 && li + 1 < ntl) issue(li + 1);
+        if (warp == 1 && li + 2 < ntl) resolve_load(li + 2);
+        const int4 td = tdesc_sm[li % 3];
         const int item = td.x, c = td.y;
         const int64_t t0 = td.z;
         const int n = td.w;
         const int b = item / g.n_kv, kvh = item % g.n_kv;
-        const int seq = a.seq_ids[b];
         const int64_t qbase = ((int64_t)b * g.n_kv * H + (int64_t)kvh * H) * D;
-        const int poff = (int)(t0 % g.P);
-        uint32_t *sc = a.sc + (a.row_base[item] + t0) * H;
-        const int32_t *ptab = a.page_table + (int64_t)seq * g.max_pages + t0 / g.P;
+        uint32_t *sc = a.sc + (trb_sm[li % 3] + t0) * H;
 
-        // each thread fetches its own rows first, so that their latency
-        // overlaps the rest of the setup
+        if (item != prev_item) {                 // the same for the whole CTA
+            prev_item = item;
+            for (int i = tid; i < H * D; i += NT) qd[(i % D) * H + i / D] = (double)a.q_rot[qbase + i];
+            __syncthreads();
+            bool big = false;
+            const double qlim = (double)g.q_lim;
+            for (int i = tid; i < H * D; i += NT) {
+                const double x = qd[i];
+                big |= (x >= qlim || x <= -qlim);
+            }
+            // |q| >= q_lim could let an FP64 partial sum pass 2^53: the item
+            // goes to the exact int64 body
+            if (__syncthreads_or(big) && tid == 0) atomicExch(&a.items[item].fail, 1);
+        }
+        // this tile's rows, staged by the bulk copies; a wait that gives up
+        // reports a timeout and, once the copy already started has landed,
+        // ends the CTA
+        const bool landed = mbar_wait(&full_bar[li & 1], (uint32_t)(li >> 1) & 1u);
+        if (__syncthreads_or(!landed)) {
+            if (tid == 0) {
+                atomicOr(a.status, ST_TIMEOUT);
+                atomicExch(&a.items[item].fail, 1);
+            }
+            if (li + 1 < ntl) mbar_wait(&full_bar[(li + 1) & 1], (uint32_t)((li + 1) >> 1) & 1u);
+            return;
+        }
+        const uint8_t *bk = dynA + SC::CTAB + (size_t)(li & 1) * SC::BUF;
+        const uint8_t *bn = bk + SC::KPL;
         uint32_t kw[R][KB * 2];
         int64_t knorm[R];
 #pragma unroll
         for (int r = 0; r < R; ++r) {
             const int row = r * NT + tid;
-            uint32_t nw = 0;
+            const bool valid = row < n;          // a tile may be empty (a sequence of length 0)
+            const uint8_t *kp = bk + (size_t)row * (KB * 8);
+            if constexpr (KB == 4) {
+                const uint4 x = *reinterpret_cast<const uint4 *>(kp);
+                const uint4 y = *reinterpret_cast<const uint4 *>(kp + 16);
+                kw[r][0] = x.x; kw[r][1] = x.y; kw[r][2] = x.z; kw[r][3] = x.w;
+                kw[r][4] = y.x; kw[r][5] = y.y; kw[r][6] = y.z; kw[r][7] = y.w;
+            } else {
 #pragma unroll
-            for (int i = 0; i < KB * 2; ++i) kw[r][i] = 0;
-            if (row < n) {                       // a tile may be empty (a sequence of length 0)
-                int pi, lr;
-                page_row(g, poff + row, pi, lr);
-                load_krow<KB>(g, a.pool + region_off(g, ptab[pi], kvh), lr, kw[r], nw);
+                for (int i = 0; i < KB; ++i) {
+                    const uint2 x = *reinterpret_cast<const uint2 *>(kp + 8 * i);
+                    kw[r][2 * i] = x.x;
+                    kw[r][2 * i + 1] = x.y;
+                }
             }
-            knorm[r] = (int64_t)(int16_t)(nw & 0xffffu);
+#pragma unroll
+            for (int i = 0; i < KB * 2; ++i) kw[r][i] = valid ? kw[r][i] : 0u;
+            const uint32_t nw = *reinterpret_cast<const uint32_t *>(bn + (size_t)row * 4);
+            knorm[r] = valid ? (int64_t)(int16_t)(nw & 0xffffu) : 0;
         }
-        __syncthreads();                         // the previous tile is done with qd
-        for (int i = tid; i < H * D; i += NT) qd[(i % D) * H + i / D] = (double)a.q_rot[qbase + i];
-        __syncthreads();
-        bool big = false;
-        const double qlim = (double)g.q_lim;
-        for (int i = tid; i < H * D; i += NT) {
-            const double x = qd[i];
-            big |= (x >= qlim || x <= -qlim);
-        }
-        // |q| >= q_lim could let an FP64 partial sum pass 2^53: the item goes
-        // to the exact int64 body
-        if (__syncthreads_or(big) && tid == 0) atomicExch(&a.items[item].fail, 1);
-        // the next tile of this CTA, into L2 while this one computes
-        if (warp == 1 && tile + (int)gridDim.x < a.n_tiles) prefetch_tile(a, tile + gridDim.x, lane, 1);
 
         double acc[R][H];
 #pragma unroll
@@ -1054,6 +1214,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
             for (int w = 1; w < NT / 32; ++w) m = wmax_sm[w][tid] > m ? wmax_sm[w][tid] : m;
             a.cmx[((int64_t)item * a.max_chunks + c) * 2 * HMAX + tid] = m;
         }
+        if (warp == 1 && li + 2 < ntl) resolve_store(li + 2);
         __syncthreads();
     }
 }
@@ -1703,19 +1864,13 @@ inline cudaError_t launch_seq(const Geo &g, const DevTables *tb, int32_t B, cons
     return cudaGetLastError();
 }
 
-// Dynamic shared memory of k_scan_scores: the replicated pair table.
-template <int KB>
-constexpr size_t score_smem() {
-    return (size_t)(1 << (2 * KB)) * 8 * sizeof(double2);
-}
-
 // Resident CTAs of the scores (WHICH 0) or values (WHICH 1) kernel on the
 // current device: the launch grid. The dynamic-smem attribute and the
 // occupancy are set and queried once per kernel and device.
 template <int H, int KB, int VB, int WHICH>
 inline int chunk_slots() {
     auto fn = WHICH == 0 ? k_scan_scores<H, KB, VB> : k_scan_values<H, KB, VB>;
-    const size_t dyn = WHICH == 0 ? score_smem<KB>() : ChunkCfg<H, KB, VB>::BYTES;
+    const size_t dyn = WHICH == 0 ? ScoreCfg<H, KB, VB>::BYTES : ChunkCfg<H, KB, VB>::BYTES;
     static std::mutex mu;
     static int cached[64] = {0};
     int dev = 0;
@@ -1808,7 +1963,7 @@ inline int launch_chunk_kernels(ChunkArgs &a, int32_t B, const int32_t *d_seq, c
                                 cudaStream_t s) {
     const int gA = chunk_slots<H, KB, VB, 0>(), gB = chunk_slots<H, KB, VB, 1>();
     if (gA < 0 || gB < 0) return INS_ECUDA;
-    k_scan_scores<H, KB, VB><<<gA < a.n_tiles ? gA : a.n_tiles, CHUNK_THREADS, score_smem<KB>(), s>>>(a);
+    k_scan_scores<H, KB, VB><<<gA < a.n_tiles ? gA : a.n_tiles, CHUNK_THREADS, ScoreCfg<H, KB, VB>::BYTES, s>>>(a);
     k_chunk_prefix<H><<<a.n_items * H, 256, 0, s>>>(a);
     k_scan_values<H, KB, VB>
         <<<gB < a.n_tiles ? gB : a.n_tiles, CHUNK_THREADS, ChunkCfg<H, KB, VB>::BYTES, s>>>(a);
@@ -1902,7 +2057,7 @@ inline int launch_split_maxima(ChunkArgs &a, cudaStream_t s) {
     ChunkArgs m = a;
     m.m_init = nullptr;
     m.parts = nullptr;
-    k_scan_scores<H, KB, VB><<<gA < m.n_tiles ? gA : m.n_tiles, CHUNK_THREADS, score_smem<KB>(), s>>>(m);
+    k_scan_scores<H, KB, VB><<<gA < m.n_tiles ? gA : m.n_tiles, CHUNK_THREADS, ScoreCfg<H, KB, VB>::BYTES, s>>>(m);
     k_chunk_prefix<H><<<m.n_items * H, 256, 0, s>>>(m);
     return cudaGetLastError() == cudaSuccess ? INS_OK : INS_ECUDA;
 }
