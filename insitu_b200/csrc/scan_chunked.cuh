@@ -928,7 +928,6 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
     using CF = ChunkCfg<H, KB, VB>;
     constexpr int NT = CF::NT, R = CF::R, CW = CF::CW;
     __shared__ __align__(16) double qd[D * H];  // [channel][head]
-    __shared__ long long wmax_sm[NT / 32][H];
     // The key centroids of a channel pair, (c[k0], c[k1]) for index k0 + k1 << KB,
     // as exact doubles, in 8 replicas: lane l reads replica l & 7, so the 8
     // lanes of a 16-byte shared-memory wavefront never meet in a bank.
@@ -941,6 +940,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
     __shared__ long long trb_sm[3];
     __shared__ int32_t pages_sm[2][SC::PGMAX];
     __shared__ __align__(8) uint64_t full_bar[2];
+    __shared__ long long tmax_sm[2][H];                // tile maxima of tiles j & 1
 
     const Geo &g = a.g;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -955,14 +955,39 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
     auto up16 = [](int x) { return (uint32_t)((x + 15) & ~15); };
 
     // Warp 1 looks up local tile j: resolve_load starts the loads, and
-    // resolve_store, a tile of arithmetic later, writes what they returned.
+    // resolve_store, a tile of arithmetic later, writes what they returned and
+    // announces the bytes of the tile's copies on its buffer's barrier (the
+    // barrier's previous phase, tile j - 2, has completed by then).
     int4 rtd = make_int4(0, 0, 0, 0);
     long long rrb = 0;
     int32_t rpg[SC::PPL];
+    // the item of the last lookup (consecutive tiles of a CTA usually share
+    // it), so that only the page ids are loaded per tile
+    int citem = -1, cseq = 0;
+    int64_t cT = 0, crb = 0;
+    const int4 run0 = a.runs[0];
     auto resolve_load = [&](int j) {
-        rtd = tile_at(a, (int)blockIdx.x + j * G);
-        rrb = a.row_base[rtd.x];
-        const int seq = a.seq_ids[rtd.x / g.n_kv];
+        const int tile = (int)blockIdx.x + j * G;
+        int item, c;
+        if (a.n_runs == 1) {
+            item = (tile - run0.y) % run0.z;
+            c = run0.x + (tile - run0.y) / run0.z;
+        } else {
+            const int4 t = tile_at(a, tile);
+            item = t.x;
+            c = t.y;
+        }
+        if (item != citem) {
+            citem = item;
+            cT = a.T[item / g.n_kv];
+            cseq = a.seq_ids[item / g.n_kv];
+            crb = a.row_base[item];
+        }
+        const int64_t tt0 = (int64_t)c * a.tile_rows;
+        const int64_t tn = cT - tt0 < a.tile_rows ? cT - tt0 : a.tile_rows;
+        rtd = make_int4(item, c, (int)tt0, (int)(tn > 0 ? tn : 0));
+        rrb = crb;
+        const int seq = cseq;
         const int poff = (int)(rtd.z % g.P);
         const int npg = rtd.w ? (poff + rtd.w + g.P - 1) / g.P : 0;
         const int32_t *pt = a.page_table + (int64_t)seq * g.max_pages + rtd.z / g.P;
@@ -971,6 +996,16 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
             const int i = lane + 32 * k;
             rpg[k] = i < npg ? __ldg(pt + i) : 0;
         }
+    };
+    auto copy_bytes = [&](int4 td) {
+        const int n = td.w, poff = (int)(td.z % g.P);
+        const int npg = n ? (poff + n + g.P - 1) / g.P : 0;
+        uint32_t bytes = 0;
+        for (int i = 0; i < npg; ++i) {
+            const int r0 = i == 0 ? poff : 0, r1 = min(g.P, poff + n - i * g.P);
+            bytes += up16((r1 - r0) * KB * 8) + up16((r1 - r0) * 4);
+        }
+        return bytes;
     };
     auto resolve_store = [&](int j) {
 #pragma unroll
@@ -981,29 +1016,25 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
         if (lane == 0) {
             tdesc_sm[j % 3] = rtd;
             trb_sm[j % 3] = rrb;
+            mbar_arrive_tx(&full_bar[j & 1], copy_bytes(rtd));
         }
     };
-    // Warp 0 starts the bulk copies of local tile j's K rows and norm words
-    // into buffer j & 1, one lane per page. Page boundaries fall on multiples
-    // of 16 rows of a tile (tiles start at multiples of C, pages hold a
-    // multiple of 16 rows), so every range starts 16-byte aligned; a range
-    // rounded up to 16 bytes stays inside its plane and its buffer.
+    // The bulk copies of local tile j's K rows and norm words into buffer
+    // j & 1: lane 0 of warp w issues those of pages w, w + 8, ... (the issue
+    // of a bulk copy takes a while; the warps issue theirs side by side).
+    // Page boundaries fall on multiples of 16 rows of a tile (tiles start at
+    // multiples of C, pages hold a multiple of 16 rows), so every range starts
+    // 16-byte aligned; a range rounded up to 16 bytes stays inside its plane
+    // and its buffer.
     auto issue = [&](int j) {
+        if (lane != 0) return;
         const int4 td = tdesc_sm[j % 3];
         const int n = td.w, kvh = td.x % g.n_kv;
         const int poff = (int)(td.z % g.P);
         const int npg = n ? (poff + n + g.P - 1) / g.P : 0;
         uint8_t *bk = dynA + SC::CTAB + (size_t)(j & 1) * SC::BUF;
         uint8_t *bn = bk + SC::KPL;
-        uint32_t bytes = 0;
-        for (int i = lane; i < npg; i += 32) {
-            const int r0 = i == 0 ? poff : 0, r1 = min(g.P, poff + n - i * g.P);
-            bytes += up16((r1 - r0) * KB * 8) + up16((r1 - r0) * 4);
-        }
-        bytes = __reduce_add_sync(FULL, bytes);
-        if (lane == 0) mbar_arrive_tx(&full_bar[j & 1], bytes);
-        __syncwarp();
-        for (int i = lane; i < npg; i += 32) {
+        for (int i = warp; i < npg; i += NT / 32) {
             const int r0 = i == 0 ? poff : 0, r1 = min(g.P, poff + n - i * g.P);
             const int row = i * g.P - poff + r0;              // the page's first row in the tile
             const uint8_t *reg = a.pool + region_off(g, pages_sm[j & 1][i], kvh);
@@ -1019,6 +1050,8 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
         mbar_init(&full_bar[1], 1);
         mbar_fence_init();
     }
+    if (tid < 2 * H) tmax_sm[tid / H][tid % H] = LLONG_MIN;
+    __syncthreads();
     if (warp == 1) {
         resolve_load(0);
         resolve_store(0);
@@ -1028,16 +1061,27 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
         }
     }
     __syncthreads();
-    if (warp == 0 && ntl > 0) issue(0);
+    if (ntl > 0) issue(0);
     int prev_item = -1;
+    int4 prev_td = make_int4(0, 0, 0, 0);
+    unsigned lost = 0;                           // buffers whose wait gave up
+    // the maximum of tile j's scores per head, once the barrier ending tile j
+    // has passed; the slot is cleared for tile j + 2
+    auto tile_max_out = [&](int j, int4 td) {
+        if (tid < H) {
+            a.cmx[((int64_t)td.x * a.max_chunks + td.y) * 2 * HMAX + tid] = tmax_sm[j & 1][tid];
+            tmax_sm[j & 1][tid] = LLONG_MIN;
+        }
+    };
 
     for (int li = 0; li < ntl; ++li) {
         const int tile = (int)blockIdx.x + li * G;
+        if (li > 0) tile_max_out(li - 1, prev_td);
         // buffer (li + 1) & 1 was released by the barrier that ended tile li - 1
-        if (warp == 0 && li + 1 < ntl) issue(li + 1);
+        if (li + 1 < ntl) issue(li + 1);
         if (warp == 1 && li + 2 < ntl) resolve_load(li + 2);
         const int4 td = tdesc_sm[li % 3];
-        const int item = td.x, c = td.y;
+        const int item = td.x;
         const int64_t t0 = td.z;
         const int n = td.w;
         const int b = item / g.n_kv, kvh = item % g.n_kv;
@@ -1059,17 +1103,13 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
             if (__syncthreads_or(big) && tid == 0) atomicExch(&a.items[item].fail, 1);
         }
         // this tile's rows, staged by the bulk copies; a wait that gives up
-        // reports a timeout and, once the copy already started has landed,
-        // ends the CTA
-        const bool landed = mbar_wait(&full_bar[li & 1], (uint32_t)(li >> 1) & 1u);
-        if (__syncthreads_or(!landed)) {
-            if (tid == 0) {
-                atomicOr(a.status, ST_TIMEOUT);
-                atomicExch(&a.items[item].fail, 1);
-            }
-            if (li + 1 < ntl) mbar_wait(&full_bar[(li + 1) & 1], (uint32_t)((li + 1) >> 1) & 1u);
-            return;
+        // reports a timeout (the launch's results are then void) and is
+        // retried, bounded, before the CTA exits
+        if (!mbar_wait(&full_bar[li & 1], (uint32_t)(li >> 1) & 1u)) {
+            lost |= 1u << (li & 1);
+            atomicOr(a.status, ST_TIMEOUT);
         }
+        prev_td = td;
         const uint8_t *bk = dynA + SC::CTAB + (size_t)(li & 1) * SC::BUF;
         const uint8_t *bn = bk + SC::KPL;
         uint32_t kw[R][KB * 2];
@@ -1206,17 +1246,18 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
             const long long wm = (long long)xhi * (1ll << 20) + (long long)xlo;
             if (wm) atomicMax(&ia.maxs, wm);
 #pragma unroll
-            for (int h = 0; h < H; ++h) wmax_sm[warp][h] = hmax[h];
-        }
-        __syncthreads();
-        if (tid < H) {
-            long long m = wmax_sm[0][tid];
-            for (int w = 1; w < NT / 32; ++w) m = wmax_sm[w][tid] > m ? wmax_sm[w][tid] : m;
-            a.cmx[((int64_t)item * a.max_chunks + c) * 2 * HMAX + tid] = m;
+            for (int h = 0; h < H; ++h) atomicMax(&tmax_sm[li & 1][h], (long long)hmax[h]);
         }
         if (warp == 1 && li + 2 < ntl) resolve_store(li + 2);
         __syncthreads();
     }
+    if (ntl > 0) tile_max_out(ntl - 1, prev_td);
+    // a copy whose wait gave up must land before the CTA's shared memory goes
+    for (int bb = 0; bb < 2; ++bb)
+        if ((lost >> bb) & 1u) {
+            const int jl = ntl - 1 - ((ntl - 1 - bb) & 1);   // the last tile that used buffer bb
+            if (jl >= 0) mbar_wait(&full_bar[bb], (uint32_t)(jl >> 1) & 1u);
+        }
 }
 
 // ---------------------------------------------------------------------------
