@@ -884,6 +884,7 @@ int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
     a.n_tiles = (int32_t)n_tiles;
     a.max_chunks = tp.max_nc;
     a.max_blocks = (tp.max_nc + GBLK - 1) / GBLK;
+    a.fold_fused = tp.max_nc <= GBLK;
     a.n_items = n_items;
     a.row_base = (const int64_t *)(p + L.desc + TD.rb);
     a.seq_ids = (const int32_t *)(p + o_seq);

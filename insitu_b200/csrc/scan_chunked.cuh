@@ -156,6 +156,7 @@ struct ChunkArgs {
     int32_t n_tiles;
     int32_t max_chunks;
     int32_t max_blocks;
+    int32_t fold_fused;           // every item fits one block: k_fold_items folds the tiles too
     int32_t n_items;
     const int64_t *row_base;      // [n_items]: first row of the item in `sc`
     const int32_t *seq_ids;
@@ -1870,9 +1871,14 @@ __global__ void __launch_bounds__(CHUNK_THREADS) k_fold_blocks(ChunkArgs a) {
 template <int H>
 __global__ void __launch_bounds__(CHUNK_THREADS) k_fold_items(ChunkArgs a) {
     __shared__ long long slots[CHUNK_THREADS / 32];
+    __shared__ int base_sm[H];
     const int item = blockIdx.x;
     const int nc = item_chunks(a, item), nblk = (nc + GBLK - 1) / GBLK;
     const int b = item / a.g.n_kv;
+    if (a.fold_fused) {                  // level 1 here: one block of at most GBLK tiles
+        merge_block<H>(a, item, 0, nc, base_sm);
+        __syncthreads();
+    }
     if (a.parts) fold_part<H>(a, item, nblk, a.T[b], slots);
     else merge_item<H>(a, item, nblk, a.T[b], (int64_t)item * H * D, slots);
     __syncthreads();
@@ -2008,7 +2014,7 @@ inline int launch_chunk_kernels(ChunkArgs &a, int32_t B, const int32_t *d_seq, c
     k_chunk_prefix<H><<<a.n_items * H, 256, 0, s>>>(a);
     k_scan_values<H, KB, VB>
         <<<gB < a.n_tiles ? gB : a.n_tiles, CHUNK_THREADS, ChunkCfg<H, KB, VB>::BYTES, s>>>(a);
-    k_fold_blocks<H><<<a.n_items * a.max_blocks, CHUNK_THREADS, 0, s>>>(a);
+    if (!a.fold_fused) k_fold_blocks<H><<<a.n_items * a.max_blocks, CHUNK_THREADS, 0, s>>>(a);
     k_fold_items<H><<<a.n_items, CHUNK_THREADS, 0, s>>>(a);
     if (cudaGetLastError() != cudaSuccess) return INS_ECUDA;
     // items whose exactness the fold could not prove are recomputed in order
@@ -2053,6 +2059,7 @@ inline int prepare_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, 
     a.n_tiles = n_tiles;
     a.max_chunks = cs.max_chunks;
     a.max_blocks = (cs.max_chunks + GBLK - 1) / GBLK;
+    a.fold_fused = tp.max_nc <= GBLK;
     a.n_items = n_items;
     a.row_base = (const int64_t *)(cs.desc + L.rb);
     a.seq_ids = d_seq;
@@ -2114,7 +2121,7 @@ inline int launch_split_part(ChunkArgs &a, cudaStream_t s) {
     k_chunk_prefix<H><<<m.n_items * H, 256, 0, s>>>(m);
     k_scan_values<H, KB, VB>
         <<<gB < m.n_tiles ? gB : m.n_tiles, CHUNK_THREADS, ChunkCfg<H, KB, VB>::BYTES, s>>>(m);
-    k_fold_blocks<H><<<m.n_items * m.max_blocks, CHUNK_THREADS, 0, s>>>(m);
+    if (!m.fold_fused) k_fold_blocks<H><<<m.n_items * m.max_blocks, CHUNK_THREADS, 0, s>>>(m);
     k_fold_items<H><<<m.n_items, CHUNK_THREADS, 0, s>>>(m);
     return cudaGetLastError() == cudaSuccess ? INS_OK : INS_ECUDA;
 }

@@ -43,7 +43,7 @@ class DecodeAttention:
         itself (the causality note of hw/vectors.py:22-30).
         """
         B = q.shape[0]
-        ids = np.arange(B, dtype=np.int32) if seq_ids is None else np.asarray(seq_ids, np.int32)
+        ids = list(range(B)) if seq_ids is None else seq_ids
         q_rot = self.pc.ingress(ids, k, v, q)
         return self.pc.scan(ids, q_rot, mode=mode, out=out, stats_out=stats_out)
 

@@ -23,11 +23,29 @@ from .tables import Tables
 
 
 def _ptr(t: torch.Tensor | None):
-    return None if t is None else C.c_void_p(t.data_ptr())
+    return None if t is None else t.data_ptr()
 
 
-def _stream(device: torch.device):
-    return C.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+if hasattr(torch._C, "_cuda_getCurrentRawStream"):
+    def _stream(device: torch.device):
+        return torch._C._cuda_getCurrentRawStream(device.index)
+else:                                                # pragma: no cover
+    def _stream(device: torch.device):
+        return torch.cuda.current_stream(device).cuda_stream
+
+
+def _host_array(x, n: int, ctype, np_dtype):
+    """``x`` (a scalar, a sequence or an array) broadcast to ``n`` entries of
+    ``ctype`` in host memory; returns (keep-alive object, address). Plain
+    Python lists take the short path: one ctypes array, no numpy."""
+    if isinstance(x, (list, tuple)) and len(x) == n:
+        arr = (ctype * n)(*x)
+        return arr, C.addressof(arr)
+    if isinstance(x, (int, np.integer)):
+        arr = (ctype * n)(*([int(x)] * n))
+        return arr, C.addressof(arr)
+    arr = np.ascontiguousarray(np.broadcast_to(np.asarray(x, dtype=np_dtype), (n,)))
+    return arr, arr.ctypes.data
 
 
 def _require_cuda():
@@ -112,6 +130,9 @@ class PagedCache:
 
     # -- tensors -------------------------------------------------------------
     def _dev_i32(self, x, shape_tail) -> torch.Tensor:
+        if (isinstance(x, torch.Tensor) and x.dtype == torch.int32 and x.device == self.device
+                and x.is_contiguous() and tuple(x.shape[1:]) == tuple(shape_tail)):
+            return x
         t = torch.as_tensor(x)
         if t.dtype != torch.int32:
             if t.dtype.is_floating_point:
@@ -137,7 +158,7 @@ class PagedCache:
         n = k.shape[0]
         if v.shape[0] != n:
             raise ValueError("k and v carry different token counts")
-        ids = np.ascontiguousarray(np.broadcast_to(np.asarray(seq_ids, dtype=np.int32), (n,)))
+        ids, ids_p = _host_array(seq_ids, n, C.c_int32, np.int32)
         q_rot = None
         if q is not None:
             q = self._dev_i32(q, (g.num_heads, g.head_dim))
@@ -145,7 +166,7 @@ class PagedCache:
                 raise ValueError("q carries a different token count")
             q_rot = torch.empty_like(q)
         flags = _lib.INS_INGRESS_PREROTATED if prerotated else 0
-        _lib.check(self._L.ins_ingress(self._h, n, ids.ctypes.data_as(C.c_void_p), _ptr(q),
+        _lib.check(self._L.ins_ingress(self._h, n, ids_p, _ptr(q),
                                        _ptr(k), _ptr(v), _ptr(q_rot), flags,
                                        _stream(self.device)))
         return q_rot
@@ -179,10 +200,8 @@ class PagedCache:
         g = self.geo
         q = self._dev_i32(q_rot, (g.num_heads, g.head_dim))
         B = q.shape[0]
-        ids = np.ascontiguousarray(np.broadcast_to(np.asarray(seq_ids, dtype=np.int32), (B,)))
-        lens = None
-        if lengths is not None:
-            lens = np.ascontiguousarray(np.broadcast_to(np.asarray(lengths, dtype=np.int64), (B,)))
+        ids, ids_p = _host_array(seq_ids, B, C.c_int32, np.int32)
+        lens, lens_p = (None, None) if lengths is None else _host_array(lengths, B, C.c_int64, np.int64)
         if out is None:
             out = torch.empty((B, g.num_heads, g.head_dim), dtype=torch.int64, device=self.device)
         st = None
@@ -190,9 +209,8 @@ class PagedCache:
             st = stats_out if stats_out is not None else torch.empty(
                 (B, g.n_kv_heads, len(_lib.STATS_FIELDS)), dtype=torch.int64, device=self.device)
         m = {"online": _lib.INS_SOFTMAX_ONLINE, "two_pass": _lib.INS_SOFTMAX_TWO_PASS}[mode]
-        _lib.check(self._L.ins_scan(self._h, B, ids.ctypes.data_as(C.c_void_p),
-                                    None if lens is None else lens.ctypes.data_as(C.c_void_p),
-                                    _ptr(q), _ptr(out), _ptr(st), m, _stream(self.device)))
+        _lib.check(self._L.ins_scan(self._h, B, ids_p, lens_p, _ptr(q), _ptr(out), _ptr(st), m,
+                                    _stream(self.device)))
         return out, st
 
     # -- context split (one sequence across shards) -------------------------------
