@@ -125,6 +125,14 @@ int ins_cache_destroy(ins_cache *cache);
  * work already enqueued by the caller's next synchronisation. */
 int ins_cache_reset(ins_cache *cache, int32_t seq);
 
+/* Tile size of the context-parallel online scan (no reference counterpart:
+ * a tuning knob of this implementation; results are identical in every mode).
+ * AUTO (the default) takes tiles of 4 rows per thread for long contexts and
+ * of 2 when the default tiles would leave SMs idle; LARGE and SMALL force one
+ * of them (shapes whose default is already 2 rows per thread ignore it). */
+enum { INS_TILES_AUTO = 0, INS_TILES_LARGE = 1, INS_TILES_SMALL = 2 };
+int ins_cache_set_tiles(ins_cache *cache, int32_t mode);
+
 /* Tokens currently held for `seq` (KVCache.length), or -1. */
 int64_t ins_cache_length(const ins_cache *cache, int32_t seq);
 

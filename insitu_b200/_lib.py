@@ -25,6 +25,7 @@ NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", 
 INS_OK, INS_EBADLEN, INS_ETIMEOUT, INS_ERANGE, INS_EINVAL, INS_ENOMEM, INS_ECUDA = 0, 4, 5, 7, 8, 9, 10
 INS_SOFTMAX_ONLINE, INS_SOFTMAX_TWO_PASS = 0, 1
 INS_INGRESS_PREROTATED = 1
+INS_TILES = {"auto": 0, "large": 1, "small": 2}
 
 
 class InsituError(RuntimeError):
@@ -83,7 +84,7 @@ SYMBOLS = ("ins_abi_version", "ins_bytes_per_token", "ins_cache_create", "ins_ca
            "ins_cache_reset", "ins_cache_length", "ins_cache_capacity", "ins_ingress", "ins_rotate",
            "ins_scores", "ins_scan", "ins_cache_export", "ins_cache_import", "ins_cache_status",
            "ins_last_error", "ins_scan_noalloc", "ins_scan_recomputed", "ins_part_bytes",
-           "ins_scan_maxima", "ins_scan_part", "ins_merge_parts")
+           "ins_scan_maxima", "ins_scan_part", "ins_merge_parts", "ins_cache_set_tiles")
 
 
 def nvcc() -> str:
@@ -148,6 +149,7 @@ def lib():
     L.ins_scan_maxima.argtypes = [vp, i32, vp, vp, vp, vp, vp]
     L.ins_scan_part.argtypes = [vp, i32, vp, vp, vp, vp, vp, vp]
     L.ins_merge_parts.argtypes = [vp, i32, i32, vp, vp, vp, vp]
+    L.ins_cache_set_tiles.argtypes = [vp, i32]
     L.ins_last_error.restype = C.c_char_p
     _lib = L
     return L

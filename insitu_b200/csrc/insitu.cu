@@ -113,6 +113,7 @@ struct ins_cache {
         std::vector<int32_t> seq;
         std::vector<int64_t> T;
         const int32_t *q_rot = nullptr;
+        int32_t rs = 0;                 // rows-per-thread instantiation phase 1 used
         ChunkArgs a{};
     } split;
 };
@@ -408,6 +409,14 @@ int64_t ins_cache_length(const ins_cache *c, int32_t seq) {
 
 int64_t ins_cache_capacity(const ins_cache *c) { return c ? capacity_of(c) : -1; }
 
+int ins_cache_set_tiles(ins_cache *c, int32_t mode) {
+    if (!c) return fail(INS_EINVAL, "cache is NULL");
+    if (mode != INS_TILES_AUTO && mode != INS_TILES_LARGE && mode != INS_TILES_SMALL)
+        return fail(INS_EINVAL, "tile mode must be INS_TILES_AUTO, _LARGE or _SMALL");
+    c->chunk.tiles_mode = mode;
+    return INS_OK;
+}
+
 int ins_cache_reset(ins_cache *c, int32_t seq) {
     if (!c) return fail(INS_EINVAL, "cache is NULL");
     DeviceGuard dg(c->device);
@@ -686,32 +695,50 @@ int stage_scan_args(ins_cache *c, int32_t B, const int32_t *seq_ids, const int64
     return INS_OK;
 }
 
-template <int H, int KB, int VB>
+template <int H, int KB, int VB, int RS>
 int split_maxima_t(ins_cache *c, int32_t B, const int32_t *d_seq, const int64_t *d_T, const int64_t *h_T,
                    const int32_t *q_rot, int64_t *maxima, cudaStream_t s) {
     ChunkArgs a;
-    if (int rc = prepare_chunked<H, KB, VB>(c->chunk, c->g, c->d_tables, B, d_seq, d_T, h_T,
+    c->split.rs = RS;
+    if (int rc = prepare_chunked<H, KB, VB, RS>(c->chunk, c->g, c->d_tables, B, d_seq, d_T, h_T,
                                             c->d_page_table, c->d_pool, q_rot, nullptr, nullptr,
                                             c->d_status, a, s))
         return fail(rc, "context-split scan scratch");
     a.maxima = (long long *)maxima;
-    if (int rc = launch_split_maxima<H, KB, VB>(a, s)) return fail(rc, "context-split scores launch");
+    if (int rc = launch_split_maxima<H, KB, VB, RS>(a, s)) return fail(rc, "context-split scores launch");
     c->split.a = a;
     return INS_OK;
 }
 
-template <int H, int KB, int VB>
+template <int H, int KB, int VB, int RS>
 int split_part_t(ins_cache *c, const int64_t *m_in, void *part, cudaStream_t s) {
     ChunkArgs a = c->split.a;
     a.m_init = (const long long *)m_in;
     a.parts = (PartRec *)part;
-    if (int rc = launch_split_part<H, KB, VB>(a, s)) return fail(rc, "context-split values launch");
+    if (int rc = launch_split_part<H, KB, VB, RS>(a, s)) return fail(rc, "context-split values launch");
     return INS_OK;
+}
+
+// The tile size of a context split is chosen by phase 1 and kept for phase 2.
+template <int H, int KB, int VB>
+int split_maxima_pick(ins_cache *c, int32_t B, const int32_t *d_seq, const int64_t *d_T, const int64_t *h_T,
+                      const int32_t *q_rot, int64_t *maxima, cudaStream_t s) {
+    if constexpr (ChunkCfg<H, KB, VB>::R == 4)
+        if (small_tiles<H, KB, VB>(c->chunk, c->g, B, h_T))
+            return split_maxima_t<H, KB, VB, 2>(c, B, d_seq, d_T, h_T, q_rot, maxima, s);
+    return split_maxima_t<H, KB, VB, 0>(c, B, d_seq, d_T, h_T, q_rot, maxima, s);
+}
+
+template <int H, int KB, int VB>
+int split_part_pick(ins_cache *c, const int64_t *m_in, void *part, cudaStream_t s) {
+    if constexpr (ChunkCfg<H, KB, VB>::R == 4)
+        if (c->split.rs == 2) return split_part_t<H, KB, VB, 2>(c, m_in, part, s);
+    return split_part_t<H, KB, VB, 0>(c, m_in, part, s);
 }
 
 int split_maxima(ins_cache *c, int variant, int32_t B, const int32_t *d_seq, const int64_t *d_T,
                  const int64_t *h_T, const int32_t *q_rot, int64_t *maxima, cudaStream_t s) {
-#define CALL(HH, KK, VV) split_maxima_t<HH, KK, VV>(c, B, d_seq, d_T, h_T, q_rot, maxima, s)
+#define CALL(HH, KK, VV) split_maxima_pick<HH, KK, VV>(c, B, d_seq, d_T, h_T, q_rot, maxima, s)
     switch (variant) {
         case 142: return CALL(1, 4, 2);
         case 242: return CALL(2, 4, 2);
@@ -725,7 +752,7 @@ int split_maxima(ins_cache *c, int variant, int32_t B, const int32_t *d_seq, con
 }
 
 int split_part(ins_cache *c, int variant, const int64_t *m_in, void *part, cudaStream_t s) {
-#define CALL(HH, KK, VV) split_part_t<HH, KK, VV>(c, m_in, part, s)
+#define CALL(HH, KK, VV) split_part_pick<HH, KK, VV>(c, m_in, part, s)
     switch (variant) {
         case 142: return CALL(1, 4, 2);
         case 242: return CALL(2, 4, 2);
@@ -844,10 +871,13 @@ int32_t g_na_seq[NOALLOC_MAX_B];
 TilePlan g_na_plan;
 std::vector<uint8_t> g_na_desc;
 
-template <int H, int KB, int VB>
+template <int H, int KB, int VB, int RS = 0>
 int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out, ins_stats *stats,
                     cudaStream_t s, NoallocState &st) {
-    using CF = ChunkCfg<H, KB, VB>;
+    if constexpr (RS == 0 && ChunkCfg<H, KB, VB>::R == 4)
+        if (small_tiles<H, KB, VB>(c->chunk, c->g, B, g_na_T))
+            return noalloc_chunked<H, KB, VB, 2>(c, B, q_rot, out, stats, s, st);
+    using CF = ChunkCfg<H, KB, VB, RS>;
     const Geo &g = c->g;
     const int n_items = B * g.n_kv;
     if (n_items > NOALLOC_MAX_B * 8) return fail(INS_EBADLEN, "too many (sequence, KV head) items");
@@ -905,7 +935,7 @@ int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
     a.items = (ItemAcc *)(p + L.items);
     a.redo = (int32_t *)(p + L.redo);
     a.status = c->d_status;
-    const int rc = launch_chunk_kernels<H, KB, VB>(a, B, a.seq_ids, a.T, s);
+    const int rc = launch_chunk_kernels<H, KB, VB, RS>(a, B, a.seq_ids, a.T, s);
     return rc ? fail(rc, "chunked scan launch") : INS_OK;
 }
 

@@ -329,6 +329,7 @@ struct ChunkScratch {
     size_t bytes = 0;
     int32_t n_items = 0, max_chunks = 0, seg_cap = 0, tile_cap = 0;
     int32_t last_items = 0;       // items of the last chunked launch (their redo flags)
+    int32_t tiles_mode = 0;       // TILES_AUTO / TILES_LARGE / TILES_SMALL
     int64_t sc_rows = 0;          // rows * H capacity of `sc`, in 32-bit words
     uint32_t *sc = nullptr;
     long long *bmg = nullptr, *cmx = nullptr;
@@ -369,10 +370,11 @@ struct ChunkScratch {
 // pair, so one 16-byte lookup adds two tokens' terms for four heads. For 3-bit
 // codes a unit is one token with 8 entries.
 // ---------------------------------------------------------------------------
-template <int H, int KB, int VB>
+template <int H, int KB, int VB, int RS = 0>
 struct ChunkCfg {
     static constexpr int NT = CHUNK_THREADS;
-    static constexpr int R = (H == 8 || VB == 3) ? 2 : 4;   // rows per thread in the score phase
+    // rows per thread in the score phase: RS, or the default for the shape
+    static constexpr int R = RS ? RS : ((H == 8 || VB == 3) ? 2 : 4);
     static constexpr int C = R * NT;                         // rows per tile
     static constexpr int CW = C / 32;                        // 32-row blocks per tile
     static constexpr int NC = 1 << VB;                       // V codes
@@ -418,9 +420,9 @@ struct ChunkCfg {
 // Shared memory of k_scan_scores: the replicated pair table, then two tile
 // buffers (the tile's K rows, then their norm words) that bulk copies fill one
 // tile ahead of the arithmetic.
-template <int H, int KB, int VB>
+template <int H, int KB, int VB, int RS = 0>
 struct ScoreCfg {
-    static constexpr int C = ChunkCfg<H, KB, VB>::C;
+    static constexpr int C = ChunkCfg<H, KB, VB, RS>::C;
     static constexpr size_t CTAB = (size_t)(1 << (2 * KB)) * 8 * 16;
     static constexpr size_t KPL = (size_t)C * KB * 8;              // K rows of a tile
     static constexpr size_t BUF = KPL + (size_t)C * 4;             // + their norm words
@@ -924,16 +926,16 @@ __device__ __forceinline__ void prefetch_tile(const ChunkArgs &a, int tile, int 
 // each warp holds one 32-row block for every r. A score is stored as its offset
 // below the block maximum (uint32; a larger gap flags the item for the exact
 // body), the block maxima and the tile maximum as int64.
-template <int H, int KB, int VB>
+template <int H, int KB, int VB, int RS = 0>
 __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
-    using CF = ChunkCfg<H, KB, VB>;
+    using CF = ChunkCfg<H, KB, VB, RS>;
     constexpr int NT = CF::NT, R = CF::R, CW = CF::CW;
     __shared__ __align__(16) double qd[D * H];  // [channel][head]
     // The key centroids of a channel pair, (c[k0], c[k1]) for index k0 + k1 << KB,
     // as exact doubles, in 8 replicas: lane l reads replica l & 7, so the 8
     // lanes of a 16-byte shared-memory wavefront never meet in a bank.
     extern __shared__ __align__(16) uint8_t dynA[];
-    using SC = ScoreCfg<H, KB, VB>;
+    using SC = ScoreCfg<H, KB, VB, RS>;
     double2 *ctab = reinterpret_cast<double2 *>(dynA);
     // The staging of the tiles: descriptors and page ids two tiles ahead (in
     // rings of 3 and 2), the rows one tile ahead (buffers j & 1).
@@ -1318,9 +1320,9 @@ __global__ void __launch_bounds__(256) k_chunk_prefix(ChunkArgs a) {
 // ---------------------------------------------------------------------------
 // Launch 3: the values
 // ---------------------------------------------------------------------------
-template <int H, int KB, int VB>
+template <int H, int KB, int VB, int RS = 0>
 __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
-    using CF = ChunkCfg<H, KB, VB>;
+    using CF = ChunkCfg<H, KB, VB, RS>;
     constexpr int NT = CF::NT, R = CF::R, C = CF::C, CW = CF::CW, NC = CF::NC, VW = CF::VW;
     constexpr int TPE = CF::TPE, NE = CF::NE, HG = CF::HG, HL = CF::HL, SUBT = CF::SUBT;
     constexpr int UNITS = CF::UNITS, USTR = CF::USTR, HPS = CF::HPS, TPW = CF::TPW, TWS = CF::TWS,
@@ -1914,10 +1916,10 @@ inline cudaError_t launch_seq(const Geo &g, const DevTables *tb, int32_t B, cons
 // Resident CTAs of the scores (WHICH 0) or values (WHICH 1) kernel on the
 // current device: the launch grid. The dynamic-smem attribute and the
 // occupancy are set and queried once per kernel and device.
-template <int H, int KB, int VB, int WHICH>
+template <int H, int KB, int VB, int WHICH, int RS = 0>
 inline int chunk_slots() {
-    auto fn = WHICH == 0 ? k_scan_scores<H, KB, VB> : k_scan_values<H, KB, VB>;
-    const size_t dyn = WHICH == 0 ? ScoreCfg<H, KB, VB>::BYTES : ChunkCfg<H, KB, VB>::BYTES;
+    auto fn = WHICH == 0 ? k_scan_scores<H, KB, VB, RS> : k_scan_values<H, KB, VB, RS>;
+    const size_t dyn = WHICH == 0 ? ScoreCfg<H, KB, VB, RS>::BYTES : ChunkCfg<H, KB, VB, RS>::BYTES;
     static std::mutex mu;
     static int cached[64] = {0};
     int dev = 0;
@@ -2005,15 +2007,15 @@ inline int reserve_scratch(ChunkScratch &cs, int n_items, int max_nc, int n_tile
 
 // The three launches of the chunked scan (plus the exact re-run of flagged
 // items) on a prepared argument block. `a` holds every pointer but the grid.
-template <int H, int KB, int VB>
+template <int H, int KB, int VB, int RS = 0>
 inline int launch_chunk_kernels(ChunkArgs &a, int32_t B, const int32_t *d_seq, const int64_t *d_T,
                                 cudaStream_t s) {
-    const int gA = chunk_slots<H, KB, VB, 0>(), gB = chunk_slots<H, KB, VB, 1>();
+    const int gA = chunk_slots<H, KB, VB, 0, RS>(), gB = chunk_slots<H, KB, VB, 1, RS>();
     if (gA < 0 || gB < 0) return INS_ECUDA;
-    k_scan_scores<H, KB, VB><<<gA < a.n_tiles ? gA : a.n_tiles, CHUNK_THREADS, ScoreCfg<H, KB, VB>::BYTES, s>>>(a);
+    k_scan_scores<H, KB, VB, RS><<<gA < a.n_tiles ? gA : a.n_tiles, CHUNK_THREADS, ScoreCfg<H, KB, VB, RS>::BYTES, s>>>(a);
     k_chunk_prefix<H><<<a.n_items * H, 256, 0, s>>>(a);
-    k_scan_values<H, KB, VB>
-        <<<gB < a.n_tiles ? gB : a.n_tiles, CHUNK_THREADS, ChunkCfg<H, KB, VB>::BYTES, s>>>(a);
+    k_scan_values<H, KB, VB, RS>
+        <<<gB < a.n_tiles ? gB : a.n_tiles, CHUNK_THREADS, ChunkCfg<H, KB, VB, RS>::BYTES, s>>>(a);
     if (!a.fold_fused) k_fold_blocks<H><<<a.n_items * a.max_blocks, CHUNK_THREADS, 0, s>>>(a);
     k_fold_items<H><<<a.n_items, CHUNK_THREADS, 0, s>>>(a);
     if (cudaGetLastError() != cudaSuccess) return INS_ECUDA;
@@ -2026,13 +2028,13 @@ inline int launch_chunk_kernels(ChunkArgs &a, int32_t B, const int32_t *d_seq, c
 
 // The tile list, the scratch and the argument block of one chunked scan; no
 // launch.
-template <int H, int KB, int VB>
+template <int H, int KB, int VB, int RS = 0>
 inline int prepare_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, int32_t B,
                            const int32_t *d_seq, const int64_t *d_T, const int64_t *h_T,
                            const int32_t *d_pt, const uint8_t *pool, const int32_t *q_rot,
                            int64_t *out, ins_stats *stats, int32_t *d_status, ChunkArgs &a,
                            cudaStream_t s) {
-    using CF = ChunkCfg<H, KB, VB>;
+    using CF = ChunkCfg<H, KB, VB, RS>;
     const int n_items = B * g.n_kv;
     TilePlan &tp = cs.plan;
     tp.build(g, B, h_T, CF::C);
@@ -2084,46 +2086,79 @@ inline int prepare_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, 
     return INS_OK;
 }
 
-template <int H, int KB, int VB>
+template <int H, int KB, int VB, int RS = 0>
 inline int launch_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, int32_t B,
                           const int32_t *d_seq, const int64_t *d_T, const int64_t *h_T,
                           const int32_t *d_pt, const uint8_t *pool, const int32_t *q_rot,
                           int64_t *out, ins_stats *stats, int32_t *d_status, cudaStream_t s) {
     ChunkArgs a;
-    if (int rc = prepare_chunked<H, KB, VB>(cs, g, tb, B, d_seq, d_T, h_T, d_pt, pool, q_rot, out, stats,
+    if (int rc = prepare_chunked<H, KB, VB, RS>(cs, g, tb, B, d_seq, d_T, h_T, d_pt, pool, q_rot, out, stats,
                                             d_status, a, s))
         return rc;
-    return launch_chunk_kernels<H, KB, VB>(a, B, d_seq, d_T, s);
+    return launch_chunk_kernels<H, KB, VB, RS>(a, B, d_seq, d_T, s);
 }
 
 // Context split, phase 1: the scores of this shard and each item's maximum
 // (a.maxima), leaving the scores in the scratch for phase 2.
-template <int H, int KB, int VB>
+template <int H, int KB, int VB, int RS = 0>
 inline int launch_split_maxima(ChunkArgs &a, cudaStream_t s) {
-    const int gA = chunk_slots<H, KB, VB, 0>();
+    const int gA = chunk_slots<H, KB, VB, 0, RS>();
     if (gA < 0) return INS_ECUDA;
     ChunkArgs m = a;
     m.m_init = nullptr;
     m.parts = nullptr;
-    k_scan_scores<H, KB, VB><<<gA < m.n_tiles ? gA : m.n_tiles, CHUNK_THREADS, ScoreCfg<H, KB, VB>::BYTES, s>>>(m);
+    k_scan_scores<H, KB, VB, RS><<<gA < m.n_tiles ? gA : m.n_tiles, CHUNK_THREADS, ScoreCfg<H, KB, VB, RS>::BYTES, s>>>(m);
     k_chunk_prefix<H><<<m.n_items * H, 256, 0, s>>>(m);
     return cudaGetLastError() == cudaSuccess ? INS_OK : INS_ECUDA;
 }
 
 // Context split, phase 2: with the running maximum entering the shard
 // (a.m_init), the values and one composite per item (a.parts).
-template <int H, int KB, int VB>
+template <int H, int KB, int VB, int RS = 0>
 inline int launch_split_part(ChunkArgs &a, cudaStream_t s) {
-    const int gB = chunk_slots<H, KB, VB, 1>();
+    const int gB = chunk_slots<H, KB, VB, 1, RS>();
     if (gB < 0) return INS_ECUDA;
     ChunkArgs m = a;
     m.maxima = nullptr;
     k_chunk_prefix<H><<<m.n_items * H, 256, 0, s>>>(m);
-    k_scan_values<H, KB, VB>
-        <<<gB < m.n_tiles ? gB : m.n_tiles, CHUNK_THREADS, ChunkCfg<H, KB, VB>::BYTES, s>>>(m);
+    k_scan_values<H, KB, VB, RS>
+        <<<gB < m.n_tiles ? gB : m.n_tiles, CHUNK_THREADS, ChunkCfg<H, KB, VB, RS>::BYTES, s>>>(m);
     if (!m.fold_fused) k_fold_blocks<H><<<m.n_items * m.max_blocks, CHUNK_THREADS, 0, s>>>(m);
     k_fold_items<H><<<m.n_items, CHUNK_THREADS, 0, s>>>(m);
     return cudaGetLastError() == cudaSuccess ? INS_OK : INS_ECUDA;
+}
+
+// Tile size. Tiles of C rows (4 rows per thread where the shape allows) keep
+// the per-tile work small against the rows; but a batch of short items cuts
+// into few tiles and leaves SMs idle. When the default tiles would not fill
+// two waves of the values launch, tiles of half the rows are used instead.
+enum : int32_t { TILES_AUTO = 0, TILES_LARGE = 1, TILES_SMALL = 2 };
+
+template <int H, int KB, int VB>
+inline bool small_tiles(const ChunkScratch &cs, const Geo &g, int32_t B, const int64_t *h_T) {
+    if constexpr (ChunkCfg<H, KB, VB>::R != 4) {
+        return false;
+    } else {
+        if (cs.tiles_mode != TILES_AUTO) return cs.tiles_mode == TILES_SMALL;
+        constexpr int C = ChunkCfg<H, KB, VB>::C;
+        int64_t tiles = 0;
+        for (int32_t b = 0; b < B; ++b) tiles += h_T[b] ? (h_T[b] + C - 1) / C : 1;
+        const int slots = chunk_slots<H, KB, VB, 1>();
+        return slots > 0 && tiles * g.n_kv < 2 * (int64_t)slots;
+    }
+}
+
+template <int H, int KB, int VB>
+inline int launch_chunked_auto(ChunkScratch &cs, const Geo &g, const DevTables *tb, int32_t B,
+                               const int32_t *d_seq, const int64_t *d_T, const int64_t *h_T,
+                               const int32_t *d_pt, const uint8_t *pool, const int32_t *q_rot,
+                               int64_t *out, ins_stats *stats, int32_t *d_status, cudaStream_t s) {
+    if constexpr (ChunkCfg<H, KB, VB>::R == 4)
+        if (small_tiles<H, KB, VB>(cs, g, B, h_T))
+            return launch_chunked<H, KB, VB, 2>(cs, g, tb, B, d_seq, d_T, h_T, d_pt, pool, q_rot, out,
+                                                stats, d_status, s);
+    return launch_chunked<H, KB, VB>(cs, g, tb, B, d_seq, d_T, h_T, d_pt, pool, q_rot, out, stats,
+                                     d_status, s);
 }
 
 // Which chunked instantiation serves a cache: 0 none, else (H, KB, VB) packed.
@@ -2139,9 +2174,9 @@ inline int launch_online(ChunkScratch &cs, const Geo &g, const DevTables *tb, in
                          const int32_t *d_pt, const uint8_t *pool, const int32_t *q_rot,
                          int64_t *out, ins_stats *stats, int32_t *d_status, int H,
                          cudaStream_t s) {
-#define INS_CH(HH, KK, VV)                                                                 \
-    return launch_chunked<HH, KK, VV>(cs, g, tb, B, d_seq, d_lens, h_lens, d_pt, pool, q_rot, \
-                                      out, stats, d_status, s)
+#define INS_CH(HH, KK, VV)                                                                      \
+    return launch_chunked_auto<HH, KK, VV>(cs, g, tb, B, d_seq, d_lens, h_lens, d_pt, pool, q_rot, \
+                                           out, stats, d_status, s)
     if (is_def_fmt(g) && g.kb == 4 && g.vb == 2) {
         switch (H) {
             case 1: INS_CH(1, 4, 2);

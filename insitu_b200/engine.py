@@ -120,6 +120,11 @@ class PagedCache:
         """Raise if a kernel latched an error (range, bounded-wait timeout)."""
         _lib.check(self._L.ins_cache_status(self._h, _stream(self.device)))
 
+    def set_tiles(self, mode: str = "auto") -> None:
+        """Tile size of the online scan (ins_cache_set_tiles): "auto", "large"
+        or "small". A tuning knob; every mode gives the same results."""
+        _lib.check(self._L.ins_cache_set_tiles(self._h, _lib.INS_TILES[mode]))
+
     def recomputed(self) -> int:
         """Items of the last online scan that the exact sequential kernel redid
         (ins_scan_recomputed); 0 when the context-parallel scan proved them all."""

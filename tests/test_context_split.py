@@ -72,6 +72,24 @@ def _rising(T, step, rng):
     return np.stack([kk] * 8, axis=1), base
 
 
+@pytest.mark.parametrize("tiles", ["large", "small"])
+def test_split_under_both_tile_sizes(tiles):
+    from insitu_b200.context import local_split_scan
+    rng = np.random.default_rng(31)
+    T = 9000
+    pc, k, v, n = _split_cache(T, [2500, 6100], rng)
+    pc.set_tiles(tiles)
+    orc = make_oracle()
+    qr = orc.rotate(_wire(rng, (1, 32, 64), 1.0 / 8.0))
+    q_rot = torch.from_numpy(qr.astype(np.int32))
+    out, st = local_split_scan(pc, [[r + 1] for r in range(n)], q_rot)
+    pc.status()
+    rows = orc.ingress_rows(k, v, threads=8)
+    want, wst = orc.decode_layer(qr, [rows], threads=8)
+    np.testing.assert_array_equal(out.cpu().numpy(), want)
+    np.testing.assert_array_equal(st.cpu().numpy(), wst)
+
+
 def test_split_with_rescales_in_every_shard():
     """Rising keys: the running maximum moves in every shard, so the composites
     carry rescale entries and the merge applies them across boundaries."""

@@ -268,6 +268,39 @@ def test_queries_at_the_edge_of_the_fp64_range():
         assert int(_np(ovf)[0]) == wovf
 
 
+@pytest.mark.parametrize("groups", [1, 2, 4])
+@pytest.mark.parametrize("tiles", ["large", "small"])
+def test_both_tile_sizes_match_oracle(groups, tiles):
+    """The scan's two tile sizes (4 or 2 rows per thread; "auto" picks by
+    context) give the oracle's bits, for a ragged batch with one sequence of
+    rising keys whose running maximum moves across tile boundaries."""
+    rng = np.random.default_rng(17 + groups)
+    lens = [0, 1, 511, 1024, 1025, 3000, 6000]
+    B = len(lens)
+    pc = _pc(n_kv=8, groups=groups, max_seqs=B, capacity=6144)
+    pc.set_tiles(tiles)
+    orc = make_oracle()
+    caches = []
+    for b, T in enumerate(lens):
+        if b == B - 1:
+            kk, _ = _rising_keys(T, 97, rng)
+            k = np.stack([kk] * 8, axis=1)
+        else:
+            k = _wire(rng, (T, 8, 64))
+        v = _wire(rng, (T, 8, 64))
+        if T:
+            pc.ingress(np.full(T, b, np.int32), k, v)
+        caches.append(orc.ingress_rows(k, v, threads=8) if T else np.zeros((0, 8, 52), np.uint8))
+    q = _wire(rng, (B, 8 * groups, 64), 1.0 / 8.0)
+    q_rot = orc.rotate(q)
+    out, st = pc.scan(np.arange(B), torch.from_numpy(q_rot.astype(np.int32)))
+    pc.status()
+    want, wst = orc.decode_layer(q_rot, caches, threads=8)
+    np.testing.assert_array_equal(_np(out), want)
+    np.testing.assert_array_equal(_np(st), wst)
+    assert wst[B - 1, :, 1].sum() > 8                   # rescales in the rising sequence
+
+
 # -- error behaviour -------------------------------------------------------------
 
 def test_capacity_overflow_raises_and_changes_nothing():
