@@ -4,11 +4,12 @@
 // running maximum m, and at every token whose score exceeds it, a rescale
 // acc = floor(acc * exp(s - m) / 2^15) before the token's own term is added.
 // This scan splits every (sequence, KV head) item into tiles of C rows and
-// still returns the reference's bits. It runs as three launches and no
-// launch ever waits on another CTA:
+// still returns the reference's bits. Its launches follow one another on the
+// stream and no launch ever waits on another CTA:
 //
 //  1. k_scan_scores: the scores of every tile (exact FP64 FMA on integer
-//     operands). Each is kept as its offset below its 32-row block's maximum;
+//     operands; the K rows staged in shared memory by bulk copies one tile
+//     ahead). Each is kept as its offset below its 32-row block's maximum;
 //     the block and tile maxima are kept too.
 //  2. k_chunk_prefix: per item, the running maximum entering every tile (the
 //     maximum of all earlier tiles' maxima).
@@ -16,16 +17,18 @@
 //     rescale points (tokens above the running maximum), p = exp(m - s) for
 //     every token, and splits its tokens into segments at the rescale points.
 //     Within a segment every term is a fixed integer, so its contribution is
-//     a plain sum. The last tile of an item to finish folds the tiles in
-//     causal order: acc = floor(acc * f / 2^15) at each rescale, + segment
-//     sums. That fold equals the per-token recurrence provided the
-//     reference's 32-bit clamp never fires; the fold proves it per tile with
+//     a plain sum; the tile writes a record of its segments.
+//  4. k_fold_blocks, k_fold_items: the records folded in causal order, per
+//     block of 32 tiles and then per item: acc = floor(acc * f / 2^15) at each
+//     rescale, + segment sums, then the finalize. That fold equals the
+//     per-token recurrence provided the reference's 32-bit clamp never fires;
+//     the fold proves it per tile with
 //     |acc at tile start| + sum_t max_k |term(t, k)| <= 2^31 - 1, which bounds
 //     every partial sum inside the tile (a rescale never grows |acc|).
 //
 // An item that fails the proof, overflows the segment pool or meets a value
 // outside the formats these kernels assume is recomputed by the exact
-// sequential kernel (a fourth launch that only touches flagged items), so the
+// sequential kernel (a last launch that only touches flagged items), so the
 // result is bit-exact in every case.
 #pragma once
 
