@@ -431,7 +431,6 @@ struct ScoreCfg {
     static constexpr size_t BUF = KPL + (size_t)C * 4;             // + their norm words
     static constexpr size_t BYTES = CTAB + 2 * BUF;
     static constexpr int PGMAX = C / 16 + 1;                       // pages a tile touches (P >= 16)
-    static constexpr int PPL = (PGMAX + 31) / 32;                  // of them per lane
     static_assert(CTAB % 16 == 0 && KPL % 16 == 0 && BUF % 16 == 0, "bulk copies need 16-byte alignment");
 };
 
@@ -892,24 +891,20 @@ __device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
-// Prefetches into L2 the rows of tile `tile` that a launch will read: the K
-// plane and norms (`which` & 1), the V plane and norms (`which` & 2), one lane
-// per page the tile touches. Every range starts 16-byte aligned inside its
-// plane and is rounded up to 16 bytes without leaving the plane.
-__device__ __forceinline__ void prefetch_tile(const ChunkArgs &a, int tile, int lane, int which) {
+// Prefetches into L2 the rows of the tile `td` whose page ids are `pages`: the
+// K plane and norms (`which` & 1), the V plane and norms (`which` & 2), one
+// lane per page. Every range starts 16-byte aligned inside its plane and is
+// rounded up to 16 bytes without leaving the plane.
+__device__ __forceinline__ void prefetch_rows(const ChunkArgs &a, int4 td, const int32_t *pages,
+                                              int lane, int which) {
     const Geo &g = a.g;
-    const int4 td = tile_at(a, tile);
-    const int item = td.x, n = td.w;
+    const int n = td.w, kvh = td.x % g.n_kv;
     if (n <= 0) return;
-    const int64_t t0 = td.z;
-    const int seq = a.seq_ids[item / g.n_kv], kvh = item % g.n_kv;
-    const int64_t p0 = t0 / g.P;
-    const int poff = (int)(t0 % g.P);
+    const int poff = (int)(td.z % g.P);
     const int npages = (poff + n + g.P - 1) / g.P;
     auto up16 = [](int x) { return (uint32_t)((x + 15) & ~15); };
     for (int i = lane; i < npages; i += 32) {
-        const int64_t page = a.page_table[(int64_t)seq * g.max_pages + p0 + i];
-        const uint8_t *reg = a.pool + region_off(g, page, kvh);
+        const uint8_t *reg = a.pool + region_off(g, pages[i], kvh);
         const int r0 = i == 0 ? poff : 0;
         const int r1 = min(g.P, poff + n - i * g.P);
         const int rows = r1 - r0;
@@ -919,7 +914,75 @@ __device__ __forceinline__ void prefetch_tile(const ChunkArgs &a, int tile, int 
     }
 }
 
+
 // ---------------------------------------------------------------------------
+// Tiles looked up two ahead of their use, for a CTA that walks its tiles
+// blockIdx.x + j * gridDim.x: load() (one warp) starts the loads of local
+// tile j's descriptor, row base and page ids; store(), a tile of work later,
+// writes what they returned to shared memory (descriptor ring of 3, page ring
+// of 2), so that no tile starts with a dependent chain of global loads. The
+// item of the last lookup is kept: consecutive tiles of a CTA usually share
+// it, and then only the page ids are loaded.
+template <int PGMAX>
+struct TileAhead {
+    static constexpr int PPL = (PGMAX + 31) / 32;           // page ids per lane
+    int4 *tdesc;                                             // [3]
+    long long *trb;                                          // [3]
+    int32_t (*pages)[PGMAX];                                 // [2][PGMAX]
+    int4 run0;
+    int citem = -1, cseq = 0;
+    int64_t cT = 0, crb = 0;
+    int4 rtd = make_int4(0, 0, 0, 0);
+    long long rrb = 0;
+    int32_t rpg[PPL];
+
+    __device__ TileAhead(const ChunkArgs &a, int4 *td, long long *rb, int32_t (*pg)[PGMAX])
+        : tdesc(td), trb(rb), pages(pg), run0(a.runs[0]) {}
+
+    __device__ __forceinline__ void load(const ChunkArgs &a, int j, int lane) {
+        const Geo &g = a.g;
+        const int tile = (int)blockIdx.x + j * (int)gridDim.x;
+        int item, c;
+        if (a.n_runs == 1) {
+            item = (tile - run0.y) % run0.z;
+            c = run0.x + (tile - run0.y) / run0.z;
+        } else {
+            const int4 t = tile_at(a, tile);
+            item = t.x;
+            c = t.y;
+        }
+        if (item != citem) {
+            citem = item;
+            cT = a.T[item / g.n_kv];
+            cseq = a.seq_ids[item / g.n_kv];
+            crb = a.row_base[item];
+        }
+        const int64_t tt0 = (int64_t)c * a.tile_rows;
+        const int64_t tn = cT - tt0 < a.tile_rows ? cT - tt0 : a.tile_rows;
+        rtd = make_int4(item, c, (int)tt0, (int)(tn > 0 ? tn : 0));
+        rrb = crb;
+        const int poff = (int)(rtd.z % g.P);
+        const int npg = rtd.w ? (poff + rtd.w + g.P - 1) / g.P : 0;
+        const int32_t *pt = a.page_table + (int64_t)cseq * g.max_pages + rtd.z / g.P;
+#pragma unroll
+        for (int k = 0; k < PPL; ++k) {
+            const int i = lane + 32 * k;
+            rpg[k] = i < npg ? __ldg(pt + i) : 0;
+        }
+    }
+    __device__ __forceinline__ void store(int j, int lane) {
+#pragma unroll
+        for (int k = 0; k < PPL; ++k) {
+            const int i = lane + 32 * k;
+            if (i < PGMAX) pages[j & 1][i] = rpg[k];
+        }
+        if (lane == 0) {
+            tdesc[j % 3] = rtd;
+            trb[j % 3] = rrb;
+        }
+    }
+};
+
 // Launch 1: the scores of every tile
 // ---------------------------------------------------------------------------
 // CompressedAttention.scores (ops/attention.py:333-359) for R rows per thread:
@@ -960,49 +1023,10 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
     const int ntl = (a.n_tiles - (int)blockIdx.x + G - 1) / G;   // this CTA's tiles: blockIdx.x + j*G
     auto up16 = [](int x) { return (uint32_t)((x + 15) & ~15); };
 
-    // Warp 1 looks up local tile j: resolve_load starts the loads, and
-    // resolve_store, a tile of arithmetic later, writes what they returned and
-    // announces the bytes of the tile's copies on its buffer's barrier (the
-    // barrier's previous phase, tile j - 2, has completed by then).
-    int4 rtd = make_int4(0, 0, 0, 0);
-    long long rrb = 0;
-    int32_t rpg[SC::PPL];
-    // the item of the last lookup (consecutive tiles of a CTA usually share
-    // it), so that only the page ids are loaded per tile
-    int citem = -1, cseq = 0;
-    int64_t cT = 0, crb = 0;
-    const int4 run0 = a.runs[0];
-    auto resolve_load = [&](int j) {
-        const int tile = (int)blockIdx.x + j * G;
-        int item, c;
-        if (a.n_runs == 1) {
-            item = (tile - run0.y) % run0.z;
-            c = run0.x + (tile - run0.y) / run0.z;
-        } else {
-            const int4 t = tile_at(a, tile);
-            item = t.x;
-            c = t.y;
-        }
-        if (item != citem) {
-            citem = item;
-            cT = a.T[item / g.n_kv];
-            cseq = a.seq_ids[item / g.n_kv];
-            crb = a.row_base[item];
-        }
-        const int64_t tt0 = (int64_t)c * a.tile_rows;
-        const int64_t tn = cT - tt0 < a.tile_rows ? cT - tt0 : a.tile_rows;
-        rtd = make_int4(item, c, (int)tt0, (int)(tn > 0 ? tn : 0));
-        rrb = crb;
-        const int seq = cseq;
-        const int poff = (int)(rtd.z % g.P);
-        const int npg = rtd.w ? (poff + rtd.w + g.P - 1) / g.P : 0;
-        const int32_t *pt = a.page_table + (int64_t)seq * g.max_pages + rtd.z / g.P;
-#pragma unroll
-        for (int k = 0; k < SC::PPL; ++k) {
-            const int i = lane + 32 * k;
-            rpg[k] = i < npg ? __ldg(pt + i) : 0;
-        }
-    };
+    // Warp 1 looks tiles up two ahead; storing tile j's lookup also announces
+    // the bytes of its copies on its buffer's barrier (the barrier's previous
+    // phase, tile j - 2, has completed by then).
+    TileAhead<SC::PGMAX> ahead(a, tdesc_sm, trb_sm, pages_sm);
     auto copy_bytes = [&](int4 td) {
         const int n = td.w, poff = (int)(td.z % g.P);
         const int npg = n ? (poff + n + g.P - 1) / g.P : 0;
@@ -1013,17 +1037,10 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
         }
         return bytes;
     };
+    auto resolve_load = [&](int j) { ahead.load(a, j, lane); };
     auto resolve_store = [&](int j) {
-#pragma unroll
-        for (int k = 0; k < SC::PPL; ++k) {
-            const int i = lane + 32 * k;
-            if (i < SC::PGMAX) pages_sm[j & 1][i] = rpg[k];
-        }
-        if (lane == 0) {
-            tdesc_sm[j % 3] = rtd;
-            trb_sm[j % 3] = rrb;
-            mbar_arrive_tx(&full_bar[j & 1], copy_bytes(rtd));
-        }
+        ahead.store(j, lane);
+        if (lane == 0) mbar_arrive_tx(&full_bar[j & 1], copy_bytes(ahead.rtd));
     };
     // The bulk copies of local tile j's K rows and norm words into buffer
     // j & 1: lane 0 of warp w issues those of pages w, w + 8, ... (the issue
@@ -1341,6 +1358,11 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
     __shared__ unsigned int lsum_sm[H][SEGMAX + 1];   // l of a tile < 2^25
     __shared__ long long bnd_sm[NT / 32][H];           // per-warp clamp-proof bounds
     __shared__ unsigned int resc_sm;
+    // tiles looked up two ahead (descriptor ring of 3, page ring of 2)
+    constexpr int PGMAX = C / 16 + 1;
+    __shared__ int4 tdesc_sm[3];
+    __shared__ long long trb_sm[3];
+    __shared__ int32_t pages_sm[2][PGMAX];
 
     const Geo &g = a.g;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1368,20 +1390,33 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
         cmax_v = ab > cmax_v ? ab : cmax_v;
     }
 
-    // Tiles are dealt round-robin; no tile waits on another.
-    for (int tile = blockIdx.x; tile < a.n_tiles; tile += gridDim.x) {
-        const int4 td = tile_at(a, tile);
+    // Tiles are dealt round-robin (this CTA's: blockIdx.x + li * gridDim.x); no
+    // tile waits on another. Warp 1 looks them up two ahead.
+    const int G = gridDim.x;
+    const int ntl = (a.n_tiles - (int)blockIdx.x + G - 1) / G;
+    TileAhead<PGMAX> ahead(a, tdesc_sm, trb_sm, pages_sm);
+    if (warp == 1) {
+        ahead.load(a, 0, lane);
+        ahead.store(0, lane);
+        if (ntl > 1) {
+            ahead.load(a, 1, lane);
+            ahead.store(1, lane);
+        }
+    }
+    __syncthreads();
+    for (int li = 0; li < ntl; ++li) {
+        const int tile = (int)blockIdx.x + li * G;
+        const int4 td = tdesc_sm[li % 3];
         const int item = td.x, c = td.y;
         const int64_t t0 = td.z;
         const int n = td.w;
-        const int b = item / g.n_kv, kvh = item % g.n_kv;
-        const int seq = a.seq_ids[b];
+        const int kvh = item % g.n_kv;
         const int rec_idx = item * a.max_chunks + c;
         const int poff = (int)(t0 % g.P);
-        const uint32_t *sc = a.sc + (a.row_base[item] + t0) * H;
+        const uint32_t *sc = a.sc + (trb_sm[li % 3] + t0) * H;
 
         // ---- 0. the tile's rows (each thread its own, first), per-tile setup ----
-        const int32_t *ptab = a.page_table + (int64_t)seq * g.max_pages + t0 / g.P;
+        const int32_t *ptab = pages_sm[li & 1];
         uint32_t vw[R][VW], nw[R], off[R][H];
 #pragma unroll
         for (int r = 0; r < R; ++r) {
@@ -1436,13 +1471,14 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
 
         // ---- 2. V codes to channel-major words; warp 1 prefetches this CTA's
         //         next tile into L2 first ------------------------------------------
-        if (warp == 1 && tile + (int)gridDim.x < a.n_tiles) {
-            const int nt = tile + gridDim.x;
-            prefetch_tile(a, nt, lane, 2);
-            if (lane == 0) {
-                const int4 t2 = tile_at(a, nt);
+        if (warp == 1) {
+            if (li + 2 < ntl) ahead.load(a, li + 2, lane);
+            if (li + 1 < ntl) {
+                const int4 t2 = tdesc_sm[(li + 1) % 3];
+                prefetch_rows(a, t2, pages_sm[(li + 1) & 1], lane, 2);
                 const uint32_t bytes = (uint32_t)t2.w * H * 4;
-                if (bytes) prefetch_l2(a.sc + (a.row_base[t2.x] + t2.z) * H, (bytes + 15) & ~15u);
+                if (lane == 0 && bytes)
+                    prefetch_l2(a.sc + (trb_sm[(li + 1) % 3] + t2.z) * H, (bytes + 15) & ~15u);
             }
         }
         // word (ch, k) holds, as nibbles, the table indices of units 8k .. 8k+7
@@ -1853,6 +1889,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
                 if (resc_sm) atomicAdd(&ia.resc, (unsigned long long)resc_sm);
             }
         }
+        if (warp == 1 && li + 2 < ntl) ahead.store(li + 2, lane);
         __syncthreads();                 // the next tile reuses shared memory
     }
 }
