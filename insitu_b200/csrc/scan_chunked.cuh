@@ -557,17 +557,25 @@ __device__ void merge_block(const ChunkArgs &a, int item, int blk, int nchunks,
                             int *base_sm /* [H] */) {
     const int c0 = blk * GBLK, c1 = min(nchunks, c0 + GBLK);
     const ChunkRec *recs = a.recs + (int64_t)item * a.max_chunks;
-    // entries each head needs = rescales in the block's tiles
-    for (int h = threadIdx.x; h < H; h += blockDim.x) {
-        int need = 0;
-        for (int c = c0; c < c1; ++c) need += ldcg(&recs[c].nseg[h]);
-        unsigned b = 0;
-        if (need) b = atomicAdd(a.seg_top, (unsigned)need);
-        if (need && b + need > (unsigned)a.seg_cap) {
-            atomicExch(&a.items[item].fail, 1);
-            need = 0;
+    // entries each head needs = rescales in the block's tiles: warp h sums
+    // head h's counts, one tile per lane (a block holds at most 32 tiles)
+    static_assert(GBLK <= 32 && HMAX <= CHUNK_THREADS / 32, "one warp per head, one lane per tile");
+    {
+        const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        if (w < H) {
+            const int c = c0 + lane;
+            int need = c < c1 ? ldcg(&recs[c].nseg[w]) : 0;
+            need = __reduce_add_sync(FULL, need);
+            if (lane == 0) {
+                unsigned b = 0;
+                if (need) b = atomicAdd(a.seg_top, (unsigned)need);
+                if (need && b + need > (unsigned)a.seg_cap) {
+                    atomicExch(&a.items[item].fail, 1);
+                    need = 0;
+                }
+                base_sm[w] = need ? (int)b : -1;
+            }
         }
-        base_sm[h] = need ? (int)b : -1;
     }
     __syncthreads();
     for (int pr = threadIdx.x; pr < H * D; pr += blockDim.x) {
@@ -656,22 +664,34 @@ __device__ void merge_item(const ChunkArgs &a, int item, int nblocks, int64_t T,
         const int pr = tid + k * CHUNK_THREADS;
         if (pr >= H * D || bad) continue;
         const int h = pr / D, ch = pr % D;
-        for (int bb = 0; bb < nblocks; ++bb) {
-            const BlockRec &br = blks[bb];
-            const int64_t Y = ldcg(&br.Y[h][ch]);
-            const int64_t Sp = ldcg(&br.Spre[h][ch]);
-            const int64_t lp = ldcg(&br.lpre[h]);
-            const int ne = ldcg(&br.nent[h]);
-            const int eb = ldcg(&br.ent_base[h]);
-            const int64_t aa = acc[k] < 0 ? -acc[k] : acc[k];
-            if (aa + Y > INT32_MAX) bad = true;
-            acc[k] += Sp;
-            l[k] += lp;
-            for (int e = 0; e < ne; ++e) {
-                const SegEntry &se = a.segs[eb + e];
-                const int64_t f = ldcg(&se.f);
-                acc[k] = ((acc[k] * f) >> a.g.prob_frac) + ldcg(&se.S[ch]);
-                l[k] = ((l[k] * f) >> a.g.prob_frac) + ldcg(&se.l);
+        // the block records in batches of 8, their loads issued together
+        for (int b0 = 0; b0 < nblocks; b0 += 8) {
+            int64_t Yv[8], Sv[8], lv[8];
+            int nev[8], ebv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                if (b0 + u < nblocks) {
+                    const BlockRec &br = blks[b0 + u];
+                    Yv[u] = ldcg(&br.Y[h][ch]);
+                    Sv[u] = ldcg(&br.Spre[h][ch]);
+                    lv[u] = ldcg(&br.lpre[h]);
+                    nev[u] = ldcg(&br.nent[h]);
+                    ebv[u] = ldcg(&br.ent_base[h]);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                if (b0 + u >= nblocks) break;
+                const int64_t aa = acc[k] < 0 ? -acc[k] : acc[k];
+                if (aa + Yv[u] > INT32_MAX) bad = true;
+                acc[k] += Sv[u];
+                l[k] += lv[u];
+                for (int e = 0; e < nev[u]; ++e) {
+                    const SegEntry &se = a.segs[ebv[u] + e];
+                    const int64_t f = ldcg(&se.f);
+                    acc[k] = ((acc[k] * f) >> a.g.prob_frac) + ldcg(&se.S[ch]);
+                    l[k] = ((l[k] * f) >> a.g.prob_frac) + ldcg(&se.l);
+                }
             }
         }
     }
