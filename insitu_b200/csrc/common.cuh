@@ -60,6 +60,12 @@ __host__ __device__ inline int64_t nplane_off(const Geo &g) {
     return (int64_t)g.P * (g.kbytes + g.vbytes);
 }
 
+// A kernel launched with programmatic stream serialization may start while
+// the kernel before it on the stream is finishing; this waits until that
+// kernel has completed and its memory is visible (a no-op for a kernel
+// launched the ordinary way).
+__device__ __forceinline__ void wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ int64_t shfl_xor64(int64_t v, int m) {
     return __shfl_xor_sync(FULL, v, m);
 }

@@ -487,6 +487,7 @@ __global__ void __launch_bounds__(H * 64)
     extern __shared__ __align__(16) uint8_t dyn[];
     __shared__ SeqSmem<H> sm;
     const int item = blockIdx.x;
+    wait_prior_grid();                   // `only` comes from the launch before
     if (only && !only[item]) return;
     const int b = item / g.n_kv, kvh = item % g.n_kv;
     const int64_t base = ((int64_t)b * g.n_kv * H + (int64_t)kvh * H) * D;

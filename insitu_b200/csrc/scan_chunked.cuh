@@ -36,6 +36,7 @@
 #include <climits>
 #include <cstring>
 #include <mutex>
+#include <utility>
 #include <vector>
 
 #include "common.cuh"
@@ -1315,6 +1316,7 @@ __global__ void __launch_bounds__(256) k_chunk_prefix(ChunkArgs a) {
     __shared__ long long wtot[8];
     const int item = blockIdx.x / H, h = blockIdx.x % H;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    wait_prior_grid();
     // the segment pool of the values launch starts empty (no launch before it
     // allocates from it)
     if (blockIdx.x == 0 && tid == 0) *a.seg_top = 0;
@@ -1423,6 +1425,9 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
             ahead.store(1, lane);
         }
     }
+    // everything above reads only what was written before the scores launch;
+    // from here on, the outputs of the launches before this one
+    wait_prior_grid();
     __syncthreads();
     for (int li = 0; li < ntl; ++li) {
         const int tile = (int)blockIdx.x + li * G;
@@ -1922,6 +1927,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
 template <int H>
 __global__ void __launch_bounds__(CHUNK_THREADS) k_fold_blocks(ChunkArgs a) {
     __shared__ int base_sm[H];
+    wait_prior_grid();
     const int item = blockIdx.x / a.max_blocks, blk = blockIdx.x % a.max_blocks;
     const int nc = item_chunks(a, item);
     if (blk * GBLK >= nc) return;
@@ -1934,6 +1940,7 @@ template <int H>
 __global__ void __launch_bounds__(CHUNK_THREADS) k_fold_items(ChunkArgs a) {
     __shared__ long long slots[CHUNK_THREADS / 32];
     __shared__ int base_sm[H];
+    wait_prior_grid();
     const int item = blockIdx.x;
     const int nc = item_chunks(a, item), nblk = (nc + GBLK - 1) / GBLK;
     const int b = item / a.g.n_kv;
@@ -1969,8 +1976,28 @@ inline cudaError_t launch_seq(const Geo &g, const DevTables *tb, int32_t B, cons
                                          : k_scan_seq<H, 0, 0>;
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    fn<<<B * g.n_kv, H * 64, smem, s>>>(g, tb, d_seq, d_lens, d_pt, pool, q_rot, out, stats, only);
-    return cudaGetLastError();
+    // k_scan_seq waits for the launch before it before it reads anything
+    return launch_after(fn, (unsigned)(B * g.n_kv), (unsigned)(H * 64), smem, s, g, tb, d_seq, d_lens,
+                        d_pt, pool, q_rot, out, stats, only);
+}
+
+// Launches `kernel` so that it may start while the previous kernel on the
+// stream finishes (programmatic stream serialization); the kernel calls
+// wait_prior_grid() before it reads that kernel's results.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_after(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem,
+                                cudaStream_t s, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // Resident CTAs of the scores (WHICH 0) or values (WHICH 1) kernel on the
@@ -2073,11 +2100,16 @@ inline int launch_chunk_kernels(ChunkArgs &a, int32_t B, const int32_t *d_seq, c
     const int gA = chunk_slots<H, KB, VB, 0, RS>(), gB = chunk_slots<H, KB, VB, 1, RS>();
     if (gA < 0 || gB < 0) return INS_ECUDA;
     k_scan_scores<H, KB, VB, RS><<<gA < a.n_tiles ? gA : a.n_tiles, CHUNK_THREADS, ScoreCfg<H, KB, VB, RS>::BYTES, s>>>(a);
-    k_chunk_prefix<H><<<a.n_items * H, 256, 0, s>>>(a);
-    k_scan_values<H, KB, VB, RS>
-        <<<gB < a.n_tiles ? gB : a.n_tiles, CHUNK_THREADS, ChunkCfg<H, KB, VB, RS>::BYTES, s>>>(a);
-    if (!a.fold_fused) k_fold_blocks<H><<<a.n_items * a.max_blocks, CHUNK_THREADS, 0, s>>>(a);
-    k_fold_items<H><<<a.n_items, CHUNK_THREADS, 0, s>>>(a);
+    // the launches after the scores may start while the one before finishes
+    // (each waits for it before reading its results)
+    const unsigned gv = (unsigned)(gB < a.n_tiles ? gB : a.n_tiles);
+    if (launch_after(k_chunk_prefix<H>, (unsigned)(a.n_items * H), 256u, 0, s, a) != cudaSuccess ||
+        launch_after(k_scan_values<H, KB, VB, RS>, gv, (unsigned)CHUNK_THREADS, ChunkCfg<H, KB, VB, RS>::BYTES,
+                     s, a) != cudaSuccess ||
+        (!a.fold_fused && launch_after(k_fold_blocks<H>, (unsigned)(a.n_items * a.max_blocks),
+                                       (unsigned)CHUNK_THREADS, 0, s, a) != cudaSuccess) ||
+        launch_after(k_fold_items<H>, (unsigned)a.n_items, (unsigned)CHUNK_THREADS, 0, s, a) != cudaSuccess)
+        return INS_ECUDA;
     if (cudaGetLastError() != cudaSuccess) return INS_ECUDA;
     // items whose exactness the fold could not prove are recomputed in order
     return launch_seq<H>(a.g, a.tb, B, d_seq, d_T, a.page_table, a.pool, a.q_rot, a.out, a.stats,
