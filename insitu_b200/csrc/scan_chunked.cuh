@@ -740,35 +740,47 @@ __device__ void fold_part(const ChunkArgs &a, int item, int nblocks, int64_t T, 
         int64_t loc = 0, Y = 0, curS = 0, curl = 0, Spre = 0, lpre = 0;
         int ne = 0;
         bool opened = false;
-        for (int bb = 0; bb < nblocks; ++bb) {
-            const BlockRec &br = blks[bb];
-            const int64_t Yb = ldcg(&br.Y[h][ch]);
-            const int64_t Sp = ldcg(&br.Spre[h][ch]);
-            const int64_t lp = ldcg(&br.lpre[h]);
-            const int nb_e = ldcg(&br.nent[h]);
-            const int eb = ldcg(&br.ent_base[h]);
-            const int64_t al = loc < 0 ? -loc : loc;
-            Y = max(Y, al + Yb);
-            loc += Sp;
-            curS += Sp;
-            curl += lp;
-            for (int e = 0; e < nb_e; ++e) {
-                const SegEntry &se = a.segs[eb + e];
-                const int64_t f = ldcg(&se.f);
-                if (!opened) {
-                    Spre = curS;
-                    lpre = curl;
-                    opened = true;
-                } else if (ne - 1 < PART_MAXE) {
-                    over |= curS < INT32_MIN || curS > INT32_MAX;
-                    pr.ent[h][ne - 1].S[ch] = (int32_t)curS;
-                    if (ch == 0) pr.ent[h][ne - 1].l = curl;
+        // the block records in batches of 8, their loads issued together
+        for (int b0 = 0; b0 < nblocks; b0 += 8) {
+            int64_t Yv[8], Sv[8], lv[8];
+            int nev[8], ebv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                if (b0 + u < nblocks) {
+                    const BlockRec &br = blks[b0 + u];
+                    Yv[u] = ldcg(&br.Y[h][ch]);
+                    Sv[u] = ldcg(&br.Spre[h][ch]);
+                    lv[u] = ldcg(&br.lpre[h]);
+                    nev[u] = ldcg(&br.nent[h]);
+                    ebv[u] = ldcg(&br.ent_base[h]);
                 }
-                if (ne < PART_MAXE && ch == 0) pr.ent[h][ne].f = (int32_t)f;
-                ++ne;
-                curS = ldcg(&se.S[ch]);
-                curl = ldcg(&se.l);
-                loc = ((loc * f) >> a.g.prob_frac) + curS;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                if (b0 + u >= nblocks) break;
+                const int64_t al = loc < 0 ? -loc : loc;
+                Y = max(Y, al + Yv[u]);
+                loc += Sv[u];
+                curS += Sv[u];
+                curl += lv[u];
+                for (int e = 0; e < nev[u]; ++e) {
+                    const SegEntry &se = a.segs[ebv[u] + e];
+                    const int64_t f = ldcg(&se.f);
+                    if (!opened) {
+                        Spre = curS;
+                        lpre = curl;
+                        opened = true;
+                    } else if (ne - 1 < PART_MAXE) {
+                        over |= curS < INT32_MIN || curS > INT32_MAX;
+                        pr.ent[h][ne - 1].S[ch] = (int32_t)curS;
+                        if (ch == 0) pr.ent[h][ne - 1].l = curl;
+                    }
+                    if (ne < PART_MAXE && ch == 0) pr.ent[h][ne].f = (int32_t)f;
+                    ++ne;
+                    curS = ldcg(&se.S[ch]);
+                    curl = ldcg(&se.l);
+                    loc = ((loc * f) >> a.g.prob_frac) + curS;
+                }
             }
         }
         if (!opened) {
