@@ -35,6 +35,10 @@ sequence + one batched scan.
 `--config 3`: 16 layer caches of 8K tokens each, decoded
 layer after layer (ingress + scan per layer); a step = one token through all
 16 layers.
+
+`--formats`: the board's byte formats around the cache -- ingress of a
+256-token batch from int32 arrays and from the 24-bit lane stream, and the DDR
+image of the 1M-token sequence (GB/s of rows gathered into planes).
 """
 
 from __future__ import annotations
@@ -70,6 +74,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--split", action="store_true",
                     help="config 5: one sequence split across the ranks (ctx = total tokens)")
+    ap.add_argument("--formats", action="store_true",
+                    help="time the lane-stream ingress and the DDR image (board formats)")
     ap.add_argument("--config", type=int, choices=(2, 3, 4, 5), default=2,
                     help="BASELINE config to time (2: the default sweep point; 5 = --split)")
     return ap.parse_args()
@@ -695,8 +701,48 @@ def run_layers(args):
         dist.destroy_process_group()
 
 
+def run_formats(args):
+    """The lane-stream ingress and the DDR image, timed with CUDA events."""
+    import torch
+    from insitu_b200 import wire
+
+    world, rank, local = _dist_setup()
+    K, W = args.steps, args.warmup
+    ctx, nb = args.ctx, 256
+    dec, gen = make_decoder(ctx, (K + W) * nb * 2 + 8, local, seed=5)
+    pc = dec.pc
+    q, k, v = step_inputs(gen, nb, local)
+    q, k, v = q[:, 0], k[:, 0], v[:, 0]
+    lanes = torch.from_numpy(wire.ingress_stream(q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy())).to(
+        f"cuda:{local}")
+    ids = [0] * nb
+    ms_i32 = _time_steps(lambda i: pc.ingress(ids, k, v, q), K, W, local)
+    ms_lanes = _time_steps(lambda i: pc.ingress_lanes(ids, lanes), K, W, local)
+    T = pc.length(0)
+    cap = T
+    ms_img = _time_steps(lambda i: pc.ddr_image(0, cap), K, W, local)
+    pc.status()
+    rows = 8 * T
+    if rank == 0:
+        print(json.dumps({
+            "metric": "board byte formats: lane-stream ingress and DDR image", "n_gpus": world,
+            "steps": K, "warmup": W, "data": "synthetic: seeded N(0,1) Q8.16 k/v, q ~ N(0,1/64)",
+            "ingress_256_tokens": {"int32_us": round(ms_i32 / K * 1e3, 2),
+                                   "lanes_us": round(ms_lanes / K * 1e3, 2),
+                                   "lane_bytes": int(lanes.numel())},
+            "ddr_image": {"tokens": T, "us": round(ms_img / K * 1e3, 2),
+                          "GB/s_rows": round(rows * ROW_BYTES / (ms_img / K * 1e-3) / 1e9, 2),
+                          "image_bytes": int(pc.ddr_image(0, cap).numel())},
+            "gpu_launches": K * 4,
+        }), flush=True)
+    dec.close()
+
+
 def main():
     args = parse()
+    if args.formats:
+        run_formats(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     elif args.split or args.config == 5:

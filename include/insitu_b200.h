@@ -163,6 +163,18 @@ int ins_ingress(ins_cache *cache, int32_t n, const int32_t *seq_ids,
                 const int32_t *q, const int32_t *k, const int32_t *v, int32_t *q_rot,
                 uint32_t flags, void *stream);
 
+/* ins_ingress fed the board's ingress stream instead of int32 arrays: the
+ * byte stream VectorSet.ingress_bytes builds (hw/vectors.py:178-196) -- per
+ * token, per KV head h, the vectors k_h, v_h, q_{h*groups} .. q_{h*groups +
+ * groups - 1}, each head_dim signed 24-bit lanes packed LSB first
+ * (pack_lanes, hw/vectors.py:72-104); 9,216 bytes per token at the BASELINE
+ * geometry (ins_lanes_bytes_per_token). lanes: device, n tokens back to back,
+ * 2-byte aligned; q_rot: device [n, n_kv*groups, d] int32, required. The lanes
+ * are sign-extended on the GPU; everything after is ins_ingress. */
+int ins_ingress_lanes(ins_cache *cache, int32_t n, const int32_t *seq_ids, const uint8_t *lanes,
+                      int32_t *q_rot, void *stream);
+int64_t ins_lanes_bytes_per_token(const ins_cache *cache);
+
 /* Rotation.apply (ops/rotate.py:170-197) alone: n vectors of head_dim int32
  * on the device, x -> y (may alias). Same Q in and out, not clamped; a result
  * that does not fit int32 latches INS_ERANGE. */
@@ -226,6 +238,16 @@ int ins_cache_export(ins_cache *cache, int32_t seq, int32_t kv_head, int64_t t0,
  * the layout of CompressedCache.buf) -- loading a cache image the way the
  * board's CMD_LOAD does (host/attn_proto.h:36). Blocks. */
 int ins_cache_import(ins_cache *cache, int32_t seq, int64_t n, const uint8_t *rows);
+
+/* The board's DDR image of one sequence's cache (DdrLayout.image,
+ * hw/ddr_layout.py:227-245): the packed rows split at their fields and into
+ * 16-byte beats, each plane padded to a 4 KB-aligned span of `capacity`
+ * tokens of the widest plane, head-major (plane_span / plane_base,
+ * hw/ddr_layout.py:181-212). img: device, ins_ddr_image_bytes(cache,
+ * capacity) bytes; stream-ordered. EBADLEN when the sequence holds more than
+ * `capacity` tokens (the reference's ValueError). */
+int64_t ins_ddr_image_bytes(const ins_cache *cache, int64_t capacity);
+int ins_cache_ddr_image(ins_cache *cache, int32_t seq, int64_t capacity, uint8_t *img, void *stream);
 
 /* Read and clear the device status word latched by earlier kernels. Blocks
  * on the stream. INS_OK when nothing went wrong. */

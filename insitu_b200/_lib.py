@@ -84,7 +84,9 @@ SYMBOLS = ("ins_abi_version", "ins_bytes_per_token", "ins_cache_create", "ins_ca
            "ins_cache_reset", "ins_cache_length", "ins_cache_capacity", "ins_ingress", "ins_rotate",
            "ins_scores", "ins_scan", "ins_cache_export", "ins_cache_import", "ins_cache_status",
            "ins_last_error", "ins_scan_noalloc", "ins_scan_recomputed", "ins_part_bytes",
-           "ins_scan_maxima", "ins_scan_part", "ins_merge_parts", "ins_cache_set_tiles")
+           "ins_scan_maxima", "ins_scan_part", "ins_merge_parts", "ins_cache_set_tiles",
+           "ins_ingress_lanes", "ins_lanes_bytes_per_token", "ins_ddr_image_bytes",
+           "ins_cache_ddr_image")
 
 
 def nvcc() -> str:
@@ -150,6 +152,12 @@ def lib():
     L.ins_scan_part.argtypes = [vp, i32, vp, vp, vp, vp, vp, vp]
     L.ins_merge_parts.argtypes = [vp, i32, i32, vp, vp, vp, vp]
     L.ins_cache_set_tiles.argtypes = [vp, i32]
+    L.ins_ingress_lanes.argtypes = [vp, i32, vp, vp, vp, vp]
+    L.ins_lanes_bytes_per_token.argtypes = [vp]
+    L.ins_lanes_bytes_per_token.restype = i64
+    L.ins_ddr_image_bytes.argtypes = [vp, i64]
+    L.ins_ddr_image_bytes.restype = i64
+    L.ins_cache_ddr_image.argtypes = [vp, i32, i64, vp, vp]
     L.ins_last_error.restype = C.c_char_p
     _lib = L
     return L

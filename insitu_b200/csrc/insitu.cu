@@ -437,16 +437,11 @@ int ins_cache_reset(ins_cache *c, int32_t seq) {
     return INS_OK;
 }
 
-int ins_ingress(ins_cache *c, int32_t n, const int32_t *seq_ids, const int32_t *q,
-                const int32_t *k, const int32_t *v, int32_t *q_rot, uint32_t flags,
-                void *stream) {
-    if (!c) return fail(INS_EINVAL, "cache is NULL");
-    if (n < 0 || (n > 0 && (!seq_ids || !k || !v))) return fail(INS_EINVAL, "ingress arguments");
-    if (q && !q_rot) return fail(INS_EINVAL, "q given without q_rot");
-    if (n == 0) return INS_OK;
-    auto aligned = [](const void *p) { return ((uintptr_t)p & 7u) == 0; };
-    if (!aligned(k) || !aligned(v) || (q && (!aligned(q) || !aligned(q_rot))))
-        return fail(INS_EINVAL, "q/k/v buffers must be 8-byte aligned");
+// The ingress launch shared by ins_ingress and ins_ingress_lanes: `lanes`,
+// when set, replaces q, k and v with the board's packed 24-bit stream.
+static int ingress_launch(ins_cache *c, int32_t n, const int32_t *seq_ids, const int32_t *q,
+                          const int32_t *k, const int32_t *v, const uint8_t *lanes, int32_t *q_rot,
+                          uint32_t flags, void *stream) {
     DeviceGuard dg(c->device);
     cudaStream_t s = (cudaStream_t)stream;
     if (int rc = sync_mirrors(c)) return rc;
@@ -458,7 +453,7 @@ int ins_ingress(ins_cache *c, int32_t n, const int32_t *seq_ids, const int32_t *
     if (int rc = reserve_slots(c, n, seq_ids, h_slots, &lo, &hi, h_new, &n_new)) return rc;
     if (int rc = c->stage_a.upload(sizeof(int64_t) * (size_t)n + sizeof(int2) * (size_t)n_new, s))
         return rc;
-    const int per_tok = (q ? c->g.n_kv * c->g.H : 0) + 2 * c->g.n_kv;
+    const int per_tok = ((q || lanes) ? c->g.n_kv * c->g.H : 0) + 2 * c->g.n_kv;
     const int64_t warps = (int64_t)n * per_tok;
     const int wpb = 8;
     const int64_t blocks = (warps + wpb - 1) / wpb;
@@ -466,8 +461,88 @@ int ins_ingress(ins_cache *c, int32_t n, const int32_t *seq_ids, const int32_t *
                                                     (const int64_t *)c->stage_a.d, q, k, v, q_rot,
                                                     c->d_pool, flags, c->d_status,
                                                     (const int2 *)((const int64_t *)c->stage_a.d + n), n_new,
-                                                    c->d_page_table);
+                                                    c->d_page_table, lanes);
     CK(cudaGetLastError());
+    return INS_OK;
+}
+
+int ins_ingress(ins_cache *c, int32_t n, const int32_t *seq_ids, const int32_t *q,
+                const int32_t *k, const int32_t *v, int32_t *q_rot, uint32_t flags,
+                void *stream) {
+    if (!c) return fail(INS_EINVAL, "cache is NULL");
+    if (n < 0 || (n > 0 && (!seq_ids || !k || !v))) return fail(INS_EINVAL, "ingress arguments");
+    if (q && !q_rot) return fail(INS_EINVAL, "q given without q_rot");
+    if (n == 0) return INS_OK;
+    auto aligned = [](const void *p) { return ((uintptr_t)p & 7u) == 0; };
+    if (!aligned(k) || !aligned(v) || (q && (!aligned(q) || !aligned(q_rot))))
+        return fail(INS_EINVAL, "q/k/v buffers must be 8-byte aligned");
+    return ingress_launch(c, n, seq_ids, q, k, v, nullptr, q_rot, flags, stream);
+}
+
+int ins_ingress_lanes(ins_cache *c, int32_t n, const int32_t *seq_ids, const uint8_t *lanes,
+                      int32_t *q_rot, void *stream) {
+    if (!c) return fail(INS_EINVAL, "cache is NULL");
+    if (n < 0 || (n > 0 && (!seq_ids || !lanes || !q_rot))) return fail(INS_EINVAL, "ingress arguments");
+    if (n == 0) return INS_OK;
+    if (((uintptr_t)lanes & 1u) || ((uintptr_t)q_rot & 7u))
+        return fail(INS_EINVAL, "lanes must be 2-byte aligned, q_rot 8-byte aligned");
+    return ingress_launch(c, n, seq_ids, nullptr, nullptr, nullptr, lanes, q_rot, 0, stream);
+}
+
+int64_t ins_lanes_bytes_per_token(const ins_cache *c) {
+    return c ? (int64_t)c->g.n_kv * (2 + c->g.H) * D * 3 : -1;
+}
+
+// The planes of the board's DDR layout for this cache's row format
+// (DdrLayout.for_quant / planes, hw/ddr_layout.py:111-179): fields first, then
+// beats of 16 bytes; every plane must be a whole beat or a whole fraction of one.
+static int ddr_planes(const ins_cache *c, DdrPlanes &pl, int &maxw) {
+    const int f[4] = {0, c->g.kbytes, c->g.kbytes + c->g.vbytes, c->g.row_bytes};
+    pl.n = 0;
+    maxw = 0;
+    for (int i = 0; i < 3; ++i)
+        for (int a = f[i]; a < f[i + 1];) {
+            const int b = a + 16 < f[i + 1] ? a + 16 : f[i + 1], w = b - a;
+            if (pl.n == 16 || w > 16 || 16 % w) return fail(INS_EINVAL, "row fields do not split into beat planes");
+            pl.lo[pl.n] = a;
+            pl.width[pl.n] = w;
+            ++pl.n;
+            maxw = w > maxw ? w : maxw;
+            a = b;
+        }
+    return INS_OK;
+}
+
+int64_t ins_ddr_image_bytes(const ins_cache *c, int64_t capacity) {
+    if (!c || capacity < 0) return -1;
+    DdrPlanes pl;
+    int maxw;
+    if (ddr_planes(c, pl, maxw)) return -1;
+    const int64_t span = (capacity * maxw + 4095) / 4096 * 4096;   // plane_span, 4 KB pages
+    return (int64_t)c->g.n_kv * pl.n * span;
+}
+
+int ins_cache_ddr_image(ins_cache *c, int32_t seq, int64_t capacity, uint8_t *img, void *stream) {
+    if (!c) return fail(INS_EINVAL, "cache is NULL");
+    if (seq < 0 || seq >= c->cfg.max_seqs) return fail(INS_EINVAL, "sequence id out of range");
+    if (!img) return fail(INS_EINVAL, "image buffer is NULL");
+    const int64_t n = c->h_seq_lens[seq];
+    if (capacity < n)
+        return fail(INS_EBADLEN, std::to_string(n) + " tokens exceeds capacity " + std::to_string(capacity));
+    DdrPlanes pl;
+    int maxw;
+    if (int rc = ddr_planes(c, pl, maxw)) return rc;
+    const int64_t span = (capacity * maxw + 4095) / 4096 * 4096;
+    const int64_t total = (int64_t)c->g.n_kv * pl.n * span;
+    DeviceGuard dg(c->device);
+    cudaStream_t s = (cudaStream_t)stream;
+    CK(cudaMemsetAsync(img, 0, (size_t)total, s));
+    const int64_t threads = n * c->g.n_kv * pl.n;
+    if (threads) {
+        k_ddr_image<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(
+            c->g, c->d_pool, c->d_page_table + (size_t)seq * c->cfg.max_pages_per_seq, n, pl, span, img);
+        CK(cudaGetLastError());
+    }
     return INS_OK;
 }
 

@@ -176,6 +176,37 @@ class PagedCache:
                                        _stream(self.device)))
         return q_rot
 
+    def ingress_lanes(self, seq_ids, lanes) -> torch.Tensor:
+        """ins_ingress from the board's ingress stream: ``lanes`` holds n tokens
+        of ``lanes_bytes_per_token`` bytes (see insitu_b200.wire). Returns the
+        rotated q (device int32, (n, n_kv*groups, d))."""
+        g = self.geo
+        per = int(self._L.ins_lanes_bytes_per_token(self._h))
+        t = torch.as_tensor(lanes)
+        if t.dtype != torch.uint8 or t.numel() % per:
+            raise ValueError(f"lanes must be uint8, a whole number of {per}-byte tokens")
+        t = t.reshape(-1).to(self.device).contiguous()
+        n = t.numel() // per
+        ids, ids_p = _host_array(seq_ids, n, C.c_int32, np.int32)
+        q_rot = torch.empty((n, g.num_heads, g.head_dim), dtype=torch.int32, device=self.device)
+        _lib.check(self._L.ins_ingress_lanes(self._h, n, ids_p, _ptr(t), _ptr(q_rot),
+                                             _stream(self.device)))
+        return q_rot
+
+    @property
+    def lanes_bytes_per_token(self) -> int:
+        return int(self._L.ins_lanes_bytes_per_token(self._h))
+
+    def ddr_image(self, seq: int, capacity: int) -> torch.Tensor:
+        """The board's DDR image of one sequence (ins_cache_ddr_image): a
+        device uint8 tensor of ins_ddr_image_bytes(capacity) bytes."""
+        nb = int(self._L.ins_ddr_image_bytes(self._h, capacity))
+        if nb < 0:
+            _lib.check(_lib.INS_EINVAL)
+        img = torch.empty(nb, dtype=torch.uint8, device=self.device)
+        _lib.check(self._L.ins_cache_ddr_image(self._h, seq, capacity, _ptr(img), _stream(self.device)))
+        return img
+
     def rotate(self, x) -> torch.Tensor:
         """Rotation.apply on the device: (..., d) int32 in, int32 out."""
         t = torch.as_tensor(x)

@@ -298,3 +298,58 @@ class Oracle:
                                       out.reshape(-1), st, threads), "decode_layer")
         stats = np.array([s.as_tuple() for s in st], np.int64).reshape(B, n_kv, 6)
         return out, stats
+
+
+# --------------------------------------------------------------------------
+# The board's byte formats around the cache, restated in numpy (small inputs)
+# --------------------------------------------------------------------------
+
+def unpack_lanes(buf, bits: int, count: int) -> np.ndarray:
+    """unpack_lanes (hw/vectors.py:95-104): LSB-first fields, sign-extended."""
+    acc = int.from_bytes(bytes(np.asarray(buf, dtype=np.uint8)), "little")
+    out = np.empty(count, dtype=np.int64)
+    for i in range(count):
+        f = (acc >> (i * bits)) & ((1 << bits) - 1)
+        out[i] = f - (1 << bits) if f >> (bits - 1) else f
+    return out
+
+
+def ingress_from_stream(stream, n_kv: int, groups: int, d: int = 64, bits: int = 24):
+    """The q, k, v of one token from its ingress stream: per KV head h the
+    vectors [k_h, v_h, q_{h*groups} ..] (VectorSet.ingress_groups,
+    hw/vectors.py:178-196). Returns q (n_kv*groups, d), k, v (n_kv, d)."""
+    vec = d * bits // 8
+    stream = np.asarray(stream, dtype=np.uint8)
+    q = np.empty((n_kv * groups, d), np.int64)
+    k = np.empty((n_kv, d), np.int64)
+    v = np.empty((n_kv, d), np.int64)
+    for h in range(n_kv):
+        base = h * (2 + groups) * vec
+        get = lambda j: unpack_lanes(stream[base + j * vec: base + (j + 1) * vec], bits, d)
+        k[h], v[h] = get(0), get(1)
+        for j in range(groups):
+            q[h * groups + j] = get(2 + j)
+    return q, k, v
+
+
+def ddr_image(rows, kbytes: int, vbytes: int, capacity: int) -> np.ndarray:
+    """DdrLayout.image (hw/ddr_layout.py:96-245) of rows (n, n_kv, row_bytes):
+    planes = the fields (K codes, V codes, norms) cut into 16-byte beats; each
+    plane spans capacity x the widest plane, rounded up to 4 KB; head-major."""
+    rows = np.asarray(rows, dtype=np.uint8)
+    n, heads, rb = rows.shape
+    planes = []
+    for lo, hi in ((0, kbytes), (kbytes, kbytes + vbytes), (kbytes + vbytes, rb)):
+        a = lo
+        while a < hi:
+            b = min(a + 16, hi)
+            planes.append((a, b))
+            a = b
+    span = -(-capacity * max(b - a for a, b in planes) // 4096) * 4096
+    img = np.zeros(heads * len(planes) * span, dtype=np.uint8)
+    for h in range(heads):
+        for p, (a, b) in enumerate(planes):
+            start = (h * len(planes) + p) * span
+            chunk = rows[:, h, a:b].reshape(-1)
+            img[start:start + chunk.size] = chunk
+    return img

@@ -223,3 +223,35 @@ def test_config1_cache_and_selected_steps(orc, config1):
         out, _ = orc.decode_layer(q[None], [rows[:step + 1]], threads=8)
         np.testing.assert_array_equal(out.reshape(-1), config1["out_online"][i],
                                       err_msg=f"step {step}")
+
+
+# -- the board's byte formats (hw/vectors.py, hw/ddr_layout.py) -------------------
+
+def test_ingress_stream_unpacks_to_the_wire_vectors(tbvec):
+    """ingress.hex is the decode token's stream: its lanes are wire_q/k/v."""
+    import oracle
+    q, k, v = oracle.ingress_from_stream(tbvec["ingress_stream"], n_kv=8, groups=4)
+    np.testing.assert_array_equal(q, tbvec["wire_q"])
+    np.testing.assert_array_equal(k, tbvec["wire_k"])
+    np.testing.assert_array_equal(v, tbvec["wire_v"])
+
+
+def test_host_stream_codec_matches_the_golden_stream(tbvec):
+    from insitu_b200 import wire
+    s = wire.ingress_stream(tbvec["wire_q"][None], tbvec["wire_k"][None], tbvec["wire_v"][None])
+    np.testing.assert_array_equal(s, tbvec["ingress_stream"])
+    np.testing.assert_array_equal(wire.unpack_lanes(wire.pack_lanes(tbvec["wire_k"][3]), 24, 64),
+                                  tbvec["wire_k"][3])
+
+
+def test_ddr_image_of_the_golden_cache(tbvec):
+    """ddr_image.hex is DdrLayout.image of the 65-row cache at capacity 65."""
+    import oracle
+    cap, total, head_stride, ports = (int(x) for x in tbvec["ddr_map"])
+    img = oracle.ddr_image(tbvec["cache_rows"], 32, 16, cap)
+    assert img.size == total == 8 * head_stride and ports == 4
+    np.testing.assert_array_equal(img, tbvec["ddr_image"])
+    from insitu_b200 import wire
+    planes = wire.ddr_planes(((0, 32), (32, 48), (48, 52)))
+    for h, t in ((0, 0), (7, 64), (3, 17)):
+        np.testing.assert_array_equal(wire.row_at(img, planes, cap, h, t), tbvec["cache_rows"][t, h])
