@@ -163,6 +163,32 @@ int ins_ingress(ins_cache *cache, int32_t n, const int32_t *seq_ids,
                 const int32_t *q, const int32_t *k, const int32_t *v, int32_t *q_rot,
                 uint32_t flags, void *stream);
 
+/* The seam on the GPU: the host half of kernel.py:211-249 after the
+ * projections. q, k, v are the projections' float32 outputs (device; q [n,
+ * n_kv*groups, d], k and v [n, n_kv, d]); per vector: QK-norm of q and k when
+ * gains are given (rms_norm, ops/norm.py:35-49), q times attn_scale, then
+ * RoPE in float64 and the round-half-even saturating cast to Q(qk_frac) in
+ * 24-bit lanes (cast_after_rope, the reference's default; ops/rope.py:181-198,
+ * ops/convert.py:44-57), or the cast and RoPE in fixed point
+ * (ops/rope.py:150-179). Writes the wire q, k, v (device int32, same shapes;
+ * ins_ingress takes them as they are) and adds to conv (device int64 [3]:
+ * values cast, values saturated, and the largest |float| as the bits of a
+ * double -- ConversionStats, ops/convert.py:25-41; zero it to start).
+ * positions: host int64 [n], each below max_position (else EINVAL, the
+ * reference's ValueError). The RoPE tables are RoPE.build's (ops/rope.py:
+ * 131-148), on the device. */
+typedef struct {
+    const float *q_norm, *k_norm;     /* device [head_dim] QK-norm gains, or NULL */
+    float norm_eps;
+    int32_t cast_after_rope;
+    double attn_scale;                /* 1 / sqrt(head_dim) in the reference */
+    const int64_t *rope_cos, *rope_sin;  /* device [max_position][head_dim / 2], Q(rope_frac) */
+    int32_t rope_frac, max_position;
+} ins_seam_cfg;
+int ins_seam(ins_cache *cache, int32_t n, const float *q, const float *k, const float *v,
+             const int64_t *positions, const ins_seam_cfg *cfg, int32_t *wq, int32_t *wk,
+             int32_t *wv, int64_t *conv, void *stream);
+
 /* ins_ingress fed the board's ingress stream instead of int32 arrays: the
  * byte stream VectorSet.ingress_bytes builds (hw/vectors.py:178-196) -- per
  * token, per KV head h, the vectors k_h, v_h, q_{h*groups} .. q_{h*groups +

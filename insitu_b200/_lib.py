@@ -79,6 +79,14 @@ class Stats(C.Structure):
 
 STATS_FIELDS = tuple(n for n, _ in Stats._fields_)
 
+
+class SeamCfg(C.Structure):
+    """ins_seam_cfg."""
+    _fields_ = [("q_norm", C.c_void_p), ("k_norm", C.c_void_p), ("norm_eps", C.c_float),
+                ("cast_after_rope", C.c_int32), ("attn_scale", C.c_double),
+                ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p), ("rope_frac", C.c_int32),
+                ("max_position", C.c_int32)]
+
 # every symbol the header declares, for the load check
 SYMBOLS = ("ins_abi_version", "ins_bytes_per_token", "ins_cache_create", "ins_cache_destroy",
            "ins_cache_reset", "ins_cache_length", "ins_cache_capacity", "ins_ingress", "ins_rotate",
@@ -86,7 +94,7 @@ SYMBOLS = ("ins_abi_version", "ins_bytes_per_token", "ins_cache_create", "ins_ca
            "ins_last_error", "ins_scan_noalloc", "ins_scan_recomputed", "ins_part_bytes",
            "ins_scan_maxima", "ins_scan_part", "ins_merge_parts", "ins_cache_set_tiles",
            "ins_ingress_lanes", "ins_lanes_bytes_per_token", "ins_ddr_image_bytes",
-           "ins_cache_ddr_image")
+           "ins_cache_ddr_image", "ins_seam")
 
 
 def nvcc() -> str:
@@ -158,6 +166,7 @@ def lib():
     L.ins_ddr_image_bytes.argtypes = [vp, i64]
     L.ins_ddr_image_bytes.restype = i64
     L.ins_cache_ddr_image.argtypes = [vp, i32, i64, vp, vp]
+    L.ins_seam.argtypes = [vp, i32, vp, vp, vp, vp, C.POINTER(SeamCfg), vp, vp, vp, vp, vp]
     L.ins_last_error.restype = C.c_char_p
     _lib = L
     return L

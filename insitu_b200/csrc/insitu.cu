@@ -104,6 +104,7 @@ struct ins_cache {
     std::vector<int32_t> free_pages;
     Staging stage_a;                    // per-call index uploads
     Staging stage_b;
+    Staging stage_c;                    // positions of ins_seam
     ChunkScratch chunk;                 // scratch of the context-parallel scan
     uint64_t gen = 0;                   // bumped by every call that rewrites `chunk`
     struct {                            // context split: phase 1 waiting for phase 2
@@ -390,6 +391,7 @@ int ins_cache_destroy(ins_cache *c) {
     cudaDeviceSynchronize();
     c->stage_a.release();
     c->stage_b.release();
+    c->stage_c.release();
     c->chunk.release();
     if (c->mirror_done) cudaEventDestroy(c->mirror_done);
     cudaFree(c->d_tables);
@@ -503,7 +505,8 @@ static int ddr_planes(const ins_cache *c, DdrPlanes &pl, int &maxw) {
     for (int i = 0; i < 3; ++i)
         for (int a = f[i]; a < f[i + 1];) {
             const int b = a + 16 < f[i + 1] ? a + 16 : f[i + 1], w = b - a;
-            if (pl.n == 16 || w > 16 || 16 % w) return fail(INS_EINVAL, "row fields do not split into beat planes");
+            if (pl.n == 16 || w > 16 || 16 % w || w % 4 || a % 4)
+                return fail(INS_EINVAL, "row fields do not split into beat planes of whole 32-bit words");
             pl.lo[pl.n] = a;
             pl.width[pl.n] = w;
             ++pl.n;
@@ -543,6 +546,49 @@ int ins_cache_ddr_image(ins_cache *c, int32_t seq, int64_t capacity, uint8_t *im
             c->g, c->d_pool, c->d_page_table + (size_t)seq * c->cfg.max_pages_per_seq, n, pl, span, img);
         CK(cudaGetLastError());
     }
+    return INS_OK;
+}
+
+int ins_seam(ins_cache *c, int32_t n, const float *q, const float *k, const float *v,
+             const int64_t *positions, const ins_seam_cfg *cfg, int32_t *wq, int32_t *wk, int32_t *wv,
+             int64_t *conv, void *stream) {
+    if (!c || !cfg) return fail(INS_EINVAL, "cache or seam config is NULL");
+    if (n < 0 || (n > 0 && (!q || !k || !v || !positions || !wq || !wk || !wv || !conv)))
+        return fail(INS_EINVAL, "seam arguments");
+    if (!cfg->rope_cos || !cfg->rope_sin || cfg->max_position < 1 || cfg->rope_frac < 0 ||
+        cfg->rope_frac > 30)
+        return fail(INS_EINVAL, "seam RoPE tables");
+    if (n == 0) return INS_OK;
+    for (int32_t i = 0; i < n; ++i)
+        if (positions[i] < 0 || positions[i] >= cfg->max_position)
+            return fail(INS_EINVAL, "position " + std::to_string(positions[i]) + " beyond the table's " +
+                                        std::to_string(cfg->max_position));
+    DeviceGuard dg(c->device);
+    cudaStream_t s = (cudaStream_t)stream;
+    if (int rc = c->stage_c.reserve(sizeof(int64_t) * (size_t)n)) return rc;
+    std::memcpy(c->stage_c.h, positions, sizeof(int64_t) * (size_t)n);
+    if (int rc = c->stage_c.upload(sizeof(int64_t) * (size_t)n, s)) return rc;
+    SeamArgs a;
+    a.q = q;
+    a.k = k;
+    a.v = v;
+    a.pos = (const int64_t *)c->stage_c.d;
+    a.q_norm = cfg->q_norm;
+    a.k_norm = cfg->k_norm;
+    a.eps = cfg->norm_eps;
+    a.attn_scale = cfg->attn_scale;
+    a.cos_t = cfg->rope_cos;
+    a.sin_t = cfg->rope_sin;
+    a.frac = cfg->rope_frac;
+    a.cast_after_rope = cfg->cast_after_rope;
+    a.wire_bits = 24;
+    a.wq = wq;
+    a.wk = wk;
+    a.wv = wv;
+    a.conv = (unsigned long long *)conv;
+    const int64_t warps = (int64_t)n * (c->g.n_kv * c->g.H + 2 * c->g.n_kv);
+    k_seam<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(c->g, a, n);
+    CK(cudaGetLastError());
     return INS_OK;
 }
 

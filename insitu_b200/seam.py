@@ -1,0 +1,117 @@
+"""The host half of a decode step on the GPU (kernel.py:197-249), up to the
+wire: projections, QK-norm, the attention scale, RoPE and the Q8.16 cast.
+
+* The projections are plain GEMMs and run as library GEMMs: fp16-rounded
+  weights and activations, fp32 products and fp32 accumulation
+  (numerics/fp.py:25-46, ``matvec``). Their accumulation order is the
+  library's, so they match the reference within float32 rounding, not bit for
+  bit -- as the reference's own note on ``matvec`` expects of any order.
+* Everything after them is ``ins_seam`` (one kernel), bit-exact with the
+  reference given the same projection outputs: rms_norm in float32 with
+  numpy's summation order, the scale in float64, RoPE in float64 or in fixed
+  point, round-half-even saturating cast.
+
+The RoPE tables are built here on the host, by the reference's own recipe
+(ops/rope.py:131-148, llama3 scaling ops/rope.py:98-109): the integers are
+the format, like the codebooks.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib
+from .engine import PagedCache, _ptr, _stream
+
+
+@dataclass(frozen=True)
+class RopeScaling:
+    """Llama 3's rescaling of the RoPE frequencies (ops/rope.py:48-109)."""
+    factor: float
+    low_freq_factor: float
+    high_freq_factor: float
+    original_max_position: int
+
+    def apply(self, inv_freq: np.ndarray) -> np.ndarray:
+        f = np.asarray(inv_freq, dtype=np.float64)
+        ctx = float(self.original_max_position)
+        wavelen = 2.0 * np.pi / f
+        low_wl, high_wl = ctx / self.low_freq_factor, ctx / self.high_freq_factor
+        scaled = np.where(wavelen > low_wl, f / self.factor, f)
+        smooth = (ctx / wavelen - self.low_freq_factor) / (self.high_freq_factor - self.low_freq_factor)
+        smoothed = (1.0 - smooth) * scaled / self.factor + smooth * scaled
+        between = (wavelen <= low_wl) & (wavelen >= high_wl)
+        return np.where(between, smoothed, scaled)
+
+
+def rope_tables(d: int, max_position: int, theta: float = 10000.0, frac: int = 15,
+                scaling: RopeScaling | None = None):
+    """(cos, sin): int64 [max_position, d/2] in Q(32, frac), round half even."""
+    if d % 2:
+        raise ValueError(f"head_dim={d} must be even")
+    half = d // 2
+    inv = 1.0 / (theta ** (np.arange(0, half, dtype=np.float64) * 2.0 / d))
+    if scaling is not None:
+        inv = scaling.apply(inv)
+    ang = np.arange(max_position, dtype=np.float64)[:, None] * inv[None, :]
+    lim = (1 << 31) - 1
+    q = lambda x: np.clip(np.rint(x * (1 << frac)).astype(np.int64), -lim - 1, lim)
+    return q(np.cos(ang)), q(np.sin(ang))
+
+
+def project(w: torch.Tensor, x: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """``matvec`` (numerics/fp.py:25-46) on the GPU: fp16-rounded operands,
+    fp32 products and accumulation. w (out, in), x (n, in) -> (n, out) fp32."""
+    w16 = w.to(torch.float16).to(torch.float32)
+    x16 = x.to(torch.float16).to(torch.float32)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False     # fp32 arithmetic, not TF32
+    try:
+        y = x16 @ w16.T
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    return y if bias is None else y + bias.to(torch.float32)
+
+
+class Seam:
+    """The seam of one layer on the cache's GPU."""
+
+    def __init__(self, pc: PagedCache, *, max_position: int = 4096, theta: float = 10000.0,
+                 scaling: RopeScaling | None = None, rope_frac: int = 15, q_norm=None, k_norm=None,
+                 norm_eps: float = 1e-6, cast_after_rope: bool = True):
+        self.pc = pc
+        d = pc.geo.head_dim
+        cos, sin = rope_tables(d, max_position, theta, rope_frac, scaling)
+        dev = pc.device
+        self.cos = torch.from_numpy(cos).to(dev)
+        self.sin = torch.from_numpy(sin).to(dev)
+        g = lambda w: None if w is None else torch.as_tensor(np.asarray(w, np.float32)).to(dev)
+        self.q_norm, self.k_norm = g(q_norm), g(k_norm)
+        self.cfg = _lib.SeamCfg(_ptr(self.q_norm), _ptr(self.k_norm), float(norm_eps),
+                                int(bool(cast_after_rope)), float(1.0 / np.sqrt(d)), _ptr(self.cos),
+                                _ptr(self.sin), rope_frac, max_position)
+
+    def __call__(self, q, k, v, positions):
+        """Projection outputs (float32: q (n, Hq, d), k and v (n, n_kv, d)) ->
+        the wire q, k, v (device int32) and the conversion statistics
+        {n_values, n_saturated, max_abs_float}."""
+        pc = self.pc
+        t = lambda x: torch.as_tensor(x).to(pc.device, torch.float32).contiguous()
+        q, k, v = t(q), t(k), t(v)
+        n = q.shape[0]
+        pos = np.ascontiguousarray(np.broadcast_to(np.asarray(positions, np.int64), (n,)))
+        wq = torch.empty(q.shape, dtype=torch.int32, device=pc.device)
+        wk = torch.empty(k.shape, dtype=torch.int32, device=pc.device)
+        wv = torch.empty(v.shape, dtype=torch.int32, device=pc.device)
+        conv = torch.zeros(3, dtype=torch.int64, device=pc.device)
+        _lib.check(pc._L.ins_seam(pc._h, n, _ptr(q), _ptr(k), _ptr(v), pos.ctypes.data,
+                                  C.byref(self.cfg), _ptr(wq), _ptr(wk), _ptr(wv), _ptr(conv),
+                                  _stream(pc.device)))
+        c = conv.cpu().numpy()
+        stats = {"n_values": int(c[0]), "n_saturated": int(c[1]),
+                 "max_abs_float": float(np.frombuffer(c[2:3].tobytes(), np.float64)[0])}
+        return wq, wk, wv, stats

@@ -39,6 +39,12 @@ What it writes, and what each file pins:
     online softmax. Stores the wire k/v of every step, the wire q and online
     output of selected steps, and the final packed cache bytes.
 
+``seam.npz``
+    The host half after the projections: seeded float32
+    projection outputs through QK-norm, the attention scale, RoPE and the
+    Q8.16 cast in both orders, with and without QK-norm, by the reference's
+    own functions; rows of its Llama-3.2 RoPE tables.
+
 ``tables.npz``
     Codebook integers (gaussian and uniform, 1..8 bits), the exp table and its
     constants, and PCG64 sign diagonals for a few seeds and round counts.
@@ -378,6 +384,72 @@ def make_tables() -> dict:
     return g
 
 
+# --------------------------------------------------------------------------
+# the seam: projection outputs -> QK-norm -> RoPE / cast -> wire (kernel.py:211-249)
+# --------------------------------------------------------------------------
+
+def make_seam() -> dict:
+    """The host half after the projections, through the reference's own
+    functions in kernel.py's order: QK-norm (ops/norm.py:35-49), the
+    attention scale, then RoPE in float and the cast (cast_after_rope, the
+    default) or the cast and RoPE in fixed point (ops/rope.py:150-198,
+    ops/convert.py:44-57). Projection outputs are seeded float32 of
+    realistic size; the RoPE tables are Llama-3.2's (theta 500000, llama3
+    scaling factor 32, low 1, high 4, original 8192)."""
+    from kernel.config import FixedFormat
+    from kernel.numerics.fixed import Q
+    from kernel.ops.convert import ConversionStats, to_fixed
+    from kernel.ops.norm import rms_norm
+    from kernel.ops.rope import RoPE, RopeScaling
+
+    rng = np.random.default_rng(2024)
+    n, hq, hk, d = 24, 32, 8, 64
+    scal = RopeScaling(factor=32.0, low_freq_factor=1.0, high_freq_factor=4.0,
+                       original_max_position=8192)
+    max_pos = 1 << 17
+    rope = RoPE.build(d, max_pos, 500000.0, 15, scal)
+    fmt = FixedFormat()
+    qk_q = Q(fmt.qk_width, fmt.qk_frac, fmt.saturate)
+    g = {}
+    g["pos"] = np.concatenate([np.arange(8), rng.integers(8, max_pos, n - 9), [max_pos - 1]]).astype(np.int64)
+    g["rope_rows"] = np.array([0, 1, 4095, 8191, 65535, max_pos - 1], dtype=np.int64)
+    g["rope_cos_rows"] = rope.cos[g["rope_rows"]]
+    g["rope_sin_rows"] = rope.sin[g["rope_rows"]]
+    q = (rng.standard_normal((n, hq, d)) * 2.5).astype(np.float32)
+    k = (rng.standard_normal((n, hk, d)) * 2.5).astype(np.float32)
+    v = (rng.standard_normal((n, hk, d)) * 1.5).astype(np.float32)
+    q[3, 5, 7] = 200.0                      # saturates the 24-bit wire after the scale
+    k[4, 1, 40] = -129.0
+    v[5, 2, 3] = 128.0
+    g["q"], g["k"], g["v"] = q, k, v
+    g["q_norm"] = (1.0 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    g["k_norm"] = (1.0 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    eps = 1e-6
+    scale = 1.0 / np.sqrt(d)
+    for norm in (False, True):
+        for after in (True, False):
+            qq, kk = q, k
+            if norm:
+                qq = rms_norm(qq, g["q_norm"], eps)
+                kk = rms_norm(kk, g["k_norm"], eps)
+            qq = qq * scale
+            conv = ConversionStats()
+            if after:
+                qf = rope.apply_float(qq, g["pos"][:, None])
+                kf = rope.apply_float(kk, g["pos"][:, None])
+                wq, wk, wv = to_fixed(qf, qk_q, conv), to_fixed(kf, qk_q, conv), to_fixed(v, qk_q, conv)
+            else:
+                wq, wk, wv = to_fixed(qq, qk_q, conv), to_fixed(kk, qk_q, conv), to_fixed(v, qk_q, conv)
+                wq = rope.apply(wq, g["pos"][:, None], fmt.qk_frac)
+                wk = rope.apply(wk, g["pos"][:, None], fmt.qk_frac)
+            tag = f"n{int(norm)}a{int(after)}"
+            g[f"wq_{tag}"], g[f"wk_{tag}"], g[f"wv_{tag}"] = (np.asarray(w, np.int32) for w in (wq, wk, wv))
+            g[f"conv_{tag}"] = np.array([conv.n_values, conv.n_saturated], dtype=np.int64)
+            g[f"convmax_{tag}"] = np.array([conv.max_abs_float], dtype=np.float64)
+    g["eps"] = np.array([eps], dtype=np.float32)
+    return g
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--ref", default="/root/reference")
@@ -387,6 +459,7 @@ def main(argv=None) -> int:
     np.savez_compressed(os.path.join(HERE, "tbvec_c64_k4v2.npz"), **make_tbvec(a.ref))
     np.savez_compressed(os.path.join(HERE, "tables.npz"), **make_tables())
     np.savez_compressed(os.path.join(HERE, "widths.npz"), **make_widths())
+    np.savez_compressed(os.path.join(HERE, "seam.npz"), **make_seam())
     if not a.skip_config1:
         np.savez_compressed(os.path.join(HERE, "config1_ctx512.npz"), **make_config1())
     for n in sorted(os.listdir(HERE)):
