@@ -37,8 +37,9 @@ layer after layer (ingress + scan per layer); a step = one token through all
 16 layers.
 
 `--formats`: the board's byte formats around the cache -- ingress of a
-256-token batch from int32 arrays and from the 24-bit lane stream, and the DDR
-image of the 1M-token sequence (GB/s of rows gathered into planes).
+256-token batch from int32 arrays and from the 24-bit lane stream, the seam
+(QK-norm, RoPE, cast) of a 256-token batch, and the DDR image of the
+1M-token sequence (GB/s of rows gathered into planes).
 """
 
 from __future__ import annotations
@@ -721,6 +722,13 @@ def run_formats(args):
     T = pc.length(0)
     cap = T
     ms_img = _time_steps(lambda i: pc.ddr_image(0, cap), K, W, local)
+    from insitu_b200.seam import Seam
+    sm = Seam(pc, max_position=1 << 17, theta=500000.0)
+    fq = torch.randn((nb, 32, D), device=f"cuda:{local}", generator=gen)
+    fk = torch.randn((nb, N_KV, D), device=f"cuda:{local}", generator=gen)
+    fv = torch.randn((nb, N_KV, D), device=f"cuda:{local}", generator=gen)
+    pos = np.arange(nb) + 1000
+    ms_seam = _time_steps(lambda i: sm(fq, fk, fv, pos), K, W, local)
     pc.status()
     rows = 8 * T
     if rank == 0:
@@ -730,6 +738,7 @@ def run_formats(args):
             "ingress_256_tokens": {"int32_us": round(ms_i32 / K * 1e3, 2),
                                    "lanes_us": round(ms_lanes / K * 1e3, 2),
                                    "lane_bytes": int(lanes.numel())},
+            "seam_256_tokens_us": round(ms_seam / K * 1e3, 2),
             "ddr_image": {"tokens": T, "us": round(ms_img / K * 1e3, 2),
                           "GB/s_rows": round(rows * ROW_BYTES / (ms_img / K * 1e-3) / 1e9, 2),
                           "image_bytes": int(pc.ddr_image(0, cap).numel())},
