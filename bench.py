@@ -38,8 +38,9 @@ layer after layer (ingress + scan per layer); a step = one token through all
 
 `--formats`: the board's byte formats around the cache -- ingress of a
 256-token batch from int32 arrays and from the 24-bit lane stream, the seam
-(QK-norm, RoPE, cast) of a 256-token batch, and the DDR image of the
-1M-token sequence (GB/s of rows gathered into planes).
+(QK-norm, RoPE, cast) of a 256-token batch, a 256-token prefill chunk on a
+32K context, and the DDR image of the 1M-token sequence (GB/s of rows
+gathered into planes).
 """
 
 from __future__ import annotations
@@ -729,6 +730,13 @@ def run_formats(args):
     fv = torch.randn((nb, N_KV, D), device=f"cuda:{local}", generator=gen)
     pos = np.arange(nb) + 1000
     ms_seam = _time_steps(lambda i: sm(fq, fk, fv, pos), K, W, local)
+    # a prefill chunk of 256 tokens on a 32K context, all KV heads
+    pdec, pgen = make_decoder(32768, (K + W) * nb + 8, local, seed=6)
+    pq, pk, pv = step_inputs(pgen, nb, local)
+    T_pre = pdec.pc.length(0)
+    ms_pre = _time_steps(lambda i: pdec.prefill_attend(0, pq[:, 0], pk[:, 0], pv[:, 0]), K, W, local)
+    pre_rows = sum(8 * sum(T_pre + (W + i) * nb + j + 1 for j in range(nb)) for i in range(K))
+    pdec.close()
     pc.status()
     rows = 8 * T
     if rank == 0:
@@ -739,6 +747,8 @@ def run_formats(args):
                                    "lanes_us": round(ms_lanes / K * 1e3, 2),
                                    "lane_bytes": int(lanes.numel())},
             "seam_256_tokens_us": round(ms_seam / K * 1e3, 2),
+            "prefill_256_on_32K": {"us": round(ms_pre / K * 1e3, 2),
+                                   "GB/s_rows": round(pre_rows * ROW_BYTES / (ms_pre * 1e-3) / 1e9, 2)},
             "ddr_image": {"tokens": T, "us": round(ms_img / K * 1e3, 2),
                           "GB/s_rows": round(rows * ROW_BYTES / (ms_img / K * 1e-3) / 1e9, 2),
                           "image_bytes": int(pc.ddr_image(0, cap).numel())},

@@ -110,6 +110,43 @@ class CompressedAttention:
         stats = AttentionStats.from_row(st[0, head].cpu().numpy())
         return y.reshape(np.shape(q_rot)), stats
 
+    def _attend_batch(self, q_rot, kv, base, mode):
+        """Query i of a prefill against cached tokens [0, base + i]: one scan
+        launch, the sequence entered once per query with its causal length."""
+        q = np.asarray(q_rot if not isinstance(q_rot, torch.Tensor) else q_rot.cpu()).astype(np.int64)
+        if q.ndim == 2:
+            q = q[:, None, :]
+        n, heads = q.shape[0], q.shape[1]
+        pc, head, T = self._resident(kv, heads)
+        lengths = base + 1 + np.arange(n, dtype=np.int64)
+        if n and lengths[-1] > T:
+            raise ValueError(f"query {n - 1} attends token {lengths[-1] - 1}; the cache holds {T}")
+        g = pc.geo
+        full = torch.zeros((n, g.num_heads, g.head_dim), dtype=torch.int32)
+        full[:, head * g.kv_groups:(head + 1) * g.kv_groups] = torch.from_numpy(q.astype(np.int32))
+        out, st = pc.scan([0] * n, full, lengths=lengths, mode=mode)
+        pc.status()
+        y = out[:, head * g.kv_groups:(head + 1) * g.kv_groups].cpu().numpy()
+        rows = st[:, head].cpu().numpy()
+        stats = AttentionStats.from_row(rows[0]) if n else AttentionStats()
+        for r in rows[1:]:
+            stats.merge(AttentionStats.from_row(r))
+        return y.reshape(np.shape(q_rot)), stats
+
+    def attend_online_batch(self, q_rot, kv, base: int = 0, trace=None):
+        """attend_online for every query token of a prefill (ops/attention.py:
+        794-871): query i attends cached tokens [0, base + i]. Outputs are the
+        per-token loop's, as the reference pins its batch form to; the
+        statistics are the per-token ones merged (AttentionStats.merge)."""
+        if self.score_mode != "fused":
+            raise ValueError("attend_online_batch runs the fused (architecture B) path only")
+        return self._attend_batch(q_rot, kv, base, "online")
+
+    def attend_causal_batch(self, q_rot, kv, base: int = 0, tile: int = 256, trace=None):
+        """attend_two_pass for every query token of a prefill
+        (ops/attention.py:517-670), causal as attend_online_batch."""
+        return self._attend_batch(q_rot, kv, base, "two_pass")
+
     def attend_online(self, q_rot, kv, trace=None):
         """One streaming pass with a running maximum (ops/attention.py:451-513)."""
         if self.score_mode != "fused":

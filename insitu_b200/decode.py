@@ -47,6 +47,18 @@ class DecodeAttention:
         q_rot = self.pc.ingress(ids, k, v, q)
         return self.pc.scan(ids, q_rot, mode=mode, out=out, stats_out=stats_out)
 
+    def prefill_attend(self, seq: int, q, k, v, *, mode: str = "online"):
+        """A prefill chunk of one sequence: append its n tokens (one ingress
+        launch), then every token attends the cache up to and including
+        itself (one scan launch, the sequence entered n times with causal
+        lengths) -- the attend_online_batch / attend_causal_batch of
+        ops/attention.py:517-871 for all KV heads. q (n, Hq, d), k/v (n, n_kv,
+        d) int32. Returns out (n, Hq, d) and stats (n, n_kv, 6)."""
+        n = k.shape[0]
+        base = self.pc.length(seq)
+        q_rot = self.pc.ingress([seq] * n, k, v, q)
+        return self.pc.scan([seq] * n, q_rot, lengths=base + 1 + np.arange(n), mode=mode)
+
     @staticmethod
     def merge_heads(out: torch.Tensor) -> torch.Tensor:
         """(B, heads, d) -> (B, heads*d), ops/project.py:67-74."""
