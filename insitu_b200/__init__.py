@@ -18,7 +18,7 @@ from .config import FixedFormat, Geometry, QuantConfig
 
 __all__ = ["FixedFormat", "Geometry", "QuantConfig", "Rotation", "KVQuantizer", "CompressedKV",
            "KVCache", "CompressedCache", "CompressedAttention", "AttentionStats",
-           "DecodeAttention", "PagedCache"]
+           "DecodeAttention", "PagedCache", "AttentionLayer"]
 
 
 def __getattr__(name):
@@ -36,6 +36,9 @@ def __getattr__(name):
     if name in ("CompressedAttention", "AttentionStats"):
         from . import attention
         return getattr(attention, name)
+    if name == "AttentionLayer":
+        from .layer import AttentionLayer
+        return AttentionLayer
     if name == "DecodeAttention":
         from .decode import DecodeAttention
         return DecodeAttention

@@ -1,0 +1,97 @@
+"""A whole attention layer's decode step on the GPU (kernel.py:178-357):
+projections, the seam, the compressed cache and its scan, and the output
+projection with the inverse rotation folded into W_o (ops/output.py:49-84,
+weights.py:70-109).
+
+Integer stages are bit-exact with the reference; the four projections are
+library GEMMs over fp16-rounded operands with fp32 products and sums, so y
+matches the reference's ``AttentionKernel.forward`` within float32 rounding
+of those sums -- and, where a float lands within that rounding of a Q8.16
+half-way point, within one wire LSB.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from .config import FixedFormat, Geometry, QuantConfig
+from .decode import DecodeAttention
+from .rotate import Rotation
+from .seam import RopeScaling, Seam, project
+
+
+def fold_o_proj(o_proj, rotation: Rotation, num_heads: int, head_dim: int) -> np.ndarray:
+    """W_o' = W_o @ blockdiag_h(R^T), once at weight-load time, in float64,
+    returned in the input's dtype (ops/output.py:49-80). o_proj is
+    (hidden, num_heads * head_dim), head-major like merge_heads."""
+    w = np.asarray(o_proj)
+    if w.shape[1] != num_heads * head_dim:
+        raise ValueError(f"o_proj takes {w.shape[1]} inputs; the block gives {num_heads} x {head_dim}")
+    r = rotation.matrix().T
+    block = np.zeros((num_heads * head_dim,) * 2, dtype=np.float64)
+    for h in range(num_heads):
+        block[h * head_dim:(h + 1) * head_dim, h * head_dim:(h + 1) * head_dim] = r
+    return (w.astype(np.float64) @ block).astype(w.dtype)
+
+
+class AttentionLayer:
+    """One layer: x (tokens, hidden) fp32 in, y (tokens, hidden) fp32 out,
+    its compressed cache on the GPU. ``w_o`` is the checkpoint's W_o; pass
+    ``o_folded=True`` when it already carries the fold."""
+
+    def __init__(self, w_q, w_k, w_v, w_o, *, hidden: int, num_heads: int, num_kv_heads: int,
+                 head_dim: int = 64, quant: QuantConfig | None = None, fmt: FixedFormat | None = None,
+                 rope_theta: float = 10000.0, max_position: int = 4096,
+                 rope_scaling: RopeScaling | None = None, q_norm=None, k_norm=None,
+                 norm_eps: float = 1e-6, biases=(None, None, None, None), o_folded: bool = False,
+                 cast_after_rope: bool = True, softmax: str = "two_pass", capacity: int = 4096,
+                 device=None):
+        # "two_pass" is AttentionKernel's default (kernel.py:117-124); the
+        # board runs "online"
+        self.softmax = softmax
+        self.quant = quant or QuantConfig(key_bits=4, value_bits=2)
+        self.fmt = fmt or FixedFormat()
+        self.hidden, self.hq, self.hk, self.d = hidden, num_heads, num_kv_heads, head_dim
+        self.dec = DecodeAttention(self.quant, self.fmt, Geometry(num_kv_heads, num_heads // num_kv_heads, head_dim),
+                                   max_seqs=1, capacity=capacity, device=device)
+        dev = self.dec.pc.device
+        if not o_folded:
+            w_o = fold_o_proj(np.asarray(w_o, np.float64), Rotation.for_quant(self.quant, head_dim),
+                              num_heads, head_dim)
+        f16 = lambda w: torch.as_tensor(np.asarray(w, dtype=np.float16)).to(dev)
+        self.w_q, self.w_k, self.w_v, self.w_o = f16(w_q), f16(w_k), f16(w_v), f16(w_o)
+        b = lambda x: None if x is None else torch.as_tensor(np.asarray(x, np.float32)).to(dev)
+        self.b_q, self.b_k, self.b_v, self.b_o = (b(x) for x in biases)
+        self.seam = Seam(self.dec.pc, max_position=max_position, theta=rope_theta, scaling=rope_scaling,
+                         rope_frac=self.fmt.centroid_frac, q_norm=q_norm, k_norm=k_norm,
+                         norm_eps=norm_eps, cast_after_rope=cast_after_rope)
+        self.conversion = {"n_values": 0, "n_saturated": 0, "max_abs_float": 0.0}
+
+    def forward(self, x, positions=None):
+        """Rows of x are decode tokens, in order (a prefill when there are
+        several). Returns y (tokens, hidden) fp32 on the device and the
+        attention output (tokens, num_heads * head_dim) int64 Q(acc_frac)."""
+        pc = self.dec.pc
+        x = torch.as_tensor(x).to(pc.device, torch.float32)
+        if x.ndim == 1:
+            x = x[None]
+        n = x.shape[0]
+        T = pc.length(0)
+        pos = np.arange(T, T + n) if positions is None else np.asarray(positions, np.int64)
+        q = project(self.w_q, x, self.b_q).reshape(n, self.hq, self.d)
+        k = project(self.w_k, x, self.b_k).reshape(n, self.hk, self.d)
+        v = project(self.w_v, x, self.b_v).reshape(n, self.hk, self.d)
+        wq, wk, wv, st = self.seam(q, k, v, pos)
+        self.last_wire = (wq, wk, wv)
+        self.conversion["n_values"] += st["n_values"]
+        self.conversion["n_saturated"] += st["n_saturated"]
+        self.conversion["max_abs_float"] = max(self.conversion["max_abs_float"], st["max_abs_float"])
+        out, _ = self.dec.prefill_attend(0, wq, wk, wv, mode=self.softmax)
+        merged = out.reshape(n, self.hq * self.d)
+        acc = merged.to(torch.float64) / float(1 << self.fmt.qk_frac)      # Q.to_float
+        y = project(self.w_o, acc, self.b_o)
+        return y, merged
+
+    def close(self) -> None:
+        self.dec.close()

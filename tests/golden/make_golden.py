@@ -45,6 +45,12 @@ What it writes, and what each file pins:
     Q8.16 cast in both orders, with and without QK-norm, by the reference's
     own functions; rows of its Llama-3.2 RoPE tables.
 
+``layer.npz``
+    A whole small Llama-shaped layer (hidden 256, 4/2 heads, d 64) decoded
+    token by token through AttentionKernel.forward: x, the fp16 weights (W_o
+    with R folded in, and without), the outputs y, the wire and attention
+    output taps; and one W_o fold (ops/output.py) on its own.
+
 ``tables.npz``
     Codebook integers (gaussian and uniform, 1..8 bits), the exp table and its
     constants, and PCG64 sign diagonals for a few seeds and round counts.
@@ -450,6 +456,43 @@ def make_seam() -> dict:
     return g
 
 
+# --------------------------------------------------------------------------
+# a whole layer: x -> projections -> seam -> cache + scan -> W_o' (kernel.py:178-357)
+# --------------------------------------------------------------------------
+
+def make_layer(n_steps: int = 40) -> dict:
+    """AttentionKernel.forward one token at a time on a small Llama-shaped
+    layer (hidden 256, 4 query heads, 2 KV heads, d 64, theta 500000,
+    4b K / 2b V), weights from Weights.random (seed 0, which folds R into
+    W_o), x ~ N(0, 1); the taps give the wire and the attention output."""
+    from kernel.config import KernelConfig, ModelConfig, QuantConfig
+    from kernel.kernel import AttentionKernel
+    from kernel.ops.output import fold_o_proj
+    from kernel.ops.rotate import Rotation
+
+    m = ModelConfig(hidden_size=256, num_heads=4, num_kv_heads=2, head_dim=64,
+                    rope_theta=500000.0, max_position=4096)
+    cfg = KernelConfig(model=m, quant=QuantConfig(key_bits=4, value_bits=2, seed=0))
+    k = AttentionKernel(cfg, capacity=n_steps + 8)
+    taps = {}
+    k.on_stage = lambda name, a: taps.setdefault(name, []).append(np.array(a))
+    rng = np.random.default_rng(256)
+    x = rng.standard_normal((n_steps, m.hidden_size)).astype(np.float32)
+    ys = [k.forward(x[i:i + 1])[0][0] for i in range(n_steps)]
+    w = k.weights
+    g = {"x": x, "y": np.stack(ys).astype(np.float32),
+         "w_q": np.asarray(w.q, np.float16), "w_k": np.asarray(w.k, np.float16),
+         "w_v": np.asarray(w.v, np.float16), "w_o_folded": np.asarray(w.o, np.float16),
+         "w_o": np.asarray(w.o_unrotated, np.float16)}
+    for name in ("wire.q", "wire.k", "wire.v", "out"):
+        g[name.replace(".", "_")] = np.concatenate(taps[name]).astype(np.int64)
+    # the fold on its own, from a float32 W_o (ops/output.py:49-80)
+    o32 = (rng.standard_normal((m.hidden_size, 256)) / 16).astype(np.float32)
+    g["fold_in"] = o32
+    g["fold_out"] = fold_o_proj(o32.astype(np.float64), Rotation.for_quant(cfg.quant, 64), m)
+    return g
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--ref", default="/root/reference")
@@ -460,6 +503,7 @@ def main(argv=None) -> int:
     np.savez_compressed(os.path.join(HERE, "tables.npz"), **make_tables())
     np.savez_compressed(os.path.join(HERE, "widths.npz"), **make_widths())
     np.savez_compressed(os.path.join(HERE, "seam.npz"), **make_seam())
+    np.savez_compressed(os.path.join(HERE, "layer.npz"), **make_layer())
     if not a.skip_config1:
         np.savez_compressed(os.path.join(HERE, "config1_ctx512.npz"), **make_config1())
     for n in sorted(os.listdir(HERE)):
