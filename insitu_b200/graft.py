@@ -33,6 +33,11 @@ class GpuKernelAttention(nn.Module):
         self.layer = layer
         self.layer_idx = layer_idx
         self.n_kv, self.head_dim = n_kv, head_dim
+        # set by a router: refuse more than one token per call, and report
+        # each call (layer index, the layer, its attention output, start and
+        # end events on the launching stream)
+        self.decode_only = False
+        self.observer = None
 
     def forward(self, hidden_states, *args, **kwargs):
         x = hidden_states
@@ -42,11 +47,21 @@ class GpuKernelAttention(nn.Module):
         if x.shape[0] != 1:
             raise NotImplementedError(f"batch of {x.shape[0]}: one sequence per grafted block "
                                       "(attention_mask is not honoured)")
+        if self.decode_only and x.shape[1] != 1:
+            raise RuntimeError(f"layer {self.layer_idx} got {x.shape[1]} tokens at once; this "
+                               "route is one token at a time")
         positions = kwargs.get("position_ids")
         if positions is None:
             positions = kwargs.get("cache_position")
         pos = None if positions is None else positions.reshape(-1).detach().cpu().numpy().astype(np.int64)
-        y, _ = self.layer.forward(x[0].float(), pos)
+        hook = self.observer
+        if hook is not None:
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0.record()
+        y, merged = self.layer.forward(x[0].float(), pos)
+        if hook is not None:
+            t1.record()
+            hook(self.layer_idx, self.layer, merged, t0, t1)
         cache = kwargs.get("past_key_values")
         if cache is not None:
             filler = torch.zeros((1, self.n_kv, x.shape[1], self.head_dim), dtype=x.dtype, device=x.device)
@@ -76,8 +91,10 @@ def _rope(config):
 
 def build_from_layer(attn_module, config, *, quant: QuantConfig | None = None,
                      fmt: FixedFormat | None = None, capacity: int = 4096, layer_idx: int = 0,
-                     device=None) -> GpuKernelAttention:
-    """A GpuKernelAttention from an attention module's weights (W_o is folded)."""
+                     device=None, decoder=None, seq: int = 0,
+                     softmax: str = "two_pass") -> GpuKernelAttention:
+    """A GpuKernelAttention from an attention module's weights (W_o is folded).
+    ``decoder``/``seq`` place its cache in a shared DecodeAttention's slot."""
     w = lambda n: getattr(attn_module, f"{n}_proj").weight.detach().float().cpu().numpy()
 
     def b(n):
@@ -98,18 +115,20 @@ def build_from_layer(attn_module, config, *, quant: QuantConfig | None = None,
                            max_position=getattr(config, "max_position_embeddings", 4096),
                            rope_scaling=scaling, q_norm=gain("q_norm"), k_norm=gain("k_norm"),
                            norm_eps=eps, biases=(b("q"), b("k"), b("v"), b("o")), capacity=capacity,
-                           device=device)
+                           device=device, decoder=decoder, seq=seq, softmax=softmax)
     return GpuKernelAttention(layer, layer_idx, hk, d)
 
 
-def graft(model, layers, **kw) -> dict:
+def graft(model, layers, *, slots: dict | None = None, **kw) -> dict:
     """Replace model.model.layers[i].self_attn for each i; returns the
-    replaced modules (for ungraft)."""
+    replaced modules (for ungraft). ``slots`` maps a layer to its sequence
+    slot in a shared ``decoder=`` passed through ``kw``."""
     original = {}
     for i in layers:
         blk = model.model.layers[i]
         original[i] = blk.self_attn
-        blk.self_attn = build_from_layer(blk.self_attn, model.config, layer_idx=i, **kw)
+        extra = {} if slots is None else {"seq": slots[i]}
+        blk.self_attn = build_from_layer(blk.self_attn, model.config, layer_idx=i, **extra, **kw)
     return original
 
 

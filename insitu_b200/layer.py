@@ -46,15 +46,25 @@ class AttentionLayer:
                  rope_scaling: RopeScaling | None = None, q_norm=None, k_norm=None,
                  norm_eps: float = 1e-6, biases=(None, None, None, None), o_folded: bool = False,
                  cast_after_rope: bool = True, softmax: str = "two_pass", capacity: int = 4096,
-                 device=None):
+                 device=None, decoder: DecodeAttention | None = None, seq: int = 0):
         # "two_pass" is AttentionKernel's default (kernel.py:117-124); the
         # board runs "online"
         self.softmax = softmax
         self.quant = quant or QuantConfig(key_bits=4, value_bits=2)
         self.fmt = fmt or FixedFormat()
         self.hidden, self.hq, self.hk, self.d = hidden, num_heads, num_kv_heads, head_dim
-        self.dec = DecodeAttention(self.quant, self.fmt, Geometry(num_kv_heads, num_heads // num_kv_heads, head_dim),
-                                   max_seqs=1, capacity=capacity, device=device)
+        geo = Geometry(num_kv_heads, num_heads // num_kv_heads, head_dim)
+        # a shared decoder holds several layers' caches as its sequences (one
+        # page pool, layer = sequence slot); this layer then does not own it
+        self._owns_dec = decoder is None
+        if decoder is None:
+            decoder = DecodeAttention(self.quant, self.fmt, geo, max_seqs=1, capacity=capacity,
+                                      device=device)
+        elif decoder.geo != geo or decoder.pc.quant != self.quant or decoder.pc.fmt != self.fmt:
+            raise ValueError("the shared decoder was built for another geometry or format")
+        if not 0 <= seq < decoder.pc.max_seqs:
+            raise ValueError(f"sequence slot {seq} outside the decoder's {decoder.pc.max_seqs}")
+        self.dec, self.seq = decoder, seq
         dev = self.dec.pc.device
         if not o_folded:
             w_o = fold_o_proj(np.asarray(w_o, np.float64), Rotation.for_quant(self.quant, head_dim),
@@ -77,21 +87,23 @@ class AttentionLayer:
         if x.ndim == 1:
             x = x[None]
         n = x.shape[0]
-        T = pc.length(0)
+        T = pc.length(self.seq)
         pos = np.arange(T, T + n) if positions is None else np.asarray(positions, np.int64)
         q = project(self.w_q, x, self.b_q).reshape(n, self.hq, self.d)
         k = project(self.w_k, x, self.b_k).reshape(n, self.hk, self.d)
         v = project(self.w_v, x, self.b_v).reshape(n, self.hk, self.d)
         wq, wk, wv, st = self.seam(q, k, v, pos)
         self.last_wire = (wq, wk, wv)
+        self.last_conversion = st
         self.conversion["n_values"] += st["n_values"]
         self.conversion["n_saturated"] += st["n_saturated"]
         self.conversion["max_abs_float"] = max(self.conversion["max_abs_float"], st["max_abs_float"])
-        out, _ = self.dec.prefill_attend(0, wq, wk, wv, mode=self.softmax)
+        out, self.last_stats = self.dec.prefill_attend(self.seq, wq, wk, wv, mode=self.softmax)
         merged = out.reshape(n, self.hq * self.d)
         acc = merged.to(torch.float64) / float(1 << self.fmt.qk_frac)      # Q.to_float
         y = project(self.w_o, acc, self.b_o)
         return y, merged
 
     def close(self) -> None:
-        self.dec.close()
+        if self._owns_dec:
+            self.dec.close()
