@@ -46,7 +46,66 @@ DEFAULT_KEY_BITS = 4
 DEFAULT_VALUE_BITS = 2
 
 
-class GpuLayers:
+class RouteCounters:
+    """What a route did, so a run can say what happened rather than that it
+    finished (the counters and summary of host/fpga_layers.py:125-134,
+    258-284). Host logic only."""
+
+    def __init__(self, n_layers: int, verified: bool):
+        self.n_layers, self.verified = n_layers, verified
+        self.steps = 0            # layer calls
+        self.tokens = 0           # tokens through those calls
+        self.agree = 0
+        self.disagree = 0
+        self.dev_ms = 0.0         # CUDA-event time of the layer calls
+        self.rescales = 0         # running-max rescales of the online softmax
+        self.overflows = 0        # score + accumulator saturations
+        self.clips = 0            # wire values saturated at the seam
+        self.flagged = 0          # calls with a saturation or overflow
+
+    def add_call(self, n_tokens: int, dev_ms: float, stats, clips: int) -> None:
+        """One layer call: its tokens, device time, scan statistics (n, n_kv, 6)
+        in AttentionStats order, and the seam's saturated-value count."""
+        st = np.asarray(stats)
+        over = int(st[..., 2].sum() + st[..., 3].sum())
+        self.steps += 1
+        self.tokens += n_tokens
+        self.dev_ms += dev_ms
+        self.rescales += int(st[..., 1].sum())
+        self.overflows += over
+        self.clips += int(clips)
+        if over or clips:
+            self.flagged += 1
+
+    def compare(self, got, want):
+        """Channel-by-channel agreement; None when equal, else what differs."""
+        got, want = np.asarray(got), np.asarray(want)
+        want = want.reshape(got.shape[0], -1) if want.size == got.size else want
+        got = got.reshape(got.shape[0], -1)
+        if got.shape == want.shape and np.array_equal(got, want):
+            self.agree += 1
+            return None
+        self.disagree += 1
+        if got.shape != want.shape:
+            return f"shape {want.shape} against {got.shape}"
+        return f"{int(np.count_nonzero(got != want))} of {got.size} channels"
+
+    def summary(self) -> str:
+        if self.steps == 0:
+            return "!!! THE GPU WAS NEVER ASKED. No layer call went through this route."
+        per = max(self.n_layers, 1)
+        lines = [f"decode steps on the GPU: {self.steps} ({self.n_layers} layers x "
+                 f"{self.steps // per} calls, {self.tokens} tokens)"]
+        if self.verified:
+            lines.append(f"  agreement with the check: {self.agree} exact, {self.disagree} different")
+        lines.append(f"  device time: {self.dev_ms:.1f} ms total, "
+                     f"{self.dev_ms * 1e3 / self.steps:.0f} us/step")
+        lines.append(f"  online rescales {self.rescales}, overflows {self.overflows}, "
+                     f"seam clips {self.clips}, steps with a range/saturation flag {self.flagged}")
+        return "\n".join(lines)
+
+
+class GpuLayers(RouteCounters):
     """Routes every grafted layer's attention to one GPU cache pool."""
 
     def __init__(self, model, layers, capacity: int, *, verify=None, quiet: bool = False,
@@ -58,6 +117,7 @@ class GpuLayers:
         self.layers = list(layers)
         if not self.layers:
             raise ValueError("no layers to route")
+        super().__init__(len(self.layers), verify is not None)
         self.verify, self.quiet, self.trace = verify, quiet, trace
         cfg = model.config
         hq, hk = cfg.num_attention_heads, cfg.num_key_value_heads
@@ -77,17 +137,6 @@ class GpuLayers:
             m.decode_only = decode_only
             m.observer = self._observe
 
-        # counters, so a run can say what happened rather than that it finished
-        self.steps = 0            # layer calls
-        self.tokens = 0           # tokens through those calls
-        self.agree = 0
-        self.disagree = 0
-        self.dev_ms = 0.0         # CUDA-event time of the layer calls
-        self.rescales = 0         # running-max rescales of the online softmax
-        self.overflows = 0        # score + accumulator saturations
-        self.clips = 0            # wire values saturated at the seam
-        self.flagged = 0          # calls with a saturation or overflow
-
     @property
     def bytes_used(self) -> int:
         """Cache bytes the route's layers can hold (capacity rows per layer)."""
@@ -96,53 +145,22 @@ class GpuLayers:
     def _observe(self, L: int, layer, merged: torch.Tensor, t0, t1) -> None:
         t1.synchronize()
         dt = t0.elapsed_time(t1)
-        n = merged.shape[0]
-        self.steps += 1
-        self.tokens += n
-        self.dev_ms += dt
-        st = layer.last_stats.cpu().numpy()          # (n, n_kv, 6), AttentionStats order
-        over = int(st[..., 2].sum() + st[..., 3].sum())
-        clip = int(layer.last_conversion["n_saturated"])
-        self.rescales += int(st[..., 1].sum())
-        self.overflows += over
-        self.clips += clip
-        if over or clip:
-            self.flagged += 1
+        self.add_call(merged.shape[0], dt, layer.last_stats.cpu().numpy(),
+                      layer.last_conversion["n_saturated"])
         self.dec.pc.status()
+        token = self.dec.pc.length(self.slots[L])
         if self.trace:
-            print(f"    L{L:<2} tok {self.dec.pc.length(self.slots[L]):<5} {dt * 1e3:8.1f} us")
+            print(f"    L{L:<2} tok {token:<5} {dt * 1e3:8.1f} us")
         if self.verify is not None:
-            wq, wk, wv = (np.asarray(w.cpu().numpy() if torch.is_tensor(w) else w)
+            wq, wk, wv = (w.cpu().numpy() if torch.is_tensor(w) else np.asarray(w)
                           for w in layer.last_wire)
-            want = np.asarray(self.verify(L, wq, wk, wv)).reshape(n, -1)
-            got = merged.cpu().numpy().reshape(n, -1)
-            if got.shape == want.shape and np.array_equal(got, want):
-                self.agree += 1
-            else:
-                self.disagree += 1
-                if not self.quiet:
-                    bad = (int(np.count_nonzero(got != want)) if got.shape == want.shape
-                           else f"shape {want.shape} vs")
-                    print(f"    !! layer {L} token {self.dec.pc.length(self.slots[L])}: {bad} of "
-                          f"{got.size} channels differ from the check")
+            bad = self.compare(merged.cpu().numpy(), self.verify(L, wq, wk, wv))
+            if bad is not None and not self.quiet:
+                print(f"    !! layer {L} token {token}: {bad} differ from the check")
 
     def reset(self) -> None:
         """Empty every layer's cache (a new sequence)."""
         self.dec.pc.reset()
-
-    def summary(self) -> str:
-        if self.steps == 0:
-            return "!!! THE GPU WAS NEVER ASKED. No layer call went through this route."
-        per = max(len(self.layers), 1)
-        lines = [f"decode steps on the GPU: {self.steps} ({len(self.layers)} layers x "
-                 f"{self.steps // per} calls, {self.tokens} tokens)"]
-        if self.verify is not None:
-            lines.append(f"  agreement with the check: {self.agree} exact, {self.disagree} different")
-        lines.append(f"  device time: {self.dev_ms:.1f} ms total, "
-                     f"{self.dev_ms * 1e3 / self.steps:.0f} us/step")
-        lines.append(f"  online rescales {self.rescales}, overflows {self.overflows}, "
-                     f"seam clips {self.clips}, steps with a range/saturation flag {self.flagged}")
-        return "\n".join(lines)
 
     def close(self) -> None:
         """Put the model's own attention modules back and free the pool."""
