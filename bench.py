@@ -78,6 +78,9 @@ def parse():
                     help="config 5: one sequence split across the ranks (ctx = total tokens)")
     ap.add_argument("--formats", action="store_true",
                     help="time the lane-stream ingress and the DDR image (board formats)")
+    ap.add_argument("--model", action="store_true",
+                    help="whole-model decode: a Llama-3.2-1B-shaped random-init transformers model "
+                         "with all 16 attention layers on the GPU path, 8K context")
     ap.add_argument("--config", type=int, choices=(2, 3, 4, 5), default=2,
                     help="BASELINE config to time (2: the default sweep point; 5 = --split)")
     return ap.parse_args()
@@ -757,10 +760,106 @@ def run_formats(args):
     dec.close()
 
 
+LLAMA_1B = dict(hidden_size=2048, intermediate_size=8192, num_hidden_layers=16,
+                num_attention_heads=32, num_key_value_heads=8, head_dim=64, vocab_size=128256,
+                max_position_embeddings=131072, rms_norm_eps=1e-5, tie_word_embeddings=True,
+                rope_parameters={"rope_type": "llama3", "rope_theta": 500000.0, "factor": 32.0,
+                                 "low_freq_factor": 1.0, "high_freq_factor": 4.0,
+                                 "original_max_position_embeddings": 8192})
+
+
+def run_model(args):
+    """One generated token through a whole Llama-3.2-1B-shaped model (random
+    init, bf16 MLPs and norms from transformers) whose 16 attention layers
+    run on the GPU path through the layer router, on an 8K context; the same
+    model with its own dense bf16 attention beside it."""
+    import torch
+    import transformers
+    from insitu_b200.router import GpuLayers
+
+    world, rank, local = _dist_setup()
+    K, W = args.steps, args.warmup
+    T, chunk = 8192, 1024
+    dev = torch.device("cuda", local)
+    torch.manual_seed(7)
+    model = transformers.LlamaForCausalLM(transformers.LlamaConfig(**LLAMA_1B)).to(
+        dev, torch.bfloat16).eval()
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(70 + rank)
+    prompt = torch.randint(0, LLAMA_1B["vocab_size"], (1, T), device=dev, generator=gen)
+
+    def decode(cache, tok):
+        def step(i):
+            out = model(input_ids=tok[:, -1:], past_key_values=cache, use_cache=True,
+                        logits_to_keep=1)
+            tok.copy_(out.logits[:, -1:].argmax(-1))
+        return step
+
+    results = {}
+    with torch.no_grad():
+        route = GpuLayers(model, range(16), capacity=T + K + W + 8, decode_only=False, device=local)
+        cache = transformers.DynamicCache()
+        for lo in range(0, T, chunk):
+            out = model(input_ids=prompt[:, lo:lo + chunk], past_key_values=cache, use_cache=True,
+                        logits_to_keep=1)
+        tok = out.logits[:, -1:].argmax(-1)
+        step = decode(cache, tok)
+        for i in range(W):
+            step(i)
+        torch.cuda.synchronize(local)
+        calls0, dev0 = route.steps, route.dev_ms
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(K):
+            step(W + i)
+        e1.record()
+        torch.cuda.synchronize(local)
+        # the router's own CUDA-event time of the 16 layer calls per token
+        results["insitu"] = (e0.elapsed_time(e1), route.dev_ms - dev0, route.steps - calls0)
+        route.dec.pc.status()
+        route.close()
+        del cache
+        torch.cuda.empty_cache()
+        cache = transformers.DynamicCache()
+        for lo in range(0, T, chunk):
+            out = model(input_ids=prompt[:, lo:lo + chunk], past_key_values=cache, use_cache=True,
+                        logits_to_keep=1)
+        tok = out.logits[:, -1:].argmax(-1)
+        results["dense"] = (_time_steps(decode(cache, tok), K, W, local), None, 0)
+    ms_q, attn_q, calls = results["insitu"]
+    ms_d = results["dense"][0]
+    mx = _max_over_ranks([ms_q, ms_d], world, local)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "whole-model decode, ms per generated token", "n_gpus": world,
+            "steps": K, "warmup": W, "higher_is_better": False, "scaling": "weak",
+            "data": "synthetic: random-init weights (seed 7), random prompt tokens",
+            "config": {"workload": "Llama-3.2-1B shape (16 layers, 32 q / 8 kv heads, d64, "
+                                   "hidden 2048), bf16 weights, batch 1, 8192-token prompt "
+                                   "prefilled in 1024-token chunks, then greedy decode",
+                       "attention": "insitu_b200 router: 4b K / 2b V compressed cache, online "
+                                    "softmax, one page pool for all 16 layers",
+                       "parallelism": f"{world} independent replica(s)"},
+            "insitu_ms_per_token": round(mx[0] / K, 3),
+            "insitu_attention_device_ms_per_token": round(attn_q / K, 3),
+            "dense_bf16_sdpa_ms_per_token": round(mx[1] / K, 3),
+            "layer_calls_timed": calls,
+            "kv_bytes_per_token_all_layers": {"insitu": 16 * N_KV * ROW_BYTES,
+                                              "dense_bf16": 16 * N_KV * D * 2 * 2},
+        }), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.formats:
         run_formats(args)
+        return
+    if args.model:
+        run_model(args)
         return
     if args.impl == "reference":
         run_reference(args)
