@@ -48,41 +48,64 @@ struct DeviceGuard {
     }
 };
 
-// A pinned host buffer and its device twin, grown on demand. Host writes wait
-// on the event of the last copy out of the buffer, so an enqueued copy never
-// reads a half-rewritten staging area.
+// Per-call uploads (sequence ids, slots, plans, positions) go through a ring
+// of pinned host / device buffer pairs. reserve() moves to the next slot and
+// waits only for that slot's previous copy, so the host can run NSLOT calls
+// ahead of the GPU rather than one; host writes into a slot wait on that
+// slot's last copy, so an enqueued copy never reads a half-rewritten area. A
+// slot that must grow takes the whole ring with it, so that steady-state
+// calls never allocate.
 struct Staging {
-    void *h = nullptr;
+    static constexpr int NSLOT = 4;
+    struct Slot {
+        void *h = nullptr;
+        void *d = nullptr;
+        cudaEvent_t done = nullptr;
+    };
+    Slot ring[NSLOT];
+    size_t cap = 0;                     // every slot's size
+    int cur = NSLOT - 1;
+    void *h = nullptr;                  // the current slot's buffers
     void *d = nullptr;
-    size_t cap = 0;
-    cudaEvent_t done = nullptr;
 
     int reserve(size_t bytes) {
-        if (!done) CK(cudaEventCreateWithFlags(&done, cudaEventDisableTiming));
-        CK(cudaEventSynchronize(done));
-        if (bytes <= cap) return INS_OK;
-        size_t want = cap ? cap : 4096;
-        while (want < bytes) want *= 2;
-        if (h) cudaFreeHost(h);
-        if (d) cudaFree(d);
-        h = d = nullptr;
-        cap = 0;
-        CK(cudaHostAlloc(&h, want, cudaHostAllocDefault));
-        CK(cudaMalloc(&d, want));
-        cap = want;
+        cur = (cur + 1) % NSLOT;
+        Slot &sl = ring[cur];
+        if (!sl.done) CK(cudaEventCreateWithFlags(&sl.done, cudaEventDisableTiming));
+        CK(cudaEventSynchronize(sl.done));
+        if (bytes > cap) {
+            size_t want = cap ? cap : 4096;
+            while (want < bytes) want *= 2;
+            for (Slot &o : ring) {
+                if (o.done) CK(cudaEventSynchronize(o.done));
+                if (o.h) cudaFreeHost(o.h);
+                if (o.d) cudaFree(o.d);
+                o.h = o.d = nullptr;
+            }
+            cap = 0;
+            for (Slot &o : ring) {
+                CK(cudaHostAlloc(&o.h, want, cudaHostAllocDefault));
+                CK(cudaMalloc(&o.d, want));
+            }
+            cap = want;
+        }
+        h = sl.h;
+        d = sl.d;
         return INS_OK;
     }
     int upload(size_t bytes, cudaStream_t s) {
         CK(cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, s));
-        CK(cudaEventRecord(done, s));
+        CK(cudaEventRecord(ring[cur].done, s));
         return INS_OK;
     }
     void release() {
-        if (done) cudaEventSynchronize(done), cudaEventDestroy(done);
-        if (h) cudaFreeHost(h);
-        if (d) cudaFree(d);
+        for (Slot &o : ring) {
+            if (o.done) cudaEventSynchronize(o.done), cudaEventDestroy(o.done);
+            if (o.h) cudaFreeHost(o.h);
+            if (o.d) cudaFree(o.d);
+            o = Slot();
+        }
         h = d = nullptr;
-        done = nullptr;
         cap = 0;
     }
 };
