@@ -809,6 +809,7 @@ def run_model(args):
         for i in range(W):
             step(i)
         torch.cuda.synchronize(local)
+        route.drain()
         calls0, dev0 = route.steps, route.dev_ms
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
@@ -816,6 +817,7 @@ def run_model(args):
             step(W + i)
         e1.record()
         torch.cuda.synchronize(local)
+        route.drain()
         # the router's own CUDA-event time of the 16 layer calls per token
         results["insitu"] = (e0.elapsed_time(e1), route.dev_ms - dev0, route.steps - calls0)
         route.dec.pc.status()

@@ -189,6 +189,16 @@ int ins_seam(ins_cache *cache, int32_t n, const float *q, const float *k, const 
              const int64_t *positions, const ins_seam_cfg *cfg, int32_t *wq, int32_t *wk,
              int32_t *wv, int64_t *conv, void *stream);
 
+/* ins_seam with positions already on the device (int64 [n]), e.g. a model's
+ * position_ids tensor, so that the call needs no device-to-host read. The
+ * kernel checks each position against max_position instead of the host: a
+ * token outside the table gets zero lanes and the next ins_cache_status
+ * returns EINVAL (the reference raises ValueError at the call,
+ * ops/rope.py:159). */
+int ins_seam_device_positions(ins_cache *cache, int32_t n, const float *q, const float *k,
+                              const float *v, const int64_t *positions, const ins_seam_cfg *cfg,
+                              int32_t *wq, int32_t *wk, int32_t *wv, int64_t *conv, void *stream);
+
 /* ins_ingress fed the board's ingress stream instead of int32 arrays: the
  * byte stream VectorSet.ingress_bytes builds (hw/vectors.py:178-196) -- per
  * token, per KV head h, the vectors k_h, v_h, q_{h*groups} .. q_{h*groups +

@@ -17,7 +17,7 @@ constexpr int MAX_ROUNDS = 8;        // rotation rounds carried in the sign mask
 constexpr uint32_t FULL = 0xffffffffu;
 
 // Device status bits, latched by kernels and read by ins_cache_status().
-enum : int32_t { ST_RANGE = 1, ST_TIMEOUT = 2, ST_INTERNAL = 4, ST_SPLIT = 8 };
+enum : int32_t { ST_RANGE = 1, ST_TIMEOUT = 2, ST_INTERNAL = 4, ST_SPLIT = 8, ST_POSITION = 16 };
 
 // Tables, one copy per cache in device global memory.
 struct DevTables {

@@ -572,9 +572,9 @@ int ins_cache_ddr_image(ins_cache *c, int32_t seq, int64_t capacity, uint8_t *im
     return INS_OK;
 }
 
-int ins_seam(ins_cache *c, int32_t n, const float *q, const float *k, const float *v,
-             const int64_t *positions, const ins_seam_cfg *cfg, int32_t *wq, int32_t *wk, int32_t *wv,
-             int64_t *conv, void *stream) {
+static int seam_launch(ins_cache *c, int32_t n, const float *q, const float *k, const float *v,
+                       const int64_t *positions, bool host_positions, const ins_seam_cfg *cfg,
+                       int32_t *wq, int32_t *wk, int32_t *wv, int64_t *conv, void *stream) {
     if (!c || !cfg) return fail(INS_EINVAL, "cache or seam config is NULL");
     if (n < 0 || (n > 0 && (!q || !k || !v || !positions || !wq || !wk || !wv || !conv)))
         return fail(INS_EINVAL, "seam arguments");
@@ -582,20 +582,27 @@ int ins_seam(ins_cache *c, int32_t n, const float *q, const float *k, const floa
         cfg->rope_frac > 30)
         return fail(INS_EINVAL, "seam RoPE tables");
     if (n == 0) return INS_OK;
-    for (int32_t i = 0; i < n; ++i)
-        if (positions[i] < 0 || positions[i] >= cfg->max_position)
-            return fail(INS_EINVAL, "position " + std::to_string(positions[i]) + " beyond the table's " +
-                                        std::to_string(cfg->max_position));
+    if (host_positions)
+        for (int32_t i = 0; i < n; ++i)
+            if (positions[i] < 0 || positions[i] >= cfg->max_position)
+                return fail(INS_EINVAL, "position " + std::to_string(positions[i]) + " beyond the table's " +
+                                            std::to_string(cfg->max_position));
     DeviceGuard dg(c->device);
     cudaStream_t s = (cudaStream_t)stream;
-    if (int rc = c->stage_c.reserve(sizeof(int64_t) * (size_t)n)) return rc;
-    std::memcpy(c->stage_c.h, positions, sizeof(int64_t) * (size_t)n);
-    if (int rc = c->stage_c.upload(sizeof(int64_t) * (size_t)n, s)) return rc;
     SeamArgs a;
+    if (host_positions) {
+        if (int rc = c->stage_c.reserve(sizeof(int64_t) * (size_t)n)) return rc;
+        std::memcpy(c->stage_c.h, positions, sizeof(int64_t) * (size_t)n);
+        if (int rc = c->stage_c.upload(sizeof(int64_t) * (size_t)n, s)) return rc;
+        a.pos = (const int64_t *)c->stage_c.d;
+    } else {
+        a.pos = positions;
+    }
+    a.max_position = cfg->max_position;
+    a.status = c->d_status;
     a.q = q;
     a.k = k;
     a.v = v;
-    a.pos = (const int64_t *)c->stage_c.d;
     a.q_norm = cfg->q_norm;
     a.k_norm = cfg->k_norm;
     a.eps = cfg->norm_eps;
@@ -613,6 +620,18 @@ int ins_seam(ins_cache *c, int32_t n, const float *q, const float *k, const floa
     k_seam<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(c->g, a, n);
     CK(cudaGetLastError());
     return INS_OK;
+}
+
+int ins_seam(ins_cache *c, int32_t n, const float *q, const float *k, const float *v,
+             const int64_t *positions, const ins_seam_cfg *cfg, int32_t *wq, int32_t *wk, int32_t *wv,
+             int64_t *conv, void *stream) {
+    return seam_launch(c, n, q, k, v, positions, true, cfg, wq, wk, wv, conv, stream);
+}
+
+int ins_seam_device_positions(ins_cache *c, int32_t n, const float *q, const float *k, const float *v,
+                              const int64_t *positions, const ins_seam_cfg *cfg, int32_t *wq,
+                              int32_t *wk, int32_t *wv, int64_t *conv, void *stream) {
+    return seam_launch(c, n, q, k, v, positions, false, cfg, wq, wk, wv, conv, stream);
 }
 
 int ins_scan(ins_cache *c, int32_t B, const int32_t *seq_ids, const int64_t *lengths,
@@ -791,6 +810,9 @@ int ins_cache_status(ins_cache *c, void *stream) {
     if (st & ST_TIMEOUT) return fail(INS_ETIMEOUT, "a bounded device wait gave up");
     if (st & ST_RANGE) return fail(INS_ERANGE, "a value escaped its fixed-point format");
     if (st & ST_INTERNAL) return fail(INS_EINVAL, "internal consistency check failed");
+    if (st & ST_POSITION)
+        return fail(INS_EINVAL, "a seam position lay outside the RoPE table (ins_seam_device_positions); "
+                                "that token's lanes were written as zero");
     if (st & ST_SPLIT)
         return fail(INS_ERANGE, "a context-split merge could not prove its result exact (a shard held "
                                 "more rescales of one head than its composite can carry, or the 32-bit "

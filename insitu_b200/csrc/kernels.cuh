@@ -676,7 +676,9 @@ __global__ void k_export_rows(Geo g, const uint8_t *__restrict__ pool,
 // ---------------------------------------------------------------------------
 struct SeamArgs {
     const float *q, *k, *v;                  // [n, n_kv*H, d], [n, n_kv, d] float32
-    const int64_t *pos;                      // [n]
+    const int64_t *pos;                      // [n], on the device
+    int64_t max_position;                    // rows of the RoPE tables
+    int32_t *status;                         // ST_POSITION when a position is outside them
     const float *q_norm, *k_norm;            // [d] gains, or null
     float eps;
     double attn_scale;
@@ -742,7 +744,16 @@ __global__ void k_seam(Geo g, SeamArgs a, int32_t n) {
     };
     int64_t olo, ohi;
     const bool rope = kind != 2;
-    const int64_t p = a.pos[tok];
+    const int64_t p = a.pos[tok];                 // one token per warp: uniform
+    if (rope && (p < 0 || p >= a.max_position)) {
+        // outside the tables (positions that came from the device are checked
+        // here, not on the host): the token's lanes are zero and the call is
+        // reported by ins_cache_status
+        dst[lane] = 0;
+        dst[lane + 32] = 0;
+        if (lane == 0) atomicOr(a.status, ST_POSITION);
+        return;
+    }
     if (rope && a.cast_after_rope) {
         const double sc = (double)(1ll << a.frac);
         const double c = (double)a.cos_t[p * (D / 2) + lane] / sc, s = (double)a.sin_t[p * (D / 2) + lane] / sc;

@@ -53,7 +53,14 @@ class GpuKernelAttention(nn.Module):
         positions = kwargs.get("position_ids")
         if positions is None:
             positions = kwargs.get("cache_position")
-        pos = None if positions is None else positions.reshape(-1).detach().cpu().numpy().astype(np.int64)
+        # positions on the GPU go to the seam as they are (checked there, no
+        # host read); others are read to the host
+        if positions is None:
+            pos = None
+        elif positions.device.type == "cuda":
+            pos = positions.detach().reshape(-1)
+        else:
+            pos = positions.reshape(-1).detach().numpy().astype(np.int64)
         hook = self.observer
         if hook is not None:
             t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

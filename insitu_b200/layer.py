@@ -18,7 +18,7 @@ import torch
 from .config import FixedFormat, Geometry, QuantConfig
 from .decode import DecodeAttention
 from .rotate import Rotation
-from .seam import RopeScaling, Seam, project
+from .seam import RopeScaling, Seam, conv_stats, project
 
 
 def fold_o_proj(o_proj, rotation: Rotation, num_heads: int, head_dim: int) -> np.ndarray:
@@ -69,14 +69,28 @@ class AttentionLayer:
         if not o_folded:
             w_o = fold_o_proj(np.asarray(w_o, np.float64), Rotation.for_quant(self.quant, head_dim),
                               num_heads, head_dim)
-        f16 = lambda w: torch.as_tensor(np.asarray(w, dtype=np.float16)).to(dev)
-        self.w_q, self.w_k, self.w_v, self.w_o = f16(w_q), f16(w_k), f16(w_v), f16(w_o)
-        b = lambda x: None if x is None else torch.as_tensor(np.asarray(x, np.float32)).to(dev)
-        self.b_q, self.b_k, self.b_v, self.b_o = (b(x) for x in biases)
+        # the weights rounded to fp16 once, held as fp32 GEMM operands; q, k
+        # and v are one GEMM over their stacked rows (each output is the same
+        # fp32 dot product of fp16-rounded operands)
+        f32 = lambda w: torch.as_tensor(np.asarray(w, dtype=np.float16)).to(dev).float()
+        self.w_qkv = torch.cat([f32(w_q), f32(w_k), f32(w_v)]).contiguous()
+        self.w_o = f32(w_o)
+        nq, nk = num_heads * head_dim, num_kv_heads * head_dim
+        bq, bk, bv, bo = biases
+        self.b_qkv = None
+        if bq is not None or bk is not None or bv is not None:
+            z = lambda x, m: np.zeros(m, np.float32) if x is None else np.asarray(x, np.float32)
+            self.b_qkv = torch.as_tensor(np.concatenate([z(bq, nq), z(bk, nk), z(bv, nk)])).to(dev)
+        self.b_o = None if bo is None else torch.as_tensor(np.asarray(bo, np.float32)).to(dev)
+        self._split = (nq, nk, nk)
         self.seam = Seam(self.dec.pc, max_position=max_position, theta=rope_theta, scaling=rope_scaling,
                          rope_frac=self.fmt.centroid_frac, q_norm=q_norm, k_norm=k_norm,
                          norm_eps=norm_eps, cast_after_rope=cast_after_rope)
-        self.conversion = {"n_values": 0, "n_saturated": 0, "max_abs_float": 0.0}
+        # ConversionStats kept on the device (values and saturations summed,
+        # the largest |float| as a float64), read when asked for
+        self._conv_n = torch.zeros(2, dtype=torch.int64, device=dev)
+        self._conv_max = torch.zeros(1, dtype=torch.float64, device=dev)
+        self._last_conv = None
 
     def forward(self, x, positions=None):
         """Rows of x are decode tokens, in order (a prefill when there are
@@ -88,21 +102,38 @@ class AttentionLayer:
             x = x[None]
         n = x.shape[0]
         T = pc.length(self.seq)
-        pos = np.arange(T, T + n) if positions is None else np.asarray(positions, np.int64)
-        q = project(self.w_q, x, self.b_q).reshape(n, self.hq, self.d)
-        k = project(self.w_k, x, self.b_k).reshape(n, self.hk, self.d)
-        v = project(self.w_v, x, self.b_v).reshape(n, self.hk, self.d)
-        wq, wk, wv, st = self.seam(q, k, v, pos)
+        if positions is None:
+            pos = np.arange(T, T + n)
+        elif torch.is_tensor(positions) and positions.device.type == "cuda":
+            pos = positions            # stays on the device; the seam kernel checks it
+        else:
+            pos = np.asarray(positions, np.int64)
+        q, k, v = project(self.w_qkv, x, self.b_qkv, rounded=True).split(self._split, dim=1)
+        q = q.reshape(n, self.hq, self.d)
+        k = k.reshape(n, self.hk, self.d)
+        v = v.reshape(n, self.hk, self.d)
+        wq, wk, wv, conv = self.seam(q, k, v, pos, host_stats=False)
         self.last_wire = (wq, wk, wv)
-        self.last_conversion = st
-        self.conversion["n_values"] += st["n_values"]
-        self.conversion["n_saturated"] += st["n_saturated"]
-        self.conversion["max_abs_float"] = max(self.conversion["max_abs_float"], st["max_abs_float"])
+        self._last_conv = conv
+        self._conv_n += conv[:2]
+        torch.maximum(self._conv_max, conv[2:].view(torch.float64), out=self._conv_max)
         out, self.last_stats = self.dec.prefill_attend(self.seq, wq, wk, wv, mode=self.softmax)
         merged = out.reshape(n, self.hq * self.d)
         acc = merged.to(torch.float64) / float(1 << self.fmt.qk_frac)      # Q.to_float
-        y = project(self.w_o, acc, self.b_o)
+        y = project(self.w_o, acc, self.b_o, rounded=True)
         return y, merged
+
+    @property
+    def conversion(self) -> dict:
+        """All calls' ConversionStats so far (reads the device: a sync)."""
+        n = self._conv_n.cpu().numpy()
+        return {"n_values": int(n[0]), "n_saturated": int(n[1]),
+                "max_abs_float": float(self._conv_max.item())}
+
+    @property
+    def last_conversion(self) -> dict | None:
+        """The last call's ConversionStats (a sync)."""
+        return None if self._last_conv is None else conv_stats(self._last_conv)
 
     def close(self) -> None:
         if self._owns_dec:

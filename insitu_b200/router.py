@@ -26,7 +26,9 @@ step's wire (q (n, Hq, d), k and v (n, n_kv, d), int32 Q8.16 on the host) and
 returning the attention output a host implementation of the below-the-seam
 half computes for it ((n, Hq, d) or (n, Hq*d) integers). With it, every step
 is compared channel by channel and counted as agreeing or not; without it
-nothing is recomputed on the host. The router itself never computes on the
+nothing is recomputed on the host, and a call does not wait for the GPU: its
+events and statistics are read in batches (``drain()``, which ``summary()``
+and ``close()`` call), so the counters are current after a drain. The router itself never computes on the
 CPU: the check is whatever the caller supplies (the reference's own numpy
 kernel, or a test's oracle).
 """
@@ -136,13 +138,26 @@ class GpuLayers(RouteCounters):
         for m in self.mods.values():
             m.decode_only = decode_only
             m.observer = self._observe
+        # without verify or trace a call's events and statistics are kept on
+        # the device and read in batches (drain), so a layer call does not
+        # wait for the GPU; a kernel's latched error then surfaces at the next
+        # drain: summary(), close(), or every DRAIN_EVERY calls
+        self._pending = []
 
     @property
     def bytes_used(self) -> int:
         """Cache bytes the route's layers can hold (capacity rows per layer)."""
         return len(self.layers) * self.capacity * self.dec.geo.n_kv_heads * self.dec.row_bytes
 
+    DRAIN_EVERY = 512
+
     def _observe(self, L: int, layer, merged: torch.Tensor, t0, t1) -> None:
+        if self.verify is None and not self.trace:
+            self._pending.append((merged.shape[0], t0, t1, layer.last_stats, layer._last_conv))
+            if len(self._pending) >= self.DRAIN_EVERY:
+                self.drain()
+            return
+        self.drain()
         t1.synchronize()
         dt = t0.elapsed_time(t1)
         self.add_call(merged.shape[0], dt, layer.last_stats.cpu().numpy(),
@@ -158,13 +173,29 @@ class GpuLayers(RouteCounters):
             if bad is not None and not self.quiet:
                 print(f"    !! layer {L} token {token}: {bad} differ from the check")
 
+    def drain(self) -> None:
+        """Fold the deferred calls into the counters (one sync)."""
+        if not self._pending:
+            return
+        pending, self._pending = self._pending, []
+        pending[-1][2].synchronize()
+        for n, t0, t1, st, conv in pending:
+            self.add_call(n, t0.elapsed_time(t1), st.cpu().numpy(), int(conv[1].item()))
+        self.dec.pc.status()
+
+    def summary(self) -> str:
+        self.drain()
+        return super().summary()
+
     def reset(self) -> None:
         """Empty every layer's cache (a new sequence)."""
+        self.drain()
         self.dec.pc.reset()
 
     def close(self) -> None:
         """Put the model's own attention modules back and free the pool."""
         if self._original is not None:
+            self.drain()
             for m in self.mods.values():
                 m.observer = None
             ungraft(self._model, self._original)

@@ -63,10 +63,12 @@ def rope_tables(d: int, max_position: int, theta: float = 10000.0, frac: int = 1
     return q(np.cos(ang)), q(np.sin(ang))
 
 
-def project(w: torch.Tensor, x: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+def project(w: torch.Tensor, x: torch.Tensor, bias: torch.Tensor | None = None, *,
+            rounded: bool = False) -> torch.Tensor:
     """``matvec`` (numerics/fp.py:25-46) on the GPU: fp16-rounded operands,
-    fp32 products and accumulation. w (out, in), x (n, in) -> (n, out) fp32."""
-    w16 = w.to(torch.float16).to(torch.float32)
+    fp32 products and accumulation. w (out, in), x (n, in) -> (n, out) fp32.
+    ``rounded``: w is already fp16-rounded and held as fp32."""
+    w16 = w if rounded else w.to(torch.float16).to(torch.float32)
     x16 = x.to(torch.float16).to(torch.float32)
     prev = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = False     # fp32 arithmetic, not TF32
@@ -95,23 +97,36 @@ class Seam:
                                 int(bool(cast_after_rope)), float(1.0 / np.sqrt(d)), _ptr(self.cos),
                                 _ptr(self.sin), rope_frac, max_position)
 
-    def __call__(self, q, k, v, positions):
+    def __call__(self, q, k, v, positions, *, host_stats: bool = True):
         """Projection outputs (float32: q (n, Hq, d), k and v (n, n_kv, d)) ->
         the wire q, k, v (device int32) and the conversion statistics
-        {n_values, n_saturated, max_abs_float}."""
+        {n_values, n_saturated, max_abs_float}; with ``host_stats=False`` the
+        statistics stay on the device as ins_seam wrote them (no sync)."""
         pc = self.pc
         t = lambda x: torch.as_tensor(x).to(pc.device, torch.float32).contiguous()
         q, k, v = t(q), t(k), t(v)
         n = q.shape[0]
-        pos = np.ascontiguousarray(np.broadcast_to(np.asarray(positions, np.int64), (n,)))
+        on_device = torch.is_tensor(positions) and positions.device.type == "cuda"
+        if on_device:       # e.g. position_ids: checked by the kernel, no host read
+            pos = positions.to(pc.device, torch.int64).reshape(-1).expand(n).contiguous() \
+                if positions.numel() == 1 else positions.to(pc.device, torch.int64).reshape(-1).contiguous()
+            if pos.numel() != n:
+                raise ValueError(f"{pos.numel()} positions for {n} tokens")
+        else:
+            pos = np.ascontiguousarray(np.broadcast_to(np.asarray(positions, np.int64), (n,)))
         wq = torch.empty(q.shape, dtype=torch.int32, device=pc.device)
         wk = torch.empty(k.shape, dtype=torch.int32, device=pc.device)
         wv = torch.empty(v.shape, dtype=torch.int32, device=pc.device)
         conv = torch.zeros(3, dtype=torch.int64, device=pc.device)
-        _lib.check(pc._L.ins_seam(pc._h, n, _ptr(q), _ptr(k), _ptr(v), pos.ctypes.data,
-                                  C.byref(self.cfg), _ptr(wq), _ptr(wk), _ptr(wv), _ptr(conv),
-                                  _stream(pc.device)))
-        c = conv.cpu().numpy()
-        stats = {"n_values": int(c[0]), "n_saturated": int(c[1]),
-                 "max_abs_float": float(np.frombuffer(c[2:3].tobytes(), np.float64)[0])}
-        return wq, wk, wv, stats
+        fn = pc._L.ins_seam_device_positions if on_device else pc._L.ins_seam
+        _lib.check(fn(pc._h, n, _ptr(q), _ptr(k), _ptr(v), pos.data_ptr() if on_device else pos.ctypes.data,
+                      C.byref(self.cfg), _ptr(wq), _ptr(wk), _ptr(wv), _ptr(conv), _stream(pc.device)))
+        return wq, wk, wv, (conv_stats(conv) if host_stats else conv)
+
+
+def conv_stats(conv: torch.Tensor) -> dict:
+    """ins_seam's statistics triple (int64: values, saturated, the bits of the
+    largest |float| as a float64) as a host dict."""
+    c = conv.cpu().numpy()
+    return {"n_values": int(c[0]), "n_saturated": int(c[1]),
+            "max_abs_float": float(np.frombuffer(c[2:3].tobytes(), np.float64)[0])}

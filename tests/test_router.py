@@ -48,20 +48,21 @@ def _model():
     return transformers.LlamaForCausalLM(transformers.LlamaConfig(**CFG)).eval()
 
 
-def _run(model, prompt, n_gen):
+def _run(model, prompt, n_gen, device="cpu"):
     """Prompt one token at a time, then greedy decode; logits of every step."""
     import torch
     import transformers
     cache = transformers.DynamicCache()
     logits = []
+    ids = lambda t: torch.tensor([[int(t)]], device=device)
     with torch.no_grad():
         for t in prompt:
-            out = model(input_ids=torch.tensor([[int(t)]]), past_key_values=cache, use_cache=True)
-            logits.append(out.logits[0, -1].numpy())
+            out = model(input_ids=ids(t), past_key_values=cache, use_cache=True)
+            logits.append(out.logits[0, -1].cpu().numpy())
         for _ in range(n_gen):
             nxt = int(out.logits[0, -1].argmax())
-            out = model(input_ids=torch.tensor([[nxt]]), past_key_values=cache, use_cache=True)
-            logits.append(out.logits[0, -1].numpy())
+            out = model(input_ids=ids(nxt), past_key_values=cache, use_cache=True)
+            logits.append(out.logits[0, -1].cpu().numpy())
     return np.stack(logits)
 
 
@@ -121,10 +122,32 @@ def test_shared_pool_equals_one_cache_per_layer():
     model = _model()
     route = GpuLayers(model, layers=range(3), capacity=64)
     a = _run(model, prompt, 4)
-    assert route.agree == route.disagree == 0 and route.steps == 30
+    assert route._pending, "without verify the calls are read in batches"
+    assert "30 (3 layers x 10 calls, 30 tokens)" in route.summary()
+    assert route.agree == route.disagree == 0 and route.steps == 30 and not route._pending
     route.close()
     original = graft(model, layers=range(3), quant=QuantConfig(key_bits=4, value_bits=2),
                      capacity=64, softmax="online")
     b = _run(model, prompt, 4)
     ungraft(model, original)
     np.testing.assert_array_equal(a, b)
+
+
+def test_router_on_a_gpu_resident_model():
+    """The model on the GPU: position_ids reach the seam as a device tensor
+    (ins_seam_device_positions, no host read). Same tokens as the model on
+    the host, logits within float rounding of the GPU's own MLPs."""
+    pytest.importorskip("transformers")
+    from insitu_b200.router import GpuLayers
+    prompt = golden("graft.npz")["prompt"][0][:6]
+    host = _model()
+    r1 = GpuLayers(host, layers=range(3), capacity=64)
+    a = _run(host, prompt, 4)
+    r1.close()
+    dev = _model().cuda()
+    r2 = GpuLayers(dev, layers=range(3), capacity=64, verify=OracleCheck(4, 2), quiet=True)
+    b = _run(dev, prompt, 4, device="cuda")
+    assert (r2.agree, r2.disagree) == (30, 0)
+    r2.close()
+    assert (a.argmax(-1) == b.argmax(-1)).all()
+    assert np.abs(a - b).max() / np.abs(a).max() < 1e-3

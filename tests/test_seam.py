@@ -55,6 +55,26 @@ def test_seam_kernel_matches_reference(seam, norm, after):
     assert q_rot.shape == (1, 32, 64)
     with pytest.raises(ValueError):
         sm(seam["q"][:1], seam["k"][:1], seam["v"][:1], [1 << 17])
+    # positions already on the GPU (ins_seam_device_positions): the same wire
+    pos_dev = torch.as_tensor(seam["pos"], dtype=torch.int64, device=pc.device)
+    wq, wk, wv, st = sm(seam["q"], seam["k"], seam["v"], pos_dev)
+    np.testing.assert_array_equal(wq.cpu().numpy(), seam[f"wq_{tag}"])
+    np.testing.assert_array_equal(wk.cpu().numpy(), seam[f"wk_{tag}"])
+    np.testing.assert_array_equal(wv.cpu().numpy(), seam[f"wv_{tag}"])
+    assert [st["n_values"], st["n_saturated"]] == list(seam[f"conv_{tag}"])
+    pc.status()
+    # a position beyond the table is caught by the kernel's own bounds check:
+    # that token's q and k lanes are zero, v is cast as usual, and the next
+    # status call raises
+    bad = pos_dev.clone()
+    bad[1] = 1 << 17
+    wq, wk, wv, _ = sm(seam["q"], seam["k"], seam["v"], bad)
+    with pytest.raises(ValueError, match="outside the RoPE table"):
+        pc.status()
+    assert not wq[1].any() and not wk[1].any()
+    np.testing.assert_array_equal(wv.cpu().numpy(), seam[f"wv_{tag}"])
+    np.testing.assert_array_equal(wq[0].cpu().numpy(), seam[f"wq_{tag}"][0])
+    pc.status()                                  # reported once, then clear
 
 
 @pytest.mark.gpu
