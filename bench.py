@@ -236,6 +236,7 @@ def run_ours(args):
     time.sleep(0.3)
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
+    launches0 = pc.launches()
     t_start.record(stream)
     for i in range(K):
         ev[i][0].record(stream)
@@ -244,6 +245,7 @@ def run_ours(args):
         out, st = pc.scan([0], q_rot)
         ev[i][2].record(stream)
     t_end.record(stream)
+    launches = pc.launches() - launches0          # this library's kernels, timed steps
     barrier()
     clk = clocks.stop()
     pc.status()
@@ -329,8 +331,9 @@ def run_ours(args):
             "e2e": {"value": round(tot_e2e / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "us_per_step": round(e2e_ms / K * 1e3, 2)},
-            # ingress, scores, prefix, values, fold_blocks, fold_items, exact re-run
-            "gpu_launches": 7 * K,
+            # counted by the library over the timed steps: ingress, scores,
+            # prefix, values, [fold_blocks], fold_items, exact re-run
+            "gpu_launches": launches,
             "clocks": clk,
         }
     dec.close()
@@ -555,19 +558,22 @@ def _fill(dec, seq: int, n: int, gen, device: int):
         del kv
 
 
-def _time_steps(step, K, W, local):
-    """W untimed steps, then K steps between CUDA events; returns ms."""
+def _time_steps(step, K, W, local, counter=None):
+    """W untimed steps, then K steps between CUDA events; returns ms (and,
+    given ``counter``, the kernels it counted over the K timed steps)."""
     import torch
     for i in range(W):
         step(i)
     torch.cuda.synchronize(local)
+    c0 = counter() if counter else 0
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(K):
         step(W + i)
     e1.record()
     torch.cuda.synchronize(local)
-    return e0.elapsed_time(e1)
+    ms = e0.elapsed_time(e1)
+    return (ms, counter() - c0) if counter else ms
 
 
 def run_batched(args):
@@ -602,7 +608,8 @@ def run_batched(args):
         rows0 = sum(my)
         if world > 1:
             dist.barrier()
-        ms = _time_steps(lambda i: dec.step(q[i], k[i], v[i]), K, W, local)
+        ms, launches = _time_steps(lambda i: dec.step(q[i], k[i], v[i]), K, W, local,
+                                   counter=dec.pc.launches)
         dec.pc.status()
         rows = sum(N_KV * (rows0 + B * (W + i + 1)) for i in range(K))
         # e2e: host q/k/v in, output back, every step
@@ -624,6 +631,7 @@ def run_batched(args):
                               "e2e_GB/s": round(tot_e2e * ROW_BYTES / (e2e_max * 1e-3) / 1e9, 2),
                               "e2e_us_per_step": round(e2e_max / K * 1e3, 2),
                               "h2d_bytes_per_step": int((qh.numel() + kh.numel() + vh.numel()) * 4),
+                              "gpu_launches": launches,
                               "d2h_bytes_per_step": int(outh.numel() * 8)}
         dec.close()
         del q, k, v
@@ -647,7 +655,7 @@ def run_batched(args):
             "e2e": {"value": main["e2e_GB/s"], "unit": "GB/s",
                     "h2d_bytes_per_step": main["h2d_bytes_per_step"],
                     "d2h_bytes_per_step": main["d2h_bytes_per_step"]},
-            "gpu_launches": 7 * K,
+            "gpu_launches": main["gpu_launches"],
         }), flush=True)
     if world > 1:
         dist.barrier()
@@ -676,7 +684,7 @@ def run_layers(args):
     def step(i):
         for li, dec in enumerate(decs):
             dec.step(q[i * L + li], k[i * L + li], v[i * L + li])
-    ms = _time_steps(step, K, W, local)
+    ms, launches = _time_steps(step, K, W, local, counter=lambda: sum(d.pc.launches() for d in decs))
     for dec in decs:
         dec.pc.status()
     rows = sum(L * N_KV * (T + W + i + 1) for i in range(K))
@@ -696,7 +704,7 @@ def run_layers(args):
                        "context": T, "parallelism": f"{world} independent replica(s)",
                        "l2": "16 x 3.4 MB of rows per step; the layer caches together exceed L2"},
             "us_per_layer_step": round(ms_max / K / L * 1e3, 2),
-            "gpu_launches": 7 * L * K,
+            "gpu_launches": launches,
         }), flush=True)
     for dec in decs:
         dec.close()
@@ -737,7 +745,8 @@ def run_formats(args):
     pdec, pgen = make_decoder(32768, (K + W) * nb + 8, local, seed=6)
     pq, pk, pv = step_inputs(pgen, nb, local)
     T_pre = pdec.pc.length(0)
-    ms_pre = _time_steps(lambda i: pdec.prefill_attend(0, pq[:, 0], pk[:, 0], pv[:, 0]), K, W, local)
+    ms_pre, pre_launches = _time_steps(lambda i: pdec.prefill_attend(0, pq[:, 0], pk[:, 0], pv[:, 0]),
+                                       K, W, local, counter=pdec.pc.launches)
     pre_rows = sum(8 * sum(T_pre + (W + i) * nb + j + 1 for j in range(nb)) for i in range(K))
     pdec.close()
     pc.status()
@@ -755,7 +764,9 @@ def run_formats(args):
             "ddr_image": {"tokens": T, "us": round(ms_img / K * 1e3, 2),
                           "GB/s_rows": round(rows * ROW_BYTES / (ms_img / K * 1e-3) / 1e9, 2),
                           "image_bytes": int(pc.ddr_image(0, cap).numel())},
-            "gpu_launches": K * 4,
+            # one per timed call of the ingress (two forms), the image and the
+            # seam; the prefill's as the library counted them
+            "gpu_launches": K * 4 + pre_launches,
         }), flush=True)
     dec.close()
 

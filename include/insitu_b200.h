@@ -139,6 +139,13 @@ int64_t ins_cache_length(const ins_cache *cache, int32_t seq);
 /* Tokens one sequence can hold (KVCache.capacity). */
 int64_t ins_cache_capacity(const ins_cache *cache);
 
+/* Kernels this cache has launched so far through ins_ingress,
+ * ins_ingress_lanes, ins_seam, ins_seam_device_positions and ins_scan (a
+ * running count, for a caller that reports what ran; the chunked online scan
+ * is 5 or 6 launches, one more when its items need more than one fold
+ * block). No reference counterpart. -1 for NULL. */
+int64_t ins_cache_launches(const ins_cache *cache);
+
 /* Flags of ins_ingress. */
 enum {
     /* k and v (and q) are already rotated, as CompressedCache.append_rotated

@@ -94,7 +94,8 @@ SYMBOLS = ("ins_abi_version", "ins_bytes_per_token", "ins_cache_create", "ins_ca
            "ins_last_error", "ins_scan_noalloc", "ins_scan_recomputed", "ins_part_bytes",
            "ins_scan_maxima", "ins_scan_part", "ins_merge_parts", "ins_cache_set_tiles",
            "ins_ingress_lanes", "ins_lanes_bytes_per_token", "ins_ddr_image_bytes",
-           "ins_cache_ddr_image", "ins_seam", "ins_seam_device_positions")
+           "ins_cache_ddr_image", "ins_seam", "ins_seam_device_positions",
+           "ins_cache_launches")
 
 
 def nvcc() -> str:
@@ -168,6 +169,8 @@ def lib():
     L.ins_cache_ddr_image.argtypes = [vp, i32, i64, vp, vp]
     L.ins_seam.argtypes = [vp, i32, vp, vp, vp, vp, C.POINTER(SeamCfg), vp, vp, vp, vp, vp]
     L.ins_seam_device_positions.argtypes = L.ins_seam.argtypes
+    L.ins_cache_launches.argtypes = [vp]
+    L.ins_cache_launches.restype = i64
     L.ins_last_error.restype = C.c_char_p
     _lib = L
     return L

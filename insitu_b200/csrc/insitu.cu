@@ -298,6 +298,7 @@ int launch_scan_h(ins_cache *c, int32_t B, const int32_t *d_seq, const int64_t *
         fn<<<grid, threads, smem, s>>>(g, c->d_tables, d_seq, d_T, c->d_page_table,
                                        c->d_pool, q_rot, out, stats);
         CK(cudaGetLastError());
+        c->chunk.launches += 1;
         return INS_OK;
     }
     return launch_online(c->chunk, g, c->d_tables, B, d_seq, d_T, h_T, c->d_page_table,
@@ -434,6 +435,8 @@ int64_t ins_cache_length(const ins_cache *c, int32_t seq) {
 
 int64_t ins_cache_capacity(const ins_cache *c) { return c ? capacity_of(c) : -1; }
 
+int64_t ins_cache_launches(const ins_cache *c) { return c ? c->chunk.launches : -1; }
+
 int ins_cache_set_tiles(ins_cache *c, int32_t mode) {
     if (!c) return fail(INS_EINVAL, "cache is NULL");
     if (mode != INS_TILES_AUTO && mode != INS_TILES_LARGE && mode != INS_TILES_SMALL)
@@ -488,6 +491,7 @@ static int ingress_launch(ins_cache *c, int32_t n, const int32_t *seq_ids, const
                                                     (const int2 *)((const int64_t *)c->stage_a.d + n), n_new,
                                                     c->d_page_table, lanes);
     CK(cudaGetLastError());
+    c->chunk.launches += 1;
     return INS_OK;
 }
 
@@ -619,6 +623,7 @@ static int seam_launch(ins_cache *c, int32_t n, const float *q, const float *k, 
     const int64_t warps = (int64_t)n * (c->g.n_kv * c->g.H + 2 * c->g.n_kv);
     k_seam<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(c->g, a, n);
     CK(cudaGetLastError());
+    c->chunk.launches += 1;
     return INS_OK;
 }
 

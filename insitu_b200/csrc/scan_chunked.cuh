@@ -334,6 +334,7 @@ struct ChunkScratch {
     int32_t n_items = 0, max_chunks = 0, seg_cap = 0, tile_cap = 0;
     int32_t last_items = 0;       // items of the last chunked launch (their redo flags)
     int32_t tiles_mode = 0;       // TILES_AUTO / TILES_LARGE / TILES_SMALL
+    int64_t launches = 0;         // kernels launched by ingress, seam and scan calls (a count)
     int64_t sc_rows = 0;          // rows * H capacity of `sc`, in 32-bit words
     uint32_t *sc = nullptr;
     long long *bmg = nullptr, *cmx = nullptr;
@@ -2199,7 +2200,10 @@ inline int launch_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, i
     if (int rc = prepare_chunked<H, KB, VB, RS>(cs, g, tb, B, d_seq, d_T, h_T, d_pt, pool, q_rot, out, stats,
                                             d_status, a, s))
         return rc;
-    return launch_chunk_kernels<H, KB, VB, RS>(a, B, d_seq, d_T, s);
+    const int rc = launch_chunk_kernels<H, KB, VB, RS>(a, B, d_seq, d_T, s);
+    // scores, prefix, values, [block fold], item fold, exact re-run
+    if (rc == INS_OK) cs.launches += a.fold_fused ? 5 : 6;
+    return rc;
 }
 
 // Context split, phase 1: the scores of this shard and each item's maximum
@@ -2304,6 +2308,7 @@ inline int launch_online(ChunkScratch &cs, const Geo &g, const DevTables *tb, in
         case 4: e = launch_seq<4>(g, tb, B, d_seq, d_lens, d_pt, pool, q_rot, out, stats, nullptr, s); break;
         case 8: e = launch_seq<8>(g, tb, B, d_seq, d_lens, d_pt, pool, q_rot, out, stats, nullptr, s); break;
     }
+    if (e == cudaSuccess) cs.launches += 1;
     return e == cudaSuccess ? INS_OK : INS_ECUDA;
 }
 

@@ -113,6 +113,10 @@ class PagedCache:
     def length(self, seq: int = 0) -> int:
         return int(self._L.ins_cache_length(self._h, seq))
 
+    def launches(self) -> int:
+        """Kernels launched so far by this cache's ingress, seam and scan calls."""
+        return int(self._L.ins_cache_launches(self._h))
+
     def reset(self, seq: int | None = None) -> None:
         _lib.check(self._L.ins_cache_reset(self._h, -1 if seq is None else seq))
 
