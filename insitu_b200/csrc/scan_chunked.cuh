@@ -608,11 +608,27 @@ __device__ void merge_block(const ChunkArgs &a, int item, int blk, int nchunks,
                 loc += S0[u];
                 curS += S0[u];
                 curl += l0[u];
-                for (int e = 0; e < ns[u]; ++e) {
-                    const SegEntry &se = a.segs[sb[u] + e];
-                    const int64_t f = ldcg(&se.f);
-                    const int64_t sS = ldcg(&se.S[ch]);
-                    const int64_t sl = ldcg(&se.l);
+                // the tile's entries four at a time (loads together, then in
+                // order); the block's own entries written below are a
+                // separate allocation, so these loads read what the values
+                // launch wrote
+                for (int e0 = 0; e0 < ns[u]; e0 += 4) {
+                  int64_t fv[4], sv[4], lw[4];
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) {
+                      if (e0 + j < ns[u]) {
+                          const SegEntry &se = a.segs[sb[u] + e0 + j];
+                          fv[j] = ldcg(&se.f);
+                          sv[j] = ldcg(&se.S[ch]);
+                          lw[j] = ldcg(&se.l);
+                      }
+                  }
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) {
+                    if (e0 + j >= ns[u]) break;
+                    const int64_t f = fv[j];
+                    const int64_t sS = sv[j];
+                    const int64_t sl = lw[j];
                     if (eb >= 0) {
                         if (!opened) {
                             Spre = curS;
@@ -628,6 +644,7 @@ __device__ void merge_block(const ChunkArgs &a, int item, int blk, int nchunks,
                     curS = sS;
                     curl = sl;
                     loc = ((loc * f) >> a.g.prob_frac) + sS;
+                  }
                 }
             }
         }
@@ -688,11 +705,25 @@ __device__ void merge_item(const ChunkArgs &a, int item, int nblocks, int64_t T,
                 if (aa + Yv[u] > INT32_MAX) bad = true;
                 acc[k] += Sv[u];
                 l[k] += lv[u];
-                for (int e = 0; e < nev[u]; ++e) {
-                    const SegEntry &se = a.segs[ebv[u] + e];
-                    const int64_t f = ldcg(&se.f);
-                    acc[k] = ((acc[k] * f) >> a.g.prob_frac) + ldcg(&se.S[ch]);
-                    l[k] = ((l[k] * f) >> a.g.prob_frac) + ldcg(&se.l);
+                // the entries four at a time: their loads issued together,
+                // then applied in order
+                for (int e0 = 0; e0 < nev[u]; e0 += 4) {
+                    int64_t fv[4], sv[4], lw[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        if (e0 + j < nev[u]) {
+                            const SegEntry &se = a.segs[ebv[u] + e0 + j];
+                            fv[j] = ldcg(&se.f);
+                            sv[j] = ldcg(&se.S[ch]);
+                            lw[j] = ldcg(&se.l);
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        if (e0 + j >= nev[u]) break;
+                        acc[k] = ((acc[k] * fv[j]) >> a.g.prob_frac) + sv[j];
+                        l[k] = ((l[k] * fv[j]) >> a.g.prob_frac) + lw[j];
+                    }
                 }
             }
         }
