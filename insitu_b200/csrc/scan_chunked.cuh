@@ -795,9 +795,23 @@ __device__ void fold_part(const ChunkArgs &a, int item, int nblocks, int64_t T, 
                 loc += Sv[u];
                 curS += Sv[u];
                 curl += lv[u];
-                for (int e = 0; e < nev[u]; ++e) {
-                    const SegEntry &se = a.segs[ebv[u] + e];
-                    const int64_t f = ldcg(&se.f);
+                // the entries four at a time (loads together, then in order);
+                // the composite written below is separate memory
+                for (int e0 = 0; e0 < nev[u]; e0 += 4) {
+                  int64_t fv[4], sv[4], lw[4];
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) {
+                      if (e0 + j < nev[u]) {
+                          const SegEntry &se = a.segs[ebv[u] + e0 + j];
+                          fv[j] = ldcg(&se.f);
+                          sv[j] = ldcg(&se.S[ch]);
+                          lw[j] = ldcg(&se.l);
+                      }
+                  }
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) {
+                    if (e0 + j >= nev[u]) break;
+                    const int64_t f = fv[j];
                     if (!opened) {
                         Spre = curS;
                         lpre = curl;
@@ -809,9 +823,10 @@ __device__ void fold_part(const ChunkArgs &a, int item, int nblocks, int64_t T, 
                     }
                     if (ne < PART_MAXE && ch == 0) pr.ent[h][ne].f = (int32_t)f;
                     ++ne;
-                    curS = ldcg(&se.S[ch]);
-                    curl = ldcg(&se.l);
+                    curS = sv[j];
+                    curl = lw[j];
                     loc = ((loc * f) >> a.g.prob_frac) + curS;
+                  }
                 }
             }
         }
