@@ -3,7 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload (BASELINE config 2 at its largest context): one Llama-3.2-1B-shaped
+Workload (benchmark config 2 at its largest context): one Llama-3.2-1B-shaped
 attention layer below the seam -- 8 KV heads x head_dim 64, 4 query heads per
 KV head, 4-bit K / 2-bit V codebooks -- holding one sequence of 1,048,576
 cached tokens per GPU. A step is one decode step of the hot path: the ingress
@@ -21,18 +21,18 @@ every rank owns its own sequence (batch sharding needs no exchange).
 oracle's C restatement of attend_online (the reference's own numpy model is
 Python and does not travel), on a bounded sample of the same workload.
 
-`--split` (under torchrun) splits ONE sequence of `--ctx`
+`--split` (benchmark config 5, under torchrun) splits ONE sequence of `--ctx`
 cached tokens (default 4M) across the N ranks, each holding a causal range,
 and times the exact context-split scan (insitu_b200.context): strong scaling.
 
-`--config 4`: batched decode of 256 sequences whose
+`--config 4` (benchmark config 4): batched decode of 256 sequences whose
 lengths are drawn uniformly from 1K-64K (seeded), in one paged cache per
 rank, 4b/2b (`value`) and 3b/3b (`k3v3`); under torchrun the sequences are
 dealt to the ranks by length so each rank holds about the same number of rows
 (strong scaling, no exchange). A step = one batched ingress of a token per
 sequence + one batched scan.
 
-`--config 3`: 16 layer caches of 8K tokens each, decoded
+`--config 3` (benchmark config 3): 16 layer caches of 8K tokens each, decoded
 layer after layer (ingress + scan per layer); a step = one token through all
 16 layers.
 
@@ -82,7 +82,7 @@ def parse():
                     help="whole-model decode: a Llama-3.2-1B-shaped random-init transformers model "
                          "with all 16 attention layers on the GPU path, 8K context")
     ap.add_argument("--config", type=int, choices=(2, 3, 4, 5), default=2,
-                    help="BASELINE config to time (2: the default sweep point; 5 = --split)")
+                    help="benchmark config to time (2: the default sweep point; 5 = --split)")
     return ap.parse_args()
 
 
@@ -169,7 +169,10 @@ class ClockSampler:
 # the workload
 # ---------------------------------------------------------------------------
 
-def make_decoder(ctx: int, extra: int, device: int, seed: int):
+def make_decoder(ctx: int, extra: int, device: int, seed: int, on_chunk=None):
+    """The config-2 cache: one sequence of ``ctx`` tokens from seeded N(0,1)
+    Q8.16 k/v through the ingress kernel. ``on_chunk(dec, lo, k, v)`` sees every
+    appended chunk (the parity tests check the rows at the benchmarked size)."""
     import torch
     from insitu_b200 import DecodeAttention, FixedFormat, Geometry, QuantConfig
     dec = DecodeAttention(QuantConfig(key_bits=4, value_bits=2), FixedFormat(),
@@ -183,6 +186,8 @@ def make_decoder(ctx: int, extra: int, device: int, seed: int):
         kv = (torch.randn((2, n, N_KV, D), device=f"cuda:{device}", generator=gen) * 65536.0)
         kv = kv.round_().clamp_(-(1 << 23), (1 << 23) - 1).to(torch.int32)
         dec.prefill(0, kv[0], kv[1])
+        if on_chunk is not None:
+            on_chunk(dec, lo, kv[0], kv[1])
         del kv
     return dec, gen
 
@@ -237,6 +242,7 @@ def run_ours(args):
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     launches0 = pc.launches()
+    redo0 = pc.recomputed_total()
     t_start.record(stream)
     for i in range(K):
         ev[i][0].record(stream)
@@ -247,6 +253,7 @@ def run_ours(args):
     t_end.record(stream)
     launches = pc.launches() - launches0          # this library's kernels, timed steps
     barrier()
+    redo = pc.recomputed_total() - redo0          # items the exact fallback redid, timed steps
     clk = clocks.stop()
     pc.status()
     ms_local = t_start.elapsed_time(t_end)
@@ -308,7 +315,7 @@ def run_ours(args):
             "data": "synthetic: seeded N(0,1) k/v in Q8.16 (24-bit lanes) through the ingress "
                     "kernel, q ~ N(0,1/64); random tokens, no checkpoint",
             "config": {
-                "workload": "BASELINE config 2 at 1M: one Llama-3.2-1B-shaped layer below the "
+                "workload": "benchmark config 2 at 1M: one Llama-3.2-1B-shaped layer below the "
                             "seam (8 KV heads x d64, 4 q heads per KV head), 4b K / 2b V, one "
                             f"sequence of {ctx} cached tokens per GPU; step = ingress of one "
                             "token + online-softmax scan of all rows",
@@ -334,6 +341,9 @@ def run_ours(args):
             # counted by the library over the timed steps: ingress, scores,
             # prefix, values, [fold_blocks], fold_items, exact re-run
             "gpu_launches": launches,
+            # (sequence, KV head) items of the timed scans that the exact
+            # sequential kernel recomputed (0: every item took the fast path)
+            "recomputed_items": redo,
             "clocks": clk,
         }
     dec.close()
@@ -438,7 +448,7 @@ def run_reference(args):
         "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int64",
         "data": "synthetic: seeded N(0,1) k/v in Q8.16, q ~ N(0,1/64)",
-        "config": {"workload": "BASELINE config 2: one layer, 8 KV heads x d64, 4b K / 2b V, one "
+        "config": {"workload": "benchmark config 2: one layer, 8 KV heads x d64, 4b K / 2b V, one "
                                "sequence; each step a bounded sample of 65536 cached tokens",
                    "context_sample": T, "parallelism": "host threads, one per KV head"},
         "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": "port",
@@ -449,7 +459,7 @@ def run_reference(args):
 
 
 def run_split(args):
-    """one sequence of args.ctx tokens split across the ranks."""
+    """benchmark config 5: one sequence of args.ctx tokens split across the ranks."""
     import torch
     import torch.distributed as dist
     from insitu_b200.context import context_split_scan
@@ -502,7 +512,7 @@ def run_split(args):
             "warmup": W, "ms_per_step": round(ms / K, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int64",
             "data": "synthetic: seeded N(0,1) k/v in Q8.16 through the ingress kernel; q ~ N(0,1/64)",
-            "config": {"workload": f"BASELINE config 5: one sequence of {share * world} cached tokens, "
+            "config": {"workload": f"benchmark config 5: one sequence of {share * world} cached tokens, "
                                    f"8 KV heads x d64, 4b K / 2b V, split along context across "
                                    f"{world} GPU(s) ({share} tokens each); step = the exact "
                                    "context-split online scan (per-rank scores, all-gather of "
@@ -547,7 +557,7 @@ def _sum_over_ranks(vals, world, local):
     return [float(x) for x in t.cpu()]
 
 
-def _fill(dec, seq: int, n: int, gen, device: int):
+def _fill(dec, seq: int, n: int, gen, device: int, on_chunk=None):
     import torch
     chunk = 1 << 17
     for lo in range(0, n, chunk):
@@ -555,6 +565,8 @@ def _fill(dec, seq: int, n: int, gen, device: int):
         kv = (torch.randn((2, m, N_KV, D), device=f"cuda:{device}", generator=gen) * 65536.0)
         kv = kv.round_().clamp_(-(1 << 23), (1 << 23) - 1).to(torch.int32)
         dec.prefill(seq, kv[0], kv[1])
+        if on_chunk is not None:
+            on_chunk(seq, lo, kv[0], kv[1])
         del kv
 
 
@@ -576,22 +588,32 @@ def _time_steps(step, K, W, local, counter=None):
     return (ms, counter() - c0) if counter else ms
 
 
+def config4_lengths():
+    """benchmark config 4's 256 context lengths, U[1K, 64K] from seed 4."""
+    return np.random.default_rng(4).integers(1024, 64 * 1024 + 1, size=256)
+
+
+def deal_by_length(lens, world: int):
+    """Sequences dealt longest first to the rank holding the fewest rows:
+    per rank, the lengths it holds."""
+    load, mine = [0] * world, [[] for _ in range(world)]
+    for b in np.argsort(-np.asarray(lens), kind="stable"):
+        r = int(np.argmin(load))
+        load[r] += int(lens[b])
+        mine[r].append(int(lens[b]))
+    return mine
+
+
 def run_batched(args):
-    """256 sequences of U[1K, 64K] tokens, 4b/2b and 3b/3b."""
+    """benchmark config 4: 256 sequences of U[1K, 64K] tokens, 4b/2b and 3b/3b."""
     import torch
     import torch.distributed as dist
     from insitu_b200 import DecodeAttention, FixedFormat, Geometry, QuantConfig
 
     world, rank, local = _dist_setup()
     K, W = args.steps, args.warmup
-    lens = np.random.default_rng(4).integers(1024, 64 * 1024 + 1, size=256)
-    # deal sequences, longest first, to the rank holding the fewest rows
-    load, mine = [0] * world, [[] for _ in range(world)]
-    for b in np.argsort(-lens, kind="stable"):
-        r = int(np.argmin(load))
-        load[r] += int(lens[b])
-        mine[r].append(int(lens[b]))
-    my = mine[rank]
+    lens = config4_lengths()
+    my = deal_by_length(lens, world)[rank]
     B = len(my)
     res = {}
     for kb, vb in ((4, 2), (3, 3)):
@@ -608,9 +630,11 @@ def run_batched(args):
         rows0 = sum(my)
         if world > 1:
             dist.barrier()
+        redo0 = dec.pc.recomputed_total()
         ms, launches = _time_steps(lambda i: dec.step(q[i], k[i], v[i]), K, W, local,
                                    counter=dec.pc.launches)
         dec.pc.status()
+        redo = dec.pc.recomputed_total() - redo0
         rows = sum(N_KV * (rows0 + B * (W + i + 1)) for i in range(K))
         # e2e: host q/k/v in, output back, every step
         qh, kh, vh = q[W].cpu().pin_memory(), k[W].cpu().pin_memory(), v[W].cpu().pin_memory()
@@ -632,6 +656,7 @@ def run_batched(args):
                               "e2e_us_per_step": round(e2e_max / K * 1e3, 2),
                               "h2d_bytes_per_step": int((qh.numel() + kh.numel() + vh.numel()) * 4),
                               "gpu_launches": launches,
+                              "recomputed_items": redo,
                               "d2h_bytes_per_step": int(outh.numel() * 8)}
         dec.close()
         del q, k, v
@@ -644,7 +669,7 @@ def run_batched(args):
             "scaling": "strong", "vs_baseline": None, "dtype": "int64",
             "data": "synthetic: seeded N(0,1) k/v in Q8.16 through the ingress kernel; q ~ N(0,1/64); "
                     "lengths ~ U[1K, 64K] from seed 4",
-            "config": {"workload": "BASELINE config 4: batched decode of 256 sequences (lengths "
+            "config": {"workload": "benchmark config 4: batched decode of 256 sequences (lengths "
                                    "U[1K, 64K], seeded), one layer, 8 KV heads x d64, paged cache; "
                                    "step = batched ingress of one token per sequence + batched "
                                    "online scan", "sequences": 256,
@@ -663,7 +688,7 @@ def run_batched(args):
 
 
 def run_layers(args):
-    """16 layer caches of 8K tokens, one token through all 16."""
+    """benchmark config 3: 16 layer caches of 8K tokens, one token through all 16."""
     import torch
     from insitu_b200 import DecodeAttention, FixedFormat, Geometry, QuantConfig
 
@@ -698,7 +723,7 @@ def run_layers(args):
             "vs_baseline": None, "dtype": "int64",
             "data": "synthetic: seeded N(0,1) k/v in Q8.16 per layer through the ingress kernel; "
                     "q ~ N(0,1/64); projections are outside this path",
-            "config": {"workload": "BASELINE config 3: 16 layer caches of 8192 tokens (8 KV heads "
+            "config": {"workload": "benchmark config 3: 16 layer caches of 8192 tokens (8 KV heads "
                                    "x d64, 4b K / 2b V), batch 1; step = one token through all 16 "
                                    "layers (ingress + online scan per layer)", "layers": L,
                        "context": T, "parallelism": f"{world} independent replica(s)",

@@ -210,8 +210,8 @@ int ins_seam_device_positions(ins_cache *cache, int32_t n, const float *q, const
  * byte stream VectorSet.ingress_bytes builds (hw/vectors.py:178-196) -- per
  * token, per KV head h, the vectors k_h, v_h, q_{h*groups} .. q_{h*groups +
  * groups - 1}, each head_dim signed 24-bit lanes packed LSB first
- * (pack_lanes, hw/vectors.py:72-104); 9,216 bytes per token at the BASELINE
- * geometry (ins_lanes_bytes_per_token). lanes: device, n tokens back to back,
+ * (pack_lanes, hw/vectors.py:72-104); 9,216 bytes per token at 8 KV heads
+ * with 4 query heads each (ins_lanes_bytes_per_token). lanes: device, n tokens back to back,
  * 2-byte aligned; q_rot: device [n, n_kv*groups, d] int32, required. The lanes
  * are sign-extended on the GPU; everything after is ins_ingress. */
 int ins_ingress_lanes(ins_cache *cache, int32_t n, const int32_t *seq_ids, const uint8_t *lanes,
@@ -230,6 +230,26 @@ int ins_rotate(ins_cache *cache, int64_t n, const int32_t *x, int32_t *y, void *
  * receives the number of scores the clamp changed. */
 int ins_scores(ins_cache *cache, int32_t seq, int32_t kv_head, int64_t t0, int64_t n,
                const int32_t *q_rot, int64_t *s, int64_t *ovf, void *stream);
+
+/* The scan's finalize on its own: _finalize (ops/attention.py:873-880) with
+ * the normalised reciprocal (reciprocal, ops/attention.py:177-250) for n
+ * (acc, l) pairs, through the very device function every scan epilogue calls,
+ * so the finalize edge cases can be driven directly (the reference treats
+ * them as finalize.sv's contract, tests/test_vectors.py:557-634).
+ * acc: device int64 [n][head_dim]; l: device int64 [n]; out: device int64
+ * [n][head_dim]; recip, shift: device int64 [n] (the reciprocal and the total
+ * shift), each may be NULL. Stream-ordered. */
+int ins_finalize(ins_cache *cache, int64_t n, const int64_t *acc, const int64_t *l, int64_t *out,
+                 int64_t *recip, int64_t *shift, void *stream);
+
+/* ExpLut.__call__ (ops/attention.py:153-159) on the device for n distances
+ * (device int64 [n], each >= 0) through the scan kernels' three forms of the
+ * lookup: p (device int32 [3][n]) row 0 the general form of the sequential
+ * and two-pass scans, row 1 its 32-bit form, row 2 the context-parallel
+ * scan's form (zero unless the cache uses the default fixed-point format).
+ * A negative distance -- the reference's ValueError (ops/attention.py:
+ * 156-157) -- gives -1 and latches INS_ERANGE for ins_cache_status. */
+int ins_exp_lut(ins_cache *cache, int64_t n, const int64_t *delta, int32_t *p, void *stream);
 
 /* The code-domain scan: one decode step of attention for B sequences, every
  * KV head, every query head of its group (kernel.py:338-346, with
@@ -257,11 +277,15 @@ int ins_scan(ins_cache *cache, int32_t B, const int32_t *seq_ids, const int64_t 
  * library holds until the process exits.
  *
  * Arguments and results are those of ins_scan with mode INS_SOFTMAX_ONLINE,
- * bit for bit. Limits: at most 4096 sequences, 65,536 (sequence x KV head x
- * 1024-row tile) tiles, and a scratch layout that fits 192 MiB (the scores
- * take 16 bytes per cached row at 4 query heads per KV head: about 8 KV heads
- * x 1.1M tokens of one sequence, or 256 sequences of 4K); a call beyond them
- * returns INS_EBADLEN before enqueuing anything. The first call on each
+ * bit for bit. Limits: at most 4096 sequences, and a scratch layout that fits
+ * 192 MiB (the scores take 16 bytes per cached row at 4 query heads per KV
+ * head: about 8 KV heads x 1.1M tokens of one sequence); a call beyond them
+ * returns INS_EBADLEN before enqueuing anything. The pool of rescale
+ * segments gets what the rest of the layout leaves (at 256 sequences of 4K,
+ * room for about 260,000 segments against the 150,000 or so such a batch
+ * needs with random keys); an item whose segments do not fit is recomputed by the
+ * sequential kernel -- still exact, only slower (ins_scan_recomputed_total
+ * counts such items). The first call on each
  * device looks up the array's device address (cudaGetSymbolAddress) with that
  * device current, so make it before any stream capture. Every call clears the
  * counters it needs at zero, but all calls share the one array: calls whose
@@ -303,9 +327,15 @@ int ins_cache_status(ins_cache *cache, void *stream);
  * reference. Blocks on the stream; -1 on error (see ins_last_error). */
 int64_t ins_scan_recomputed(ins_cache *cache, void *stream);
 
+/* The running count, since the cache was created, of items that the exact
+ * sequential kernel recomputed after the context-parallel online scan could
+ * not prove them exact (ins_scan_recomputed counts the last scan only), so
+ * that a caller timing many scans can report whether any took the slow path.
+ * No reference counterpart. Blocks on the stream; -1 on error. */
+int64_t ins_scan_recomputed_total(ins_cache *cache, void *stream);
+
 /* Context split (one sequence's cached tokens held by several shards -- GPUs
- * or caches -- each a causal range; SURVEY e2 / BASELINE config 5). No
- * reference function does this; the reference scans one sequence in one
+ * or caches -- each a causal range). No reference function does this; the reference scans one sequence in one
  * process (ops/attention.py:451-513), and the merged result is that scan's
  * output bit for bit whenever the merge can prove the 32-bit accumulator
  * clamp never fires (otherwise it latches INS_ERANGE, read by

@@ -95,7 +95,8 @@ SYMBOLS = ("ins_abi_version", "ins_bytes_per_token", "ins_cache_create", "ins_ca
            "ins_scan_maxima", "ins_scan_part", "ins_merge_parts", "ins_cache_set_tiles",
            "ins_ingress_lanes", "ins_lanes_bytes_per_token", "ins_ddr_image_bytes",
            "ins_cache_ddr_image", "ins_seam", "ins_seam_device_positions",
-           "ins_cache_launches")
+           "ins_cache_launches", "ins_finalize", "ins_exp_lut",
+           "ins_scan_recomputed_total")
 
 
 def nvcc() -> str:
@@ -155,6 +156,8 @@ def lib():
     L.ins_cache_status.argtypes = [vp, vp]
     L.ins_scan_recomputed.argtypes = [vp, vp]
     L.ins_scan_recomputed.restype = i64
+    L.ins_scan_recomputed_total.argtypes = [vp, vp]
+    L.ins_scan_recomputed_total.restype = i64
     L.ins_part_bytes.argtypes = [vp, i32]
     L.ins_part_bytes.restype = i64
     L.ins_scan_maxima.argtypes = [vp, i32, vp, vp, vp, vp, vp]
@@ -169,6 +172,8 @@ def lib():
     L.ins_cache_ddr_image.argtypes = [vp, i32, i64, vp, vp]
     L.ins_seam.argtypes = [vp, i32, vp, vp, vp, vp, C.POINTER(SeamCfg), vp, vp, vp, vp, vp]
     L.ins_seam_device_positions.argtypes = L.ins_seam.argtypes
+    L.ins_finalize.argtypes = [vp, i64, vp, vp, vp, vp, vp, vp]
+    L.ins_exp_lut.argtypes = [vp, i64, vp, vp, vp]
     L.ins_cache_launches.argtypes = [vp]
     L.ins_cache_launches.restype = i64
     L.ins_last_error.restype = C.c_char_p

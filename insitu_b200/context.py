@@ -1,5 +1,5 @@
 """One sequence's decode-step scan across shards that each hold a causal range
-of its cached tokens (the context split of BASELINE config 5).
+of its cached tokens (the context split of benchmark config 5).
 
 The reference scans a sequence in one process (``attend_online``,
 ops/attention.py:451-513). Here shard r holds tokens [T_r, T_{r+1}) in its own

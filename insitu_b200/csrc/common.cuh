@@ -165,6 +165,16 @@ __device__ __forceinline__ void reciprocal(const Geo &g, int64_t l, int64_t &r, 
     shift = 62 - g.prob_frac + k;
 }
 
+// _finalize (ops/attention.py:873-880) of one channel: acc times the
+// normalised reciprocal of l, floored by the total shift; no clamp. Every
+// scan's epilogue and ins_finalize go through this one function.
+__device__ __forceinline__ int64_t finalize_out(const Geo &g, int64_t acc, int64_t l) {
+    int64_t r;
+    int shift;
+    reciprocal(g, l, r, shift);
+    return (acc * r) >> shift;
+}
+
 // Code `j` of a row held as 32-bit words, `kb` bits per code, LSB first
 // (ops/quantize.py:271-275).
 template <int KB>

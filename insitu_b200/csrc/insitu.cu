@@ -120,6 +120,7 @@ struct ins_cache {
     uint8_t *d_pool = nullptr;
     int32_t *d_page_table = nullptr;   // [max_seqs, max_pages]
     int32_t *d_status = nullptr;
+    unsigned long long *d_redo_total = nullptr;   // items the sequential kernel recomputed, running
     // host mirrors (pinned, so their copies can be asynchronous)
     int32_t *h_page_table = nullptr;
     int32_t *h_seq_lens = nullptr;
@@ -385,6 +386,7 @@ int ins_cache_create(const ins_config *cfg, const ins_tables *tb, int32_t device
         cudaMalloc(&c->d_pool, pool_bytes) != cudaSuccess ||
         cudaMalloc(&c->d_page_table, sizeof(int32_t) * pt) != cudaSuccess ||
         cudaMalloc(&c->d_status, sizeof(int32_t)) != cudaSuccess ||
+        cudaMalloc(&c->d_redo_total, sizeof(unsigned long long)) != cudaSuccess ||
         cudaHostAlloc(&c->h_page_table, sizeof(int32_t) * pt, cudaHostAllocDefault) != cudaSuccess ||
         cudaHostAlloc(&c->h_seq_lens, sizeof(int32_t) * cfg->max_seqs, cudaHostAllocDefault) !=
             cudaSuccess) {
@@ -394,6 +396,7 @@ int ins_cache_create(const ins_config *cfg, const ins_tables *tb, int32_t device
     }
     if (cudaEventCreateWithFlags(&c->mirror_done, cudaEventDisableTiming) != cudaSuccess)
         return cleanup(fail(INS_ECUDA, "event creation failed"));
+    c->chunk.redo_total = c->d_redo_total;
     std::memset(c->h_page_table, 0xff, sizeof(int32_t) * pt);
     std::memset(c->h_seq_lens, 0, sizeof(int32_t) * cfg->max_seqs);
     c->free_pages.reserve((size_t)cfg->n_pages);
@@ -402,6 +405,7 @@ int ins_cache_create(const ins_config *cfg, const ins_tables *tb, int32_t device
         cudaMemcpy(c->d_page_table, c->h_page_table, sizeof(int32_t) * pt, cudaMemcpyHostToDevice) !=
             cudaSuccess ||
         cudaMemset(c->d_status, 0, sizeof(int32_t)) != cudaSuccess ||
+        cudaMemset(c->d_redo_total, 0, sizeof(unsigned long long)) != cudaSuccess ||
         cudaMemset(c->d_pool, 0, pool_bytes) != cudaSuccess)
         return cleanup(fail(INS_ECUDA, "initial copies failed"));
     if (cudaDeviceSynchronize() != cudaSuccess) return cleanup(fail(INS_ECUDA, "init sync failed"));
@@ -422,6 +426,7 @@ int ins_cache_destroy(ins_cache *c) {
     cudaFree(c->d_pool);
     cudaFree(c->d_page_table);
     cudaFree(c->d_status);
+    cudaFree(c->d_redo_total);
     if (c->h_page_table) cudaFreeHost(c->h_page_table);
     if (c->h_seq_lens) cudaFreeHost(c->h_seq_lens);
     delete c;
@@ -805,6 +810,16 @@ int64_t ins_scan_recomputed(ins_cache *c, void *stream) {
     return k;
 }
 
+int64_t ins_scan_recomputed_total(ins_cache *c, void *stream) {
+    if (!c) return fail(INS_EINVAL, "cache is NULL"), -1;
+    DeviceGuard dg(c->device);
+    unsigned long long k = 0;
+    if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess ||
+        cudaMemcpy(&k, c->d_redo_total, sizeof(k), cudaMemcpyDeviceToHost) != cudaSuccess)
+        return fail(INS_ECUDA, "reading the recompute count"), -1;
+    return (int64_t)k;
+}
+
 int ins_cache_status(ins_cache *c, void *stream) {
     if (!c) return fail(INS_EINVAL, "cache is NULL");
     DeviceGuard dg(c->device);
@@ -822,6 +837,82 @@ int ins_cache_status(ins_cache *c, void *stream) {
         return fail(INS_ERANGE, "a context-split merge could not prove its result exact (a shard held "
                                 "more rescales of one head than its composite can carry, or the 32-bit "
                                 "accumulator could have clamped); those items' outputs were not written");
+    return INS_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// The scan's scalar stages on their own: the finalize and the exp lookup, run
+// by the same device functions the scan kernels call, over caller arrays.
+// ---------------------------------------------------------------------------
+namespace ins {
+
+__global__ void k_finalize_rows(Geo g, int64_t n, const int64_t *__restrict__ acc,
+                                const int64_t *__restrict__ l, int64_t *__restrict__ out,
+                                int64_t *__restrict__ recip, int64_t *__restrict__ shift) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n * D) return;
+    const int64_t row = i / D;
+    out[i] = finalize_out(g, acc[i], l[row]);
+    if ((i % D) == 0 && (recip || shift)) {
+        int64_t r;
+        int sh;
+        reciprocal(g, l[row], r, sh);
+        if (recip) recip[row] = r;
+        if (shift) shift[row] = sh;
+    }
+}
+
+// Row 0: exp_lut (the sequential and two-pass kernels); row 1: exp_lut32;
+// row 2: exp_lut_def (the context-parallel scan, default format only, else 0).
+// A negative distance, which the reference refuses (ops/attention.py:156-157),
+// latches ST_RANGE and gives -1.
+__global__ void k_exp_values(Geo g, const DevTables *__restrict__ tb, int64_t n,
+                             const int64_t *__restrict__ delta, int32_t *__restrict__ p,
+                             int32_t def_fmt, int32_t *status) {
+    __shared__ int32_t tab[256];
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) tab[i] = tb->exp_tab[i];
+    __syncthreads();
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t d = delta[i];
+        if (d < 0) {
+            atomicOr(status, ST_RANGE);
+            p[i] = p[n + i] = p[2 * n + i] = -1;
+            continue;
+        }
+        p[i] = exp_lut(g, tab, d);
+        p[n + i] = exp_lut32(g, tab, d);
+        p[2 * n + i] = def_fmt ? (int32_t)exp_lut_def(tab, d) : 0;
+    }
+}
+
+}  // namespace ins
+
+extern "C" {
+
+int ins_finalize(ins_cache *c, int64_t n, const int64_t *acc, const int64_t *l, int64_t *out,
+                 int64_t *recip, int64_t *shift, void *stream) {
+    if (!c) return fail(INS_EINVAL, "cache is NULL");
+    if (n < 0 || (n > 0 && (!acc || !l || !out))) return fail(INS_EINVAL, "finalize arguments");
+    if (n == 0) return INS_OK;
+    DeviceGuard dg(c->device);
+    const int64_t threads = n * D;
+    k_finalize_rows<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(c->g, n, acc, l, out,
+                                                                                     recip, shift);
+    CK(cudaGetLastError());
+    return INS_OK;
+}
+
+int ins_exp_lut(ins_cache *c, int64_t n, const int64_t *delta, int32_t *p, void *stream) {
+    if (!c) return fail(INS_EINVAL, "cache is NULL");
+    if (n < 0 || (n > 0 && (!delta || !p))) return fail(INS_EINVAL, "exp arguments");
+    if (n == 0) return INS_OK;
+    DeviceGuard dg(c->device);
+    const int64_t blocks = (n + 255) / 256;
+    k_exp_values<<<(unsigned)(blocks < 1184 ? blocks : 1184), 256, 0, (cudaStream_t)stream>>>(
+        c->g, c->d_tables, n, delta, p, is_def_fmt(c->g) ? 1 : 0, c->d_status);
+    CK(cudaGetLastError());
     return INS_OK;
 }
 
@@ -1026,7 +1117,6 @@ int ins_merge_parts(ins_cache *c, int32_t B, int32_t n_parts, const void *parts,
 namespace {
 
 constexpr size_t NOALLOC_BYTES = (size_t)192 << 20;
-constexpr int NOALLOC_SEGS = 4096;            // rescale segments; beyond, items are recomputed
 constexpr int NOALLOC_MAX_B = 4096;           // sequences per call
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_BYTES];
@@ -1055,13 +1145,25 @@ int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
     TilePlan &tp = g_na_plan;
     tp.build(g, B, g_na_T, CF::C);
     const int64_t n_tiles = tp.n_tiles;
+    if (n_tiles > INT32_MAX / 2) return fail(INS_EBADLEN, "too many tiles for one scan");
+    const int tiles = (int)(n_tiles < 1 ? 1 : n_tiles);
+    const size_t staging = ((sizeof(int64_t) * (size_t)B + 255) & ~(size_t)255) + sizeof(int32_t) * (size_t)B;
+    // the rescale-segment pool takes what the rest of the carve leaves, up to
+    // what ins_scan would reserve; an item whose segments do not fit is
+    // recomputed by the sequential kernel (still exact, only slower)
+    const ScratchLayout L0(n_items, tp.max_nc, 0, tiles, H, CF::CW, tp.rows);
+    if (L0.total + staging > NOALLOC_BYTES)
+        return fail(INS_EBADLEN, "this scan needs " + std::to_string(L0.total + staging) + " B of scratch; "
+                                 "ins_scan_noalloc holds " + std::to_string(NOALLOC_BYTES) + " B");
+    const int64_t seg_want = 2 * (64 * (int64_t)n_items * H) + 4 * (int64_t)tiles;
+    const int64_t seg_fit = (int64_t)((NOALLOC_BYTES - L0.total - staging - 256) / sizeof(SegEntry));
+    const int seg_cap = (int)std::min<int64_t>(std::min(seg_want, seg_fit), INT32_MAX);
     // the carve, in the same order ins_scan's scratch uses
-    const ScratchLayout L(n_items, tp.max_nc, NOALLOC_SEGS, (int)(n_tiles < 1 ? 1 : n_tiles), H, CF::CW,
-                          tp.rows);
+    const ScratchLayout L(n_items, tp.max_nc, seg_cap, tiles, H, CF::CW, tp.rows);
     const size_t o_T = L.total;
     const size_t o_seq = o_T + ((sizeof(int64_t) * (size_t)B + 255) & ~(size_t)255);
     const size_t o_end = o_seq + sizeof(int32_t) * (size_t)B;
-    if (o_end > NOALLOC_BYTES || n_tiles > INT32_MAX / 2)
+    if (o_end > NOALLOC_BYTES)
         return fail(INS_EBADLEN, "this scan needs " + std::to_string(o_end) + " B of scratch; "
                                  "ins_scan_noalloc holds " + std::to_string(NOALLOC_BYTES) + " B");
     const TileDesc TD(n_items);
@@ -1102,12 +1204,16 @@ int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
     a.blks = (BlockRec *)(p + L.blk);
     a.segs = (SegEntry *)(p + L.seg);
     a.seg_top = (unsigned int *)(p + L.top);
-    a.seg_cap = NOALLOC_SEGS;
+    a.seg_cap = seg_cap;
     a.items = (ItemAcc *)(p + L.items);
     a.redo = (int32_t *)(p + L.redo);
+    a.redo_total = c->d_redo_total;
     a.status = c->d_status;
     const int rc = launch_chunk_kernels<H, KB, VB, RS>(a, B, a.seq_ids, a.T, s);
-    return rc ? fail(rc, "chunked scan launch") : INS_OK;
+    if (rc) return fail(rc, "chunked scan launch");
+    // scores, prefix, values, [block fold], item fold, exact re-run
+    c->chunk.launches += a.fold_fused ? 5 : 6;
+    return INS_OK;
 }
 
 template <int H>
@@ -1126,6 +1232,7 @@ int noalloc_dispatch(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out
     const int32_t *d_seq = (const int32_t *)(p + ((sizeof(int64_t) * (size_t)B + 255) & ~(size_t)255));
     CK(launch_seq<H>(g, c->d_tables, B, d_seq, (const int64_t *)p, c->d_page_table, c->d_pool,
                      q_rot, out, stats, nullptr, s));
+    c->chunk.launches += 1;
     return INS_OK;
 }
 

@@ -461,10 +461,7 @@ __device__ void seq_scan_item(const Geo &g, const DevTables *__restrict__ tb, in
         __syncthreads();
     }
 
-    int64_t r;
-    int shift;
-    reciprocal(g, l, r, shift);
-    if (owner) out_row[h * D + j] = (acc * r) >> shift;
+    if (owner) out_row[h * D + j] = finalize_out(g, acc, l);
     if (st_out) {
         if (aovf) atomicAdd(&sm.aovf, (unsigned long long)aovf);
         if (owner) atomicMax(&sm.max_acc, (long long)(acc < 0 ? -acc : acc));
@@ -594,10 +591,7 @@ __global__ void __launch_bounds__(H * 64)
     bool hit;
     acc = qclamp(acc, g.acc_width, g.saturate, hit);
     const int64_t l = (int64_t)lsum[h];
-    int64_t r;
-    int shift;
-    reciprocal(g, l, r, shift);
-    out[((int64_t)b * g.n_kv * H + (int64_t)kvh * H + h) * D + j] = (acc * r) >> shift;
+    out[((int64_t)b * g.n_kv * H + (int64_t)kvh * H + h) * D + j] = finalize_out(g, acc, l);
     if (stats) {
         if (hit) atomicAdd(&sm.aovf, 1ull);
         atomicMax(&sm.max_acc, (long long)(acc < 0 ? -acc : acc));

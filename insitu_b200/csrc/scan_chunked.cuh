@@ -184,6 +184,7 @@ struct ChunkArgs {
     const long long *m_init;      // [n_items][H] running maximum entering the first tile, or null
     long long *maxima;            // [n_items][H] k_chunk_prefix writes each item's maximum, or null
     PartRec *parts;               // [n_items] composites instead of finalized outputs, or null
+    unsigned long long *redo_total;  // running count of items handed to the sequential kernel, or null
 };
 
 // Chunks of an item: one per tile_rows rows, and one (empty) for an empty item.
@@ -344,6 +345,7 @@ struct ChunkScratch {
     unsigned int *seg_top = nullptr;
     ItemAcc *items = nullptr;
     int32_t *redo = nullptr;
+    unsigned long long *redo_total = nullptr;   // set by the cache: its running recompute count
     uint8_t *desc = nullptr;      // the tile plan (TileDesc layout), uploaded per call
     PinnedRing up;                // host side of the tile-plan uploads
     TilePlan plan;                // the last call's plan (its vectors keep their capacity)
@@ -729,7 +731,10 @@ __device__ void merge_item(const ChunkArgs &a, int item, int nblocks, int64_t T,
         }
     }
     bad = __syncthreads_or(bad);
-    if (tid == 0) a.redo[item] = bad ? 1 : 0;
+    if (tid == 0) {
+        a.redo[item] = bad ? 1 : 0;
+        if (bad && a.redo_total) atomicAdd(a.redo_total, 1ull);
+    }
     if (bad) return;
     int64_t *out_row = a.out + qbase;
     long long mx = 0;
@@ -737,10 +742,7 @@ __device__ void merge_item(const ChunkArgs &a, int item, int nblocks, int64_t T,
     for (int k = 0; k < NP; ++k) {
         const int pr = tid + k * CHUNK_THREADS;
         if (pr >= H * D) continue;
-        int64_t r;
-        int shift;
-        reciprocal(a.g, l[k], r, shift);
-        out_row[pr] = (acc[k] * r) >> shift;
+        out_row[pr] = finalize_out(a.g, acc[k], l[k]);
         const long long ab = acc[k] < 0 ? -acc[k] : acc[k];
         mx = ab > mx ? ab : mx;
     }
@@ -909,10 +911,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS) k_merge_parts(Geo g, const Part
     for (int k = 0; k < NP; ++k) {
         const int pi = tid + k * CHUNK_THREADS;
         if (pi >= H * D) continue;
-        int64_t r;
-        int shift;
-        reciprocal(g, l[k], r, shift);
-        out_row[pi] = (acc[k] * r) >> shift;
+        out_row[pi] = finalize_out(g, acc[k], l[k]);
         const long long ab = acc[k] < 0 ? -acc[k] : acc[k];
         mx = ab > mx ? ab : mx;
     }
@@ -2232,6 +2231,7 @@ inline int prepare_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, 
     a.seg_cap = cs.seg_cap;
     a.items = cs.items;
     a.redo = cs.redo;
+    a.redo_total = cs.redo_total;
     a.status = d_status;
     cs.last_items = n_items;
     return INS_OK;

@@ -137,6 +137,14 @@ class PagedCache:
             _lib.check(_lib.INS_ECUDA)
         return int(k)
 
+    def recomputed_total(self) -> int:
+        """Items the exact sequential kernel redid over every online scan of
+        this cache so far (ins_scan_recomputed_total)."""
+        k = self._L.ins_scan_recomputed_total(self._h, _stream(self.device))
+        if k < 0:
+            _lib.check(_lib.INS_ECUDA)
+        return int(k)
+
     # -- tensors -------------------------------------------------------------
     def _dev_i32(self, x, shape_tail) -> torch.Tensor:
         if (isinstance(x, torch.Tensor) and x.dtype == torch.int32 and x.device == self.device
@@ -233,6 +241,30 @@ class PagedCache:
         _lib.check(self._L.ins_scores(self._h, seq, kv_head, t0, n, _ptr(q), _ptr(s), _ptr(ovf),
                                       _stream(self.device)))
         return s, ovf
+
+    def finalize(self, acc, l):
+        """_finalize (ops/attention.py:873-880) on the device for n (acc, l)
+        pairs: acc (n, d) and l (n,) int64 -> (out (n, d), reciprocal (n,),
+        total shift (n,)), by the scan epilogue's own device function."""
+        a = torch.as_tensor(acc, dtype=torch.int64).to(self.device).contiguous()
+        lv = torch.as_tensor(l, dtype=torch.int64).to(self.device).contiguous()
+        n = lv.numel()
+        if a.shape != (n, self.geo.head_dim):
+            raise ValueError(f"acc must be (n, {self.geo.head_dim}) for n = {n} values of l")
+        out = torch.empty_like(a)
+        r = torch.empty(n, dtype=torch.int64, device=self.device)
+        sh = torch.empty(n, dtype=torch.int64, device=self.device)
+        _lib.check(self._L.ins_finalize(self._h, n, _ptr(a), _ptr(lv), _ptr(out), _ptr(r), _ptr(sh),
+                                        _stream(self.device)))
+        return out, r, sh
+
+    def exp_lut(self, delta) -> torch.Tensor:
+        """ExpLut.__call__ (ops/attention.py:153-159) on the device through the
+        scan kernels' three forms of the lookup: (3, n) int32."""
+        d = torch.as_tensor(delta, dtype=torch.int64).to(self.device).contiguous().reshape(-1)
+        p = torch.empty((3, d.numel()), dtype=torch.int32, device=self.device)
+        _lib.check(self._L.ins_exp_lut(self._h, d.numel(), _ptr(d), _ptr(p), _stream(self.device)))
+        return p
 
     def scan(self, seq_ids, q_rot, *, lengths=None, mode: str = "online", stats: bool = True,
              out: torch.Tensor | None = None, stats_out: torch.Tensor | None = None):

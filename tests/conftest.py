@@ -67,3 +67,23 @@ def cuda_available() -> bool:
         return torch.cuda.is_available()
     except Exception:
         return False
+
+
+LONG_T = 32768
+LONG_SEEDS = {(4, 2): 3242, (3, 3): 3333}
+
+
+def long_inputs(kb: int, vb: int, T: int = LONG_T):
+    """k, v (T, 8, 64) and q (32, 64) of ``tests/golden/long32k.npz``, from the
+    seeds its generator used (numpy PCG64 normals, Q8.16 in 24-bit lanes); the
+    fixture's SHA-256 of the packed rows confirms the regeneration."""
+    rng = np.random.default_rng(LONG_SEEDS[(kb, vb)])
+
+    def wire(shape, scale=1.0):
+        x = np.rint(rng.standard_normal(shape) * scale * 65536.0).astype(np.int64)
+        return np.clip(x, -(1 << 23), (1 << 23) - 1)
+
+    k = wire((T, 8, 64))
+    v = wire((T, 8, 64))
+    q = wire((32, 64), 1.0 / 8.0)
+    return k, v, q

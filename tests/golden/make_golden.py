@@ -6,7 +6,7 @@ container that has the reference checked out; the fixtures it writes are small
 ``.npz`` files committed next to it, so the tests need nothing but numpy on any
 machine.
 
-    python tests/golden/make_golden.py --ref /path/to/INSITU
+    python tests/golden/make_golden.py --ref /path/to/INSITU [--only NAME ...]
 
 What it writes, and what each file pins:
 
@@ -32,7 +32,7 @@ What it writes, and what each file pins:
     accumulator clamp fires (``ops/attention.py:502-503``).
 
 ``config1_ctx512.npz``
-    one Llama-3.2-1B-shaped attention layer (hidden 2048,
+    benchmark config 1: one Llama-3.2-1B-shaped attention layer (hidden 2048,
     32 q heads, 8 KV heads, d 64, rope_theta 500000), W ~ N(0, 0.02) fp32 from
     seed 0 through ``Weights.prepare`` (``weights.py:70``), x ~ N(0,1), 512
     sequential decode steps through ``AttentionKernel.forward`` with the
@@ -40,7 +40,7 @@ What it writes, and what each file pins:
     output of selected steps, and the final packed cache bytes.
 
 ``seam.npz``
-    The host half after the projections (SURVEY row f1): seeded float32
+    The host half after the projections: seeded float32
     projection outputs through QK-norm, the attention scale, RoPE and the
     Q8.16 cast in both orders, with and without QK-norm, by the reference's
     own functions; rows of its Llama-3.2 RoPE tables.
@@ -55,6 +55,14 @@ What it writes, and what each file pins:
     Greedy decoding of a seeded random-init small ``LlamaForCausalLM`` with
     every attention block grafted by the reference's adapter: per-step logits
     and tokens.
+
+``long32k.npz``
+    The long-context pin of the C oracle: for 4b/2b and 3b/3b, one sequence
+    of 32,768 tokens in all 8 KV heads (k, v ~ N(0,1) in Q8.16 from a stored
+    seed) and 32 query heads, encoded, packed and scanned by the reference's
+    numpy ``attend_online`` (``ops/attention.py:451-513``), one KV group at a
+    time. Stores the seeds, the SHA-256 of the packed rows, the outputs and the
+    statistics; the tests regenerate k, v and q from the seeds.
 
 ``tables.npz``
     Codebook integers (gaussian and uniform, 1..8 bits), the exp table and its
@@ -323,7 +331,63 @@ def make_widths() -> dict:
 
 
 # --------------------------------------------------------------------------
-# BASELINE config 1
+# the long-context pin (32K tokens, every KV group)
+# --------------------------------------------------------------------------
+
+LONG_T = 32768
+LONG_SEEDS = {(4, 2): 3242, (3, 3): 3333}
+
+
+def long_inputs(kb: int, vb: int, T: int = LONG_T):
+    """The seeded k, v (T, 8, 64) and q (32, 64) of the long fixture, as the
+    tests regenerate them (numpy's PCG64 normal stream, Q8.16 in 24 bits)."""
+    rng = np.random.default_rng(LONG_SEEDS[(kb, vb)])
+    k = _wire(rng, (T, 8, 64))
+    v = _wire(rng, (T, 8, 64))
+    q = _wire(rng, (32, 64), 1.0 / 8.0)
+    return k, v, q
+
+
+def make_long32k() -> dict:
+    import hashlib
+    import time
+    from kernel.config import FixedFormat, QuantConfig
+    from kernel.ops.attention import CompressedAttention
+    from kernel.ops.quantize import KVQuantizer
+
+    fmt = FixedFormat()
+    out = {}
+    for (kb, vb), seed in LONG_SEEDS.items():
+        tag = f"k{kb}v{vb}"
+        quant = QuantConfig(key_bits=kb, value_bits=vb, seed=0)
+        qz = KVQuantizer(64, quant, fmt)
+        att = CompressedAttention(qz, fmt, quant)
+        k, v, q = long_inputs(kb, vb)
+        qr = qz.rotation.apply(q)
+        rows = np.empty((LONG_T, 8, qz.bytes_per_token), dtype=np.uint8)
+        outs, stats = [], []
+        t0 = time.time()
+        for h in range(8):
+            kv = qz.encode(qz.rotation.apply(k[:, h]), qz.rotation.apply(v[:, h]))
+            rows[:, h] = qz.pack(kv)
+            o, st = att.attend_online(qr[4 * h:4 * h + 4], kv)
+            outs.append(np.asarray(o, dtype=np.int64))
+            stats.append([st.n_tokens, st.rescale_events, st.score_overflows, st.acc_overflows,
+                          st.max_abs_score, st.max_abs_acc])
+        out.update({
+            f"{tag}_seed": np.array([seed]),
+            f"{tag}_rows_sha256": np.frombuffer(hashlib.sha256(rows.tobytes()).digest(), np.uint8),
+            f"{tag}_q_rot": np.asarray(qr, dtype=np.int64),
+            f"{tag}_online": np.concatenate(outs).reshape(32, 64),
+            f"{tag}_online_stats": np.array(stats, dtype=np.int64),
+        })
+        print(f"long32k {tag}: {time.time() - t0:.1f} s, rescales "
+              f"{[s[1] for s in stats]}")
+    return out
+
+
+# --------------------------------------------------------------------------
+# benchmark config 1
 # --------------------------------------------------------------------------
 
 CONFIG1_STEPS = (0, 1, 2, 7, 63, 64, 255, 256, 257, 510, 511)
@@ -535,18 +599,25 @@ def make_graft(n_prompt: int = 8, n_new: int = 6) -> dict:
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="a checkout of the INSITU repository")
     ap.add_argument("--skip-config1", action="store_true")
+    ap.add_argument("--only", nargs="+", default=None,
+                    help="regenerate only these fixtures (names without .npz)")
     a = ap.parse_args(argv)
     _import_reference(a.ref)
-    np.savez_compressed(os.path.join(HERE, "tbvec_c64_k4v2.npz"), **make_tbvec(a.ref))
-    np.savez_compressed(os.path.join(HERE, "tables.npz"), **make_tables())
-    np.savez_compressed(os.path.join(HERE, "widths.npz"), **make_widths())
-    np.savez_compressed(os.path.join(HERE, "seam.npz"), **make_seam())
-    np.savez_compressed(os.path.join(HERE, "layer.npz"), **make_layer())
-    np.savez_compressed(os.path.join(HERE, "graft.npz"), **make_graft())
-    if not a.skip_config1:
-        np.savez_compressed(os.path.join(HERE, "config1_ctx512.npz"), **make_config1())
+    makers = {
+        "tbvec_c64_k4v2": lambda: make_tbvec(a.ref),
+        "tables": make_tables,
+        "widths": make_widths,
+        "seam": make_seam,
+        "layer": make_layer,
+        "graft": make_graft,
+        "long32k": make_long32k,
+        "config1_ctx512": make_config1,
+    }
+    names = a.only or [n for n in makers if not (a.skip_config1 and n == "config1_ctx512")]
+    for n in names:
+        np.savez_compressed(os.path.join(HERE, f"{n}.npz"), **makers[n]())
     for n in sorted(os.listdir(HERE)):
         if n.endswith(".npz"):
             print(f"{n}: {os.path.getsize(os.path.join(HERE, n)) / 1024:.0f} KiB")

@@ -1,4 +1,4 @@
-"""BASELINE configs 3 and 4 at test size: the CUDA path against the oracle.
+"""Benchmark configs 3 and 4 at test size: the CUDA path against the oracle.
 
 Config 4 is batched decode over a paged cache whose sequences have lengths
 drawn uniformly (seeded), for the 4b/2b and 3b/3b codebooks: here 12

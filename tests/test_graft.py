@@ -1,4 +1,4 @@
-"""The GPU layer grafted into a transformers LlamaForCausalLM (SURVEY row f3):
+"""The GPU layer grafted into a transformers LlamaForCausalLM:
 greedy decoding of a seeded random-init small model with every attention block
 replaced, against the same model grafted with the reference's own adapter
 (tests/golden/graft.npz, made by importing the reference)."""

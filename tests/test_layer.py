@@ -1,4 +1,4 @@
-"""A whole layer on the GPU (SURVEY row f3): the W_o fold, and
+"""A whole layer on the GPU: the W_o fold, and
 AttentionLayer.forward against the reference's AttentionKernel.forward on a
 small Llama-shaped layer (tests/golden/layer.npz, made by importing the
 reference). The integer stages are exact; the four projections are library

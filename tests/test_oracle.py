@@ -212,7 +212,7 @@ def test_saturation_clamps_like_the_reference(orc, widths):
     assert list(st2) == g("two_pass_stats").tolist()
 
 
-# -- BASELINE config 1 --------------------------------------------------------
+# -- benchmark config 1 --------------------------------------------------------
 
 def test_config1_cache_and_selected_steps(orc, config1):
     wk, wv = config1["wire_k"].astype(np.int64), config1["wire_v"].astype(np.int64)
@@ -255,3 +255,26 @@ def test_ddr_image_of_the_golden_cache(tbvec):
     planes = wire.ddr_planes(((0, 32), (32, 48), (48, 52)))
     for h, t in ((0, 0), (7, 64), (3, 17)):
         np.testing.assert_array_equal(wire.row_at(img, planes, cap, h, t), tbvec["cache_rows"][t, h])
+
+
+# -- the long-context pin: 32K tokens, every KV group, against the reference's numpy --
+
+@pytest.mark.parametrize("kb,vb", [(4, 2), (3, 3)])
+def test_oracle_matches_reference_numpy_at_32k(kb, vb):
+    """The reference's own attend_online (ops/attention.py:451-513) over 32,768
+    tokens in all 8 KV groups (about 45 rescales each) is the fixture; the C
+    oracle must give its outputs and statistics bit for bit, from rows whose
+    bytes hash to the reference's packed rows."""
+    import hashlib
+    from conftest import golden, long_inputs
+    g = golden("long32k.npz")
+    tag = f"k{kb}v{vb}"
+    k, v, q = long_inputs(kb, vb)
+    orc = make_oracle(kb, vb)
+    rows = orc.ingress_rows(k, v, threads=8)
+    assert hashlib.sha256(rows.tobytes()).digest() == g[f"{tag}_rows_sha256"].tobytes()
+    qr = orc.rotate(q)
+    np.testing.assert_array_equal(qr, g[f"{tag}_q_rot"])
+    out, st = orc.decode_layer(qr[None], [rows], threads=8)
+    np.testing.assert_array_equal(out[0], g[f"{tag}_online"])
+    np.testing.assert_array_equal(st[0], g[f"{tag}_online_stats"])

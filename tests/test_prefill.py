@@ -1,4 +1,4 @@
-"""Prefill through the same cache (SURVEY row f4): every token of a chunk
+"""Prefill through the same cache: every token of a chunk
 attends the cache up to and including itself, as attend_online_batch /
 attend_causal_batch do (ops/attention.py:517-871) -- which the reference pins
 bit-identical to the per-token loop, the loop the oracle restates."""

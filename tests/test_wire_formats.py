@@ -1,5 +1,5 @@
 """The board's byte formats on the GPU: the 24-bit lane ingress stream and the
-DDR image of a cache (SURVEY-scope row f2), bit for bit against the
+DDR image of a cache, bit for bit against the
 reference's own golden files and the oracle."""
 
 from __future__ import annotations

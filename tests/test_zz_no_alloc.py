@@ -91,3 +91,28 @@ def test_noalloc_scan_refuses_work_beyond_its_array():
     out, _ = pc.scan(np.arange(1), q_rot)
     torch.cuda.synchronize(pc.device)
     assert out.shape == (1, 32, 64)
+
+
+def test_noalloc_scan_of_a_large_batch_stays_on_the_fast_path():
+    """256 sequences of 4K tokens: the rescale-segment pool gets the room the
+    rest of the array leaves, so no item is handed to the sequential kernel,
+    and the result equals ins_scan's on two calls in a row."""
+    rng = np.random.default_rng(35)
+    B, T = 256, 4096
+    pc = _pc(max_seqs=B, capacity=T)
+    g = torch.Generator(device=pc.device)
+    g.manual_seed(36)
+    for b in range(B):
+        kv = (torch.randn((2, T, 8, 64), generator=g, device=pc.device) * 65536.0).round_().clamp_(
+            -(1 << 23), (1 << 23) - 1).to(torch.int32)
+        pc.ingress(np.full(T, b, np.int32), kv[0], kv[1])
+    q_rot = pc.rotate(torch.from_numpy(_wire(rng, (B, 32, 64), 1.0 / 8.0)))
+    ids = np.arange(B)
+    want, want_st = pc.scan(ids, q_rot)
+    for call in range(2):
+        before = pc.recomputed_total()
+        out, st = _noalloc(pc, ids, q_rot)
+        pc.status()
+        assert pc.recomputed_total() == before, f"call {call}: items left the fast path"
+        assert torch.equal(out, want), f"call {call}: outputs differ"
+        assert torch.equal(st, want_st), f"call {call}: stats differ"
