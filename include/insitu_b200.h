@@ -133,6 +133,28 @@ int ins_cache_reset(ins_cache *cache, int32_t seq);
 enum { INS_TILES_AUTO = 0, INS_TILES_LARGE = 1, INS_TILES_SMALL = 2 };
 int ins_cache_set_tiles(ins_cache *cache, int32_t mode);
 
+/* Which kernels run the context-parallel online scan (no reference
+ * counterpart; results are identical either way). FUSED, the default: one
+ * persistent launch that scores each tile, finds the running maximum entering
+ * it from the tiles before (a bounded look-back on words the other CTAs
+ * publish), accumulates V and folds the tile records, followed by the exact
+ * re-run of items it could not prove. SPLIT: separate score, prefix-maximum,
+ * value and fold launches with the scores kept in global memory between them
+ * (the context split always uses these). */
+enum { INS_SCAN_FUSED = 0, INS_SCAN_SPLIT = 1 };
+int ins_cache_set_scan_kernel(ins_cache *cache, int32_t mode);
+
+/* A test of the fused scan's failure path, with no reference counterpart and
+ * no use outside tests: every look-back wait gives up after `poll_limit`
+ * polls (default 2^22, about a second), and the word that tile `chunk` of
+ * item `item` (sequence b, KV head h: item b * n_kv + h, in the order of the
+ * scan's seq_ids) publishes for query head `head` is withheld, so the tiles
+ * after it wait for a word nothing writes. Their waits give up, the launch
+ * still finishes, and ins_cache_status returns INS_ETIMEOUT; no GPU fault is
+ * involved. item < 0 withholds nothing. */
+int ins_cache_set_wait_test(ins_cache *cache, int32_t poll_limit, int32_t item, int32_t chunk,
+                            int32_t head);
+
 /* Tokens currently held for `seq` (KVCache.length), or -1. */
 int64_t ins_cache_length(const ins_cache *cache, int32_t seq);
 
@@ -141,9 +163,10 @@ int64_t ins_cache_capacity(const ins_cache *cache);
 
 /* Kernels this cache has launched so far through ins_ingress,
  * ins_ingress_lanes, ins_seam, ins_seam_device_positions and ins_scan (a
- * running count, for a caller that reports what ran; the chunked online scan
- * is 5 or 6 launches, one more when its items need more than one fold
- * block). No reference counterpart. -1 for NULL. */
+ * running count, for a caller that reports what ran; the online scan is 2
+ * launches with the fused kernels, or 5 or 6 with the separate ones, one more
+ * when its items need more than one fold block). No reference counterpart.
+ * -1 for NULL. */
 int64_t ins_cache_launches(const ins_cache *cache);
 
 /* Flags of ins_ingress. */
@@ -272,25 +295,28 @@ int ins_scan(ins_cache *cache, int32_t B, const int32_t *seq_ids, const int64_t 
  * all of HBM to its own pool at start-up, a runtime whose allocator may not be
  * entered from the decode thread, host code that must never block on an
  * allocation mid-step. ins_scan grows its scratch with cudaMalloc when a larger
- * batch or context first arrives; this call instead carves the same scratch
- * out of one static device array of 192 MiB that every GPU loading this
+ * batch or context first arrives; this call instead carves the scratch of the
+ * single-launch scan (INS_SCAN_FUSED, whatever ins_cache_set_scan_kernel
+ * says) out of one static device array of 192 MiB that every GPU loading this
  * library holds until the process exits.
  *
  * Arguments and results are those of ins_scan with mode INS_SOFTMAX_ONLINE,
  * bit for bit. Limits: at most 4096 sequences, and a scratch layout that fits
- * 192 MiB (the scores take 16 bytes per cached row at 4 query heads per KV
- * head: about 8 KV heads x 1.1M tokens of one sequence); a call beyond them
- * returns INS_EBADLEN before enqueuing anything. The pool of rescale
- * segments gets what the rest of the layout leaves (at 256 sequences of 4K,
- * room for about 260,000 segments against the 150,000 or so such a batch
- * needs with random keys); an item whose segments do not fit is recomputed by the
- * sequential kernel -- still exact, only slower (ins_scan_recomputed_total
- * counts such items). The first call on each
- * device looks up the array's device address (cudaGetSymbolAddress) with that
- * device current, so make it before any stream capture. Every call clears the
- * counters it needs at zero, but all calls share the one array: calls whose
- * GPU work overlaps (other streams, other threads, other caches on the same
- * device) race on it, so order them. */
+ * 192 MiB -- about 2.4 KB per (sequence, KV head, 1,024-token tile) plus
+ * about 8.5 KB per (sequence, KV head): some 9M tokens of one sequence at 8
+ * KV heads, or about 1,200 sequences of 4K; a call beyond them returns
+ * INS_EBADLEN before enqueuing anything. The pool of rescale segments gets
+ * what the rest of the layout leaves (at 256 sequences of 4K, room for about
+ * 310,000 segments
+ * against the 150,000 or so such a batch needs with random keys); an item
+ * whose segments do not fit is recomputed by the sequential kernel -- still
+ * exact, only slower (ins_scan_recomputed_total counts such items). The first
+ * call on each device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current, so make it before any
+ * stream capture. Every call clears the parts of the array that must start
+ * at zero, but all calls share the one array: calls whose GPU work overlaps
+ * (other streams, other threads, other caches on the same device) race on
+ * it, so order them. */
 int ins_scan_noalloc(ins_cache *cache, int32_t B, const int32_t *seq_ids, const int64_t *lengths,
                      const int32_t *q_rot, int64_t *out, ins_stats *stats, void *stream);
 

@@ -15,7 +15,8 @@ import subprocess
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 LIB_PATH = os.path.join(HERE, "libinsitu_b200.so")
-SOURCES = ("csrc/insitu.cu", "csrc/common.cuh", "csrc/kernels.cuh", "csrc/scan_chunked.cuh")
+SOURCES = ("csrc/insitu.cu", "csrc/common.cuh", "csrc/kernels.cuh", "csrc/scan_chunked.cuh",
+           "csrc/scan_fused.cuh")
 HEADER = os.path.join(ROOT, "include", "insitu_b200.h")
 
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", "-std=c++17",
@@ -26,6 +27,7 @@ INS_OK, INS_EBADLEN, INS_ETIMEOUT, INS_ERANGE, INS_EINVAL, INS_ENOMEM, INS_ECUDA
 INS_SOFTMAX_ONLINE, INS_SOFTMAX_TWO_PASS = 0, 1
 INS_INGRESS_PREROTATED = 1
 INS_TILES = {"auto": 0, "large": 1, "small": 2}
+INS_SCAN = {"fused": 0, "split": 1}
 
 
 class InsituError(RuntimeError):
@@ -96,7 +98,7 @@ SYMBOLS = ("ins_abi_version", "ins_bytes_per_token", "ins_cache_create", "ins_ca
            "ins_ingress_lanes", "ins_lanes_bytes_per_token", "ins_ddr_image_bytes",
            "ins_cache_ddr_image", "ins_seam", "ins_seam_device_positions",
            "ins_cache_launches", "ins_finalize", "ins_exp_lut",
-           "ins_scan_recomputed_total")
+           "ins_scan_recomputed_total", "ins_cache_set_scan_kernel", "ins_cache_set_wait_test")
 
 
 def nvcc() -> str:
@@ -164,6 +166,8 @@ def lib():
     L.ins_scan_part.argtypes = [vp, i32, vp, vp, vp, vp, vp, vp]
     L.ins_merge_parts.argtypes = [vp, i32, i32, vp, vp, vp, vp]
     L.ins_cache_set_tiles.argtypes = [vp, i32]
+    L.ins_cache_set_scan_kernel.argtypes = [vp, i32]
+    L.ins_cache_set_wait_test.argtypes = [vp, i32, i32, i32, i32]
     L.ins_ingress_lanes.argtypes = [vp, i32, vp, vp, vp, vp]
     L.ins_lanes_bytes_per_token.argtypes = [vp]
     L.ins_lanes_bytes_per_token.restype = i64

@@ -16,6 +16,7 @@
 #include "common.cuh"
 #include "kernels.cuh"
 #include "scan_chunked.cuh"
+#include "scan_fused.cuh"
 
 using namespace ins;
 
@@ -447,6 +448,25 @@ int ins_cache_set_tiles(ins_cache *c, int32_t mode) {
     if (mode != INS_TILES_AUTO && mode != INS_TILES_LARGE && mode != INS_TILES_SMALL)
         return fail(INS_EINVAL, "tile mode must be INS_TILES_AUTO, _LARGE or _SMALL");
     c->chunk.tiles_mode = mode;
+    return INS_OK;
+}
+
+int ins_cache_set_scan_kernel(ins_cache *c, int32_t mode) {
+    if (!c) return fail(INS_EINVAL, "cache is NULL");
+    if (mode != INS_SCAN_FUSED && mode != INS_SCAN_SPLIT)
+        return fail(INS_EINVAL, "scan kernel must be INS_SCAN_FUSED or INS_SCAN_SPLIT");
+    c->chunk.scan_kernel = mode;
+    return INS_OK;
+}
+
+int ins_cache_set_wait_test(ins_cache *c, int32_t poll_limit, int32_t item, int32_t chunk, int32_t head) {
+    if (!c) return fail(INS_EINVAL, "cache is NULL");
+    if (poll_limit < 1 || head < 0 || head >= c->g.H || chunk < 0)
+        return fail(INS_EINVAL, "wait test arguments");
+    c->chunk.poll_limit = poll_limit;
+    c->chunk.hold_item = item;
+    c->chunk.hold_chunk = chunk;
+    c->chunk.hold_head = head;
     return INS_OK;
 }
 
@@ -1148,10 +1168,12 @@ int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
     if (n_tiles > INT32_MAX / 2) return fail(INS_EBADLEN, "too many tiles for one scan");
     const int tiles = (int)(n_tiles < 1 ? 1 : n_tiles);
     const size_t staging = ((sizeof(int64_t) * (size_t)B + 255) & ~(size_t)255) + sizeof(int32_t) * (size_t)B;
-    // the rescale-segment pool takes what the rest of the carve leaves, up to
-    // what ins_scan would reserve; an item whose segments do not fit is
-    // recomputed by the sequential kernel (still exact, only slower)
-    const ScratchLayout L0(n_items, tp.max_nc, 0, tiles, H, CF::CW, tp.rows);
+    // The single-launch scan keeps scores in shared memory, so the carve needs
+    // no per-row area: records per tile and per item, look-back words, and the
+    // rescale-segment pool, which takes what the rest leaves, up to what
+    // ins_scan would reserve; an item whose segments do not fit is recomputed
+    // by the sequential kernel (still exact, only slower).
+    const ScratchLayout L0(n_items, tp.max_nc, 0, 1, H, CF::CW, 0);
     if (L0.total + staging > NOALLOC_BYTES)
         return fail(INS_EBADLEN, "this scan needs " + std::to_string(L0.total + staging) + " B of scratch; "
                                  "ins_scan_noalloc holds " + std::to_string(NOALLOC_BYTES) + " B");
@@ -1159,7 +1181,7 @@ int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
     const int64_t seg_fit = (int64_t)((NOALLOC_BYTES - L0.total - staging - 256) / sizeof(SegEntry));
     const int seg_cap = (int)std::min<int64_t>(std::min(seg_want, seg_fit), INT32_MAX);
     // the carve, in the same order ins_scan's scratch uses
-    const ScratchLayout L(n_items, tp.max_nc, seg_cap, tiles, H, CF::CW, tp.rows);
+    const ScratchLayout L(n_items, tp.max_nc, seg_cap, 1, H, CF::CW, 0);
     const size_t o_T = L.total;
     const size_t o_seq = o_T + ((sizeof(int64_t) * (size_t)B + 255) & ~(size_t)255);
     const size_t o_end = o_seq + sizeof(int32_t) * (size_t)B;
@@ -1170,10 +1192,13 @@ int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
     g_na_desc.assign(TD.total, 0);
     tp.write(g_na_desc.data(), TD);
     uint8_t *p = (uint8_t *)st.ptr;
-    // what the kernels expect at zero: the per-item accumulators (the array
-    // keeps whatever the previous call left in it; the segment counter is
-    // cleared by the launch itself)
+    // what the kernel expects at zero, since the array keeps whatever the
+    // previous call left in it, laid out for that call's shape: the segment
+    // counter, the per-item accumulators, the look-back words (read with
+    // epoch 1, which a cleared word never carries) and the fold counters
+    CK(cudaMemsetAsync(p + L.top, 0, 8, s));
     CK(cudaMemsetAsync(p + L.items, 0, sizeof(ItemAcc) * (size_t)n_items, s));
+    CK(cudaMemsetAsync(p + L.lbw, 0, L.sdone + sizeof(unsigned int) - L.lbw, s));
     CK(cudaMemcpyAsync(p + L.desc, g_na_desc.data(), g_na_desc.size(), cudaMemcpyHostToDevice, s));
     CK(cudaMemcpyAsync(p + o_T, g_na_T, sizeof(int64_t) * (size_t)B, cudaMemcpyHostToDevice, s));
     CK(cudaMemcpyAsync(p + o_seq, g_na_seq, sizeof(int32_t) * (size_t)B, cudaMemcpyHostToDevice, s));
@@ -1197,9 +1222,6 @@ int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
     a.q_rot = q_rot;
     a.out = out;
     a.stats = stats;
-    a.sc = (uint32_t *)(p + L.sc);
-    a.bmg = (long long *)(p + L.bmg);
-    a.cmx = (long long *)(p + L.cmx);
     a.recs = (ChunkRec *)(p + L.rec);
     a.blks = (BlockRec *)(p + L.blk);
     a.segs = (SegEntry *)(p + L.seg);
@@ -1209,10 +1231,17 @@ int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
     a.redo = (int32_t *)(p + L.redo);
     a.redo_total = c->d_redo_total;
     a.status = c->d_status;
-    const int rc = launch_chunk_kernels<H, KB, VB, RS>(a, B, a.seq_ids, a.T, s);
-    if (rc) return fail(rc, "chunked scan launch");
-    // scores, prefix, values, [block fold], item fold, exact re-run
-    c->chunk.launches += a.fold_fused ? 5 : 6;
+    FusedExtra x;
+    x.lbw = (unsigned long long *)(p + L.lbw);
+    x.blk_done = (unsigned int *)(p + L.bdone);
+    x.item_done = (unsigned int *)(p + L.idone);
+    x.scan_done = (unsigned int *)(p + L.sdone);
+    x.epoch = 1;
+    x.poll_limit = c->chunk.poll_limit;
+    x.hold_word = -1;
+    const int rc = launch_fused_kernels<H, KB, VB, RS>(a, x, B, a.seq_ids, a.T, s);
+    if (rc) return fail(rc, "scan launch");
+    c->chunk.launches += 2;                    // the scan, the exact re-run
     return INS_OK;
 }
 

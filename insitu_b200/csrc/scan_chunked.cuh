@@ -335,6 +335,14 @@ struct ChunkScratch {
     int32_t n_items = 0, max_chunks = 0, seg_cap = 0, tile_cap = 0;
     int32_t last_items = 0;       // items of the last chunked launch (their redo flags)
     int32_t tiles_mode = 0;       // TILES_AUTO / TILES_LARGE / TILES_SMALL
+    int32_t scan_kernel = 0;      // SCAN_FUSED (one launch) / SCAN_SPLIT (separate launches)
+    int32_t poll_limit = 1 << 22; // polls before a look-back wait of the fused scan gives up
+    int32_t hold_item = -1, hold_chunk = 0, hold_head = 0;   // a look-back word left unpublished
+                                                              // (the test of the bounded wait)
+    unsigned long long *lbw = nullptr;   // look-back words of the fused scan
+    size_t lbw_words = 0;
+    unsigned int *bdone = nullptr, *idone = nullptr, *sdone = nullptr;
+    unsigned int epoch = 0;       // of the last fused scan, 1 .. 4095
     int64_t launches = 0;         // kernels launched by ingress, seam and scan calls (a count)
     int64_t sc_rows = 0;          // rows * H capacity of `sc`, in 32-bit words
     uint32_t *sc = nullptr;
@@ -2082,12 +2090,17 @@ inline int chunk_slots() {
 
 // Byte layout of the scratch of one scan: `o` offsets in the order carved.
 struct ScratchLayout {
-    size_t top, cmx, rec, blk, seg, items, redo, desc, bmg, sc, total;
+    size_t top, cmx, rec, blk, seg, items, redo, desc, bmg, sc, lbw, bdone, idone, sdone, total;
     ScratchLayout(int ni, int mc, int sc_cap, int tc, int H, int CW, int64_t rows) {
         auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
         const int mb = (mc + GBLK - 1) / GBLK;
         size_t o = 0;
         top = o; o += al(8);
+        // the single-launch scan's look-back words and fold counters
+        lbw = o; o += al(sizeof(unsigned long long) * (size_t)ni * mc * H);
+        bdone = o; o += al(sizeof(unsigned int) * (size_t)ni * mb);
+        idone = o; o += al(sizeof(unsigned int) * (size_t)ni);
+        sdone = o; o += al(sizeof(unsigned int));
         cmx = o; o += al(sizeof(long long) * (size_t)ni * mc * 2 * HMAX);
         rec = o; o += al(sizeof(ChunkRec) * (size_t)ni * mc);
         blk = o; o += al(sizeof(BlockRec) * (size_t)ni * mb);
@@ -2142,6 +2155,12 @@ inline int reserve_scratch(ChunkScratch &cs, int n_items, int max_nc, int n_tile
     cs.desc = p + L.desc;
     cs.bmg = (long long *)(p + L.bmg);
     cs.sc = (uint32_t *)(p + L.sc);
+    cs.lbw = (unsigned long long *)(p + L.lbw);
+    cs.bdone = (unsigned int *)(p + L.bdone);
+    cs.idone = (unsigned int *)(p + L.idone);
+    cs.sdone = (unsigned int *)(p + L.sdone);
+    cs.lbw_words = (size_t)ni * mc * HMAX;
+    cs.epoch = 0;
     cs.n_items = ni;
     cs.max_chunks = mc;
     cs.seg_cap = sc;
@@ -2183,14 +2202,17 @@ inline int prepare_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, 
                            const int32_t *d_seq, const int64_t *d_T, const int64_t *h_T,
                            const int32_t *d_pt, const uint8_t *pool, const int32_t *q_rot,
                            int64_t *out, ins_stats *stats, int32_t *d_status, ChunkArgs &a,
-                           cudaStream_t s) {
+                           cudaStream_t s, bool score_rows = true) {
     using CF = ChunkCfg<H, KB, VB, RS>;
     const int n_items = B * g.n_kv;
     TilePlan &tp = cs.plan;
     tp.build(g, B, h_T, CF::C);
     if (tp.n_tiles > INT32_MAX / 2) return INS_EBADLEN;
     const int n_tiles = (int)tp.n_tiles;
-    if (int rc = reserve_scratch(cs, n_items, tp.max_nc, n_tiles, H, CF::CW, tp.rows, s)) return rc;
+    // the separate-launch scan keeps every row's score offsets in global
+    // memory; the single-launch scan keeps them in shared memory
+    if (int rc = reserve_scratch(cs, n_items, tp.max_nc, n_tiles, H, CF::CW, score_rows ? tp.rows : 0, s))
+        return rc;
     const TileDesc L(n_items);
     {
         int slot = 0;
@@ -2287,6 +2309,9 @@ inline int launch_split_part(ChunkArgs &a, cudaStream_t s) {
 // into few tiles and leaves SMs idle. When the default tiles would not fill
 // two waves of the values launch, tiles of half the rows are used instead.
 enum : int32_t { TILES_AUTO = 0, TILES_LARGE = 1, TILES_SMALL = 2 };
+// Online scan kernels: one persistent launch (scan_fused.cuh) or the separate
+// score, prefix, value and fold launches of this file.
+enum : int32_t { SCAN_FUSED = 0, SCAN_SPLIT = 1 };
 
 template <int H, int KB, int VB>
 inline bool small_tiles(const ChunkScratch &cs, const Geo &g, int32_t B, const int64_t *h_T) {
@@ -2302,60 +2327,12 @@ inline bool small_tiles(const ChunkScratch &cs, const Geo &g, int32_t B, const i
     }
 }
 
-template <int H, int KB, int VB>
-inline int launch_chunked_auto(ChunkScratch &cs, const Geo &g, const DevTables *tb, int32_t B,
-                               const int32_t *d_seq, const int64_t *d_T, const int64_t *h_T,
-                               const int32_t *d_pt, const uint8_t *pool, const int32_t *q_rot,
-                               int64_t *out, ins_stats *stats, int32_t *d_status, cudaStream_t s) {
-    if constexpr (ChunkCfg<H, KB, VB>::R == 4)
-        if (small_tiles<H, KB, VB>(cs, g, B, h_T))
-            return launch_chunked<H, KB, VB, 2>(cs, g, tb, B, d_seq, d_T, h_T, d_pt, pool, q_rot, out,
-                                                stats, d_status, s);
-    return launch_chunked<H, KB, VB>(cs, g, tb, B, d_seq, d_T, h_T, d_pt, pool, q_rot, out, stats,
-                                     d_status, s);
-}
-
 // Which chunked instantiation serves a cache: 0 none, else (H, KB, VB) packed.
 inline int chunk_variant(const Geo &g, int H) {
     if (!is_def_fmt(g)) return 0;
     if (g.kb == 4 && g.vb == 2 && (H == 1 || H == 2 || H == 4 || H == 8)) return H * 100 + 42;
     if (g.kb == 3 && g.vb == 3 && (H == 4 || H == 8)) return H * 100 + 33;
     return 0;
-}
-
-inline int launch_online(ChunkScratch &cs, const Geo &g, const DevTables *tb, int32_t B,
-                         const int32_t *d_seq, const int64_t *d_lens, const int64_t *h_lens,
-                         const int32_t *d_pt, const uint8_t *pool, const int32_t *q_rot,
-                         int64_t *out, ins_stats *stats, int32_t *d_status, int H,
-                         cudaStream_t s) {
-#define INS_CH(HH, KK, VV)                                                                      \
-    return launch_chunked_auto<HH, KK, VV>(cs, g, tb, B, d_seq, d_lens, h_lens, d_pt, pool, q_rot, \
-                                           out, stats, d_status, s)
-    if (is_def_fmt(g) && g.kb == 4 && g.vb == 2) {
-        switch (H) {
-            case 1: INS_CH(1, 4, 2);
-            case 2: INS_CH(2, 4, 2);
-            case 4: INS_CH(4, 4, 2);
-            case 8: INS_CH(8, 4, 2);
-        }
-    }
-    if (is_def_fmt(g) && g.kb == 3 && g.vb == 3) {
-        switch (H) {
-            case 4: INS_CH(4, 3, 3);
-            case 8: INS_CH(8, 3, 3);
-        }
-    }
-#undef INS_CH
-    cs.last_items = 0;
-    cudaError_t e = cudaErrorInvalidValue;
-    switch (H) {
-        case 1: e = launch_seq<1>(g, tb, B, d_seq, d_lens, d_pt, pool, q_rot, out, stats, nullptr, s); break;
-        case 2: e = launch_seq<2>(g, tb, B, d_seq, d_lens, d_pt, pool, q_rot, out, stats, nullptr, s); break;
-        case 4: e = launch_seq<4>(g, tb, B, d_seq, d_lens, d_pt, pool, q_rot, out, stats, nullptr, s); break;
-        case 8: e = launch_seq<8>(g, tb, B, d_seq, d_lens, d_pt, pool, q_rot, out, stats, nullptr, s); break;
-    }
-    if (e == cudaSuccess) cs.launches += 1;
-    return e == cudaSuccess ? INS_OK : INS_ECUDA;
 }
 
 }  // namespace ins

@@ -129,6 +129,16 @@ class PagedCache:
         or "small". A tuning knob; every mode gives the same results."""
         _lib.check(self._L.ins_cache_set_tiles(self._h, _lib.INS_TILES[mode]))
 
+    def set_scan_kernel(self, mode: str = "fused") -> None:
+        """Kernels of the online scan (ins_cache_set_scan_kernel): "fused" (one
+        persistent launch) or "split" (separate launches). Same results."""
+        _lib.check(self._L.ins_cache_set_scan_kernel(self._h, _lib.INS_SCAN[mode]))
+
+    def set_wait_test(self, poll_limit: int = 1 << 22, item: int = -1, chunk: int = 0,
+                      head: int = 0) -> None:
+        """Test hook of the fused scan's bounded waits (ins_cache_set_wait_test)."""
+        _lib.check(self._L.ins_cache_set_wait_test(self._h, poll_limit, item, chunk, head))
+
     def recomputed(self) -> int:
         """Items of the last online scan that the exact sequential kernel redid
         (ins_scan_recomputed); 0 when the context-parallel scan proved them all."""

@@ -310,9 +310,10 @@ def test_queries_at_the_edge_of_the_fp64_range():
         assert int(_np(ovf)[0]) == wovf
 
 
-@pytest.mark.parametrize("groups", [1, 2, 4])
+@pytest.mark.parametrize("groups", [1, 2, 4, 8])
 @pytest.mark.parametrize("tiles", ["large", "small"])
-def test_both_tile_sizes_match_oracle(groups, tiles):
+@pytest.mark.parametrize("kernel", ["fused", "split"])
+def test_both_tile_sizes_match_oracle(groups, tiles, kernel):
     """The scan's two tile sizes (4 or 2 rows per thread; "auto" picks by
     context) give the oracle's bits, for a ragged batch with one sequence of
     rising keys whose running maximum moves across tile boundaries."""
@@ -321,6 +322,7 @@ def test_both_tile_sizes_match_oracle(groups, tiles):
     B = len(lens)
     pc = _pc(n_kv=8, groups=groups, max_seqs=B, capacity=6144)
     pc.set_tiles(tiles)
+    pc.set_scan_kernel(kernel)
     orc = make_oracle()
     caches = []
     for b, T in enumerate(lens):
@@ -428,13 +430,15 @@ def _rising_keys(T, step, rng):
     return np.clip(k, -(1 << 23), (1 << 23) - 1).astype(np.int32), base
 
 
-@pytest.mark.parametrize("T,step", [(5000, 97), (3000, 1)])
-def test_rescales_across_chunks_and_fallback(T, step):
+@pytest.mark.parametrize("T,step", [(5000, 97), (3000, 1), (70000, 211)])
+@pytest.mark.parametrize("kernel", ["fused", "split"])
+def test_rescales_across_chunks_and_fallback(T, step, kernel):
     rng = np.random.default_rng(T + step)
     kk, base = _rising_keys(T, step, rng)
     k = np.stack([kk] * 8, axis=1)
     v = _wire(rng, (T, 8, 64))
     pc = _pc(capacity=T)
+    pc.set_scan_kernel(kernel)
     pc.ingress(np.zeros(T, np.int32), k, v)
     orc = make_oracle()
     qr = orc.rotate(np.tile(base[None, None, :] // 4, (1, 32, 1)))
@@ -450,3 +454,32 @@ def test_rescales_across_chunks_and_fallback(T, step):
     out2, st2 = pc.scan([0], q_rot)
     np.testing.assert_array_equal(_np(out2), want)
     np.testing.assert_array_equal(_np(st2), wst)
+
+
+# -- failure detection: a bounded wait that runs out ---------------------------------
+
+def test_a_lookback_wait_that_runs_out_is_reported_and_the_context_survives():
+    """The single-launch scan's tiles wait (bounded) for words the tiles
+    before them publish. Withholding one word -- a flag nothing sets -- makes
+    the waits behind it give up after the lowered poll limit: the launch
+    still finishes, ins_cache_status reports INS_ETIMEOUT (DeviceTimeout),
+    and the next scan on the same context is exact again. Nothing faults."""
+    from insitu_b200._lib import DeviceTimeout
+    rng = np.random.default_rng(66)
+    T = 40000                              # 40 tiles of 1024 rows per item
+    pc = _pc(capacity=T)
+    k, v = _wire(rng, (T, 8, 64)), _wire(rng, (T, 8, 64))
+    pc.ingress(np.zeros(T, np.int32), k, v)
+    orc = make_oracle()
+    qr = orc.rotate(_wire(rng, (1, 32, 64), 1.0 / 8.0))
+    q_rot = torch.from_numpy(qr.astype(np.int32))
+    want, wst = orc.decode_layer(qr, [orc.ingress_rows(k, v, threads=8)], threads=8)
+    pc.set_wait_test(poll_limit=64, item=3, chunk=5, head=2)
+    pc.scan([0], q_rot)
+    with pytest.raises(DeviceTimeout):
+        pc.status()
+    pc.set_wait_test()                     # the defaults: nothing withheld
+    out, st = pc.scan([0], q_rot)
+    pc.status()
+    np.testing.assert_array_equal(_np(out), want)
+    np.testing.assert_array_equal(_np(st), wst)

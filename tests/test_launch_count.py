@@ -1,7 +1,8 @@
 """The library's own count of the kernels it launched (ins_cache_launches),
-which bench.py reports as gpu_launches: one ingress per step, and a chunked
-scan of 5 launches when every item's tiles fit one fold block, 6 when they do
-not (the block fold runs as its own launch)."""
+which bench.py reports as gpu_launches: one ingress per step, then the online
+scan -- 2 launches with the single-launch kernels (the scan and the exact
+re-run of unproven items), or, with the separate launches, 5 when every item's
+tiles fit one fold block and 6 when they do not."""
 
 from __future__ import annotations
 
@@ -16,13 +17,15 @@ def _wire(rng, shape, scale=1.0):
     return np.clip(x, -(1 << 23), (1 << 23) - 1).astype(np.int32)
 
 
-@pytest.mark.parametrize("T,per_step", [(4096, 6), (48 * 1024, 7)])
-def test_launches_per_decode_step(T, per_step):
+@pytest.mark.parametrize("T,kernel,per_step", [(4096, "fused", 3), (48 * 1024, "fused", 3),
+                                               (4096, "split", 6), (48 * 1024, "split", 7)])
+def test_launches_per_decode_step(T, kernel, per_step):
     pytest.importorskip("torch")
     from insitu_b200 import DecodeAttention, FixedFormat, Geometry, QuantConfig
     rng = np.random.default_rng(T)
     dec = DecodeAttention(QuantConfig(key_bits=4, value_bits=2), FixedFormat(), Geometry(8, 4, 64),
                           max_seqs=1, capacity=T + 8)
+    dec.pc.set_scan_kernel(kernel)
     dec.prefill(0, _wire(rng, (T, 8, 64)), _wire(rng, (T, 8, 64)))
     before = dec.pc.launches()
     for _ in range(3):

@@ -72,25 +72,19 @@ def test_noalloc_scan_equals_scan_on_two_calls_in_a_row():
 
 def test_noalloc_scan_refuses_work_beyond_its_array():
     from insitu_b200._lib import CapacityError
-    # one sequence of 1.5M tokens: its score offsets alone (8 KV heads x 4
-    # query heads x 4 bytes per row) need more than the 192 MiB array
-    T, step = 1_500_000, 250_000
-    pc = _pc(max_seqs=1, capacity=T)
-    g = torch.Generator(device=pc.device)
-    g.manual_seed(33)
-    for t0 in range(0, T, step):
-        k = torch.randint(-(1 << 20), 1 << 20, (step, 8, 64), generator=g, device=pc.device,
-                          dtype=torch.int32)
-        v = torch.randint(-(1 << 20), 1 << 20, (step, 8, 64), generator=g, device=pc.device,
-                          dtype=torch.int32)
-        pc.ingress(np.zeros(step, np.int32), k, v)
-    q_rot = pc.rotate(torch.from_numpy(_wire(np.random.default_rng(32), (1, 32, 64), 1.0 / 8.0)))
+    # 4096 sequences of one token each: 32,768 (sequence, KV head) items,
+    # each with its tile and block records, need more than the 192 MiB array
+    B = 4096
+    pc = _pc(max_seqs=B, capacity=256)
+    rng = np.random.default_rng(33)
+    pc.ingress(np.arange(B, dtype=np.int32), _wire(rng, (B, 8, 64)), _wire(rng, (B, 8, 64)))
+    q_rot = pc.rotate(torch.from_numpy(_wire(rng, (B, 32, 64), 1.0 / 8.0)))
     with pytest.raises(CapacityError, match="scratch"):
-        _noalloc(pc, np.arange(1), q_rot)
+        _noalloc(pc, np.arange(B), q_rot)
     # the regular entry point still serves the same scan
-    out, _ = pc.scan(np.arange(1), q_rot)
+    out, _ = pc.scan(np.arange(B), q_rot)
     torch.cuda.synchronize(pc.device)
-    assert out.shape == (1, 32, 64)
+    assert out.shape == (B, 32, 64)
 
 
 def test_noalloc_scan_of_a_large_batch_stays_on_the_fast_path():
