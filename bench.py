@@ -415,11 +415,36 @@ def cpu_baseline(device: int, sample_tokens: int = 1 << 18):
     t0 = time.perf_counter()
     orc.decode_layer(qr, [rows], threads=threads)
     dt = time.perf_counter() - t0
-    return {"value": round(N_KV * sample_tokens * ROW_BYTES / dt / 1e9, 4), "unit": "GB/s",
-            "cores": min(threads, N_KV), "kind": "port",
-            "sample": f"attend_online (oracle C port) over {sample_tokens} cached tokens x 8 KV "
-                      f"heads x 4 q heads, one decode step, {dt:.2f} s on "
-                      f"{min(threads, N_KV)} host threads (one per KV head)"}
+    # the same port on one thread, over one KV head's rows of the sample
+    t0 = time.perf_counter()
+    orc.decode_layer(qr[:, :GROUPS], [rows[:, :1]], threads=1)
+    dt1 = time.perf_counter() - t0
+    res = {"value": round(N_KV * sample_tokens * ROW_BYTES / dt / 1e9, 4), "unit": "GB/s",
+           "cores": min(threads, N_KV), "kind": "port",
+           "sample": f"attend_online (oracle C port) over {sample_tokens} cached tokens x 8 KV "
+                     f"heads x 4 q heads, one decode step, {dt:.2f} s on "
+                     f"{min(threads, N_KV)} host threads (one per KV head)",
+           "port_one_thread": {"value": round(sample_tokens * ROW_BYTES / dt1 / 1e9, 4), "unit": "GB/s",
+                               "cores": 1, "sample": f"one KV head of the same sample, {dt1:.2f} s"}}
+    # the reference's own numpy path, timed where the reference is installed
+    # (it does not travel to the GPU machine): tests/golden/time_reference.py
+    try:
+        with open(os.path.join(ROOT, "tests", "golden", "cpu_reference_timings.json")) as f:
+            ref = json.load(f)
+        r = ref["32768"]
+        res["reference_numpy"] = {
+            "attend_online_GBps": r["attend_online_GBps"],
+            "attend_two_pass_GBps": r["attend_two_pass_GBps"],
+            "attend_online_us_per_token": r["attend_online_us_per_token"],
+            "attend_two_pass_us_per_token": r["attend_two_pass_us_per_token"],
+            "encode_pack_us_per_token": r["encode_pack_us_per_token"],
+            "cores": ref["cores_used"],
+            "where": f"the build machine's CPU ({ref['cpu_count']} cores, numpy {ref['numpy']}), "
+                     "one KV head x 4 query heads at 32K tokens",
+        }
+    except (OSError, KeyError, ValueError):
+        pass
+    return res
 
 
 # ---------------------------------------------------------------------------

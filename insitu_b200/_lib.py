@@ -20,7 +20,7 @@ SOURCES = ("csrc/insitu.cu", "csrc/common.cuh", "csrc/kernels.cuh", "csrc/scan_c
 HEADER = os.path.join(ROOT, "include", "insitu_b200.h")
 
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", "-std=c++17",
-              "-Xcompiler", "-fPIC", "-shared"]
+              "-Xcompiler", "-fPIC", "-shared", "-Xlinker", "-soname=libinsitu_b200.so"]
 
 # status codes (insitu_b200.h)
 INS_OK, INS_EBADLEN, INS_ETIMEOUT, INS_ERANGE, INS_EINVAL, INS_ENOMEM, INS_ECUDA = 0, 4, 5, 7, 8, 9, 10
@@ -122,6 +122,57 @@ def build(force: bool = False, verbose: bool = False) -> str:
     subprocess.run(cmd, check=True, cwd=HERE)
     os.replace(tmp, LIB_PATH)
     return LIB_PATH
+
+
+TORCH_OPS_PATH = os.path.join(HERE, "libinsitu_torch.so")
+TORCH_OPS_SOURCE = os.path.join(HERE, "csrc", "torch_ops.cpp")
+
+
+def build_torch_ops(force: bool = False, verbose: bool = False) -> str:
+    """Compile the thin torch extension (``csrc/torch_ops.cpp``) in-tree,
+    linked against ``libinsitu_b200.so`` (found next to it at run time)."""
+    import sysconfig
+
+    import torch
+    from torch.utils import cpp_extension
+    srcs = [TORCH_OPS_SOURCE, HEADER]
+    if not force and os.path.exists(TORCH_OPS_PATH):
+        if os.path.getmtime(TORCH_OPS_PATH) >= max(os.path.getmtime(s) for s in srcs):
+            return TORCH_OPS_PATH
+    build(verbose=verbose)
+    inc = [f"-I{p}" for p in cpp_extension.include_paths(device_type="cuda")]
+    libdirs = [f"-L{p}" for p in cpp_extension.library_paths(device_type="cuda")]
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    tmp = TORCH_OPS_PATH + ".tmp"
+    cmd = [shutil.which("g++") or "g++", "-O2", "-std=c++17", "-fPIC", "-shared",
+           f"-D_GLIBCXX_USE_CXX11_ABI={abi}", *inc, f"-I{sysconfig.get_paths()['include']}",
+           TORCH_OPS_SOURCE, "-o", tmp, *libdirs, f"-L{HERE}", "-linsitu_b200",
+           "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda",
+           "-Wl,-rpath,$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd))
+    subprocess.run(cmd, check=True, cwd=HERE)
+    os.replace(tmp, TORCH_OPS_PATH)
+    return TORCH_OPS_PATH
+
+
+_ops = None
+
+
+def ops():
+    """The torch operators of the extension (torch.ops.insitu). Raises if the
+    extension was never built -- there is no fallback."""
+    global _ops
+    if _ops is not None:
+        return _ops
+    import torch
+    lib()                                   # the C ABI first, so the extension resolves against it
+    if not os.path.exists(TORCH_OPS_PATH):
+        raise RuntimeError(f"{TORCH_OPS_PATH} is missing: build it with "
+                           "insitu_b200._lib.build_torch_ops(). insitu_b200 has no fallback.")
+    torch.ops.load_library(TORCH_OPS_PATH)
+    _ops = torch.ops.insitu
+    return _ops
 
 
 _lib = None

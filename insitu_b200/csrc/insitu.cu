@@ -1173,7 +1173,7 @@ int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
     // rescale-segment pool, which takes what the rest leaves, up to what
     // ins_scan would reserve; an item whose segments do not fit is recomputed
     // by the sequential kernel (still exact, only slower).
-    const ScratchLayout L0(n_items, tp.max_nc, 0, 1, H, CF::CW, 0);
+    const ScratchLayout L0(n_items, tp.max_nc, 0, tiles, H, CF::CW, 0);
     if (L0.total + staging > NOALLOC_BYTES)
         return fail(INS_EBADLEN, "this scan needs " + std::to_string(L0.total + staging) + " B of scratch; "
                                  "ins_scan_noalloc holds " + std::to_string(NOALLOC_BYTES) + " B");
@@ -1181,7 +1181,7 @@ int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
     const int64_t seg_fit = (int64_t)((NOALLOC_BYTES - L0.total - staging - 256) / sizeof(SegEntry));
     const int seg_cap = (int)std::min<int64_t>(std::min(seg_want, seg_fit), INT32_MAX);
     // the carve, in the same order ins_scan's scratch uses
-    const ScratchLayout L(n_items, tp.max_nc, seg_cap, 1, H, CF::CW, 0);
+    const ScratchLayout L(n_items, tp.max_nc, seg_cap, tiles, H, CF::CW, 0);
     const size_t o_T = L.total;
     const size_t o_seq = o_T + ((sizeof(int64_t) * (size_t)B + 255) & ~(size_t)255);
     const size_t o_end = o_seq + sizeof(int32_t) * (size_t)B;
@@ -1236,6 +1236,7 @@ int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
     x.blk_done = (unsigned int *)(p + L.bdone);
     x.item_done = (unsigned int *)(p + L.idone);
     x.scan_done = (unsigned int *)(p + L.sdone);
+    x.fold_at = p + L.foldat;
     x.epoch = 1;
     x.poll_limit = c->chunk.poll_limit;
     x.hold_word = -1;

@@ -342,6 +342,7 @@ struct ChunkScratch {
     unsigned long long *lbw = nullptr;   // look-back words of the fused scan
     size_t lbw_words = 0;
     unsigned int *bdone = nullptr, *idone = nullptr, *sdone = nullptr;
+    uint8_t *fold_at = nullptr;
     unsigned int epoch = 0;       // of the last fused scan, 1 .. 4095
     int64_t launches = 0;         // kernels launched by ingress, seam and scan calls (a count)
     int64_t sc_rows = 0;          // rows * H capacity of `sc`, in 32-bit words
@@ -2090,7 +2091,7 @@ inline int chunk_slots() {
 
 // Byte layout of the scratch of one scan: `o` offsets in the order carved.
 struct ScratchLayout {
-    size_t top, cmx, rec, blk, seg, items, redo, desc, bmg, sc, lbw, bdone, idone, sdone, total;
+    size_t top, cmx, rec, blk, seg, items, redo, desc, bmg, sc, lbw, bdone, idone, sdone, foldat, total;
     ScratchLayout(int ni, int mc, int sc_cap, int tc, int H, int CW, int64_t rows) {
         auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
         const int mb = (mc + GBLK - 1) / GBLK;
@@ -2101,6 +2102,7 @@ struct ScratchLayout {
         bdone = o; o += al(sizeof(unsigned int) * (size_t)ni * mb);
         idone = o; o += al(sizeof(unsigned int) * (size_t)ni);
         sdone = o; o += al(sizeof(unsigned int));
+        foldat = o; o += al((size_t)tc);
         cmx = o; o += al(sizeof(long long) * (size_t)ni * mc * 2 * HMAX);
         rec = o; o += al(sizeof(ChunkRec) * (size_t)ni * mc);
         blk = o; o += al(sizeof(BlockRec) * (size_t)ni * mb);
@@ -2108,7 +2110,8 @@ struct ScratchLayout {
         items = o; o += al(sizeof(ItemAcc) * (size_t)ni);
         redo = o; o += al(sizeof(int32_t) * (size_t)ni);
         desc = o; o += al(TileDesc(ni).total);
-        bmg = o; o += al(sizeof(long long) * (size_t)tc * H * CW);
+        // block maxima and score offsets: the separate-launch scan only
+        bmg = o; o += al(sizeof(long long) * (size_t)(rows > 0 ? tc : 1) * H * CW);
         sc = o; o += al(sizeof(uint32_t) * (size_t)(rows > 0 ? rows : 1) * H);
         total = o;
     }
@@ -2159,6 +2162,7 @@ inline int reserve_scratch(ChunkScratch &cs, int n_items, int max_nc, int n_tile
     cs.bdone = (unsigned int *)(p + L.bdone);
     cs.idone = (unsigned int *)(p + L.idone);
     cs.sdone = (unsigned int *)(p + L.sdone);
+    cs.fold_at = p + L.foldat;
     cs.lbw_words = (size_t)ni * mc * HMAX;
     cs.epoch = 0;
     cs.n_items = ni;

@@ -80,6 +80,7 @@ struct FusedExtra {
     unsigned int *blk_done;       // [n_items][max_blocks] tiles folded into each block so far
     unsigned int *item_done;      // [n_items] blocks folded into each item so far
     unsigned int *scan_done;      // items finished in this launch
+    uint8_t *fold_at;             // [n_tiles] 1: the tile completed its block, which its CTA folds
     unsigned int epoch;           // 1 .. 2^12 - 1
     int32_t poll_limit;           // polls before a look-back wait gives up
     int64_t hold_word;            // a word index never published (test of the bounded wait), or -1
@@ -199,7 +200,6 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
                   VS = CF::VS;
     constexpr int UPW = 32 / H;                 // table units per warp in the build
     constexpr int PGMAX = C / 16 + 1;           // pages a tile touches (P >= 16)
-    constexpr int PPL = (PGMAX + 31) / 32;
     extern __shared__ __align__(16) uint8_t dyn[];
     __shared__ __align__(16) double qd[D * H];   // [channel][head] of the item being scored
     __shared__ int32_t vcent[16];
@@ -212,8 +212,9 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
     __shared__ unsigned int lsum_sm[H][SEGMAX + 1];    // l of a tile < 2^25
     __shared__ long long bnd_sm[NT / 32][H];           // per-warp clamp-proof bounds
     __shared__ unsigned int resc_sm;
-    __shared__ int4 tdesc_sm[3];                       // tiles li-1, li, li+1 (ring of 3)
-    __shared__ int32_t pages_sm[3][PGMAX];
+    __shared__ int4 tdesc_sm[4];                       // tiles li-1 .. li+2 (ring of 4)
+    __shared__ int32_t pages_sm[4][PGMAX];
+    __shared__ int prev_item_sm, gave_up_sm;
 
     const double2 *ctab = reinterpret_cast<const double2 *>(dyn);
     uint32_t *d_sm = reinterpret_cast<uint32_t *>(dyn + FC::OFF_S);
@@ -238,13 +239,11 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
         }
         for (int i = tid; i < 256; i += NT) exp_tab[i] = a.tb->exp_tab[i];
         if (tid < 16) vcent[tid] = tid < NC ? (int32_t)a.tb->v_cent[tid] : 0;
+        if (tid == 0) {
+            prev_item_sm = -1;
+            gave_up_sm = 0;
+        }
     }
-    int64_t cmax_v = 0;                         // max |V centroid|
-    for (int k = 0; k < NC; ++k) {
-        const int64_t ab = a.tb->v_cent[k] < 0 ? -a.tb->v_cent[k] : a.tb->v_cent[k];
-        cmax_v = ab > cmax_v ? ab : cmax_v;
-    }
-    const double2 *myc = ctab + (lane & 7);
     const int G = gridDim.x;
     const int ntl = (a.n_tiles - (int)blockIdx.x + G - 1) / G;
     constexpr long long s_lo = DefFmt::S_LO;
@@ -252,14 +251,9 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
     // everything below reads what the launches before this one wrote
     wait_prior_grid();
 
-    // Tile lookups, one step ahead of their first use: warp 1 loads tile j's
-    // descriptor and page ids into registers (look_load) and stores them into
-    // ring slot j % 3 later (look_store).
-    int citem = -1, cseq = 0;
-    int64_t cT = 0;
-    int4 rtd = make_int4(0, 0, 0, 0);
-    int32_t rpg[PPL];
-    auto look_load = [&](int j) {
+    // Tile j's descriptor and page ids into ring slot j % 4, by one warp:
+    // loaded and stored at once, so that nothing of it stays in registers.
+    auto look = [&](int j) {
         const int tile = (int)blockIdx.x + j * G;
         int item, c;
         if (a.n_runs == 1) {
@@ -271,63 +265,43 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
             item = t.x;
             c = t.y;
         }
-        if (item != citem) {
-            citem = item;
-            cT = a.T[item / g.n_kv];
-            cseq = a.seq_ids[item / g.n_kv];
-        }
+        const int64_t T = a.T[item / g.n_kv];
+        const int seq = a.seq_ids[item / g.n_kv];
         const int64_t tt0 = (int64_t)c * a.tile_rows;
-        const int64_t tn = cT - tt0 < a.tile_rows ? cT - tt0 : a.tile_rows;
-        rtd = make_int4(item, c, (int)tt0, (int)(tn > 0 ? tn : 0));
-        const int poff = (int)(rtd.z % g.P);
-        const int npg = rtd.w ? (poff + rtd.w + g.P - 1) / g.P : 0;
-        const int32_t *pt = a.page_table + (int64_t)cseq * g.max_pages + rtd.z / g.P;
-#pragma unroll
-        for (int k = 0; k < PPL; ++k) {
-            const int i = lane + 32 * k;
-            rpg[k] = i < npg ? __ldg(pt + i) : 0;
-        }
+        const int64_t tn = T - tt0 < a.tile_rows ? T - tt0 : a.tile_rows;
+        const int4 td = make_int4(item, c, (int)tt0, (int)(tn > 0 ? tn : 0));
+        const int poff = (int)(td.z % g.P);
+        const int npg = td.w ? (poff + td.w + g.P - 1) / g.P : 0;
+        const int32_t *pt = a.page_table + (int64_t)seq * g.max_pages + td.z / g.P;
+        for (int i = lane; i < PGMAX; i += 32) pages_sm[j & 3][i] = i < npg ? __ldg(pt + i) : 0;
+        if (lane == 0) tdesc_sm[j & 3] = td;
     };
-    auto look_store = [&](int j) {
-#pragma unroll
-        for (int k = 0; k < PPL; ++k) {
-            const int i = lane + 32 * k;
-            if (i < PGMAX) pages_sm[j % 3][i] = rpg[k];
-        }
-        if (lane == 0) tdesc_sm[j % 3] = rtd;
-    };
-    if (warp == 1) {
-        if (ntl > 0) {
-            look_load(0);
-            look_store(0);
-        }
-        if (ntl > 1) {
-            look_load(1);
-            look_store(1);
-        }
+    constexpr int LOOK_WARP = NT / 32 - 1;
+    if (warp == LOOK_WARP) {
+        if (ntl > 0) look(0);
+        if (ntl > 1) look(1);
+        __syncwarp();
         if (ntl > 0) prefetch_rows(a, tdesc_sm[0], pages_sm[0], lane, 3);
     }
     __syncthreads();
 
-    int prev_item = -1;
-    bool gave_up = false;
     for (int li = 0; li <= ntl; ++li) {
-        // tile li + 2 is looked up while this step runs
-        if (warp == 1 && li + 2 < ntl) look_load(li + 2);
+        // tile li + 2 is looked up while this step runs (its ring slot is free)
+        if (warp == LOOK_WARP && li + 2 < ntl) look(li + 2);
 
         // =====================================================================
         // values(li - 1)
         // =====================================================================
         if (li >= 1) {
             const int vj = li - 1;
-            const int4 td = tdesc_sm[vj % 3];
+            const int4 td = tdesc_sm[vj & 3];
             const int item = td.x, c = td.y;
             const int64_t t0 = td.z;
             const int n = td.w;
             const int kvh = item % g.n_kv;
             const int rec_idx = item * a.max_chunks + c;
             const int poff = (int)(t0 % g.P);
-            const int32_t *ptab = pages_sm[vj % 3];
+            const int32_t *ptab = pages_sm[vj & 3];
 
             // ---- 0. the tile's V rows (each thread its own) ------------------
             uint32_t vw[R][VW], nw[R];
@@ -364,7 +338,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
                 const long long tm = warp_max_score(bm);
                 if (lane == 0) {
                     m_in_sm[warp] = m_in;
-                    if (late) gave_up = true;
+                    if (late) gave_up_sm = 1;
                     const int64_t wi = ((int64_t)item * a.max_chunks + c) * H + warp;
                     if (wi != x.hold_word)
                         st_relaxed_gpu(x.lbw + wi, lb_word(tm > m_in ? tm : m_in, LB_PRE, x.epoch));
@@ -745,6 +719,11 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
                     rec.l0[h] = (int64_t)lsum_sm[h][0];
                     long long sw = 0;
                     for (int w = 0; w < NT / 32; ++w) sw += bnd_sm[w][h];
+                    int64_t cmax_v = 0;                  // max |V centroid|
+                    for (int k = 0; k < NC; ++k) {
+                        const int64_t ab = vcent[k] < 0 ? -(int64_t)vcent[k] : (int64_t)vcent[k];
+                        cmax_v = ab > cmax_v ? ab : cmax_v;
+                    }
                     rec.B[h] = ((sw * cmax_v) >> DefFmt::ACC_SHIFT) + n;
                     rec.nseg[h] = seg_ok ? nseg_sm[h] : 0;
                     rec.seg_base[h] = segbase_sm[h];
@@ -763,7 +742,9 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
                 last_sm = old == (unsigned)(ntb - 1);
             }
             __syncthreads();
-            if (last_sm) fold_block_and_item<H>(a, x, item, c);
+            // the fold itself waits for the end of the loop (a call here would
+            // cost the loop its registers)
+            if (tid == 0) x.fold_at[blockIdx.x + vj * G] = (uint8_t)last_sm;
             __syncthreads();                 // the tile's shared memory is reused below
         }
 
@@ -771,14 +752,14 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
         // scores(li)
         // =====================================================================
         if (li < ntl) {
-            const int4 td = tdesc_sm[li % 3];
+            const int4 td = tdesc_sm[li & 3];
             const int item = td.x, c = td.y;
             const int64_t t0 = td.z;
             const int n = td.w;
             const int b = item / g.n_kv, kvh = item % g.n_kv;
             const int64_t qbase = ((int64_t)b * g.n_kv * H + (int64_t)kvh * H) * D;
             const int poff = (int)(t0 % g.P);
-            const int32_t *ptab = pages_sm[li % 3];
+            const int32_t *ptab = pages_sm[li & 3];
 
             // the rows first, so their loads overlap the query setup
             uint32_t kw[R][KB * 2];
@@ -798,10 +779,11 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
                 knorm[r] = row < n ? (int64_t)(int16_t)(nwr & 0xffffu) : 0;
             }
             // the next tile's rows into L2 while this one computes
-            if (warp == 1 && li + 1 < ntl) prefetch_rows(a, tdesc_sm[(li + 1) % 3], pages_sm[(li + 1) % 3], lane, 3);
+            if (warp == 1 && li + 1 < ntl) prefetch_rows(a, tdesc_sm[(li + 1) & 3], pages_sm[(li + 1) & 3], lane, 3);
             if (tid < H) tmax_sm[tid] = LLONG_MIN;
-            if (item != prev_item) {
-                prev_item = item;
+            if (item != prev_item_sm) {
+                __syncthreads();                 // every thread has read prev_item_sm
+                if (tid == 0) prev_item_sm = item;
                 for (int i = tid; i < H * D; i += NT) qd[(i % D) * H + i / D] = (double)a.q_rot[qbase + i];
                 __syncthreads();
                 bool big = false;
@@ -825,7 +807,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
                 double c0[R], c1[R];
 #pragma unroll
                 for (int r = 0; r < R; ++r) {
-                    const double2 cc = myc[kpair<KB>(kw[r], p) * 8];
+                    const double2 cc = ctab[(lane & 7) + kpair<KB>(kw[r], p) * 8];
                     c0[r] = cc.x;
                     c1[r] = cc.y;
                 }
@@ -911,11 +893,17 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
                 if (wi != x.hold_word) st_relaxed_gpu(x.lbw + wi, lb_word(tmax_sm[tid], LB_AGG, x.epoch));
             }
         }
-        // the lookup of tile li + 2 takes the ring slot tile li - 1 used
-        if (warp == 1 && li + 2 < ntl) look_store(li + 2);
         __syncthreads();
     }
-    if (gave_up) atomicOr(a.status, ST_TIMEOUT);
+    // the blocks whose last tile this CTA wrote, folded now
+    for (int li = 0; li < ntl; ++li) {
+        const int tile = (int)blockIdx.x + li * G;
+        if (!x.fold_at[tile]) continue;       // the same value for every thread
+        const int4 t = tile_at(a, tile);
+        fold_block_and_item<H>(a, x, t.x, t.y);
+        __syncthreads();
+    }
+    if (tid == 0 && gave_up_sm) atomicOr(a.status, ST_TIMEOUT);
 }
 
 // ---------------------------------------------------------------------------
@@ -989,6 +977,7 @@ inline int launch_online_tiles(ChunkScratch &cs, const Geo &g, const DevTables *
     x.blk_done = cs.bdone;
     x.item_done = cs.idone;
     x.scan_done = cs.sdone;
+    x.fold_at = cs.fold_at;
     x.epoch = cs.epoch;
     x.poll_limit = cs.poll_limit;
     x.hold_word = cs.hold_item < 0 || cs.hold_item >= a.n_items || cs.hold_chunk >= a.max_chunks

@@ -44,6 +44,8 @@ class DecodeAttention:
         """
         B = q.shape[0]
         ids = list(range(B)) if seq_ids is None else seq_ids
+        if out is None and stats_out is None:
+            return self.pc.step(ids, q, k, v, mode=mode)
         q_rot = self.pc.ingress(ids, k, v, q)
         return self.pc.scan(ids, q_rot, mode=mode, out=out, stats_out=stats_out)
 

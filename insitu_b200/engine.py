@@ -48,6 +48,16 @@ def _host_array(x, n: int, ctype, np_dtype):
     return arr, arr.ctypes.data
 
 
+def _ids(x, n: int) -> list:
+    """``x`` (a scalar, a sequence or an array) as a list of ``n`` Python ints,
+    the form the torch operators take."""
+    if isinstance(x, list) and len(x) == n:
+        return x
+    if isinstance(x, (int, np.integer)):
+        return [int(x)] * n
+    return np.broadcast_to(np.asarray(x, dtype=np.int64), (n,)).tolist()
+
+
 def _require_cuda():
     if not torch.cuda.is_available():
         raise RuntimeError("insitu_b200 needs a CUDA device (sm_100a); there is no CPU path")
@@ -88,6 +98,7 @@ class PagedCache:
         p = lambda a: a.ctypes.data_as(C.POINTER(C.c_int64))
         tb = _lib.Tables(*(p(a) for a in self._keep), t.log2e, t.delta_max)
         self._L = _lib.lib()
+        self._ops = _lib.ops()                 # the torch operators of the per-step calls
         h = C.c_void_p()
         _lib.check(self._L.ins_cache_create(C.byref(self.cfg), C.byref(tb), self.device.index,
                                             C.byref(h)))
@@ -185,18 +196,12 @@ class PagedCache:
         n = k.shape[0]
         if v.shape[0] != n:
             raise ValueError("k and v carry different token counts")
-        ids, ids_p = _host_array(seq_ids, n, C.c_int32, np.int32)
-        q_rot = None
         if q is not None:
             q = self._dev_i32(q, (g.num_heads, g.head_dim))
             if q.shape[0] != n:
                 raise ValueError("q carries a different token count")
-            q_rot = torch.empty_like(q)
-        flags = _lib.INS_INGRESS_PREROTATED if prerotated else 0
-        _lib.check(self._L.ins_ingress(self._h, n, ids_p, _ptr(q),
-                                       _ptr(k), _ptr(v), _ptr(q_rot), flags,
-                                       _stream(self.device)))
-        return q_rot
+        return self._ops.ingress(self._h.value, _ids(seq_ids, n), k, v, q, g.n_kv_heads, g.num_heads,
+                                 prerotated)
 
     def ingress_lanes(self, seq_ids, lanes) -> torch.Tensor:
         """ins_ingress from the board's ingress stream: ``lanes`` holds n tokens
@@ -282,18 +287,28 @@ class PagedCache:
         g = self.geo
         q = self._dev_i32(q_rot, (g.num_heads, g.head_dim))
         B = q.shape[0]
-        ids, ids_p = _host_array(seq_ids, B, C.c_int32, np.int32)
-        lens, lens_p = (None, None) if lengths is None else _host_array(lengths, B, C.c_int64, np.int64)
-        if out is None:
-            out = torch.empty((B, g.num_heads, g.head_dim), dtype=torch.int64, device=self.device)
-        st = None
-        if stats:
-            st = stats_out if stats_out is not None else torch.empty(
-                (B, g.n_kv_heads, len(_lib.STATS_FIELDS)), dtype=torch.int64, device=self.device)
+        lens = None if lengths is None else _ids(lengths, B)
         m = {"online": _lib.INS_SOFTMAX_ONLINE, "two_pass": _lib.INS_SOFTMAX_TWO_PASS}[mode]
-        _lib.check(self._L.ins_scan(self._h, B, ids_p, lens_p, _ptr(q), _ptr(out), _ptr(st), m,
-                                    _stream(self.device)))
-        return out, st
+        res, st = self._ops.scan(self._h.value, _ids(seq_ids, B), lens, q, g.n_kv_heads, m,
+                                 bool(stats or stats_out is not None))
+        if out is not None:
+            out.copy_(res)
+            res = out
+        if stats_out is not None:
+            stats_out.copy_(st)
+            st = stats_out
+        return res, (st if stats else None)
+
+    def step(self, seq_ids, q, k, v, *, mode: str = "online", stats: bool = True):
+        """One decode token per sequence in one call (the ``insitu::step``
+        operator): the ingress of q, k, v (B rows, one per sequence), then the
+        scan of every sequence with the new token. Returns (out, stats)."""
+        g = self.geo
+        k = self._dev_i32(k, (g.n_kv_heads, g.head_dim))
+        v = self._dev_i32(v, (g.n_kv_heads, g.head_dim))
+        q = self._dev_i32(q, (g.num_heads, g.head_dim))
+        m = {"online": _lib.INS_SOFTMAX_ONLINE, "two_pass": _lib.INS_SOFTMAX_TWO_PASS}[mode]
+        return self._ops.step(self._h.value, _ids(seq_ids, q.shape[0]), q, k, v, g.n_kv_heads, m, stats)
 
     # -- context split (one sequence across shards) -------------------------------
     S_LO = -(1 << 47)   # the running maximum before any token (score_width 48)

@@ -61,30 +61,45 @@ class Plane:
         return total // 8
 
 
+# The row format (ops/quantize.py:237-264): a field of d codes of `bits` bits
+# is the little-endian integer sum(code_j << (bits * j)) in d * bits / 8
+# bytes, and a norm is a little-endian two's-complement integer of norm_bits.
+# Eight consecutive codes fill exactly `bits` bytes, so each group of eight is
+# assembled as one 64-bit word (the ingress kernel packs 32-bit words the same
+# way) and its low `bits` bytes are kept.
+
 def _pack_codes(idx: np.ndarray, bits: int) -> np.ndarray:
-    flat = np.asarray(idx, dtype=np.uint8).reshape(-1, idx.shape[-1])
-    bit = np.unpackbits(flat[:, :, None], axis=2, bitorder="little")[:, :, :bits]
-    return np.packbits(bit.reshape(flat.shape[0], -1), axis=1, bitorder="little").reshape(
-        *idx.shape[:-1], -1)
+    idx = np.asarray(idx)
+    d = idx.shape[-1]
+    groups = idx.astype(np.uint64).reshape(*idx.shape[:-1], d // 8, 8)
+    words = (groups << (np.uint64(bits) * np.arange(8, dtype=np.uint64))).sum(axis=-1, dtype=np.uint64)
+    raw = words.astype("<u8").view(np.uint8).reshape(*words.shape, 8)
+    return np.ascontiguousarray(raw[..., :bits]).reshape(*idx.shape[:-1], d // 8 * bits)
 
 
 def _unpack_codes(buf: np.ndarray, bits: int, d: int) -> np.ndarray:
-    flat = buf.astype(np.uint8).reshape(-1, buf.shape[-1])
-    bit = np.unpackbits(flat, axis=1, bitorder="little")[:, :d * bits].reshape(-1, d, bits)
-    weights = (1 << np.arange(bits, dtype=np.uint16))
-    return (bit.astype(np.uint16) * weights).sum(axis=2).astype(np.uint8).reshape(
-        *buf.shape[:-1], d)
+    buf = np.asarray(buf, dtype=np.uint8)
+    lead = buf.shape[:-1]
+    raw = np.zeros((*lead, d // 8, 8), dtype=np.uint8)
+    raw[..., :bits] = buf.reshape(*lead, d // 8, bits)
+    words = raw.view("<u8")                     # (..., d // 8, 1)
+    codes = (words >> (np.uint64(bits) * np.arange(8, dtype=np.uint64))) & np.uint64((1 << bits) - 1)
+    return codes.astype(np.uint8).reshape(*lead, d)
 
 
 def _pack_word(x: np.ndarray, bits: int) -> np.ndarray:
-    a = np.asarray(x, dtype=np.int64) & ((1 << bits) - 1)
-    return np.stack([(a >> (8 * i)) & 0xFF for i in range(bits // 8)], axis=-1).astype(np.uint8)
+    nb = bits // 8
+    raw = np.asarray(x, dtype=np.int64).astype("<i8").view(np.uint8)
+    return np.ascontiguousarray(raw.reshape(*np.shape(x), 8)[..., :nb])
 
 
 def _unpack_word(buf: np.ndarray, bits: int) -> np.ndarray:
-    v = sum(buf[..., i].astype(np.int64) << (8 * i) for i in range(bits // 8))
-    sign = 1 << (bits - 1)
-    return (v ^ sign) - sign
+    buf = np.asarray(buf, dtype=np.uint8)
+    raw = np.zeros((*buf.shape[:-1], 8), dtype=np.uint8)
+    raw[..., :bits // 8] = buf
+    v = raw.view("<i8")[..., 0]
+    # two's complement of `bits` bits: the top bit of the field carries -2^(bits-1)
+    return v - (((v >> (bits - 1)) & 1) << bits)
 
 
 class KVQuantizer:

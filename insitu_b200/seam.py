@@ -37,15 +37,21 @@ class RopeScaling:
     original_max_position: int
 
     def apply(self, inv_freq: np.ndarray) -> np.ndarray:
-        f = np.asarray(inv_freq, dtype=np.float64)
-        ctx = float(self.original_max_position)
-        wavelen = 2.0 * np.pi / f
-        low_wl, high_wl = ctx / self.low_freq_factor, ctx / self.high_freq_factor
-        scaled = np.where(wavelen > low_wl, f / self.factor, f)
-        smooth = (ctx / wavelen - self.low_freq_factor) / (self.high_freq_factor - self.low_freq_factor)
-        smoothed = (1.0 - smooth) * scaled / self.factor + smooth * scaled
-        between = (wavelen <= low_wl) & (wavelen >= high_wl)
-        return np.where(between, smoothed, scaled)
+        # Frequencies whose wavelength exceeds original_max_position /
+        # low_freq_factor are divided by `factor`; those below
+        # original_max_position / high_freq_factor are kept; in between they
+        # blend linearly in original_max_position / wavelength. The float64
+        # operations are those of the reference, in its order, because the
+        # RoPE tables built from them are integers of the wire format.
+        freq = np.asarray(inv_freq, dtype=np.float64)
+        span = float(self.original_max_position)
+        period = 2.0 * np.pi / freq
+        long_edge, short_edge = span / self.low_freq_factor, span / self.high_freq_factor
+        base = np.where(period > long_edge, freq / self.factor, freq)
+        t = (span / period - self.low_freq_factor) / (self.high_freq_factor - self.low_freq_factor)
+        blend = (1.0 - t) * base / self.factor + t * base
+        mid = (period <= long_edge) & (period >= short_edge)
+        return np.where(mid, blend, base)
 
 
 def rope_tables(d: int, max_position: int, theta: float = 10000.0, frac: int = 15,
