@@ -81,8 +81,8 @@ def parse():
     ap.add_argument("--model", action="store_true",
                     help="whole-model decode: a Llama-3.2-1B-shaped random-init transformers model "
                          "with all 16 attention layers on the GPU path, 8K context")
-    ap.add_argument("--scan-kernel", choices=("fused", "split"), default="fused",
-                    help="the online scan as one launch (default) or as separate launches")
+    ap.add_argument("--scan-kernel", choices=("fused", "split"), default="split",
+                    help="the online scan as separate launches (default) or as one launch")
     ap.add_argument("--config", type=int, choices=(2, 3, 4, 5), default=2,
                     help="benchmark config to time (2: the default sweep point; 5 = --split)")
     return ap.parse_args()

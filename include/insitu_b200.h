@@ -134,13 +134,14 @@ enum { INS_TILES_AUTO = 0, INS_TILES_LARGE = 1, INS_TILES_SMALL = 2 };
 int ins_cache_set_tiles(ins_cache *cache, int32_t mode);
 
 /* Which kernels run the context-parallel online scan (no reference
- * counterpart; results are identical either way). FUSED, the default: one
- * persistent launch that scores each tile, finds the running maximum entering
- * it from the tiles before (a bounded look-back on words the other CTAs
- * publish), accumulates V and folds the tile records, followed by the exact
- * re-run of items it could not prove. SPLIT: separate score, prefix-maximum,
- * value and fold launches with the scores kept in global memory between them
- * (the context split always uses these). */
+ * counterpart; results are identical either way). SPLIT, the default:
+ * separate score, prefix-maximum, value and fold launches with the scores
+ * kept in global memory between them (the context split always uses these).
+ * FUSED: one persistent launch that scores each tile, finds the running
+ * maximum entering it from the tiles before (a bounded look-back on words the
+ * other CTAs publish), accumulates V and folds the tile records, followed by
+ * the exact re-run of items it could not prove; fewer launches, no per-row
+ * scratch (ins_scan_noalloc always uses it). */
 enum { INS_SCAN_FUSED = 0, INS_SCAN_SPLIT = 1 };
 int ins_cache_set_scan_kernel(ins_cache *cache, int32_t mode);
 

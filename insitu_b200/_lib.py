@@ -187,7 +187,7 @@ def lib():
         raise RuntimeError(
             f"{LIB_PATH} is missing: build it with insitu_b200._lib.build() (nvcc, sm_100a). "
             "insitu_b200 has no CPU fallback.")
-    L = C.CDLL(LIB_PATH)
+    L = C.CDLL(LIB_PATH, mode=C.RTLD_GLOBAL)   # the torch extension binds to this copy
     vp, i32, i64 = C.c_void_p, C.c_int32, C.c_int64
     L.ins_abi_version.restype = i32
     L.ins_bytes_per_token.argtypes = [C.POINTER(Config)]

@@ -335,7 +335,7 @@ struct ChunkScratch {
     int32_t n_items = 0, max_chunks = 0, seg_cap = 0, tile_cap = 0;
     int32_t last_items = 0;       // items of the last chunked launch (their redo flags)
     int32_t tiles_mode = 0;       // TILES_AUTO / TILES_LARGE / TILES_SMALL
-    int32_t scan_kernel = 0;      // SCAN_FUSED (one launch) / SCAN_SPLIT (separate launches)
+    int32_t scan_kernel = 1;      // SCAN_FUSED (one launch) / SCAN_SPLIT (separate launches, the default)
     int32_t poll_limit = 1 << 22; // polls before a look-back wait of the fused scan gives up
     int32_t hold_item = -1, hold_chunk = 0, hold_head = 0;   // a look-back word left unpublished
                                                               // (the test of the bounded wait)
@@ -1426,6 +1426,86 @@ __global__ void __launch_bounds__(256) k_chunk_prefix(ChunkArgs a) {
     }
 }
 
+// The p-pass of a tile (4a below): p = exp(m - s) and w = v_norm * p for
+// every (token, head), w written over the score offset in place; the l of
+// every segment into lsum (shared atomics) and each warp's sum of |w| per head
+// (the clamp-proof bound) into bnd. Thread tid owns tokens tid + r*NT, so its
+// warp holds block r*NT/32 + warp for each r. All distances are loaded before
+// any w is stored (the stores reuse the slots the loads read), and the
+// distance arithmetic is 32-bit: the block bases are kept clamped at
+// delta_max + 1 (dbase32) and each offset is clamped the same way, which
+// leaves every p unchanged (any distance past delta_max gives p = 0).
+template <int H, int R, int NT, int C, int CW>
+__device__ __forceinline__ void p_pass(const int32_t *exp_tab, uint32_t *d_sm, const uint32_t *dbase32,
+                                       const int32_t *vn_sm, const uint32_t *grew, const int32_t *gpre,
+                                       unsigned int (*lsum)[SEGMAX + 1], long long (*bnd)[H], int n) {
+    constexpr uint32_t DCAP = (uint32_t)DefFmt::DELTA_MAX + 1u;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    uint32_t dd[R][H];
+    int32_t vnt[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int t = r * NT + tid;
+        vnt[r] = t < n ? vn_sm[t] : 0;
+#pragma unroll
+        for (int h = 0; h < H; ++h) dd[r][h] = min(d_sm[h * C + t], DCAP) + dbase32[h * CW + (t >> 5)];
+    }
+    uint32_t pv[R][H];
+    unsigned whi[H], wlo[H];
+#pragma unroll
+    for (int h = 0; h < H; ++h) whi[h] = wlo[h] = 0u;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int t = r * NT + tid;
+        const bool valid = t < n;
+#pragma unroll
+        for (int h = 0; h < H; ++h) {
+            const uint32_t p = valid ? exp_lut_def(exp_tab, (int64_t)dd[r][h]) : 0u;
+            const int32_t w = vnt[r] * (int32_t)p;           // |w| <= 2^30
+            if (valid) d_sm[h * C + t] = (uint32_t)w;
+            const uint32_t aw = (uint32_t)(w < 0 ? -w : w);
+            whi[h] += aw >> 16;
+            wlo[h] += aw & 0xFFFFu;
+            pv[r][h] = p;
+        }
+    }
+    // l: when the warp's R blocks are quiet for a head and share one segment
+    // (the common case), one warp sum and one atomic per head
+#pragma unroll
+    for (int h = 0; h < H; ++h) {
+        const int sg0 = gpre[h * CW + warp];
+        bool uni = true;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int blk = r * (NT / 32) + warp;
+            uni &= grew[h * CW + blk] == 0u && gpre[h * CW + blk] == sg0;
+        }
+        if (uni) {
+            unsigned ps = 0;
+#pragma unroll
+            for (int r = 0; r < R; ++r) ps += pv[r][h];
+            const unsigned sum = __reduce_add_sync(FULL, ps);   // <= R * 32 * 2^15
+            if (lane == 0 && sum && sg0 <= SEGMAX) atomicAdd(&lsum[h][sg0], sum);
+        } else {
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int blk = r * (NT / 32) + warp;
+                const uint32_t gw = grew[h * CW + blk];
+                const int sg = gpre[h * CW + blk] + __popc(gw & ((2u << lane) - 1u));
+                if (pv[r][h] && sg <= SEGMAX) atomicAdd(&lsum[h][sg], pv[r][h]);
+            }
+        }
+    }
+    // sum of |w| per head over the warp, exact: the high and low 16-bit parts
+    // summed apart (each well inside 32 bits) and recombined
+#pragma unroll
+    for (int h = 0; h < H; ++h) {
+        const unsigned hs = __reduce_add_sync(FULL, whi[h]);
+        const unsigned ls = __reduce_add_sync(FULL, wlo[h]);
+        if (lane == 0) bnd[warp][h] = ((long long)hs << 16) + (long long)ls;
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Launch 3: the values
 // ---------------------------------------------------------------------------
@@ -1438,7 +1518,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
                   VS = CF::VS;
     constexpr int UPW = 32 / H;                 // table units per warp in the build
     extern __shared__ __align__(16) uint8_t dyn[];
-    __shared__ int32_t vcent[256];
+    __shared__ int32_t vcent[16];
     __shared__ int32_t exp_tab[256];
     __shared__ long long m_in_sm[H];
     __shared__ int fail_sm;
@@ -1466,13 +1546,12 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
     int32_t *gpre = reinterpret_cast<int32_t *>(dyn + CF::OFF_PRE);     // [H][CW]
     long long *bmax = reinterpret_cast<long long *>(dyn + CF::OFF_BMAX);  // [H][CW]
     long long *bcar = reinterpret_cast<long long *>(dyn + CF::OFF_BCAR);  // [H][CW]
-    long long *dbase = reinterpret_cast<long long *>(dyn + CF::OFF_DB);   // [H][CW]: carry - block max
+    uint32_t *dbase = reinterpret_cast<uint32_t *>(dyn + CF::OFF_DB);     // [H][CW]: carry - block max,
+                                                                           // clamped at delta_max + 1
     int32_t *s0p = reinterpret_cast<int32_t *>(dyn + CF::OFF_S0);
 
-    for (int i = tid; i < 256; i += NT) {
-        vcent[i] = (int32_t)a.tb->v_cent[i];
-        exp_tab[i] = a.tb->exp_tab[i];
-    }
+    for (int i = tid; i < 256; i += NT) exp_tab[i] = a.tb->exp_tab[i];
+    if (tid < 16) vcent[tid] = tid < NC ? (int32_t)a.tb->v_cent[tid] : 0;
     int64_t cmax_v = 0;                       // max |V centroid|
     for (int k = 0; k < NC; ++k) {
         const int64_t ab = a.tb->v_cent[k] < 0 ? -a.tb->v_cent[k] : a.tb->v_cent[k];
@@ -1634,7 +1713,8 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
             if (lane < CW) {
                 bcar[h * CW + lane] = car;
                 // a token's distance below the running maximum is dbase + its offset
-                dbase[h * CW + lane] = lane < nb ? car - bmax[h * CW + lane] : 0;
+                const int64_t db = lane < nb ? car - bmax[h * CW + lane] : 0;
+                dbase[h * CW + lane] = (uint32_t)(db < DefFmt::DELTA_MAX ? db : DefFmt::DELTA_MAX + 1);
                 grew[h * CW + lane] = 0u;
             }
             __syncwarp();
@@ -1733,64 +1813,8 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
         // ---- 4. V ------------------------------------------------------------------
         // 4a. p-pass: p = exp(carry - s') and w = v_norm * p for every (token,
         //     head); w replaces the score in place. The l of every segment and
-        //     the clamp-proof bound are summed here. Thread tid owns tokens
-        //     tid + r*NT: its warp holds block r*NT/32 + warp for each r.
-        {
-            uint32_t pv[R][H];
-            int64_t sumw[H];                          // sum of |w|, for the clamp-proof bound
-#pragma unroll
-            for (int h = 0; h < H; ++h) sumw[h] = 0;
-#pragma unroll
-            for (int r = 0; r < R; ++r) {
-                const int t = r * NT + tid;
-                const bool valid = t < n;
-                const int blk = t >> 5;
-                const int32_t vnt = valid ? vn_sm[t] : 0;
-#pragma unroll
-                for (int h = 0; h < H; ++h) {
-                    const uint32_t p =
-                        valid ? exp_lut_def(exp_tab, dbase[h * CW + blk] + (int64_t)d_sm[h * C + t]) : 0u;
-                    const int32_t w = vnt * (int32_t)p;      // |w| <= 2^30
-                    if (valid) d_sm[h * C + t] = (uint32_t)w;
-                    sumw[h] += w < 0 ? -(int64_t)w : (int64_t)w;
-                    pv[r][h] = p;
-                }
-            }
-            // l: when the warp's R blocks are quiet for a head and share one
-            // segment (the common case), one warp sum and one atomic per head
-#pragma unroll
-            for (int h = 0; h < H; ++h) {
-                const int sg0 = gpre[h * CW + warp];
-                bool uni = true;
-#pragma unroll
-                for (int r = 0; r < R; ++r) {
-                    const int blk = r * (NT / 32) + warp;
-                    uni &= grew[h * CW + blk] == 0u && gpre[h * CW + blk] == sg0;
-                }
-                if (uni) {
-                    unsigned ps = 0;
-#pragma unroll
-                    for (int r = 0; r < R; ++r) ps += pv[r][h];
-                    const unsigned sum = __reduce_add_sync(FULL, ps);   // <= R * 32 * 2^15
-                    if (lane == 0 && sum && sg0 <= SEGMAX) atomicAdd(&lsum_sm[h][sg0], sum);
-                } else {
-#pragma unroll
-                    for (int r = 0; r < R; ++r) {
-                        const int blk = r * (NT / 32) + warp;
-                        const uint32_t gw = grew[h * CW + blk];
-                        const int sg = gpre[h * CW + blk] + __popc(gw & ((2u << lane) - 1u));
-                        if (pv[r][h] && sg <= SEGMAX) atomicAdd(&lsum_sm[h][sg], pv[r][h]);
-                    }
-                }
-            }
-#pragma unroll
-            for (int h = 0; h < H; ++h) {
-                unsigned long long v = (unsigned long long)sumw[h];
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
-                if (lane == 0) bnd_sm[warp][h] = (long long)v;
-            }
-        }
+        //     the clamp-proof bound are summed here.
+        p_pass<H, R, NT, C, CW>(exp_tab, d_sm, dbase, vn_sm, grew, gpre, lsum_sm, bnd_sm, n);
         __syncthreads();
 
         // 4b. term tables per sub-tile, and the lookups
@@ -1804,7 +1828,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
                     const int l = task & 31;
                     const int u = (task >> 5) * UPW + l % UPW, h = l / UPW;
                     const int t = st + u * TPE;
-                    int64_t w[TPE];
+                    int32_t w[TPE];                // |w| <= 2^30, |c| < 2^17: 32 x 32 -> 64-bit products
                     if constexpr (TPE == 2) {
                         const int2 w2 = *reinterpret_cast<const int2 *>(&d_sm[h * C + t]);
                         w[0] = t < n ? w2.x : 0;
@@ -1817,7 +1841,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
                     for (int e = 0; e < TPE; ++e)
 #pragma unroll
                         for (int k = 0; k < NC; ++k)
-                            T[e][k] = (int32_t)((w[e] * (int64_t)vcent[k]) >> DefFmt::ACC_SHIFT);
+                            T[e][k] = (int32_t)(((long long)w[e] * (long long)vcent[k]) >> DefFmt::ACC_SHIFT);
                     int32_t *dst = tab + u * USTR + (H == 1 ? 0 : (h >> 1) * HPS + (h & 1));
                     constexpr int ES = H == 1 ? 1 : 2;         // words per entry
 #pragma unroll

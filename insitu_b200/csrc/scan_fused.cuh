@@ -226,7 +226,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
     uint32_t *grew = reinterpret_cast<uint32_t *>(dyn + FC::OFF_GREW);
     uint32_t *anyg = grew + H * CW;
     int32_t *gpre = reinterpret_cast<int32_t *>(dyn + FC::OFF_PRE);
-    long long *dbase = reinterpret_cast<long long *>(dyn + FC::OFF_DB);
+    uint32_t *dbase = reinterpret_cast<uint32_t *>(dyn + FC::OFF_DB);   // clamped at delta_max + 1
     int32_t *s0p = reinterpret_cast<int32_t *>(dyn + FC::OFF_S0);
 
     const Geo &g = a.g;
@@ -405,7 +405,8 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
                 car = car > m_in ? car : m_in;
                 const bool scanb = lane < nb && bmax[h * CW + lane] > car;
                 if (lane < CW) {
-                    dbase[h * CW + lane] = lane < nb ? car - bmax[h * CW + lane] : 0;
+                    const int64_t db = lane < nb ? car - bmax[h * CW + lane] : 0;
+                    dbase[h * CW + lane] = (uint32_t)(db < DefFmt::DELTA_MAX ? db : DefFmt::DELTA_MAX + 1);
                     grew[h * CW + lane] = 0u;
                 }
                 __syncwarp();
@@ -495,60 +496,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
             }
 
             // ---- 5a. p-pass: p = exp(carry - s'), w = v_norm * p in place --------
-            {
-                uint32_t pv[R][H];
-                int64_t sumw[H];
-#pragma unroll
-                for (int h = 0; h < H; ++h) sumw[h] = 0;
-#pragma unroll
-                for (int r = 0; r < R; ++r) {
-                    const int t = r * NT + tid;
-                    const bool valid = t < n;
-                    const int blk = t >> 5;
-                    const int32_t vnt = valid ? vn_sm[t] : 0;
-#pragma unroll
-                    for (int h = 0; h < H; ++h) {
-                        const uint32_t p =
-                            valid ? exp_lut_def(exp_tab, dbase[h * CW + blk] + (int64_t)d_sm[h * C + t]) : 0u;
-                        const int32_t w = vnt * (int32_t)p;
-                        if (valid) d_sm[h * C + t] = (uint32_t)w;
-                        sumw[h] += w < 0 ? -(int64_t)w : (int64_t)w;
-                        pv[r][h] = p;
-                    }
-                }
-#pragma unroll
-                for (int h = 0; h < H; ++h) {
-                    const int sg0 = gpre[h * CW + warp];
-                    bool uni = true;
-#pragma unroll
-                    for (int r = 0; r < R; ++r) {
-                        const int blk = r * (NT / 32) + warp;
-                        uni &= grew[h * CW + blk] == 0u && gpre[h * CW + blk] == sg0;
-                    }
-                    if (uni) {
-                        unsigned ps = 0;
-#pragma unroll
-                        for (int r = 0; r < R; ++r) ps += pv[r][h];
-                        const unsigned sum = __reduce_add_sync(FULL, ps);
-                        if (lane == 0 && sum && sg0 <= SEGMAX) atomicAdd(&lsum_sm[h][sg0], sum);
-                    } else {
-#pragma unroll
-                        for (int r = 0; r < R; ++r) {
-                            const int blk = r * (NT / 32) + warp;
-                            const uint32_t gw = grew[h * CW + blk];
-                            const int sg = gpre[h * CW + blk] + __popc(gw & ((2u << lane) - 1u));
-                            if (pv[r][h] && sg <= SEGMAX) atomicAdd(&lsum_sm[h][sg], pv[r][h]);
-                        }
-                    }
-                }
-#pragma unroll
-                for (int h = 0; h < H; ++h) {
-                    unsigned long long v = (unsigned long long)sumw[h];
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
-                    if (lane == 0) bnd_sm[warp][h] = (long long)v;
-                }
-            }
+            p_pass<H, R, NT, C, CW>(exp_tab, d_sm, dbase, vn_sm, grew, gpre, lsum_sm, bnd_sm, n);
             __syncthreads();
 
             // ---- 5b. term tables per sub-tile, and the lookups ------------------
@@ -560,7 +508,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
                         const int l = task & 31;
                         const int u = (task >> 5) * UPW + l % UPW, h = l / UPW;
                         const int t = st + u * TPE;
-                        int64_t w[TPE];
+                        int32_t w[TPE];            // |w| <= 2^30, |c| < 2^17: 32 x 32 -> 64-bit products
                         if constexpr (TPE == 2) {
                             const int2 w2 = *reinterpret_cast<const int2 *>(&d_sm[h * C + t]);
                             w[0] = t < n ? w2.x : 0;
@@ -573,7 +521,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
                         for (int e = 0; e < TPE; ++e)
 #pragma unroll
                             for (int k = 0; k < NC; ++k)
-                                T[e][k] = (int32_t)((w[e] * (int64_t)vcent[k]) >> DefFmt::ACC_SHIFT);
+                                T[e][k] = (int32_t)(((long long)w[e] * (long long)vcent[k]) >> DefFmt::ACC_SHIFT);
                         int32_t *dst = tab + u * USTR + (H == 1 ? 0 : (h >> 1) * HPS + (h & 1));
                         constexpr int ES = H == 1 ? 1 : 2;
 #pragma unroll

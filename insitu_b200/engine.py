@@ -58,6 +58,17 @@ def _ids(x, n: int) -> list:
     return np.broadcast_to(np.asarray(x, dtype=np.int64), (n,)).tolist()
 
 
+def _raise_mapped(err: Exception):
+    """Re-raise an operator's error as the C ABI's exception class for its
+    status (the message starts with "[status N]"), e.g. CapacityError."""
+    msg = str(err)
+    i = msg.find("[status ")
+    if i >= 0:
+        code = int(msg[i + 8:msg.index("]", i)])
+        raise _lib._ERRORS.get(code, _lib.InsituError)(code, msg[msg.index("]", i) + 2:].split("\n")[0]) from None
+    raise err
+
+
 def _require_cuda():
     if not torch.cuda.is_available():
         raise RuntimeError("insitu_b200 needs a CUDA device (sm_100a); there is no CPU path")
@@ -140,9 +151,10 @@ class PagedCache:
         or "small". A tuning knob; every mode gives the same results."""
         _lib.check(self._L.ins_cache_set_tiles(self._h, _lib.INS_TILES[mode]))
 
-    def set_scan_kernel(self, mode: str = "fused") -> None:
-        """Kernels of the online scan (ins_cache_set_scan_kernel): "fused" (one
-        persistent launch) or "split" (separate launches). Same results."""
+    def set_scan_kernel(self, mode: str = "split") -> None:
+        """Kernels of the online scan (ins_cache_set_scan_kernel): "split"
+        (separate launches, the default) or "fused" (one persistent launch).
+        Same results."""
         _lib.check(self._L.ins_cache_set_scan_kernel(self._h, _lib.INS_SCAN[mode]))
 
     def set_wait_test(self, poll_limit: int = 1 << 22, item: int = -1, chunk: int = 0,
@@ -200,8 +212,11 @@ class PagedCache:
             q = self._dev_i32(q, (g.num_heads, g.head_dim))
             if q.shape[0] != n:
                 raise ValueError("q carries a different token count")
-        return self._ops.ingress(self._h.value, _ids(seq_ids, n), k, v, q, g.n_kv_heads, g.num_heads,
-                                 prerotated)
+        try:
+            return self._ops.ingress(self._h.value, _ids(seq_ids, n), k, v, q, g.n_kv_heads, g.num_heads,
+                                     prerotated)
+        except (RuntimeError, ValueError) as e:
+            _raise_mapped(e)
 
     def ingress_lanes(self, seq_ids, lanes) -> torch.Tensor:
         """ins_ingress from the board's ingress stream: ``lanes`` holds n tokens
@@ -289,8 +304,11 @@ class PagedCache:
         B = q.shape[0]
         lens = None if lengths is None else _ids(lengths, B)
         m = {"online": _lib.INS_SOFTMAX_ONLINE, "two_pass": _lib.INS_SOFTMAX_TWO_PASS}[mode]
-        res, st = self._ops.scan(self._h.value, _ids(seq_ids, B), lens, q, g.n_kv_heads, m,
-                                 bool(stats or stats_out is not None))
+        try:
+            res, st = self._ops.scan(self._h.value, _ids(seq_ids, B), lens, q, g.n_kv_heads, m,
+                                     bool(stats or stats_out is not None))
+        except (RuntimeError, ValueError) as e:
+            _raise_mapped(e)
         if out is not None:
             out.copy_(res)
             res = out
@@ -308,7 +326,10 @@ class PagedCache:
         v = self._dev_i32(v, (g.n_kv_heads, g.head_dim))
         q = self._dev_i32(q, (g.num_heads, g.head_dim))
         m = {"online": _lib.INS_SOFTMAX_ONLINE, "two_pass": _lib.INS_SOFTMAX_TWO_PASS}[mode]
-        return self._ops.step(self._h.value, _ids(seq_ids, q.shape[0]), q, k, v, g.n_kv_heads, m, stats)
+        try:
+            return self._ops.step(self._h.value, _ids(seq_ids, q.shape[0]), q, k, v, g.n_kv_heads, m, stats)
+        except (RuntimeError, ValueError) as e:
+            _raise_mapped(e)
 
     # -- context split (one sequence across shards) -------------------------------
     S_LO = -(1 << 47)   # the running maximum before any token (score_width 48)

@@ -474,6 +474,7 @@ def test_a_lookback_wait_that_runs_out_is_reported_and_the_context_survives():
     qr = orc.rotate(_wire(rng, (1, 32, 64), 1.0 / 8.0))
     q_rot = torch.from_numpy(qr.astype(np.int32))
     want, wst = orc.decode_layer(qr, [orc.ingress_rows(k, v, threads=8)], threads=8)
+    pc.set_scan_kernel("fused")            # the single-launch scan is the one that waits
     pc.set_wait_test(poll_limit=64, item=3, chunk=5, head=2)
     pc.scan([0], q_rot)
     with pytest.raises(DeviceTimeout):
