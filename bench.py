@@ -515,9 +515,13 @@ def run_split(args):
          ).round_().to(torch.int32)
     q_rot = [pc.rotate(q[i]) for i in range(K + W)]
 
+    from insitu_b200.context import PHASES
+    phase_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(PHASES) + 1)]
+                for _ in range(K + W)]
+
     def step(i):
         if world > 1:
-            return context_split_scan(pc, [0], q_rot[i])
+            return context_split_scan(pc, [0], q_rot[i], events=phase_ev[i])
         return pc.scan([0], q_rot[i])
 
     for i in range(W):
@@ -533,9 +537,15 @@ def run_split(args):
     e1.record()
     torch.cuda.synchronize(local)
     pc.status()
-    ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=f"cuda:{local}")
+    per_phase = [0.0] * len(PHASES)
+    if world > 1:
+        for i in range(W, W + K):
+            for j in range(len(PHASES)):
+                per_phase[j] += phase_ev[i][j].elapsed_time(phase_ev[i][j + 1]) / K
+    ms = torch.tensor([e0.elapsed_time(e1), *per_phase], dtype=torch.float64, device=f"cuda:{local}")
     if world > 1:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    phase_us = {n: round(float(ms[1 + j]) * 1e3, 2) for j, n in enumerate(PHASES)}
     ms = float(ms[0])
     rows = N_KV * share * world
     if rank == 0:
@@ -552,6 +562,11 @@ def run_split(args):
                                    "maxima, per-rank composites, all-gather, causal merge)",
                        "context": share * world, "parallelism": f"context split x{world}"},
             "us_per_step": round(ms / K * 1e3, 2),
+            # CUDA-event time of each phase of a step, the max over ranks of its
+            # mean over the timed steps (the all-gathers include waiting for
+            # the slowest rank's previous phase)
+            "phase_us": phase_us if world > 1 else None,
+            "composite_bytes_per_rank": int(pc.part_bytes(1)),
         }), flush=True)
     dec.close()
     if world > 1:

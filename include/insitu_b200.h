@@ -164,10 +164,11 @@ int64_t ins_cache_capacity(const ins_cache *cache);
 
 /* Kernels this cache has launched so far through ins_ingress,
  * ins_ingress_lanes, ins_seam, ins_seam_device_positions and ins_scan (a
- * running count, for a caller that reports what ran; the online scan is 2
- * launches with the fused kernels, or 5 or 6 with the separate ones, one more
- * when its items need more than one fold block). No reference counterpart.
- * -1 for NULL. */
+ * running count, for a caller that reports what ran). The online scan is 6
+ * launches with the separate kernels (queries, scores, prefix maxima, values,
+ * item fold, exact re-run), 7 when its items need more than one fold block,
+ * and 3 with the fused kernel (queries, scan, exact re-run). No reference
+ * counterpart. -1 for NULL. */
 int64_t ins_cache_launches(const ins_cache *cache);
 
 /* Flags of ins_ingress. */
@@ -254,6 +255,19 @@ int ins_rotate(ins_cache *cache, int64_t n, const int32_t *x, int32_t *y, void *
  * receives the number of scores the clamp changed. */
 int ins_scores(ins_cache *cache, int32_t seq, int32_t kv_head, int64_t t0, int64_t n,
                const int32_t *q_rot, int64_t *s, int64_t *ovf, void *stream);
+
+/* The projections of the host half (matvec, numerics/fp.py:25-62, used by
+ * kernel.py:197-210 and the output projection, ops/output.py:80-84) as a
+ * kernel of this library: y[t][o] = sum_i w16[o][i] * fp16(x[t][i]) (+ bias[o])
+ * with exact fp32 products and fp32 sums, in another order than numpy's (the
+ * results agree to float32 rounding). w16: device fp16 [out_dim][in_dim]
+ * (raw 16-bit words; the fp16-rounded weights of Weights.prepare,
+ * weights.py:70-109), 16-byte aligned; x: device fp32 [n][in_dim]; bias:
+ * device fp32 [out_dim] or NULL; y: device fp32 [n][out_dim]. in_dim a
+ * multiple of 8 in [8, 8192]. No cache is involved; runs on the device of
+ * the current context, stream-ordered. */
+int ins_project(int32_t n, int32_t in_dim, int32_t out_dim, const uint16_t *w16, const float *x,
+                const float *bias, float *y, void *stream);
 
 /* The scan's finalize on its own: _finalize (ops/attention.py:873-880) with
  * the normalised reciprocal (reciprocal, ops/attention.py:177-250) for n

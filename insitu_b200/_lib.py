@@ -16,7 +16,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 LIB_PATH = os.path.join(HERE, "libinsitu_b200.so")
 SOURCES = ("csrc/insitu.cu", "csrc/common.cuh", "csrc/kernels.cuh", "csrc/scan_chunked.cuh",
-           "csrc/scan_fused.cuh")
+           "csrc/scan_fused.cuh", "csrc/project.cuh")
 HEADER = os.path.join(ROOT, "include", "insitu_b200.h")
 
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", "-std=c++17",
@@ -98,7 +98,8 @@ SYMBOLS = ("ins_abi_version", "ins_bytes_per_token", "ins_cache_create", "ins_ca
            "ins_ingress_lanes", "ins_lanes_bytes_per_token", "ins_ddr_image_bytes",
            "ins_cache_ddr_image", "ins_seam", "ins_seam_device_positions",
            "ins_cache_launches", "ins_finalize", "ins_exp_lut",
-           "ins_scan_recomputed_total", "ins_cache_set_scan_kernel", "ins_cache_set_wait_test")
+           "ins_scan_recomputed_total", "ins_cache_set_scan_kernel", "ins_cache_set_wait_test",
+           "ins_project")
 
 
 def nvcc() -> str:
@@ -229,6 +230,7 @@ def lib():
     L.ins_seam_device_positions.argtypes = L.ins_seam.argtypes
     L.ins_finalize.argtypes = [vp, i64, vp, vp, vp, vp, vp, vp]
     L.ins_exp_lut.argtypes = [vp, i64, vp, vp, vp]
+    L.ins_project.argtypes = [i32, i32, i32, vp, vp, vp, vp, vp]
     L.ins_cache_launches.argtypes = [vp]
     L.ins_cache_launches.restype = i64
     L.ins_last_error.restype = C.c_char_p

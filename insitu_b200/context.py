@@ -39,20 +39,38 @@ def exclusive_prefix_max(maxima_by_shard, shard: int) -> torch.Tensor:
     return m
 
 
-def context_split_scan(pc, seq_ids, q_rot, *, lengths=None, group=None, stats: bool = True):
+PHASES = ("scores", "gather_maxima", "values", "gather_parts", "merge")
+
+
+def context_split_scan(pc, seq_ids, q_rot, *, lengths=None, group=None, stats: bool = True,
+                       events=None):
     """Steps 1-4 on every rank of ``group``; rank order is causal order. Every
-    rank returns the merged (out, stats) for its ``seq_ids``."""
+    rank returns the merged (out, stats) for its ``seq_ids``. ``events``, a
+    list of len(PHASES) + 1 CUDA events, is recorded between the phases
+    (scores, all-gather of the maxima, values, all-gather of the composites,
+    merge) on the current stream."""
     import torch.distributed as dist
 
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
+    mark = (lambda i: events[i].record()) if events is not None else (lambda i: None)
+    mark(0)
     maxima = pc.scan_maxima(seq_ids, q_rot, lengths=lengths)
-    gathered = [torch.empty_like(maxima) for _ in range(world)]
-    dist.all_gather(gathered, maxima, group=group)
+    mark(1)
+    gathered = torch.empty((world * maxima.shape[0], *maxima.shape[1:]), dtype=maxima.dtype,
+                           device=maxima.device)
+    dist.all_gather_into_tensor(gathered, maxima, group=group)
+    gathered = gathered.view(world, *maxima.shape)
+    mark(2)
     part = pc.scan_part(seq_ids, exclusive_prefix_max(gathered, rank), lengths=lengths)
-    parts = [torch.empty_like(part) for _ in range(world)]
-    dist.all_gather(parts, part, group=group)
-    return pc.merge_parts(torch.stack(parts), maxima.shape[0], stats=stats)
+    mark(3)
+    parts = torch.empty((world * part.numel(),), dtype=part.dtype, device=part.device)
+    dist.all_gather_into_tensor(parts, part, group=group)
+    parts = parts.view(world, part.numel())
+    mark(4)
+    res = pc.merge_parts(parts, maxima.shape[0], stats=stats)
+    mark(5)
+    return res
 
 
 def local_split_scan(pc, shard_seq_ids, q_rot, *, stats: bool = True):

@@ -17,6 +17,7 @@
 #include "kernels.cuh"
 #include "scan_chunked.cuh"
 #include "scan_fused.cuh"
+#include "project.cuh"
 
 using namespace ins;
 
@@ -911,6 +912,28 @@ __global__ void k_exp_values(Geo g, const DevTables *__restrict__ tb, int64_t n,
 
 extern "C" {
 
+int ins_project(int32_t n, int32_t in_dim, int32_t out_dim, const uint16_t *w16, const float *x,
+                const float *bias, float *y, void *stream) {
+    if (n < 0 || in_dim < 8 || in_dim % 8 || in_dim > 8192 || out_dim < 1)
+        return fail(INS_EINVAL, "project: n >= 0, in_dim a multiple of 8 in [8, 8192], out_dim >= 1");
+    if (n == 0) return INS_OK;
+    if (!w16 || !x || !y) return fail(INS_EINVAL, "project: NULL buffer");
+    if ((uintptr_t)w16 & 15u) return fail(INS_EINVAL, "project: weights must be 16-byte aligned");
+    const size_t smem = (size_t)PROJ_TT * in_dim * sizeof(__half);
+    CK(cudaFuncSetAttribute(k_project, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    int dev = 0, sms = 148;
+    CK(cudaGetDevice(&dev));
+    CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int rows_per_cta = PROJ_WARPS;
+    int grid = (out_dim + rows_per_cta - 1) / rows_per_cta;
+    grid = grid < 2 * sms ? grid : 2 * sms;
+    k_project<<<grid, PROJ_WARPS * 32, smem, (cudaStream_t)stream>>>(n, in_dim, out_dim,
+                                                                     reinterpret_cast<const __half *>(w16), x,
+                                                                     bias, y);
+    CK(cudaGetLastError());
+    return INS_OK;
+}
+
 int ins_finalize(ins_cache *c, int64_t n, const int64_t *acc, const int64_t *l, int64_t *out,
                  int64_t *recip, int64_t *shift, void *stream) {
     if (!c) return fail(INS_EINVAL, "cache is NULL");
@@ -1230,6 +1253,7 @@ int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
     a.items = (ItemAcc *)(p + L.items);
     a.redo = (int32_t *)(p + L.redo);
     a.redo_total = c->d_redo_total;
+    a.qdg = (double *)(p + L.qdg);
     a.status = c->d_status;
     FusedExtra x;
     x.lbw = (unsigned long long *)(p + L.lbw);
@@ -1242,7 +1266,7 @@ int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
     x.hold_word = -1;
     const int rc = launch_fused_kernels<H, KB, VB, RS>(a, x, B, a.seq_ids, a.T, s);
     if (rc) return fail(rc, "scan launch");
-    c->chunk.launches += 2;                    // the scan, the exact re-run
+    c->chunk.launches += 3;                    // the queries, the scan, the exact re-run
     return INS_OK;
 }
 

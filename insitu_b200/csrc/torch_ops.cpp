@@ -118,6 +118,28 @@ std::tuple<at::Tensor, c10::optional<at::Tensor>> step(int64_t h, at::IntArrayRe
     return scan(h, seq_ids, c10::nullopt, *q_rot, n_kv, mode, with_stats);
 }
 
+// ins_project: y = fp16(x) @ w16^T (+ bias) with fp32 products and sums;
+// w16 (out, in) fp16, x (n, in) fp32, bias (out) fp32 or none -> y (n, out) fp32.
+at::Tensor project(const at::Tensor &w16, const at::Tensor &x, const c10::optional<at::Tensor> &bias) {
+    TORCH_CHECK(w16.is_cuda() && w16.scalar_type() == at::kHalf && w16.dim() == 2 && w16.is_contiguous(),
+                "insitu: w16 must be a contiguous (out, in) float16 CUDA tensor");
+    TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kFloat && x.dim() == 2 && x.is_contiguous() &&
+                    x.size(1) == w16.size(1),
+                "insitu: x must be a contiguous (n, in) float32 CUDA tensor");
+    c10::cuda::CUDAGuard guard(x.device());
+    at::Tensor y = at::empty({x.size(0), w16.size(0)}, x.options());
+    const float *b = nullptr;
+    if (bias.has_value()) {
+        TORCH_CHECK(bias->scalar_type() == at::kFloat && bias->is_contiguous() && bias->numel() == w16.size(0),
+                    "insitu: bias must be a contiguous float32 tensor of out elements");
+        b = bias->data_ptr<float>();
+    }
+    check(ins_project((int32_t)x.size(0), (int32_t)x.size(1), (int32_t)w16.size(0),
+                      reinterpret_cast<const uint16_t *>(w16.data_ptr<at::Half>()), x.data_ptr<float>(), b,
+                      y.data_ptr<float>(), at::cuda::getCurrentCUDAStream().stream()));
+    return y;
+}
+
 }  // namespace
 
 TORCH_LIBRARY(insitu, m) {
@@ -127,10 +149,12 @@ TORCH_LIBRARY(insitu, m) {
           "bool with_stats) -> (Tensor, Tensor?)");
     m.def("step(int handle, int[] seq_ids, Tensor q, Tensor k, Tensor v, int n_kv, int mode, "
           "bool with_stats) -> (Tensor, Tensor?)");
+    m.def("project(Tensor w16, Tensor x, Tensor? bias) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(insitu, CUDA, m) {
     m.impl("ingress", ingress);
     m.impl("scan", scan);
     m.impl("step", step);
+    m.impl("project", project);
 }

@@ -69,12 +69,13 @@ class AttentionLayer:
         if not o_folded:
             w_o = fold_o_proj(np.asarray(w_o, np.float64), Rotation.for_quant(self.quant, head_dim),
                               num_heads, head_dim)
-        # the weights rounded to fp16 once, held as fp32 GEMM operands; q, k
-        # and v are one GEMM over their stacked rows (each output is the same
-        # fp32 dot product of fp16-rounded operands)
-        f32 = lambda w: torch.as_tensor(np.asarray(w, dtype=np.float16)).to(dev).float()
-        self.w_qkv = torch.cat([f32(w_q), f32(w_k), f32(w_v)]).contiguous()
-        self.w_o = f32(w_o)
+        # the weights rounded to fp16 once and held as fp16 for the projection
+        # kernel (ins_project); q, k and v are one projection over their
+        # stacked rows (each output is the same fp32 dot product of
+        # fp16-rounded operands)
+        f16 = lambda w: torch.as_tensor(np.asarray(w, dtype=np.float16)).to(dev)
+        self.w_qkv = torch.cat([f16(w_q), f16(w_k), f16(w_v)]).contiguous()
+        self.w_o = f16(w_o)
         nq, nk = num_heads * head_dim, num_kv_heads * head_dim
         bq, bk, bv, bo = biases
         self.b_qkv = None

@@ -71,18 +71,16 @@ def rope_tables(d: int, max_position: int, theta: float = 10000.0, frac: int = 1
 
 def project(w: torch.Tensor, x: torch.Tensor, bias: torch.Tensor | None = None, *,
             rounded: bool = False) -> torch.Tensor:
-    """``matvec`` (numerics/fp.py:25-46) on the GPU: fp16-rounded operands,
-    fp32 products and accumulation. w (out, in), x (n, in) -> (n, out) fp32.
-    ``rounded``: w is already fp16-rounded and held as fp32."""
-    w16 = w if rounded else w.to(torch.float16).to(torch.float32)
-    x16 = x.to(torch.float16).to(torch.float32)
-    prev = torch.backends.cuda.matmul.allow_tf32
-    torch.backends.cuda.matmul.allow_tf32 = False     # fp32 arithmetic, not TF32
-    try:
-        y = x16 @ w16.T
-    finally:
-        torch.backends.cuda.matmul.allow_tf32 = prev
-    return y if bias is None else y + bias.to(torch.float32)
+    """``matvec`` (numerics/fp.py:25-46) on the GPU through this library's
+    projection kernel (ins_project): fp16-rounded operands, exact fp32
+    products, fp32 sums. w (out, in): float16, or float32 to be rounded to
+    fp16 (``rounded``: already fp16-exact, converted without change);
+    x (n, in) -> (n, out) fp32."""
+    from . import _lib
+    w16 = w if w.dtype == torch.float16 else w.to(torch.float16)
+    x32 = x.to(torch.float32).contiguous()
+    b = None if bias is None else bias.to(device=x32.device, dtype=torch.float32).contiguous()
+    return _lib.ops().project(w16.contiguous(), x32, b)
 
 
 class Seam:

@@ -78,18 +78,25 @@ def test_seam_kernel_matches_reference(seam, norm, after):
 
 
 @pytest.mark.gpu
-def test_projection_gemm_within_float32_rounding():
+@pytest.mark.parametrize("n,out_dim,in_dim,bias", [(4, 512, 2048, False), (1, 3072, 2048, False),
+                                                   (13, 2048, 2048, True), (3, 67, 64, True)])
+def test_projection_kernel_within_float32_rounding(n, out_dim, in_dim, bias):
+    """ins_project, the library's own projection kernel, against matvec
+    (numerics/fp.py:25-46): fp16 operands, fp32 products and sums. The float64
+    sum of the same fp16-rounded products is the order-free target; the
+    kernel's float32 sums, in its own order, stay within the standard bound
+    in_dim * eps * sum |products| (plus the bias's one rounding)."""
     torch = pytest.importorskip("torch")
     from insitu_b200.seam import project
-    rng = np.random.default_rng(7)
-    w = (rng.standard_normal((512, 2048)) * 0.02).astype(np.float32)
-    x = rng.standard_normal((4, 2048)).astype(np.float32)
-    # matvec (numerics/fp.py:25-46): fp16 operands, fp32 products and sums; the
-    # float64 sum of the same fp16-rounded products is the order-free target
-    want = (x.astype(np.float16).astype(np.float64) @ w.astype(np.float16).astype(np.float64).T)
-    got = project(torch.from_numpy(w).cuda(), torch.from_numpy(x).cuda()).cpu().numpy()
-    assert got.dtype == np.float32
+    rng = np.random.default_rng(7 + n)
+    w = (rng.standard_normal((out_dim, in_dim)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((n, in_dim)).astype(np.float32)
+    b = rng.standard_normal(out_dim).astype(np.float32) if bias else None
+    w16, x16 = w.astype(np.float16).astype(np.float64), x.astype(np.float16).astype(np.float64)
+    want = x16 @ w16.T + (0.0 if b is None else b.astype(np.float64))
+    got = project(torch.from_numpy(w).cuda(), torch.from_numpy(x).cuda(),
+                  None if b is None else torch.from_numpy(b).cuda()).cpu().numpy()
+    assert got.dtype == np.float32 and got.shape == (n, out_dim)
     err = np.abs(got.astype(np.float64) - want)
-    bound = 2048 * np.finfo(np.float32).eps * (np.abs(x.astype(np.float16).astype(np.float64))
-                                               @ np.abs(w.astype(np.float16).astype(np.float64)).T)
+    bound = (in_dim + 1) * np.finfo(np.float32).eps * (np.abs(x16) @ np.abs(w16).T + np.abs(want))
     assert np.all(err <= bound)
