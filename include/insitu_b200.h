@@ -164,10 +164,10 @@ int64_t ins_cache_capacity(const ins_cache *cache);
 
 /* Kernels this cache has launched so far through ins_ingress,
  * ins_ingress_lanes, ins_seam, ins_seam_device_positions and ins_scan (a
- * running count, for a caller that reports what ran). The online scan is 6
- * launches with the separate kernels (queries, scores, prefix maxima, values,
- * item fold, exact re-run), 7 when its items need more than one fold block,
- * and 3 with the fused kernel (queries, scan, exact re-run). No reference
+ * running count, for a caller that reports what ran). The online scan is 5
+ * launches with the separate kernels (scores, prefix maxima, values, item
+ * fold, exact re-run), 6 when its items need more than one fold block, and 2
+ * with the fused kernel (the scan, the exact re-run). No reference
  * counterpart. -1 for NULL. */
 int64_t ins_cache_launches(const ins_cache *cache);
 

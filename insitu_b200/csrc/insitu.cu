@@ -1253,7 +1253,6 @@ int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
     a.items = (ItemAcc *)(p + L.items);
     a.redo = (int32_t *)(p + L.redo);
     a.redo_total = c->d_redo_total;
-    a.qdg = (double *)(p + L.qdg);
     a.status = c->d_status;
     FusedExtra x;
     x.lbw = (unsigned long long *)(p + L.lbw);
@@ -1266,7 +1265,7 @@ int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
     x.hold_word = -1;
     const int rc = launch_fused_kernels<H, KB, VB, RS>(a, x, B, a.seq_ids, a.T, s);
     if (rc) return fail(rc, "scan launch");
-    c->chunk.launches += 3;                    // the queries, the scan, the exact re-run
+    c->chunk.launches += 2;                    // the scan, the exact re-run
     return INS_OK;
 }
 

@@ -185,7 +185,6 @@ struct ChunkArgs {
     long long *maxima;            // [n_items][H] k_chunk_prefix writes each item's maximum, or null
     PartRec *parts;               // [n_items] composites instead of finalized outputs, or null
     unsigned long long *redo_total;  // running count of items handed to the sequential kernel, or null
-    double *qdg;                  // [n_items][D][H] each item's rotated queries as doubles (k_q_double)
 };
 
 // Chunks of an item: one per tile_rows rows, and one (empty) for an empty item.
@@ -344,7 +343,6 @@ struct ChunkScratch {
     size_t lbw_words = 0;
     unsigned int *bdone = nullptr, *idone = nullptr, *sdone = nullptr;
     uint8_t *fold_at = nullptr;
-    double *qdg = nullptr;        // the queries as doubles, [n_items][D][HMAX]
     unsigned int epoch = 0;       // of the last fused scan, 1 .. 4095
     int64_t launches = 0;         // kernels launched by ingress, seam and scan calls (a count)
     int64_t sc_rows = 0;          // rows * H capacity of `sc`, in 32-bit words
@@ -1073,27 +1071,6 @@ struct TileAhead {
     }
 };
 
-// Launch 0: each item's rotated queries as exact doubles, [channel][head], in
-// global memory, where every warp of the score loop reads them at one address
-// (a warp-uniform load costs one L1 wavefront, where a broadcast 16-byte
-// shared-memory load costs four). A query at or beyond q_lim could let an FP64
-// partial sum pass 2^53: its item goes to the exact int64 body.
-// ---------------------------------------------------------------------------
-template <int H>
-__global__ void __launch_bounds__(256) k_q_double(ChunkArgs a) {
-    const int item = blockIdx.x;
-    const int b = item / a.g.n_kv, kvh = item % a.g.n_kv;
-    const int64_t qbase = ((int64_t)b * a.g.n_kv * H + (int64_t)kvh * H) * D;
-    wait_prior_grid();
-    bool big = false;
-    for (int i = threadIdx.x; i < H * D; i += blockDim.x) {
-        const int32_t q = a.q_rot[qbase + i];
-        a.qdg[((int64_t)item * D + i % D) * H + i / D] = (double)q;
-        big |= q >= a.g.q_lim || q <= -a.g.q_lim;
-    }
-    if (__syncthreads_or(big) && threadIdx.x == 0) atomicExch(&a.items[item].fail, 1);
-}
-
 // Launch 1: the scores of every tile
 // ---------------------------------------------------------------------------
 // CompressedAttention.scores (ops/attention.py:333-359) for R rows per thread:
@@ -1112,6 +1089,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
     // lanes of a 16-byte shared-memory wavefront never meet in a bank.
     extern __shared__ __align__(16) uint8_t dynA[];
     using SC = ScoreCfg<H, KB, VB, RS>;
+    __shared__ __align__(16) double qd[D * H];  // [channel][head]
     double2 *ctab = reinterpret_cast<double2 *>(dynA);
     // The staging of the tiles: descriptors and page ids two tiles ahead (in
     // rings of 3 and 2), the rows one tile ahead (buffers j & 1).
@@ -1195,8 +1173,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
     }
     __syncthreads();
     if (ntl > 0) issue(0);
-    // the queries come from the launch before this one (k_q_double)
-    wait_prior_grid();
+    int prev_item = -1;
     int4 prev_td = make_int4(0, 0, 0, 0);
     unsigned lost = 0;                           // buffers whose wait gave up
     // the maximum of tile j's scores per head, once the barrier ending tile j
@@ -1218,9 +1195,24 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
         const int item = td.x;
         const int64_t t0 = td.z;
         const int n = td.w;
+        const int b = item / g.n_kv, kvh = item % g.n_kv;
+        const int64_t qbase = ((int64_t)b * g.n_kv * H + (int64_t)kvh * H) * D;
         uint32_t *sc = a.sc + (trb_sm[li % 3] + t0) * H;
 
-        const double *qdi = a.qdg + (int64_t)item * D * H;   // this item's queries (k_q_double)
+        if (item != prev_item) {                 // the same for the whole CTA
+            prev_item = item;
+            for (int i = tid; i < H * D; i += NT) qd[(i % D) * H + i / D] = (double)a.q_rot[qbase + i];
+            __syncthreads();
+            bool big = false;
+            const double qlim = (double)g.q_lim;
+            for (int i = tid; i < H * D; i += NT) {
+                const double x = qd[i];
+                big |= (x >= qlim || x <= -qlim);
+            }
+            // |q| >= q_lim could let an FP64 partial sum pass 2^53: the item
+            // goes to the exact int64 body
+            if (__syncthreads_or(big) && tid == 0) atomicExch(&a.items[item].fail, 1);
+        }
         // this tile's rows, staged by the bulk copies; a wait that gives up
         // reports a timeout (the launch's results are then void) and is
         // retried, bounded, before the CTA exits
@@ -1278,12 +1270,12 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
                 if constexpr (H >= 2) {
 #pragma unroll
                     for (int h = 0; h < H; h += 2) {
-                        const double2 q2 = __ldg(reinterpret_cast<const double2 *>(qdi + j * H + h));
+                        const double2 q2 = *reinterpret_cast<const double2 *>(&qd[j * H + h]);
                         qv[h] = q2.x;
                         qv[h + 1] = q2.y;
                     }
                 } else {
-                    qv[0] = __ldg(qdi + j);
+                    qv[0] = qd[j];
                 }
 #pragma unroll
                 for (int h = 0; h < H; ++h)
@@ -2123,7 +2115,7 @@ inline int chunk_slots() {
 
 // Byte layout of the scratch of one scan: `o` offsets in the order carved.
 struct ScratchLayout {
-    size_t top, cmx, rec, blk, seg, items, redo, desc, bmg, sc, lbw, bdone, idone, sdone, foldat, qdg, total;
+    size_t top, cmx, rec, blk, seg, items, redo, desc, bmg, sc, lbw, bdone, idone, sdone, foldat, total;
     ScratchLayout(int ni, int mc, int sc_cap, int tc, int H, int CW, int64_t rows) {
         auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
         const int mb = (mc + GBLK - 1) / GBLK;
@@ -2135,7 +2127,6 @@ struct ScratchLayout {
         idone = o; o += al(sizeof(unsigned int) * (size_t)ni);
         sdone = o; o += al(sizeof(unsigned int));
         foldat = o; o += al((size_t)tc);
-        qdg = o; o += al(sizeof(double) * (size_t)ni * D * H);
         cmx = o; o += al(sizeof(long long) * (size_t)ni * mc * 2 * HMAX);
         rec = o; o += al(sizeof(ChunkRec) * (size_t)ni * mc);
         blk = o; o += al(sizeof(BlockRec) * (size_t)ni * mb);
@@ -2196,7 +2187,6 @@ inline int reserve_scratch(ChunkScratch &cs, int n_items, int max_nc, int n_tile
     cs.idone = (unsigned int *)(p + L.idone);
     cs.sdone = (unsigned int *)(p + L.sdone);
     cs.fold_at = p + L.foldat;
-    cs.qdg = (double *)(p + L.qdg);
     cs.lbw_words = (size_t)ni * mc * HMAX;
     cs.epoch = 0;
     cs.n_items = ni;
@@ -2214,13 +2204,11 @@ inline int launch_chunk_kernels(ChunkArgs &a, int32_t B, const int32_t *d_seq, c
                                 cudaStream_t s) {
     const int gA = chunk_slots<H, KB, VB, 0, RS>(), gB = chunk_slots<H, KB, VB, 1, RS>();
     if (gA < 0 || gB < 0) return INS_ECUDA;
-    k_q_double<H><<<a.n_items, 256, 0, s>>>(a);
-    // the launches after it may start while the one before finishes (each
-    // waits for it before reading its results)
+    k_scan_scores<H, KB, VB, RS><<<gA < a.n_tiles ? gA : a.n_tiles, CHUNK_THREADS, ScoreCfg<H, KB, VB, RS>::BYTES, s>>>(a);
+    // the launches after the scores may start while the one before finishes
+    // (each waits for it before reading its results)
     const unsigned gv = (unsigned)(gB < a.n_tiles ? gB : a.n_tiles);
-    if (launch_after(k_scan_scores<H, KB, VB, RS>, (unsigned)(gA < a.n_tiles ? gA : a.n_tiles),
-                     (unsigned)CHUNK_THREADS, ScoreCfg<H, KB, VB, RS>::BYTES, s, a) != cudaSuccess ||
-        launch_after(k_chunk_prefix<H>, (unsigned)(a.n_items * H), 256u, 0, s, a) != cudaSuccess ||
+    if (launch_after(k_chunk_prefix<H>, (unsigned)(a.n_items * H), 256u, 0, s, a) != cudaSuccess ||
         launch_after(k_scan_values<H, KB, VB, RS>, gv, (unsigned)CHUNK_THREADS, ChunkCfg<H, KB, VB, RS>::BYTES,
                      s, a) != cudaSuccess ||
         (!a.fold_fused && launch_after(k_fold_blocks<H>, (unsigned)(a.n_items * a.max_blocks),
@@ -2294,7 +2282,6 @@ inline int prepare_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, 
     a.items = cs.items;
     a.redo = cs.redo;
     a.redo_total = cs.redo_total;
-    a.qdg = cs.qdg;
     a.status = d_status;
     cs.last_items = n_items;
     return INS_OK;
@@ -2310,8 +2297,8 @@ inline int launch_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, i
                                             d_status, a, s))
         return rc;
     const int rc = launch_chunk_kernels<H, KB, VB, RS>(a, B, d_seq, d_T, s);
-    // queries, scores, prefix, values, [block fold], item fold, exact re-run
-    if (rc == INS_OK) cs.launches += a.fold_fused ? 6 : 7;
+    // scores, prefix, values, [block fold], item fold, exact re-run
+    if (rc == INS_OK) cs.launches += a.fold_fused ? 5 : 6;
     return rc;
 }
 
@@ -2324,7 +2311,6 @@ inline int launch_split_maxima(ChunkArgs &a, cudaStream_t s) {
     ChunkArgs m = a;
     m.m_init = nullptr;
     m.parts = nullptr;
-    k_q_double<H><<<m.n_items, 256, 0, s>>>(m);
     k_scan_scores<H, KB, VB, RS><<<gA < m.n_tiles ? gA : m.n_tiles, CHUNK_THREADS, ScoreCfg<H, KB, VB, RS>::BYTES, s>>>(m);
     k_chunk_prefix<H><<<m.n_items * H, 256, 0, s>>>(m);
     return cudaGetLastError() == cudaSuccess ? INS_OK : INS_ECUDA;

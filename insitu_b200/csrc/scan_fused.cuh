@@ -201,6 +201,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
     constexpr int UPW = 32 / H;                 // table units per warp in the build
     constexpr int PGMAX = C / 16 + 1;           // pages a tile touches (P >= 16)
     extern __shared__ __align__(16) uint8_t dyn[];
+    __shared__ __align__(16) double qd[D * H];   // [channel][head] of the item being scored
     __shared__ int32_t vcent[16];
     __shared__ int32_t exp_tab[256];
     __shared__ long long m_in_sm[H];
@@ -213,7 +214,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
     __shared__ unsigned int resc_sm;
     __shared__ int4 tdesc_sm[4];                       // tiles li-1 .. li+2 (ring of 4)
     __shared__ int32_t pages_sm[4][PGMAX];
-    __shared__ int gave_up_sm;
+    __shared__ int prev_item_sm, gave_up_sm;
 
     const double2 *ctab = reinterpret_cast<const double2 *>(dyn);
     uint32_t *d_sm = reinterpret_cast<uint32_t *>(dyn + FC::OFF_S);
@@ -238,7 +239,10 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
         }
         for (int i = tid; i < 256; i += NT) exp_tab[i] = a.tb->exp_tab[i];
         if (tid < 16) vcent[tid] = tid < NC ? (int32_t)a.tb->v_cent[tid] : 0;
-        if (tid == 0) gave_up_sm = 0;
+        if (tid == 0) {
+            prev_item_sm = -1;
+            gave_up_sm = 0;
+        }
     }
     const int G = gridDim.x;
     const int ntl = (a.n_tiles - (int)blockIdx.x + G - 1) / G;
@@ -700,7 +704,8 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
             const int item = td.x, c = td.y;
             const int64_t t0 = td.z;
             const int n = td.w;
-            const int kvh = item % g.n_kv;
+            const int b = item / g.n_kv, kvh = item % g.n_kv;
+            const int64_t qbase = ((int64_t)b * g.n_kv * H + (int64_t)kvh * H) * D;
             const int poff = (int)(t0 % g.P);
             const int32_t *ptab = pages_sm[li & 3];
 
@@ -724,8 +729,23 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
             // the next tile's rows into L2 while this one computes
             if (warp == 1 && li + 1 < ntl) prefetch_rows(a, tdesc_sm[(li + 1) & 3], pages_sm[(li + 1) & 3], lane, 3);
             if (tid < H) tmax_sm[tid] = LLONG_MIN;
-            __syncthreads();
-            const double *qdi = a.qdg + (int64_t)item * D * H;   // this item's queries (k_q_double)
+            if (item != prev_item_sm) {
+                __syncthreads();                 // every thread has read prev_item_sm
+                if (tid == 0) prev_item_sm = item;
+                for (int i = tid; i < H * D; i += NT) qd[(i % D) * H + i / D] = (double)a.q_rot[qbase + i];
+                __syncthreads();
+                bool big = false;
+                const double qlim = (double)g.q_lim;
+                for (int i = tid; i < H * D; i += NT) {
+                    const double xq = qd[i];
+                    big |= (xq >= qlim || xq <= -qlim);
+                }
+                // |q| >= q_lim could let an FP64 partial sum pass 2^53: the
+                // item goes to the exact int64 body
+                if (__syncthreads_or(big) && tid == 0) atomicExch(&a.items[item].fail, 1);
+            } else {
+                __syncthreads();
+            }
 
             double acc[R][H];
 #pragma unroll
@@ -748,12 +768,12 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
                     if constexpr (H >= 2) {
 #pragma unroll
                         for (int h = 0; h < H; h += 2) {
-                            const double2 q2 = __ldg(reinterpret_cast<const double2 *>(qdi + j * H + h));
+                            const double2 q2 = *reinterpret_cast<const double2 *>(&qd[j * H + h]);
                             qv[h] = q2.x;
                             qv[h + 1] = q2.y;
                         }
                     } else {
-                        qv[0] = __ldg(qdi + j);
+                        qv[0] = qd[j];
                     }
 #pragma unroll
                     for (int h = 0; h < H; ++h)
@@ -880,7 +900,6 @@ inline int launch_fused_kernels(ChunkArgs &a, const FusedExtra &x, int32_t B, co
     const int G = fused_slots<H, KB, VB, RS>();
     if (G < 0) return INS_ECUDA;
     const unsigned grid = (unsigned)(G < a.n_tiles ? G : a.n_tiles);
-    k_q_double<H><<<a.n_items, 256, 0, s>>>(a);
     if (launch_after(k_scan_fused<H, KB, VB, RS>, grid, (unsigned)CHUNK_THREADS,
                      FusedCfg<H, KB, VB, RS>::BYTES, s, a, x) != cudaSuccess)
         return INS_ECUDA;
@@ -915,7 +934,7 @@ inline int launch_online_tiles(ChunkScratch &cs, const Geo &g, const DevTables *
                       ? -1
                       : ((int64_t)cs.hold_item * a.max_chunks + cs.hold_chunk) * H + cs.hold_head;
     const int rc = launch_fused_kernels<H, KB, VB, RS>(a, x, B, d_seq, d_T, s);
-    if (rc == INS_OK) cs.launches += 3;          // the queries, the scan, the exact re-run
+    if (rc == INS_OK) cs.launches += 2;          // the scan, the exact re-run
     return rc;
 }
 
