@@ -83,6 +83,8 @@ def parse():
                          "with all 16 attention layers on the GPU path, 8K context")
     ap.add_argument("--scan-kernel", choices=("fused", "split"), default="split",
                     help="the online scan as separate launches (default) or as one launch")
+    ap.add_argument("--tiles", choices=("auto", "large", "small"), default="auto",
+                    help="tile size of the online scan (ins_cache_set_tiles)")
     ap.add_argument("--config", type=int, choices=(2, 3, 4, 5), default=2,
                     help="benchmark config to time (2: the default sweep point; 5 = --split)")
     return ap.parse_args()
@@ -226,6 +228,7 @@ def run_ours(args):
     q_all, k_all, v_all = step_inputs(gen, K + W, device)
     pc = dec.pc
     pc.set_scan_kernel(args.scan_kernel)
+    pc.set_tiles(args.tiles)
     stream = torch.cuda.current_stream(device)
 
     def barrier():
@@ -338,15 +341,15 @@ def run_ours(args):
                          "peak_kind": peak_kind,
                          "traffic": (round(tpr * N_KV * T_mid) if tpr else None),
                          "kernel": ("the online scan: k_scan_fused (one persistent launch: "
-                                    "scores, look-back, values, folds) and k_scan_seq (exact "
+                                    "scores, look-back, values), k_fold and k_scan_seq (exact "
                                     "re-run of unproven items)") if args.scan_kernel == "fused" else
-                                   ("the online scan: k_scan_scores, k_chunk_prefix, k_scan_values, "
-                                    "k_fold_blocks, k_fold_items, k_scan_seq (exact re-run)")},
+                                   ("the online scan: k_scan_scores, k_scan_values, k_fold, "
+                                    "k_scan_seq (exact re-run of unproven items)")},
             "e2e": {"value": round(tot_e2e / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "us_per_step": round(e2e_ms / K * 1e3, 2)},
             # counted by the library over the timed steps: ingress, scores,
-            # prefix, values, [fold_blocks], fold_items, exact re-run
+            # values, fold, exact re-run
             "gpu_launches": launches,
             # (sequence, KV head) items of the timed scans that the exact
             # sequential kernel recomputed (0: every item took the fast path)

@@ -134,14 +134,14 @@ enum { INS_TILES_AUTO = 0, INS_TILES_LARGE = 1, INS_TILES_SMALL = 2 };
 int ins_cache_set_tiles(ins_cache *cache, int32_t mode);
 
 /* Which kernels run the context-parallel online scan (no reference
- * counterpart; results are identical either way). SPLIT, the default:
- * separate score, prefix-maximum, value and fold launches with the scores
- * kept in global memory between them (the context split always uses these).
+ * counterpart; results are identical either way). SPLIT, the default: a
+ * score launch, then a value launch, with the scores kept in global memory
+ * between them (the context split always uses these).
  * FUSED: one persistent launch that scores each tile, finds the running
  * maximum entering it from the tiles before (a bounded look-back on words the
- * other CTAs publish), accumulates V and folds the tile records, followed by
- * the exact re-run of items it could not prove; fewer launches, no per-row
- * scratch (ins_scan_noalloc always uses it). */
+ * other CTAs publish) and accumulates V; no per-row scratch (ins_scan_noalloc
+ * always uses it). Either way a fold launch and the exact re-run of items the
+ * fold could not prove follow. */
 enum { INS_SCAN_FUSED = 0, INS_SCAN_SPLIT = 1 };
 int ins_cache_set_scan_kernel(ins_cache *cache, int32_t mode);
 
@@ -164,11 +164,10 @@ int64_t ins_cache_capacity(const ins_cache *cache);
 
 /* Kernels this cache has launched so far through ins_ingress,
  * ins_ingress_lanes, ins_seam, ins_seam_device_positions and ins_scan (a
- * running count, for a caller that reports what ran). The online scan is 5
- * launches with the separate kernels (scores, prefix maxima, values, item
- * fold, exact re-run), 6 when its items need more than one fold block, and 2
- * with the fused kernel (the scan, the exact re-run). No reference
- * counterpart. -1 for NULL. */
+ * running count, for a caller that reports what ran). The online scan is 4
+ * launches with the separate kernels (scores, values, fold, exact re-run)
+ * and 3 with the fused kernel (the scan, the fold, the exact re-run). No
+ * reference counterpart. -1 for NULL. */
 int64_t ins_cache_launches(const ins_cache *cache);
 
 /* Flags of ins_ingress. */

@@ -1235,7 +1235,6 @@ int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
     a.n_tiles = (int32_t)n_tiles;
     a.max_chunks = tp.max_nc;
     a.max_blocks = (tp.max_nc + GBLK - 1) / GBLK;
-    a.fold_fused = tp.max_nc <= GBLK;
     a.n_items = n_items;
     a.row_base = (const int64_t *)(p + L.desc + TD.rb);
     a.seq_ids = (const int32_t *)(p + o_seq);
@@ -1256,16 +1255,14 @@ int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
     a.status = c->d_status;
     FusedExtra x;
     x.lbw = (unsigned long long *)(p + L.lbw);
-    x.blk_done = (unsigned int *)(p + L.bdone);
-    x.item_done = (unsigned int *)(p + L.idone);
-    x.scan_done = (unsigned int *)(p + L.sdone);
-    x.fold_at = p + L.foldat;
+    a.item_done = (unsigned int *)(p + L.idone);
+    a.scan_done = (unsigned int *)(p + L.sdone);
     x.epoch = 1;
     x.poll_limit = c->chunk.poll_limit;
     x.hold_word = -1;
     const int rc = launch_fused_kernels<H, KB, VB, RS>(a, x, B, a.seq_ids, a.T, s);
     if (rc) return fail(rc, "scan launch");
-    c->chunk.launches += 2;                    // the scan, the exact re-run
+    c->chunk.launches += 3;                    // the scan, the fold, the exact re-run
     return INS_OK;
 }
 

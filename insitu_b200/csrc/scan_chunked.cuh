@@ -4,25 +4,25 @@
 // running maximum m, and at every token whose score exceeds it, a rescale
 // acc = floor(acc * exp(s - m) / 2^15) before the token's own term is added.
 // This scan splits every (sequence, KV head) item into tiles of C rows and
-// still returns the reference's bits. Its launches follow one another on the
-// stream and no launch ever waits on another CTA:
+// still returns the reference's bits. It is three launches, and no CTA ever
+// waits on another:
 //
 //  1. k_scan_scores: the scores of every tile (exact FP64 FMA on integer
 //     operands; the K rows staged in shared memory by bulk copies one tile
 //     ahead). Each is kept as its offset below its 32-row block's maximum;
 //     the block and tile maxima are kept too.
-//  2. k_chunk_prefix: per item, the running maximum entering every tile (the
-//     maximum of all earlier tiles' maxima).
-//  3. k_scan_values: knowing its incoming maximum m_in, a tile finds the exact
-//     rescale points (tokens above the running maximum), p = exp(m - s) for
-//     every token, and splits its tokens into segments at the rescale points.
-//     Within a segment every term is a fixed integer, so its contribution is
-//     a plain sum; the tile writes a record of its segments.
-//  4. k_fold_blocks, k_fold_items: the records folded in causal order, per
-//     block of 32 tiles and then per item: acc = floor(acc * f / 2^15) at each
-//     rescale, + segment sums, then the finalize. That fold equals the
-//     per-token recurrence provided the reference's 32-bit clamp never fires;
-//     the fold proves it per tile with
+//  2. k_scan_values, per tile: the running maximum entering it (m_in, the
+//     maximum of the earlier tiles' maxima), the exact rescale points (tokens
+//     above the running maximum), p = exp(m - s) for every token, and its
+//     tokens split into segments at the rescale points. Within a segment
+//     every term is a fixed integer, so its contribution is a plain sum; the
+//     tile writes a record of its segments.
+//  3. k_fold: a CTA per block of 32 tiles folds their records in causal
+//     order, and the one that completes an item's last block folds the blocks
+//     and finalizes: acc = floor(acc * f / 2^15) at each rescale, + segment
+//     sums.
+//     That fold equals the per-token recurrence provided the reference's
+//     32-bit clamp never fires; the fold proves it per tile with
 //     |acc at tile start| + sum_t max_k |term(t, k)| <= 2^31 - 1, which bounds
 //     every partial sum inside the tile (a rescale never grows |acc|).
 //
@@ -48,6 +48,7 @@ constexpr int HMAX = 8;
 constexpr int SEGMAX = 32;               // rescales one head's tile can hold
 constexpr int GBLK = 32;                 // tiles folded per level-1 block
 constexpr int CHUNK_THREADS = 256;
+constexpr int FB = 8;                     // records a fold loads at once
 
 struct SegEntry {          // a rescale and the translation that follows it
     int64_t S[D];          // sum of terms after the rescale (per channel)
@@ -160,7 +161,6 @@ struct ChunkArgs {
     int32_t n_tiles;
     int32_t max_chunks;
     int32_t max_blocks;
-    int32_t fold_fused;           // every item fits one block: k_fold_items folds the tiles too
     int32_t n_items;
     const int64_t *row_base;      // [n_items]: first row of the item in `sc`
     const int32_t *seq_ids;
@@ -182,9 +182,12 @@ struct ChunkArgs {
     int32_t *redo;                // [n_items]: 1 = recompute with the sequential body
     int32_t *status;
     const long long *m_init;      // [n_items][H] running maximum entering the first tile, or null
-    long long *maxima;            // [n_items][H] k_chunk_prefix writes each item's maximum, or null
+    long long *maxima;            // [n_items][H] k_item_maxima writes each item's maximum, or null
     PartRec *parts;               // [n_items] composites instead of finalized outputs, or null
     unsigned long long *redo_total;  // running count of items handed to the sequential kernel, or null
+    // counters of the fold launch that reset themselves on the last arrival
+    unsigned int *item_done;      // [n_items] blocks folded into each item so far
+    unsigned int *scan_done;      // items finished in this launch
 };
 
 // Chunks of an item: one per tile_rows rows, and one (empty) for an empty item.
@@ -341,8 +344,7 @@ struct ChunkScratch {
                                                               // (the test of the bounded wait)
     unsigned long long *lbw = nullptr;   // look-back words of the fused scan
     size_t lbw_words = 0;
-    unsigned int *bdone = nullptr, *idone = nullptr, *sdone = nullptr;
-    uint8_t *fold_at = nullptr;
+    unsigned int *idone = nullptr, *sdone = nullptr;
     unsigned int epoch = 0;       // of the last fused scan, 1 .. 4095
     int64_t launches = 0;         // kernels launched by ingress, seam and scan calls (a count)
     int64_t sc_rows = 0;          // rows * H capacity of `sc`, in 32-bit words
@@ -597,11 +599,11 @@ __device__ void merge_block(const ChunkArgs &a, int item, int blk, int nchunks,
         int64_t loc = 0, Y = 0, curS = 0, curl = 0, Spre = 0, lpre = 0;
         int ne = 0;
         bool opened = false;
-        for (int cb = c0; cb < c1; cb += 8) {
-            int32_t S0[8], ns[8], sb[8];
+        for (int cb = c0; cb < c1; cb += FB) {
+            int32_t S0[FB], ns[FB], sb[FB];
             int64_t Bk[8], l0[8];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < FB; ++u) {
                 const int c = cb + u;
                 if (c < c1) {
                     S0[u] = ldcg(&recs[c].S0[h][ch]);
@@ -612,7 +614,7 @@ __device__ void merge_block(const ChunkArgs &a, int item, int blk, int nchunks,
                 }
             }
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < FB; ++u) {
                 if (cb + u >= c1) break;
                 const int64_t al = loc < 0 ? -loc : loc;
                 Y = max(Y, al + Bk[u]);
@@ -695,11 +697,11 @@ __device__ void merge_item(const ChunkArgs &a, int item, int nblocks, int64_t T,
         if (pr >= H * D || bad) continue;
         const int h = pr / D, ch = pr % D;
         // the block records in batches of 8, their loads issued together
-        for (int b0 = 0; b0 < nblocks; b0 += 8) {
-            int64_t Yv[8], Sv[8], lv[8];
-            int nev[8], ebv[8];
+        for (int b0 = 0; b0 < nblocks; b0 += FB) {
+            int64_t Yv[FB], Sv[FB], lv[FB];
+            int nev[FB], ebv[FB];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < FB; ++u) {
                 if (b0 + u < nblocks) {
                     const BlockRec &br = blks[b0 + u];
                     Yv[u] = ldcg(&br.Y[h][ch]);
@@ -710,7 +712,7 @@ __device__ void merge_item(const ChunkArgs &a, int item, int nblocks, int64_t T,
                 }
             }
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < FB; ++u) {
                 if (b0 + u >= nblocks) break;
                 const int64_t aa = acc[k] < 0 ? -acc[k] : acc[k];
                 if (aa + Yv[u] > INT32_MAX) bad = true;
@@ -784,11 +786,11 @@ __device__ void fold_part(const ChunkArgs &a, int item, int nblocks, int64_t T, 
         int ne = 0;
         bool opened = false;
         // the block records in batches of 8, their loads issued together
-        for (int b0 = 0; b0 < nblocks; b0 += 8) {
-            int64_t Yv[8], Sv[8], lv[8];
-            int nev[8], ebv[8];
+        for (int b0 = 0; b0 < nblocks; b0 += FB) {
+            int64_t Yv[FB], Sv[FB], lv[FB];
+            int nev[FB], ebv[FB];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < FB; ++u) {
                 if (b0 + u < nblocks) {
                     const BlockRec &br = blks[b0 + u];
                     Yv[u] = ldcg(&br.Y[h][ch]);
@@ -799,7 +801,7 @@ __device__ void fold_part(const ChunkArgs &a, int item, int nblocks, int64_t T, 
                 }
             }
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < FB; ++u) {
                 if (b0 + u >= nblocks) break;
                 const int64_t al = loc < 0 ? -loc : loc;
                 Y = max(Y, al + Yv[u]);
@@ -869,6 +871,113 @@ __device__ void fold_part(const ChunkArgs &a, int item, int nblocks, int64_t T, 
         pr.maxs = ia.maxs;
         a.redo[item] = 0;            // a shard's item is not re-run here
     }
+}
+
+// Fold block c / GBLK of `item`; the CTA that completes the item's last block
+// also folds the item and finalizes it (or writes a context shard's
+// composite). A counter per item that resets itself on the last arrival
+// (atomicInc) decides who is last; the last item of the launch empties the
+// segment pool. Called by every thread of the CTA.
+template <int H>
+__device__ __forceinline__ void fold_block_and_item(const ChunkArgs &a, int item, int c) {
+    __shared__ int flag_sm;
+    __shared__ int base_sm[H];
+    __shared__ long long slots[CHUNK_THREADS / 32];
+    const int tid = threadIdx.x;
+    const int nc = item_chunks(a, item);
+    const int blk = c / GBLK, nblk = (nc + GBLK - 1) / GBLK;
+    __threadfence();
+    merge_block<H>(a, item, blk, nc, base_sm);
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const unsigned old = atomicInc(&a.item_done[item], (unsigned)(nblk - 1));
+        flag_sm = old == (unsigned)(nblk - 1);
+    }
+    __syncthreads();
+    if (!flag_sm) return;
+    __threadfence();
+    const int64_t T = a.T[item / a.g.n_kv];
+    if (a.parts) fold_part<H>(a, item, nblk, T, slots);
+    else merge_item<H>(a, item, nblk, T, (int64_t)item * H * D, slots);
+    __syncthreads();
+    if (tid == 0) {
+        ItemAcc &ia = a.items[item];
+        ia.done_blocks = 0;
+        ia.resc = 0;
+        ia.sovf = 0;
+        ia.maxs = 0;
+        ia.fail = 0;
+        __threadfence();
+        // the last item of the launch empties the segment pool
+        if (atomicInc(a.scan_done, (unsigned)(a.n_items - 1)) == (unsigned)(a.n_items - 1)) *a.seg_top = 0;
+    }
+}
+
+// Max over a warp of values in [-2^47, 2^47) or LLONG_MIN, as two 32-bit
+// reductions of the offset from -2^47 - 1.
+__device__ __forceinline__ long long warp_max_score(long long v) {
+    const long long base = -(1ll << 47) - 1;
+    const long long u = v < base ? 0 : v - base;            // < 2^48
+    const int hi = (int)(u >> 20);
+    const int mhi = __reduce_max_sync(FULL, hi);
+    const unsigned mlo = __reduce_max_sync(FULL, hi == mhi ? (unsigned)(u & 0xFFFFF) : 0u);
+    const long long m = ((long long)mhi << 20) | (long long)mlo;
+    return m == 0 ? LLONG_MIN : m + base;
+}
+
+// The running maximum entering tile c of an item, for one warp: the maximum
+// of the maxima of the item's tiles 0 .. c-1 (which the score launch wrote)
+// and of the seed (the maximum entering a context shard, or the lowest
+// score). Lane h returns head h's. The state lives in shared memory (the
+// values loop has no registers to spare): a warp that walks an item's tiles
+// in increasing order only reads the maxima since the tile it resolved last.
+template <int H>
+struct RunMax {
+    long long m[H];
+    int item, c;
+};
+
+template <int H>
+__device__ __forceinline__ void run_max_init(RunMax<H> &r, int lane) {
+    if (lane == 0) {
+        r.item = -1;
+        r.c = 0;
+    }
+    __syncwarp();
+}
+
+template <int H>
+__device__ __forceinline__ long long run_max_at(RunMax<H> &r, const ChunkArgs &a, int nitem, int nc, int lane) {
+    int lo = 0;
+    long long m;
+    if (nitem == r.item && nc >= r.c) {
+        lo = r.c;
+        m = lane < H ? r.m[lane] : LLONG_MIN;
+    } else {
+        m = DefFmt::S_LO;
+        if (a.m_init && lane < H) {
+            const long long sd = a.m_init[(int64_t)nitem * H + lane];
+            m = sd > m ? sd : m;
+        }
+    }
+    const long long *v = a.cmx + (int64_t)nitem * a.max_chunks * 2 * HMAX;
+    for (int j0 = lo; j0 < nc; j0 += 32) {
+        const int j = j0 + lane;
+#pragma unroll
+        for (int h = 0; h < H; ++h) {
+            const long long mh = warp_max_score(j < nc ? ldcg(v + (int64_t)j * 2 * HMAX + h) : LLONG_MIN);
+            if (lane == h && mh > m) m = mh;
+        }
+    }
+    __syncwarp();
+    if (lane < H) r.m[lane] = m;
+    if (lane == 0) {
+        r.item = nitem;
+        r.c = nc;
+    }
+    __syncwarp();
+    return m;
 }
 
 // The context-split merge: one CTA per item folds the shards' composites in
@@ -1160,6 +1269,10 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
         mbar_init(&full_bar[0], 1);
         mbar_init(&full_bar[1], 1);
         mbar_fence_init();
+        // the segment pool of the values launch starts empty (the folds of the
+        // scan before this one empty it too; this keeps a scan that never
+        // reached its folds from leaking into the next)
+        if (blockIdx.x == 0) *a.seg_top = 0;
     }
     if (tid < 2 * H) tmax_sm[tid / H][tid % H] = LLONG_MIN;
     __syncthreads();
@@ -1372,58 +1485,25 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// Launch 2: the running maximum entering every tile
+// A context shard's item maxima (the exchange between ranks): one warp per
+// (item, head) maxes the tile maxima the score launch wrote.
 // ---------------------------------------------------------------------------
-// One CTA per (item, head): m_in(c) = max(-2^(score_width-1), max of the maxima
-// of tiles 0 .. c-1), the m the recurrence carries into tile c. Each thread
-// folds a run of consecutive tiles; the runs' maxima are scanned across the
-// CTA.
 template <int H>
-__global__ void __launch_bounds__(256) k_chunk_prefix(ChunkArgs a) {
-    __shared__ long long wtot[8];
-    const int item = blockIdx.x / H, h = blockIdx.x % H;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+__global__ void __launch_bounds__(256) k_item_maxima(ChunkArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int wi = (int)blockIdx.x * 8 + (threadIdx.x >> 5);
     wait_prior_grid();
-    // the segment pool of the values launch starts empty (no launch before it
-    // allocates from it)
-    if (blockIdx.x == 0 && tid == 0) *a.seg_top = 0;
+    if (wi >= a.n_items * H) return;
+    const int item = wi / H, h = wi % H;
     const int nc = item_chunks(a, item);
-    long long *v = a.cmx + (int64_t)item * a.max_chunks * 2 * HMAX;
-    const long long s_lo = -(1ll << (a.g.score_width - 1));
-    const long long seed = a.m_init ? (a.m_init[(int64_t)item * H + h] > s_lo ? a.m_init[(int64_t)item * H + h] : s_lo)
-                                    : s_lo;
-    const int per = (nc + 255) / 256;                 // tiles per thread
-    const int c0 = tid * per, c1 = min(nc, c0 + per);
-    long long run = LLONG_MIN;
-    for (int c = c0; c < c1; ++c) {
-        const long long x = v[(int64_t)c * 2 * HMAX + h];
-        run = x > run ? x : run;
+    const long long *v = a.cmx + (int64_t)item * a.max_chunks * 2 * HMAX + h;
+    long long m = LLONG_MIN;
+    for (int c = lane; c < nc; c += 32) {
+        const long long x = v[(int64_t)c * 2 * HMAX];
+        m = x > m ? x : m;
     }
-    // exclusive scan of the runs' maxima across the CTA
-    long long x = run;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-        const long long y = __shfl_up_sync(FULL, x, off);
-        if (lane >= off) x = y > x ? y : x;
-    }
-    if (lane == 31) wtot[warp] = x;
-    __syncthreads();
-    long long before = seed;
-    for (int w = 0; w < warp; ++w) before = wtot[w] > before ? wtot[w] : before;
-    long long ex = __shfl_up_sync(FULL, x, 1);
-    if (lane == 0) ex = LLONG_MIN;
-    ex = ex > before ? ex : before;
-    for (int c = c0; c < c1; ++c) {
-        v[(int64_t)c * 2 * HMAX + HMAX + h] = ex;
-        const long long y = v[(int64_t)c * 2 * HMAX + h];
-        ex = y > ex ? y : ex;
-    }
-    // the item's own maximum (with no seed), for a context-split exchange
-    if (a.maxima && c1 == nc && c0 < c1) {
-        long long m = LLONG_MIN;
-        for (int w = 0; w < 8; ++w) m = wtot[w] > m ? wtot[w] : m;
-        a.maxima[(int64_t)item * H + h] = m > s_lo ? m : s_lo;
-    }
+    m = warp_max_score(m);
+    if (lane == 0) a.maxima[(int64_t)item * H + h] = m > DefFmt::S_LO ? m : DefFmt::S_LO;
 }
 
 // The p-pass of a tile (4a below): p = exp(m - s) and w = v_norm * p for
@@ -1520,7 +1600,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
     extern __shared__ __align__(16) uint8_t dyn[];
     __shared__ int32_t vcent[16];
     __shared__ int32_t exp_tab[256];
-    __shared__ long long m_in_sm[H];
+    __shared__ long long min_sm[3][H];                 // m_in of the tiles in the descriptor ring
     __shared__ int fail_sm;
     __shared__ int nseg_sm[H], segbase_sm[H];
     __shared__ int32_t rl_f[H][SEGMAX];
@@ -1559,11 +1639,14 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
     }
 
     // Tiles are dealt round-robin (this CTA's: blockIdx.x + li * gridDim.x); no
-    // tile waits on another. Warp 1 looks them up two ahead.
+    // tile waits on another. Warp 1 looks them up two ahead, with the running
+    // maximum entering each.
     const int G = gridDim.x;
     const int ntl = (a.n_tiles - (int)blockIdx.x + G - 1) / G;
     TileAhead<PGMAX> ahead(a, tdesc_sm, trb_sm, pages_sm);
+    __shared__ RunMax<H> runmax;
     if (warp == 1) {
+        run_max_init(runmax, lane);
         ahead.load(a, 0, lane);
         ahead.store(0, lane);
         if (ntl > 1) {
@@ -1574,6 +1657,14 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
     // everything above reads only what was written before the scores launch;
     // from here on, the outputs of the launches before this one
     wait_prior_grid();
+    if (warp == 1) {
+        __syncwarp();                            // lane 0 stored the descriptors
+        for (int j = 0; j < 2 && j < ntl; ++j) {
+            const int4 t = tdesc_sm[j];
+            const long long m = run_max_at(runmax, a, t.x, t.y, lane);
+            if (lane < H) min_sm[j][lane] = m;
+        }
+    }
     __syncthreads();
     for (int li = 0; li < ntl; ++li) {
         const int tile = (int)blockIdx.x + li * G;
@@ -1614,10 +1705,8 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
             }
         }
         for (int i = tid; i < H * CW; i += NT) bmax[i] = a.bmg[(int64_t)tile * H * CW + i];
-        if (tid < H) {
-            m_in_sm[tid] = a.cmx[((int64_t)item * a.max_chunks + c) * 2 * HMAX + HMAX + tid];
+        if (tid < H)
             for (int k = 0; k <= SEGMAX; ++k) lsum_sm[tid][k] = 0;
-        }
         if (tid == 0) {
             resc_sm = 0;
             fail_sm = 0;
@@ -1643,7 +1732,12 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
         // ---- 2. V codes to channel-major words; warp 1 prefetches this CTA's
         //         next tile into L2 first ------------------------------------------
         if (warp == 1) {
-            if (li + 2 < ntl) ahead.load(a, li + 2, lane);
+            if (li + 2 < ntl) {
+                ahead.load(a, li + 2, lane);
+                // slot (li + 2) % 3 last served tile li - 1
+                const long long m = run_max_at(runmax, a, ahead.rtd.x, ahead.rtd.y, lane);
+                if (lane < H) min_sm[(li + 2) % 3][lane] = m;
+            }
             if (li + 1 < ntl) {
                 const int4 t2 = tdesc_sm[(li + 1) % 3];
                 prefetch_rows(a, t2, pages_sm[(li + 1) & 1], lane, 2);
@@ -1699,7 +1793,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
         // build finds p = exp(carry - s') for it as for every other token.
         for (int h = warp; h < H; h += NT / 32) {
             const int nb = (n + 31) / 32;
-            const int64_t m_in = m_in_sm[h];
+            const int64_t m_in = min_sm[li % 3][h];
             int64_t x = lane < nb ? bmax[h * CW + lane] : LLONG_MIN;
 #pragma unroll
             for (int off = 1; off < 32; off <<= 1) {
@@ -2011,45 +2105,19 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// Launches 4 and 5: the fold, after every tile's record is written (the
-// stream orders it; no fence or counter is needed)
+// The fold, after every tile's record is written (the stream orders it): one
+// CTA per (item, block of GBLK tiles) folds the block's records; the CTA that
+// folds an item's last block folds the item's blocks and finalizes it (or
+// writes a context shard's composite). The folds are a launch of their own:
+// their code in the loop kernels, called or inlined, costs those loops their
+// register allocation (the value loop ran at half speed).
 // ---------------------------------------------------------------------------
-// Level 1: one CTA per (item, block of GBLK tiles).
 template <int H>
-__global__ void __launch_bounds__(CHUNK_THREADS) k_fold_blocks(ChunkArgs a) {
-    __shared__ int base_sm[H];
+__global__ void __launch_bounds__(CHUNK_THREADS) k_fold(ChunkArgs a) {
     wait_prior_grid();
     const int item = blockIdx.x / a.max_blocks, blk = blockIdx.x % a.max_blocks;
-    const int nc = item_chunks(a, item);
-    if (blk * GBLK >= nc) return;
-    merge_block<H>(a, item, blk, nc, base_sm);
-}
-
-// Level 2: one CTA per item folds its blocks and finalizes (or, for a context
-// shard, writes its composite), then clears the item's accumulators.
-template <int H>
-__global__ void __launch_bounds__(CHUNK_THREADS) k_fold_items(ChunkArgs a) {
-    __shared__ long long slots[CHUNK_THREADS / 32];
-    __shared__ int base_sm[H];
-    wait_prior_grid();
-    const int item = blockIdx.x;
-    const int nc = item_chunks(a, item), nblk = (nc + GBLK - 1) / GBLK;
-    const int b = item / a.g.n_kv;
-    if (a.fold_fused) {                  // level 1 here: one block of at most GBLK tiles
-        merge_block<H>(a, item, 0, nc, base_sm);
-        __syncthreads();
-    }
-    if (a.parts) fold_part<H>(a, item, nblk, a.T[b], slots);
-    else merge_item<H>(a, item, nblk, a.T[b], (int64_t)item * H * D, slots);
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        ItemAcc &ia = a.items[item];
-        ia.done_blocks = 0;
-        ia.resc = 0;
-        ia.sovf = 0;
-        ia.maxs = 0;
-        ia.fail = 0;
-    }
+    if (blk * GBLK >= item_chunks(a, item)) return;
+    fold_block_and_item<H>(a, item, blk * GBLK);
 }
 
 // ---------------------------------------------------------------------------
@@ -2115,18 +2183,16 @@ inline int chunk_slots() {
 
 // Byte layout of the scratch of one scan: `o` offsets in the order carved.
 struct ScratchLayout {
-    size_t top, cmx, rec, blk, seg, items, redo, desc, bmg, sc, lbw, bdone, idone, sdone, foldat, total;
+    size_t top, cmx, rec, blk, seg, items, redo, desc, bmg, sc, lbw, idone, sdone, total;
     ScratchLayout(int ni, int mc, int sc_cap, int tc, int H, int CW, int64_t rows) {
         auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
         const int mb = (mc + GBLK - 1) / GBLK;
         size_t o = 0;
         top = o; o += al(8);
-        // the single-launch scan's look-back words and fold counters
+        // the single-launch scan's look-back words; the fold's counters
         lbw = o; o += al(sizeof(unsigned long long) * (size_t)ni * mc * H);
-        bdone = o; o += al(sizeof(unsigned int) * (size_t)ni * mb);
         idone = o; o += al(sizeof(unsigned int) * (size_t)ni);
         sdone = o; o += al(sizeof(unsigned int));
-        foldat = o; o += al((size_t)tc);
         cmx = o; o += al(sizeof(long long) * (size_t)ni * mc * 2 * HMAX);
         rec = o; o += al(sizeof(ChunkRec) * (size_t)ni * mc);
         blk = o; o += al(sizeof(BlockRec) * (size_t)ni * mb);
@@ -2183,10 +2249,8 @@ inline int reserve_scratch(ChunkScratch &cs, int n_items, int max_nc, int n_tile
     cs.bmg = (long long *)(p + L.bmg);
     cs.sc = (uint32_t *)(p + L.sc);
     cs.lbw = (unsigned long long *)(p + L.lbw);
-    cs.bdone = (unsigned int *)(p + L.bdone);
     cs.idone = (unsigned int *)(p + L.idone);
     cs.sdone = (unsigned int *)(p + L.sdone);
-    cs.fold_at = p + L.foldat;
     cs.lbw_words = (size_t)ni * mc * HMAX;
     cs.epoch = 0;
     cs.n_items = ni;
@@ -2205,15 +2269,13 @@ inline int launch_chunk_kernels(ChunkArgs &a, int32_t B, const int32_t *d_seq, c
     const int gA = chunk_slots<H, KB, VB, 0, RS>(), gB = chunk_slots<H, KB, VB, 1, RS>();
     if (gA < 0 || gB < 0) return INS_ECUDA;
     k_scan_scores<H, KB, VB, RS><<<gA < a.n_tiles ? gA : a.n_tiles, CHUNK_THREADS, ScoreCfg<H, KB, VB, RS>::BYTES, s>>>(a);
-    // the launches after the scores may start while the one before finishes
-    // (each waits for it before reading its results)
+    // the values may start while the scores finish (they wait for them before
+    // reading their results)
     const unsigned gv = (unsigned)(gB < a.n_tiles ? gB : a.n_tiles);
-    if (launch_after(k_chunk_prefix<H>, (unsigned)(a.n_items * H), 256u, 0, s, a) != cudaSuccess ||
-        launch_after(k_scan_values<H, KB, VB, RS>, gv, (unsigned)CHUNK_THREADS, ChunkCfg<H, KB, VB, RS>::BYTES,
+    if (launch_after(k_scan_values<H, KB, VB, RS>, gv, (unsigned)CHUNK_THREADS, ChunkCfg<H, KB, VB, RS>::BYTES,
                      s, a) != cudaSuccess ||
-        (!a.fold_fused && launch_after(k_fold_blocks<H>, (unsigned)(a.n_items * a.max_blocks),
-                                       (unsigned)CHUNK_THREADS, 0, s, a) != cudaSuccess) ||
-        launch_after(k_fold_items<H>, (unsigned)a.n_items, (unsigned)CHUNK_THREADS, 0, s, a) != cudaSuccess)
+        launch_after(k_fold<H>, (unsigned)(a.n_items * a.max_blocks), (unsigned)CHUNK_THREADS, 0, s, a) !=
+            cudaSuccess)
         return INS_ECUDA;
     if (cudaGetLastError() != cudaSuccess) return INS_ECUDA;
     // items whose exactness the fold could not prove are recomputed in order
@@ -2261,7 +2323,6 @@ inline int prepare_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, 
     a.n_tiles = n_tiles;
     a.max_chunks = cs.max_chunks;
     a.max_blocks = (cs.max_chunks + GBLK - 1) / GBLK;
-    a.fold_fused = tp.max_nc <= GBLK;
     a.n_items = n_items;
     a.row_base = (const int64_t *)(cs.desc + L.rb);
     a.seq_ids = d_seq;
@@ -2283,6 +2344,8 @@ inline int prepare_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, 
     a.redo = cs.redo;
     a.redo_total = cs.redo_total;
     a.status = d_status;
+    a.item_done = cs.idone;
+    a.scan_done = cs.sdone;
     cs.last_items = n_items;
     return INS_OK;
 }
@@ -2297,8 +2360,8 @@ inline int launch_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, i
                                             d_status, a, s))
         return rc;
     const int rc = launch_chunk_kernels<H, KB, VB, RS>(a, B, d_seq, d_T, s);
-    // scores, prefix, values, [block fold], item fold, exact re-run
-    if (rc == INS_OK) cs.launches += a.fold_fused ? 5 : 6;
+    // scores, values, fold, exact re-run
+    if (rc == INS_OK) cs.launches += 4;
     return rc;
 }
 
@@ -2312,7 +2375,7 @@ inline int launch_split_maxima(ChunkArgs &a, cudaStream_t s) {
     m.m_init = nullptr;
     m.parts = nullptr;
     k_scan_scores<H, KB, VB, RS><<<gA < m.n_tiles ? gA : m.n_tiles, CHUNK_THREADS, ScoreCfg<H, KB, VB, RS>::BYTES, s>>>(m);
-    k_chunk_prefix<H><<<m.n_items * H, 256, 0, s>>>(m);
+    k_item_maxima<H><<<(m.n_items * H + 7) / 8, 256, 0, s>>>(m);
     return cudaGetLastError() == cudaSuccess ? INS_OK : INS_ECUDA;
 }
 
@@ -2324,11 +2387,9 @@ inline int launch_split_part(ChunkArgs &a, cudaStream_t s) {
     if (gB < 0) return INS_ECUDA;
     ChunkArgs m = a;
     m.maxima = nullptr;
-    k_chunk_prefix<H><<<m.n_items * H, 256, 0, s>>>(m);
     k_scan_values<H, KB, VB, RS>
         <<<gB < m.n_tiles ? gB : m.n_tiles, CHUNK_THREADS, ChunkCfg<H, KB, VB, RS>::BYTES, s>>>(m);
-    if (!m.fold_fused) k_fold_blocks<H><<<m.n_items * m.max_blocks, CHUNK_THREADS, 0, s>>>(m);
-    k_fold_items<H><<<m.n_items, CHUNK_THREADS, 0, s>>>(m);
+    k_fold<H><<<m.n_items * m.max_blocks, CHUNK_THREADS, 0, s>>>(m);
     return cudaGetLastError() == cudaSuccess ? INS_OK : INS_ECUDA;
 }
 

@@ -6,8 +6,8 @@
 //
 //   values(li - 1)  the V side of the tile it scored one step earlier: V rows,
 //                   the running maximum entering the tile (below), rescale
-//                   points, p = exp(m - s), term tables, segment sums, the
-//                   tile record, and the folds that record completes;
+//                   points, p = exp(m - s), term tables, segment sums and
+//                   the tile record;
 //   scores(li)      the exact FP64 scores of the next tile, kept in shared
 //                   memory as offsets below their 32-row block maxima (no
 //                   round trip through HBM), and the tile's maximum published.
@@ -30,11 +30,9 @@
 // gives up sets ST_TIMEOUT, takes what it has, and lets the launch finish
 // (its results are then void; ins_cache_status reports INS_ETIMEOUT).
 //
-// Folds: the CTA that finishes the last tile of a 32-tile block folds the
-// block (merge_block), and the one that finishes an item's last block folds
-// the item and finalizes it (merge_item); counters that reset themselves on
-// the last arrival (atomicInc) decide who is last. Items whose exactness the
-// folds cannot prove are recomputed by k_scan_seq, the only other launch.
+// The records are folded by k_fold, the launch after this one (the fold's
+// code inside this kernel cost its loop most of its speed), and items whose
+// exactness the folds cannot prove are recomputed by k_scan_seq.
 #pragma once
 
 #include "scan_chunked.cuh"
@@ -62,25 +60,9 @@ __device__ __forceinline__ void st_relaxed_gpu(unsigned long long *p, unsigned l
     asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-// Max over a warp of values in [-2^47, 2^47) or LLONG_MIN, as two 32-bit
-// reductions of the offset from -2^47 - 1.
-__device__ __forceinline__ long long warp_max_score(long long v) {
-    const long long base = -(1ll << 47) - 1;
-    const long long u = v < base ? 0 : v - base;            // < 2^48
-    const int hi = (int)(u >> 20);
-    const int mhi = __reduce_max_sync(FULL, hi);
-    const unsigned mlo = __reduce_max_sync(FULL, hi == mhi ? (unsigned)(u & 0xFFFFF) : 0u);
-    const long long m = ((long long)mhi << 20) | (long long)mlo;
-    return m == 0 ? LLONG_MIN : m + base;
-}
-
 // The scratch the fused launch needs beyond the chunked scan's records.
 struct FusedExtra {
     unsigned long long *lbw;      // [n_items][max_chunks][H] look-back words
-    unsigned int *blk_done;       // [n_items][max_blocks] tiles folded into each block so far
-    unsigned int *item_done;      // [n_items] blocks folded into each item so far
-    unsigned int *scan_done;      // items finished in this launch
-    uint8_t *fold_at;             // [n_tiles] 1: the tile completed its block, which its CTA folds
     unsigned int epoch;           // 1 .. 2^12 - 1
     int32_t poll_limit;           // polls before a look-back wait gives up
     int64_t hold_word;            // a word index never published (test of the bounded wait), or -1
@@ -148,48 +130,6 @@ __device__ __forceinline__ long long look_back(const ChunkArgs &a, const FusedEx
     return m;
 }
 
-// The CTA that wrote the last record of a block of GBLK tiles folds the
-// block; if that completes the item's last block, it folds the item and
-// finalizes it (or writes a context shard's composite). Called by every
-// thread of that CTA, on the rare tile that completes a block; kept out of
-// line so that its batched 64-bit loads do not weigh on the registers of
-// the scan loop.
-template <int H>
-__device__ __noinline__ void fold_block_and_item(const ChunkArgs &a, const FusedExtra &x, int item, int c) {
-    __shared__ int flag_sm;
-    __shared__ int base_sm[H];
-    __shared__ long long slots[CHUNK_THREADS / 32];
-    const int tid = threadIdx.x;
-    const int nc = item_chunks(a, item);
-    const int blk = c / GBLK, nblk = (nc + GBLK - 1) / GBLK;
-    __threadfence();
-    merge_block<H>(a, item, blk, nc, base_sm);
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        const unsigned old = atomicInc(&x.item_done[item], (unsigned)(nblk - 1));
-        flag_sm = old == (unsigned)(nblk - 1);
-    }
-    __syncthreads();
-    if (!flag_sm) return;
-    __threadfence();
-    const int64_t T = a.T[item / a.g.n_kv];
-    if (a.parts) fold_part<H>(a, item, nblk, T, slots);
-    else merge_item<H>(a, item, nblk, T, (int64_t)item * H * D, slots);
-    __syncthreads();
-    if (tid == 0) {
-        ItemAcc &ia = a.items[item];
-        ia.done_blocks = 0;
-        ia.resc = 0;
-        ia.sovf = 0;
-        ia.maxs = 0;
-        ia.fail = 0;
-        __threadfence();
-        // the last item of the launch empties the segment pool
-        if (atomicInc(x.scan_done, (unsigned)(a.n_items - 1)) == (unsigned)(a.n_items - 1)) *a.seg_top = 0;
-    }
-}
-
 template <int H, int KB, int VB, int RS = 0>
 __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, FusedExtra x) {
     using CF = ChunkCfg<H, KB, VB, RS>;
@@ -206,7 +146,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
     __shared__ int32_t exp_tab[256];
     __shared__ long long m_in_sm[H];
     __shared__ long long tmax_sm[H];
-    __shared__ int fail_sm, last_sm;
+    __shared__ int fail_sm;
     __shared__ int nseg_sm[H], segbase_sm[H];
     __shared__ int32_t rl_f[H][SEGMAX];
     __shared__ unsigned int lsum_sm[H][SEGMAX + 1];    // l of a tile < 2^25
@@ -679,20 +619,6 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
                 if (tid == 0 && resc_sm) atomicAdd(&a.items[item].resc, (unsigned long long)resc_sm);
             }
 
-            // ---- 7. the folds this record completes: a ticket per block --------
-            __threadfence();
-            __syncthreads();
-            if (tid == 0) {
-                const int nc = item_chunks(a, item), blk = c / GBLK;
-                const int ntb = min(GBLK, nc - blk * GBLK);
-                const unsigned old =
-                    atomicInc(&x.blk_done[(int64_t)item * a.max_blocks + blk], (unsigned)(ntb - 1));
-                last_sm = old == (unsigned)(ntb - 1);
-            }
-            __syncthreads();
-            // the fold itself waits for the end of the loop (a call here would
-            // cost the loop its registers)
-            if (tid == 0) x.fold_at[blockIdx.x + vj * G] = (uint8_t)last_sm;
             __syncthreads();                 // the tile's shared memory is reused below
         }
 
@@ -845,14 +771,6 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_fused(ChunkArgs a, Fu
         }
         __syncthreads();
     }
-    // the blocks whose last tile this CTA wrote, folded now
-    for (int li = 0; li < ntl; ++li) {
-        const int tile = (int)blockIdx.x + li * G;
-        if (!x.fold_at[tile]) continue;       // the same value for every thread
-        const int4 t = tile_at(a, tile);
-        fold_block_and_item<H>(a, x, t.x, t.y);
-        __syncthreads();
-    }
     if (tid == 0 && gave_up_sm) atomicOr(a.status, ST_TIMEOUT);
 }
 
@@ -901,7 +819,9 @@ inline int launch_fused_kernels(ChunkArgs &a, const FusedExtra &x, int32_t B, co
     if (G < 0) return INS_ECUDA;
     const unsigned grid = (unsigned)(G < a.n_tiles ? G : a.n_tiles);
     if (launch_after(k_scan_fused<H, KB, VB, RS>, grid, (unsigned)CHUNK_THREADS,
-                     FusedCfg<H, KB, VB, RS>::BYTES, s, a, x) != cudaSuccess)
+                     FusedCfg<H, KB, VB, RS>::BYTES, s, a, x) != cudaSuccess ||
+        launch_after(k_fold<H>, (unsigned)(a.n_items * a.max_blocks), (unsigned)CHUNK_THREADS, 0, s, a) !=
+            cudaSuccess)
         return INS_ECUDA;
     return launch_seq<H>(a.g, a.tb, B, d_seq, d_T, a.page_table, a.pool, a.q_rot, a.out, a.stats,
                          a.redo, s) == cudaSuccess
@@ -924,17 +844,13 @@ inline int launch_online_tiles(ChunkScratch &cs, const Geo &g, const DevTables *
     if (int rc = next_epoch(cs, s)) return rc;
     FusedExtra x;
     x.lbw = cs.lbw;
-    x.blk_done = cs.bdone;
-    x.item_done = cs.idone;
-    x.scan_done = cs.sdone;
-    x.fold_at = cs.fold_at;
     x.epoch = cs.epoch;
     x.poll_limit = cs.poll_limit;
     x.hold_word = cs.hold_item < 0 || cs.hold_item >= a.n_items || cs.hold_chunk >= a.max_chunks
                       ? -1
                       : ((int64_t)cs.hold_item * a.max_chunks + cs.hold_chunk) * H + cs.hold_head;
     const int rc = launch_fused_kernels<H, KB, VB, RS>(a, x, B, d_seq, d_T, s);
-    if (rc == INS_OK) cs.launches += 2;          // the scan, the exact re-run
+    if (rc == INS_OK) cs.launches += 3;          // the scan, the fold, the exact re-run
     return rc;
 }
 
