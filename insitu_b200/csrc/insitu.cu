@@ -287,7 +287,7 @@ int reserve_slots(ins_cache *c, int32_t n, const int32_t *seq_ids, int64_t *slot
 template <int H>
 int launch_scan_h(ins_cache *c, int32_t B, const int32_t *d_seq, const int64_t *d_T,
                   const int64_t *h_T, const int32_t *q_rot, int64_t *out, ins_stats *stats,
-                  ins_softmax mode, cudaStream_t s) {
+                  ins_softmax mode, cudaStream_t s, const int32_t *h_seq) {
     const Geo &g = c->g;
     const int threads = H * 64;
     const dim3 grid(B * g.n_kv);
@@ -305,7 +305,7 @@ int launch_scan_h(ins_cache *c, int32_t B, const int32_t *d_seq, const int64_t *
         return INS_OK;
     }
     return launch_online(c->chunk, g, c->d_tables, B, d_seq, d_T, h_T, c->d_page_table,
-                         c->d_pool, q_rot, out, stats, c->d_status, H, s);
+                         c->d_pool, q_rot, out, stats, c->d_status, H, s, h_seq);
 }
 
 }  // namespace
@@ -695,15 +695,21 @@ int ins_scan(ins_cache *c, int32_t B, const int32_t *seq_ids, const int64_t *len
         hT[i] = T;
         hS[i] = sq;
     }
-    if (int rc = c->stage_b.upload(bytes, s)) return rc;
-    const int64_t *d_T = (const int64_t *)c->stage_b.d;
-    const int32_t *d_seq = (const int32_t *)(d_T + B);
+    // the context-parallel online scan uploads the lengths and ids with its
+    // tile plan (one copy); the other kernels read them from this upload
+    const int64_t *d_T = nullptr;
+    const int32_t *d_seq = nullptr;
+    if (mode != INS_SOFTMAX_ONLINE || !chunk_variant(c->g, c->g.H)) {
+        if (int rc = c->stage_b.upload(bytes, s)) return rc;
+        d_T = (const int64_t *)c->stage_b.d;
+        d_seq = (const int32_t *)(d_T + B);
+    }
     ++c->gen;
     switch (c->g.H) {
-        case 1: return launch_scan_h<1>(c, B, d_seq, d_T, hT, q_rot, out, stats, mode, s);
-        case 2: return launch_scan_h<2>(c, B, d_seq, d_T, hT, q_rot, out, stats, mode, s);
-        case 4: return launch_scan_h<4>(c, B, d_seq, d_T, hT, q_rot, out, stats, mode, s);
-        case 8: return launch_scan_h<8>(c, B, d_seq, d_T, hT, q_rot, out, stats, mode, s);
+        case 1: return launch_scan_h<1>(c, B, d_seq, d_T, hT, q_rot, out, stats, mode, s, hS);
+        case 2: return launch_scan_h<2>(c, B, d_seq, d_T, hT, q_rot, out, stats, mode, s, hS);
+        case 4: return launch_scan_h<4>(c, B, d_seq, d_T, hT, q_rot, out, stats, mode, s, hS);
+        case 8: return launch_scan_h<8>(c, B, d_seq, d_T, hT, q_rot, out, stats, mode, s, hS);
     }
     return fail(INS_EINVAL, "kv_groups");
 }

@@ -46,9 +46,9 @@ namespace ins {
 
 constexpr int HMAX = 8;
 constexpr int SEGMAX = 32;               // rescales one head's tile can hold
-constexpr int GBLK = 32;                 // tiles folded per level-1 block
+constexpr int GBLK = 64;                 // tiles folded per level-1 block
 constexpr int CHUNK_THREADS = 256;
-constexpr int FB = 8;                     // records a fold loads at once
+constexpr int FB = 8;                     // block records an item fold loads at once
 
 struct SegEntry {          // a rescale and the translation that follows it
     int64_t S[D];          // sum of terms after the rescale (per channel)
@@ -269,13 +269,17 @@ struct PinnedRing {
 // Device layout of the tile plan of `ni` items: the runs, each item's first
 // row in the score-offset array, the item order (see ChunkArgs::runs).
 struct TileDesc {
-    size_t runs, rb, ord, total;
-    explicit TileDesc(int ni) {
+    size_t runs, rb, ord, lens, seqs, total;
+    // ni items; B > 0: the scan's lengths and sequence ids ride in the same
+    // upload (one copy per scan)
+    explicit TileDesc(int ni, int B = 0) {
         auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
         runs = 0;
         rb = al(sizeof(int4) * (size_t)(ni + 1));
         ord = rb + al(sizeof(int64_t) * (size_t)ni);
-        total = ord + sizeof(int32_t) * (size_t)ni;
+        lens = al(ord + sizeof(int32_t) * (size_t)ni);
+        seqs = lens + sizeof(int64_t) * (size_t)B;
+        total = seqs + sizeof(int32_t) * (size_t)B;
     }
 };
 
@@ -565,182 +569,108 @@ __device__ __forceinline__ long long cta_max_nonneg(long long v, long long *slot
     return m;
 }
 
-// Level 1: fold the tiles of block `blk` of `item` into a BlockRec. The CTA's
-// threads take the (head, channel) pairs in turn.
+// The folds stage what they read in shared memory, so that a fold costs a few
+// rounds of loads instead of one round per record with rescales.
+//
+// Rescale entries: up to ECAP per head (the first ones in causal order) of up
+// to NR consecutive records (the tiles of a block, or 32 blocks of an item)
+// are staged; an entry past that is read from global memory where it is
+// applied.
 template <int H>
-__device__ void merge_block(const ChunkArgs &a, int item, int blk, int nchunks,
-                            int *base_sm /* [H] */) {
-    const int c0 = blk * GBLK, c1 = min(nchunks, c0 + GBLK);
-    const ChunkRec *recs = a.recs + (int64_t)item * a.max_chunks;
-    // entries each head needs = rescales in the block's tiles: warp h sums
-    // head h's counts, one tile per lane (a block holds at most 32 tiles)
-    static_assert(GBLK <= 32 && HMAX <= CHUNK_THREADS / 32, "one warp per head, one lane per tile");
-    {
-        const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-        if (w < H) {
-            const int c = c0 + lane;
-            int need = c < c1 ? ldcg(&recs[c].nseg[w]) : 0;
-            need = __reduce_add_sync(FULL, need);
-            if (lane == 0) {
-                unsigned b = 0;
-                if (need) b = atomicAdd(a.seg_top, (unsigned)need);
-                if (need && b + need > (unsigned)a.seg_cap) {
-                    atomicExch(&a.items[item].fail, 1);
-                    need = 0;
-                }
-                base_sm[w] = need ? (int)b : -1;
+struct FoldCfg {
+    static constexpr int ECAP = 128 / H;                           // staged entries per head
+    static constexpr size_t OFF_ES = 0;                            // int64 [H][ECAP][D]: S
+    static constexpr size_t OFF_S0 = OFF_ES + (size_t)H * ECAP * D * 8;  // int32 [GBLK][H][D]: tile sums
+    static constexpr size_t BYTES = OFF_S0 + (size_t)GBLK * H * D * 4;
+};
+
+// The staged entries of one fold step; `cnt`/`bas`: per (head, record) the
+// entry count and first entry index, for nrec <= NR records.
+template <int H, int NR>
+struct EntStage {
+    static constexpr int ECAP = FoldCfg<H>::ECAP;
+    int ex[H][NR + 1];          // entries before each record; [h][NR] = the head's total
+    int idx[H * ECAP];
+    int32_t f[H * ECAP];
+    long long l[H * ECAP];
+};
+
+template <int H, int NR>
+__device__ void stage_entries(const ChunkArgs &a, const int (*cnt)[NR], const int (*bas)[NR], int nrec,
+                              EntStage<H, NR> &st, long long *eS /* [H][ECAP][D] */) {
+    constexpr int ECAP = FoldCfg<H>::ECAP;
+    static_assert(NR % 32 == 0, "records in whole warps");
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (w < H) {                               // warp h: head h, records lane, lane + 32, ...
+        int before = 0;
+#pragma unroll
+        for (int i = 0; i < NR / 32; ++i) {
+            const int r = i * 32 + lane;
+            const int c = r < nrec ? cnt[w][r] : 0;
+            int x = c;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const int y = __shfl_up_sync(FULL, x, off);
+                if (lane >= off) x += y;
             }
+            const int ex = before + x - c;
+            st.ex[w][r] = ex;
+            for (int j = 0; j < c && ex + j < ECAP; ++j) st.idx[w * ECAP + ex + j] = bas[w][r] + j;
+            before += __shfl_sync(FULL, x, 31);
         }
+        if (lane == 0) st.ex[w][NR] = before;
     }
     __syncthreads();
-    for (int pr = threadIdx.x; pr < H * D; pr += blockDim.x) {
-        const int h = pr / D, ch = pr % D;
-        const int eb = base_sm[h];
-        int64_t loc = 0, Y = 0, curS = 0, curl = 0, Spre = 0, lpre = 0;
-        int ne = 0;
-        bool opened = false;
-        for (int cb = c0; cb < c1; cb += FB) {
-            int32_t S0[FB], ns[FB], sb[FB];
-            int64_t Bk[8], l0[8];
+    // only the staged entries, head after head, their loads issued together
+    int off = 0;
 #pragma unroll
-            for (int u = 0; u < FB; ++u) {
-                const int c = cb + u;
-                if (c < c1) {
-                    S0[u] = ldcg(&recs[c].S0[h][ch]);
-                    Bk[u] = ldcg(&recs[c].B[h]);
-                    l0[u] = ldcg(&recs[c].l0[h]);
-                    ns[u] = ldcg(&recs[c].nseg[h]);
-                    sb[u] = ldcg(&recs[c].seg_base[h]);
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < FB; ++u) {
-                if (cb + u >= c1) break;
-                const int64_t al = loc < 0 ? -loc : loc;
-                Y = max(Y, al + Bk[u]);
-                loc += S0[u];
-                curS += S0[u];
-                curl += l0[u];
-                // the tile's entries four at a time (loads together, then in
-                // order); the block's own entries written below are a
-                // separate allocation, so these loads read what the values
-                // launch wrote
-                for (int e0 = 0; e0 < ns[u]; e0 += 4) {
-                  int64_t fv[4], sv[4], lw[4];
-#pragma unroll
-                  for (int j = 0; j < 4; ++j) {
-                      if (e0 + j < ns[u]) {
-                          const SegEntry &se = a.segs[sb[u] + e0 + j];
-                          fv[j] = ldcg(&se.f);
-                          sv[j] = ldcg(&se.S[ch]);
-                          lw[j] = ldcg(&se.l);
-                      }
-                  }
-#pragma unroll
-                  for (int j = 0; j < 4; ++j) {
-                    if (e0 + j >= ns[u]) break;
-                    const int64_t f = fv[j];
-                    const int64_t sS = sv[j];
-                    const int64_t sl = lw[j];
-                    if (eb >= 0) {
-                        if (!opened) {
-                            Spre = curS;
-                            lpre = curl;
-                            opened = true;
-                        } else {
-                            a.segs[eb + ne - 1].S[ch] = curS;
-                            if (ch == 0) a.segs[eb + ne - 1].l = curl;
-                        }
-                        if (ch == 0) a.segs[eb + ne].f = (int32_t)f;
-                        ++ne;
-                    }
-                    curS = sS;
-                    curl = sl;
-                    loc = ((loc * f) >> a.g.prob_frac) + sS;
-                  }
-                }
+    for (int h = 0; h < H; ++h) {
+        const int nk = min(st.ex[h][NR], ECAP);
+        const int end = off + nk * D;
+#pragma unroll 4
+        for (int i = off + (int)threadIdx.x; i < end; i += blockDim.x) {
+            const int k = (i - off) / D, ch = (i - off) % D;
+            const SegEntry &se = a.segs[st.idx[h * ECAP + k]];
+            eS[((size_t)h * ECAP + k) * D + ch] = ldcg(&se.S[ch]);
+            if (ch == 0) {
+                st.f[h * ECAP + k] = ldcg(&se.f);
+                st.l[h * ECAP + k] = ldcg(&se.l);
             }
         }
-        if (!opened) {
-            Spre = curS;
-            lpre = curl;
-        } else if (eb >= 0) {
-            a.segs[eb + ne - 1].S[ch] = curS;
-            if (ch == 0) a.segs[eb + ne - 1].l = curl;
-        }
-        BlockRec &br = a.blks[(int64_t)item * a.max_blocks + blk];
-        br.Spre[h][ch] = Spre;
-        br.Y[h][ch] = Y;
-        if (ch == 0) {
-            br.lpre[h] = lpre;
-            br.nent[h] = eb >= 0 ? ne : 0;
-            br.ent_base[h] = eb >= 0 ? eb : 0;
-        }
+        off = end;
+    }
+    __syncthreads();
+}
+
+// Entry j of record r of head h (f, S[ch], l), staged or from global memory.
+template <int H, int NR>
+__device__ __forceinline__ void entry_at(const ChunkArgs &a, const EntStage<H, NR> &st, const long long *eS,
+                                         const int (*bas)[NR], int h, int r, int j, int ch,
+                                         int64_t &f, int64_t &S, int64_t &l) {
+    constexpr int ECAP = FoldCfg<H>::ECAP;
+    const int k = st.ex[h][r] + j;
+    if (k < ECAP) {
+        f = st.f[h * ECAP + k];
+        S = eS[((size_t)h * ECAP + k) * D + ch];
+        l = st.l[h * ECAP + k];
+    } else {
+        const SegEntry &se = a.segs[bas[h][r] + j];
+        f = ldcg(&se.f);
+        S = ldcg(&se.S[ch]);
+        l = ldcg(&se.l);
     }
 }
 
-// Level 2: fold the item's blocks; finalize or mark the item for the exact
-// sequential recomputation.
+// The end of an item's fold: the item goes to the exact sequential kernel if
+// any thread's proof failed (or the item was flagged), else its outputs are
+// finalized and its statistics written. Called by every thread of the CTA.
 template <int H>
-__device__ void merge_item(const ChunkArgs &a, int item, int nblocks, int64_t T,
-                           int64_t qbase, long long *slots /* [NT/32] */) {
-    constexpr int NP = (H * D + CHUNK_THREADS - 1) / CHUNK_THREADS;   // pairs per thread
+__device__ __forceinline__ void finalize_item(const ChunkArgs &a, int item, int64_t T, int64_t qbase,
+                                              const int64_t (&acc)[(H * D + CHUNK_THREADS - 1) / CHUNK_THREADS],
+                                              const int64_t (&l)[(H * D + CHUNK_THREADS - 1) / CHUNK_THREADS],
+                                              bool bad, long long *slots /* [NT/32] */) {
+    constexpr int NP = (H * D + CHUNK_THREADS - 1) / CHUNK_THREADS;
     const int tid = threadIdx.x;
-    const BlockRec *blks = a.blks + (int64_t)item * a.max_blocks;
-    int64_t acc[NP], l[NP];
-    bool bad = *reinterpret_cast<volatile int32_t *>(&a.items[item].fail) != 0;
-#pragma unroll
-    for (int k = 0; k < NP; ++k) {
-        acc[k] = 0;
-        l[k] = 0;
-        const int pr = tid + k * CHUNK_THREADS;
-        if (pr >= H * D || bad) continue;
-        const int h = pr / D, ch = pr % D;
-        // the block records in batches of 8, their loads issued together
-        for (int b0 = 0; b0 < nblocks; b0 += FB) {
-            int64_t Yv[FB], Sv[FB], lv[FB];
-            int nev[FB], ebv[FB];
-#pragma unroll
-            for (int u = 0; u < FB; ++u) {
-                if (b0 + u < nblocks) {
-                    const BlockRec &br = blks[b0 + u];
-                    Yv[u] = ldcg(&br.Y[h][ch]);
-                    Sv[u] = ldcg(&br.Spre[h][ch]);
-                    lv[u] = ldcg(&br.lpre[h]);
-                    nev[u] = ldcg(&br.nent[h]);
-                    ebv[u] = ldcg(&br.ent_base[h]);
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < FB; ++u) {
-                if (b0 + u >= nblocks) break;
-                const int64_t aa = acc[k] < 0 ? -acc[k] : acc[k];
-                if (aa + Yv[u] > INT32_MAX) bad = true;
-                acc[k] += Sv[u];
-                l[k] += lv[u];
-                // the entries four at a time: their loads issued together,
-                // then applied in order
-                for (int e0 = 0; e0 < nev[u]; e0 += 4) {
-                    int64_t fv[4], sv[4], lw[4];
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        if (e0 + j < nev[u]) {
-                            const SegEntry &se = a.segs[ebv[u] + e0 + j];
-                            fv[j] = ldcg(&se.f);
-                            sv[j] = ldcg(&se.S[ch]);
-                            lw[j] = ldcg(&se.l);
-                        }
-                    }
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        if (e0 + j >= nev[u]) break;
-                        acc[k] = ((acc[k] * fv[j]) >> a.g.prob_frac) + sv[j];
-                        l[k] = ((l[k] * fv[j]) >> a.g.prob_frac) + lw[j];
-                    }
-                }
-            }
-        }
-    }
     bad = __syncthreads_or(bad);
     if (tid == 0) {
         a.redo[item] = bad ? 1 : 0;
@@ -770,6 +700,269 @@ __device__ void merge_item(const ChunkArgs &a, int item, int nblocks, int64_t T,
         st.max_abs_acc = mx;
         a.stats[item] = st;
     }
+}
+
+// Items of at most this many tiles are folded and finalized by one CTA in one
+// pass over their tiles (GBLK at a time), without block records.
+constexpr int DIRECT_TILES = 4 * GBLK;
+
+// Level 1: fold the tiles of block `blk` of `item` into a BlockRec. The
+// records come into shared memory first (the scalars by one warp per head,
+// the sums S0 and the rescale entries by the whole CTA); then each thread
+// takes a (head, channel) pair and walks the tiles in order. `direct`: the
+// CTA walks all the item's tiles (GBLK at a time) and, the walk's running
+// accumulator being the item's, proves and finalizes it here.
+template <int H>
+__device__ void merge_block(const ChunkArgs &a, int item, int blk, int nchunks, int *base_sm /* [H] */,
+                            uint8_t *dyn /* FoldCfg<H>::BYTES */, bool direct, long long *slots) {
+    constexpr int NR = GBLK;
+    constexpr int NP = (H * D + CHUNK_THREADS - 1) / CHUNK_THREADS;   // pairs per thread
+    const ChunkRec *recs = a.recs + (int64_t)item * a.max_chunks;
+    int32_t *s0_sm = reinterpret_cast<int32_t *>(dyn + FoldCfg<H>::OFF_S0);
+    long long *eS = reinterpret_cast<long long *>(dyn + FoldCfg<H>::OFF_ES);
+    __shared__ long long bk_s[H][NR], l0_s[H][NR];
+    __shared__ int ns_s[H][NR], sb_s[H][NR];
+    __shared__ unsigned long long quiet_s[H];          // bit u: tile u has no entry for the head
+    __shared__ EntStage<H, NR> st;
+    static_assert(NR == 64 && HMAX <= CHUNK_THREADS / 32, "one warp per head, two tiles per lane");
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // per (head, channel) pair: the running fold
+    int64_t loc[NP], Y[NP], curS[NP], curl[NP], Spre[NP], lpre[NP], lrun[NP];
+    int ne[NP];
+    bool opened[NP];
+#pragma unroll
+    for (int k = 0; k < NP; ++k) {
+        loc[k] = Y[k] = curS[k] = curl[k] = Spre[k] = lpre[k] = lrun[k] = 0;
+        ne[k] = 0;
+        opened[k] = false;
+    }
+    if (w < H && lane == 0) base_sm[w] = -1;
+    const int cbeg = direct ? 0 : blk * GBLK, cend = direct ? nchunks : min(nchunks, blk * GBLK + GBLK);
+    for (int c0 = cbeg; c0 < cend; c0 += GBLK) {
+        const int nt = min(GBLK, cend - c0);
+        // warp h: head h's scalars, tiles lane and lane + 32, and (one block)
+        // the entries the head's block record needs = the rescales in its tiles
+        if (w < H) {
+            int need = 0;
+            unsigned long long qm = 0;
+#pragma unroll
+            for (int i = 0; i < NR / 32; ++i) {
+                const int r = i * 32 + lane, c = c0 + r;
+                int ns = 0, sb = 0;
+                if (c < c0 + nt) {
+                    bk_s[w][r] = ldcg(&recs[c].B[w]);
+                    l0_s[w][r] = ldcg(&recs[c].l0[w]);
+                    ns = ldcg(&recs[c].nseg[w]);
+                    sb = ldcg(&recs[c].seg_base[w]);
+                }
+                ns_s[w][r] = ns;
+                sb_s[w][r] = sb;
+                need += ns;
+                qm |= (unsigned long long)__ballot_sync(FULL, ns == 0) << (32 * i);
+            }
+            need = __reduce_add_sync(FULL, need);
+            if (lane == 0) {
+                quiet_s[w] = qm;
+                if (!direct) {
+                    unsigned b = 0;
+                    if (need) b = atomicAdd(a.seg_top, (unsigned)need);
+                    if (need && b + need > (unsigned)a.seg_cap) {
+                        atomicExch(&a.items[item].fail, 1);
+                        need = 0;
+                    }
+                    base_sm[w] = need ? (int)b : -1;
+                }
+            }
+        }
+        // S0 of every tile, 16 bytes a load: [tile][head][channel]
+        {
+            constexpr int Q = D / 4;                   // 16-byte pieces per (tile, head)
+            const int n16 = nt * H * Q;
+#pragma unroll 4
+            for (int i = threadIdx.x; i < n16; i += blockDim.x) {
+                const int u = i / (H * Q), r = i % (H * Q), h = r / Q, q = r % Q;
+                const int4 x = ldcg(reinterpret_cast<const int4 *>(&recs[c0 + u].S0[h][0]) + q);
+                reinterpret_cast<int4 *>(s0_sm + ((size_t)u * H + h) * D)[q] = x;
+            }
+        }
+        __syncthreads();
+        // the tiles' entries; the block's own entries written below are a
+        // separate allocation, so these read what the values launch wrote
+        stage_entries<H, NR>(a, ns_s, sb_s, nt, st, eS);
+#pragma unroll
+        for (int k = 0; k < NP; ++k) {
+            const int pr = threadIdx.x + k * CHUNK_THREADS;
+            if (pr >= H * D) continue;
+            const int h = pr / D, ch = pr % D;
+            const int eb = base_sm[h];
+            const unsigned long long qm = quiet_s[h];
+            const int32_t *s0h = s0_sm + (size_t)h * D + ch;      // tile u at s0h[u * H * D]
+            int u = 0;
+            while (u < nt) {
+                // four tiles with no rescale for the head: plain translations
+                if (u + 4 <= nt && ((qm >> u) & 15ull) == 15ull) {
+                    int32_t S[4];
+                    long long Bv[4], lv[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        S[j] = s0h[(size_t)(u + j) * H * D];
+                        Bv[j] = bk_s[h][u + j];
+                        lv[j] = l0_s[h][u + j];
+                    }
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int64_t al = loc[k] < 0 ? -loc[k] : loc[k];
+                        Y[k] = max(Y[k], al + (int64_t)Bv[j]);
+                        loc[k] += S[j];
+                        curS[k] += S[j];
+                        curl[k] += lv[j];
+                        lrun[k] += lv[j];
+                    }
+                    u += 4;
+                    continue;
+                }
+                const int32_t S0 = s0h[(size_t)u * H * D];
+                const int64_t al = loc[k] < 0 ? -loc[k] : loc[k];
+                Y[k] = max(Y[k], al + (int64_t)bk_s[h][u]);
+                loc[k] += S0;
+                curS[k] += S0;
+                curl[k] += l0_s[h][u];
+                lrun[k] += l0_s[h][u];
+                const int ns = ns_s[h][u];
+                for (int j = 0; j < ns; ++j) {
+                    int64_t f, sS, sl;
+                    entry_at<H, NR>(a, st, eS, sb_s, h, u, j, ch, f, sS, sl);
+                    if (eb >= 0) {
+                        if (!opened[k]) {
+                            Spre[k] = curS[k];
+                            lpre[k] = curl[k];
+                            opened[k] = true;
+                        } else {
+                            a.segs[eb + ne[k] - 1].S[ch] = curS[k];
+                            if (ch == 0) a.segs[eb + ne[k] - 1].l = curl[k];
+                        }
+                        if (ch == 0) a.segs[eb + ne[k]].f = (int32_t)f;
+                        ++ne[k];
+                    }
+                    curS[k] = sS;
+                    curl[k] = sl;
+                    loc[k] = ((loc[k] * f) >> a.g.prob_frac) + sS;
+                    lrun[k] = ((lrun[k] * f) >> a.g.prob_frac) + sl;
+                }
+                ++u;
+            }
+        }
+        __syncthreads();                  // the stage is reused by the next GBLK tiles
+    }
+    if (direct) {
+        // the item's recurrence from zero: its proof is the walk's Y
+        bool bad = *reinterpret_cast<volatile int32_t *>(&a.items[item].fail) != 0;
+#pragma unroll
+        for (int k = 0; k < NP; ++k) bad |= threadIdx.x + k * CHUNK_THREADS < H * D && Y[k] > INT32_MAX;
+        finalize_item<H>(a, item, a.T[item / a.g.n_kv], (int64_t)item * H * D, loc, lrun, bad, slots);
+        return;
+    }
+#pragma unroll
+    for (int k = 0; k < NP; ++k) {
+        const int pr = threadIdx.x + k * CHUNK_THREADS;
+        if (pr >= H * D) continue;
+        const int h = pr / D, ch = pr % D;
+        const int eb = base_sm[h];
+        if (!opened[k]) {
+            Spre[k] = curS[k];
+            lpre[k] = curl[k];
+        } else if (eb >= 0) {
+            a.segs[eb + ne[k] - 1].S[ch] = curS[k];
+            if (ch == 0) a.segs[eb + ne[k] - 1].l = curl[k];
+        }
+        BlockRec &br = a.blks[(int64_t)item * a.max_blocks + blk];
+        br.Spre[h][ch] = Spre[k];
+        br.Y[h][ch] = Y[k];
+        if (ch == 0) {
+            br.lpre[h] = lpre[k];
+            br.nent[h] = eb >= 0 ? ne[k] : 0;
+            br.ent_base[h] = eb >= 0 ? eb : 0;
+        }
+    }
+}
+
+// Level 2: fold the item's blocks; finalize or mark the item for the exact
+// sequential recomputation. The blocks go 32 at a time: their scalars (one
+// warp per head, one block per lane) and rescale entries into shared memory,
+// each thread's Y and Spre in batches of FB loads issued together.
+template <int H>
+__device__ void merge_item(const ChunkArgs &a, int item, int nblocks, int64_t T,
+                           int64_t qbase, long long *slots /* [NT/32] */, uint8_t *dyn) {
+    constexpr int NP = (H * D + CHUNK_THREADS - 1) / CHUNK_THREADS;   // pairs per thread
+    const int tid = threadIdx.x;
+    const BlockRec *blks = a.blks + (int64_t)item * a.max_blocks;
+    long long *eS = reinterpret_cast<long long *>(dyn + FoldCfg<H>::OFF_ES);
+    __shared__ long long lp_s[H][32];
+    __shared__ int ne_s[H][32], eb_s[H][32];
+    __shared__ EntStage<H, 32> st;
+    int64_t acc[NP], l[NP];
+#pragma unroll
+    for (int k = 0; k < NP; ++k) acc[k] = l[k] = 0;
+    bool bad = *reinterpret_cast<volatile int32_t *>(&a.items[item].fail) != 0;
+    bad = __syncthreads_or(bad);
+    for (int g0 = 0; g0 < nblocks; g0 += 32) {
+        if (bad) break;                    // the same for every thread
+        const int nb = min(32, nblocks - g0);
+        {
+            const int w = tid >> 5, lane = tid & 31;
+            if (w < H) {
+                const int b = g0 + lane;
+                long long lp = 0;
+                int ne = 0, eb = 0;
+                if (lane < nb) {
+                    lp = ldcg(&blks[b].lpre[w]);
+                    ne = ldcg(&blks[b].nent[w]);
+                    eb = ldcg(&blks[b].ent_base[w]);
+                }
+                lp_s[w][lane] = lp;
+                ne_s[w][lane] = ne;
+                eb_s[w][lane] = eb;
+            }
+        }
+        __syncthreads();
+        stage_entries<H, 32>(a, ne_s, eb_s, nb, st, eS);
+#pragma unroll
+        for (int k = 0; k < NP; ++k) {
+            const int pr = tid + k * CHUNK_THREADS;
+            if (pr >= H * D) continue;
+            const int h = pr / D, ch = pr % D;
+            for (int u0 = 0; u0 < nb; u0 += FB) {
+                int64_t Yv[FB], Sv[FB];
+#pragma unroll
+                for (int u = 0; u < FB; ++u) {
+                    if (u0 + u < nb) {
+                        const BlockRec &br = blks[g0 + u0 + u];
+                        Yv[u] = ldcg(&br.Y[h][ch]);
+                        Sv[u] = ldcg(&br.Spre[h][ch]);
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < FB; ++u) {
+                    if (u0 + u >= nb) break;
+                    const int r = u0 + u;
+                    const int64_t aa = acc[k] < 0 ? -acc[k] : acc[k];
+                    if (aa + Yv[u] > INT32_MAX) bad = true;
+                    acc[k] += Sv[u];
+                    l[k] += lp_s[h][r];
+                    const int ne = ne_s[h][r];
+                    for (int j = 0; j < ne; ++j) {
+                        int64_t f, sS, sl;
+                        entry_at<H, 32>(a, st, eS, eb_s, h, r, j, ch, f, sS, sl);
+                        acc[k] = ((acc[k] * f) >> a.g.prob_frac) + sS;
+                        l[k] = ((l[k] * f) >> a.g.prob_frac) + sl;
+                    }
+                }
+            }
+        }
+        // the stage is reused by the next 32 blocks; a failed proof ends the fold
+        bad = __syncthreads_or(bad);
+    }
+    finalize_item<H>(a, item, T, qbase, acc, l, bad, slots);
 }
 
 // A context shard's item: fold its blocks into the item's PartRec instead of
@@ -879,27 +1072,33 @@ __device__ void fold_part(const ChunkArgs &a, int item, int nblocks, int64_t T, 
 // (atomicInc) decides who is last; the last item of the launch empties the
 // segment pool. Called by every thread of the CTA.
 template <int H>
-__device__ __forceinline__ void fold_block_and_item(const ChunkArgs &a, int item, int c) {
+__device__ __forceinline__ void fold_block_and_item(const ChunkArgs &a, int item, int c, uint8_t *dyn) {
     __shared__ int flag_sm;
     __shared__ int base_sm[H];
     __shared__ long long slots[CHUNK_THREADS / 32];
     const int tid = threadIdx.x;
     const int nc = item_chunks(a, item);
     const int blk = c / GBLK, nblk = (nc + GBLK - 1) / GBLK;
+    // a short item (not a context shard) is folded and finalized by the CTA of
+    // its first block, in one pass over its tiles
+    const bool direct = nc <= DIRECT_TILES && !a.parts;
+    if (direct && blk > 0) return;
     __threadfence();
-    merge_block<H>(a, item, blk, nc, base_sm);
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        const unsigned old = atomicInc(&a.item_done[item], (unsigned)(nblk - 1));
-        flag_sm = old == (unsigned)(nblk - 1);
+    merge_block<H>(a, item, blk, nc, base_sm, dyn, direct, slots);
+    if (!direct) {
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) {
+            const unsigned old = atomicInc(&a.item_done[item], (unsigned)(nblk - 1));
+            flag_sm = old == (unsigned)(nblk - 1);
+        }
+        __syncthreads();
+        if (!flag_sm) return;
+        __threadfence();
+        const int64_t T = a.T[item / a.g.n_kv];
+        if (a.parts) fold_part<H>(a, item, nblk, T, slots);
+        else merge_item<H>(a, item, nblk, T, (int64_t)item * H * D, slots, dyn);
     }
-    __syncthreads();
-    if (!flag_sm) return;
-    __threadfence();
-    const int64_t T = a.T[item / a.g.n_kv];
-    if (a.parts) fold_part<H>(a, item, nblk, T, slots);
-    else merge_item<H>(a, item, nblk, T, (int64_t)item * H * D, slots);
     __syncthreads();
     if (tid == 0) {
         ItemAcc &ia = a.items[item];
@@ -962,11 +1161,18 @@ __device__ __forceinline__ long long run_max_at(RunMax<H> &r, const ChunkArgs &a
         }
     }
     const long long *v = a.cmx + (int64_t)nitem * a.max_chunks * 2 * HMAX;
-    for (int j0 = lo; j0 < nc; j0 += 32) {
-        const int j = j0 + lane;
+    // 64 tiles a step, every load of a step issued before any is used
+    for (int j0 = lo; j0 < nc; j0 += 64) {
+        const int ja = j0 + lane, jb = ja + 32;
+        long long x[2][H];
 #pragma unroll
         for (int h = 0; h < H; ++h) {
-            const long long mh = warp_max_score(j < nc ? ldcg(v + (int64_t)j * 2 * HMAX + h) : LLONG_MIN);
+            x[0][h] = ja < nc ? ldcg(v + (int64_t)ja * 2 * HMAX + h) : LLONG_MIN;
+            x[1][h] = jb < nc ? ldcg(v + (int64_t)jb * 2 * HMAX + h) : LLONG_MIN;
+        }
+#pragma unroll
+        for (int h = 0; h < H; ++h) {
+            const long long mh = warp_max_score(x[0][h] > x[1][h] ? x[0][h] : x[1][h]);
             if (lane == h && mh > m) m = mh;
         }
     }
@@ -1639,14 +1845,16 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
     }
 
     // Tiles are dealt round-robin (this CTA's: blockIdx.x + li * gridDim.x); no
-    // tile waits on another. Warp 1 looks them up two ahead, with the running
-    // maximum entering each.
+    // tile waits on another. Warp 1 looks them up two ahead; the last warp
+    // resolves the running maximum entering each one tile ahead, during the
+    // control phase (whose warps are one per head).
+    constexpr int WRM = NT / 32 - 1;
     const int G = gridDim.x;
     const int ntl = (a.n_tiles - (int)blockIdx.x + G - 1) / G;
     TileAhead<PGMAX> ahead(a, tdesc_sm, trb_sm, pages_sm);
     __shared__ RunMax<H> runmax;
+    if (warp == WRM) run_max_init(runmax, lane);
     if (warp == 1) {
-        run_max_init(runmax, lane);
         ahead.load(a, 0, lane);
         ahead.store(0, lane);
         if (ntl > 1) {
@@ -1657,15 +1865,12 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
     // everything above reads only what was written before the scores launch;
     // from here on, the outputs of the launches before this one
     wait_prior_grid();
-    if (warp == 1) {
-        __syncwarp();                            // lane 0 stored the descriptors
-        for (int j = 0; j < 2 && j < ntl; ++j) {
-            const int4 t = tdesc_sm[j];
-            const long long m = run_max_at(runmax, a, t.x, t.y, lane);
-            if (lane < H) min_sm[j][lane] = m;
-        }
-    }
     __syncthreads();
+    if (warp == WRM && ntl > 0) {
+        const int4 t = tdesc_sm[0];
+        const long long m = run_max_at(runmax, a, t.x, t.y, lane);
+        if (lane < H) min_sm[0][lane] = m;
+    }
     for (int li = 0; li < ntl; ++li) {
         const int tile = (int)blockIdx.x + li * G;
         const int4 td = tdesc_sm[li % 3];
@@ -1732,12 +1937,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
         // ---- 2. V codes to channel-major words; warp 1 prefetches this CTA's
         //         next tile into L2 first ------------------------------------------
         if (warp == 1) {
-            if (li + 2 < ntl) {
-                ahead.load(a, li + 2, lane);
-                // slot (li + 2) % 3 last served tile li - 1
-                const long long m = run_max_at(runmax, a, ahead.rtd.x, ahead.rtd.y, lane);
-                if (lane < H) min_sm[(li + 2) % 3][lane] = m;
-            }
+            if (li + 2 < ntl) ahead.load(a, li + 2, lane);
             if (li + 1 < ntl) {
                 const int4 t2 = tdesc_sm[(li + 1) % 3];
                 prefetch_rows(a, t2, pages_sm[(li + 1) & 1], lane, 2);
@@ -1862,6 +2062,13 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
                 nseg_sm[h] = nres;
                 atomicAdd(&resc_sm, (unsigned)nres);
             }
+        }
+        // the running maximum entering the next tile (its descriptor is in
+        // the ring; slot (li + 1) % 3 last served tile li - 2)
+        if (warp == WRM && li + 1 < ntl) {
+            const int4 t = tdesc_sm[(li + 1) % 3];
+            const long long m = run_max_at(runmax, a, t.x, t.y, lane);
+            if (lane < H) min_sm[(li + 1) % 3][lane] = m;
         }
         __syncthreads();
         for (int i = tid; i < CW; i += NT) {
@@ -2113,11 +2320,27 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
 // register allocation (the value loop ran at half speed).
 // ---------------------------------------------------------------------------
 template <int H>
-__global__ void __launch_bounds__(CHUNK_THREADS) k_fold(ChunkArgs a) {
+__global__ void __launch_bounds__(CHUNK_THREADS, 2) k_fold(ChunkArgs a) {
+    extern __shared__ __align__(16) uint8_t dyn[];
     wait_prior_grid();
     const int item = blockIdx.x / a.max_blocks, blk = blockIdx.x % a.max_blocks;
     if (blk * GBLK >= item_chunks(a, item)) return;
-    fold_block_and_item<H>(a, item, blk * GBLK);
+    fold_block_and_item<H>(a, item, blk * GBLK, dyn);
+}
+
+// k_fold's shared memory, granted once per device and head count.
+template <int H>
+inline cudaError_t fold_prepare() {
+    static std::mutex mu;
+    static bool done[64] = {false};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lk(mu);
+    if (done[dev]) return cudaSuccess;
+    const cudaError_t e =
+        cudaFuncSetAttribute(k_fold<H>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)FoldCfg<H>::BYTES);
+    done[dev] = e == cudaSuccess;
+    return e;
 }
 
 // ---------------------------------------------------------------------------
@@ -2199,7 +2422,7 @@ struct ScratchLayout {
         seg = o; o += al(sizeof(SegEntry) * (size_t)sc_cap);
         items = o; o += al(sizeof(ItemAcc) * (size_t)ni);
         redo = o; o += al(sizeof(int32_t) * (size_t)ni);
-        desc = o; o += al(TileDesc(ni).total);
+        desc = o; o += al(TileDesc(ni, ni).total);
         // block maxima and score offsets: the separate-launch scan only
         bmg = o; o += al(sizeof(long long) * (size_t)(rows > 0 ? tc : 1) * H * CW);
         sc = o; o += al(sizeof(uint32_t) * (size_t)(rows > 0 ? rows : 1) * H);
@@ -2274,12 +2497,15 @@ inline int launch_chunk_kernels(ChunkArgs &a, int32_t B, const int32_t *d_seq, c
     const unsigned gv = (unsigned)(gB < a.n_tiles ? gB : a.n_tiles);
     if (launch_after(k_scan_values<H, KB, VB, RS>, gv, (unsigned)CHUNK_THREADS, ChunkCfg<H, KB, VB, RS>::BYTES,
                      s, a) != cudaSuccess ||
-        launch_after(k_fold<H>, (unsigned)(a.n_items * a.max_blocks), (unsigned)CHUNK_THREADS, 0, s, a) !=
-            cudaSuccess)
+        fold_prepare<H>() != cudaSuccess ||
+        launch_after(k_fold<H>, (unsigned)(a.n_items * a.max_blocks), (unsigned)CHUNK_THREADS,
+                     FoldCfg<H>::BYTES, s, a) != cudaSuccess)
         return INS_ECUDA;
     if (cudaGetLastError() != cudaSuccess) return INS_ECUDA;
     // items whose exactness the fold could not prove are recomputed in order
-    return launch_seq<H>(a.g, a.tb, B, d_seq, d_T, a.page_table, a.pool, a.q_rot, a.out, a.stats,
+    (void)d_seq;
+    (void)d_T;
+    return launch_seq<H>(a.g, a.tb, B, a.seq_ids, a.T, a.page_table, a.pool, a.q_rot, a.out, a.stats,
                          a.redo, s) == cudaSuccess
                ? INS_OK
                : INS_ECUDA;
@@ -2292,7 +2518,7 @@ inline int prepare_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, 
                            const int32_t *d_seq, const int64_t *d_T, const int64_t *h_T,
                            const int32_t *d_pt, const uint8_t *pool, const int32_t *q_rot,
                            int64_t *out, ins_stats *stats, int32_t *d_status, ChunkArgs &a,
-                           cudaStream_t s, bool score_rows = true) {
+                           cudaStream_t s, bool score_rows = true, const int32_t *h_seq = nullptr) {
     using CF = ChunkCfg<H, KB, VB, RS>;
     const int n_items = B * g.n_kv;
     TilePlan &tp = cs.plan;
@@ -2303,12 +2529,21 @@ inline int prepare_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, 
     // memory; the single-launch scan keeps them in shared memory
     if (int rc = reserve_scratch(cs, n_items, tp.max_nc, n_tiles, H, CF::CW, score_rows ? tp.rows : 0, s))
         return rc;
-    const TileDesc L(n_items);
+    // no device lengths given: the host's lengths and sequence ids ride in
+    // the tile plan's upload
+    const bool ride = d_T == nullptr;
+    const TileDesc L(n_items, ride ? B : 0);
     {
         int slot = 0;
         uint8_t *h = (uint8_t *)cs.up.take(L.total, slot);
         if (!h) return INS_ECUDA;
         tp.write(h, L);
+        if (ride) {
+            std::memcpy(h + L.lens, h_T, sizeof(int64_t) * (size_t)B);
+            std::memcpy(h + L.seqs, h_seq, sizeof(int32_t) * (size_t)B);
+            d_T = (const int64_t *)(cs.desc + L.lens);
+            d_seq = (const int32_t *)(cs.desc + L.seqs);
+        }
         if (cudaMemcpyAsync(cs.desc, h, L.total, cudaMemcpyHostToDevice, s) != cudaSuccess ||
             cs.up.done(slot, s))
             return INS_ECUDA;
@@ -2354,12 +2589,13 @@ template <int H, int KB, int VB, int RS = 0>
 inline int launch_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, int32_t B,
                           const int32_t *d_seq, const int64_t *d_T, const int64_t *h_T,
                           const int32_t *d_pt, const uint8_t *pool, const int32_t *q_rot,
-                          int64_t *out, ins_stats *stats, int32_t *d_status, cudaStream_t s) {
+                          int64_t *out, ins_stats *stats, int32_t *d_status, cudaStream_t s,
+                          const int32_t *h_seq = nullptr) {
     ChunkArgs a;
     if (int rc = prepare_chunked<H, KB, VB, RS>(cs, g, tb, B, d_seq, d_T, h_T, d_pt, pool, q_rot, out, stats,
-                                            d_status, a, s))
+                                            d_status, a, s, true, h_seq))
         return rc;
-    const int rc = launch_chunk_kernels<H, KB, VB, RS>(a, B, d_seq, d_T, s);
+    const int rc = launch_chunk_kernels<H, KB, VB, RS>(a, B, a.seq_ids, a.T, s);
     // scores, values, fold, exact re-run
     if (rc == INS_OK) cs.launches += 4;
     return rc;
@@ -2389,14 +2625,16 @@ inline int launch_split_part(ChunkArgs &a, cudaStream_t s) {
     m.maxima = nullptr;
     k_scan_values<H, KB, VB, RS>
         <<<gB < m.n_tiles ? gB : m.n_tiles, CHUNK_THREADS, ChunkCfg<H, KB, VB, RS>::BYTES, s>>>(m);
-    k_fold<H><<<m.n_items * m.max_blocks, CHUNK_THREADS, 0, s>>>(m);
+    if (fold_prepare<H>() != cudaSuccess) return INS_ECUDA;
+    k_fold<H><<<m.n_items * m.max_blocks, CHUNK_THREADS, FoldCfg<H>::BYTES, s>>>(m);
     return cudaGetLastError() == cudaSuccess ? INS_OK : INS_ECUDA;
 }
 
 // Tile size. Tiles of C rows (4 rows per thread where the shape allows) keep
 // the per-tile work small against the rows; but a batch of short items cuts
 // into few tiles and leaves SMs idle. When the default tiles would not fill
-// two waves of the values launch, tiles of half the rows are used instead.
+// half a wave of the values launch, tiles of half the rows are used instead
+// (up to a wave, fewer and larger tiles also make the fold shorter).
 enum : int32_t { TILES_AUTO = 0, TILES_LARGE = 1, TILES_SMALL = 2 };
 // Online scan kernels: one persistent launch (scan_fused.cuh) or the separate
 // score, prefix, value and fold launches of this file.
@@ -2412,7 +2650,7 @@ inline bool small_tiles(const ChunkScratch &cs, const Geo &g, int32_t B, const i
         int64_t tiles = 0;
         for (int32_t b = 0; b < B; ++b) tiles += h_T[b] ? (h_T[b] + C - 1) / C : 1;
         const int slots = chunk_slots<H, KB, VB, 1>();
-        return slots > 0 && tiles * g.n_kv < 2 * (int64_t)slots;
+        return slots > 0 && 2 * tiles * g.n_kv < (int64_t)slots;
     }
 }
 

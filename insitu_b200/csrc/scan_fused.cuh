@@ -820,10 +820,13 @@ inline int launch_fused_kernels(ChunkArgs &a, const FusedExtra &x, int32_t B, co
     const unsigned grid = (unsigned)(G < a.n_tiles ? G : a.n_tiles);
     if (launch_after(k_scan_fused<H, KB, VB, RS>, grid, (unsigned)CHUNK_THREADS,
                      FusedCfg<H, KB, VB, RS>::BYTES, s, a, x) != cudaSuccess ||
-        launch_after(k_fold<H>, (unsigned)(a.n_items * a.max_blocks), (unsigned)CHUNK_THREADS, 0, s, a) !=
-            cudaSuccess)
+        fold_prepare<H>() != cudaSuccess ||
+        launch_after(k_fold<H>, (unsigned)(a.n_items * a.max_blocks), (unsigned)CHUNK_THREADS,
+                     FoldCfg<H>::BYTES, s, a) != cudaSuccess)
         return INS_ECUDA;
-    return launch_seq<H>(a.g, a.tb, B, d_seq, d_T, a.page_table, a.pool, a.q_rot, a.out, a.stats,
+    (void)d_seq;
+    (void)d_T;
+    return launch_seq<H>(a.g, a.tb, B, a.seq_ids, a.T, a.page_table, a.pool, a.q_rot, a.out, a.stats,
                          a.redo, s) == cudaSuccess
                ? INS_OK
                : INS_ECUDA;
@@ -833,13 +836,14 @@ template <int H, int KB, int VB, int RS = 0>
 inline int launch_online_tiles(ChunkScratch &cs, const Geo &g, const DevTables *tb, int32_t B,
                                const int32_t *d_seq, const int64_t *d_T, const int64_t *h_T,
                                const int32_t *d_pt, const uint8_t *pool, const int32_t *q_rot,
-                               int64_t *out, ins_stats *stats, int32_t *d_status, cudaStream_t s) {
+                               int64_t *out, ins_stats *stats, int32_t *d_status, cudaStream_t s,
+                               const int32_t *h_seq) {
     if (cs.scan_kernel == SCAN_SPLIT)
         return launch_chunked<H, KB, VB, RS>(cs, g, tb, B, d_seq, d_T, h_T, d_pt, pool, q_rot, out, stats,
-                                             d_status, s);
+                                             d_status, s, h_seq);
     ChunkArgs a;
     if (int rc = prepare_chunked<H, KB, VB, RS>(cs, g, tb, B, d_seq, d_T, h_T, d_pt, pool, q_rot, out, stats,
-                                                d_status, a, s, false))
+                                                d_status, a, s, false, h_seq))
         return rc;
     if (int rc = next_epoch(cs, s)) return rc;
     FusedExtra x;
@@ -849,7 +853,7 @@ inline int launch_online_tiles(ChunkScratch &cs, const Geo &g, const DevTables *
     x.hold_word = cs.hold_item < 0 || cs.hold_item >= a.n_items || cs.hold_chunk >= a.max_chunks
                       ? -1
                       : ((int64_t)cs.hold_item * a.max_chunks + cs.hold_chunk) * H + cs.hold_head;
-    const int rc = launch_fused_kernels<H, KB, VB, RS>(a, x, B, d_seq, d_T, s);
+    const int rc = launch_fused_kernels<H, KB, VB, RS>(a, x, B, a.seq_ids, a.T, s);
     if (rc == INS_OK) cs.launches += 3;          // the scan, the fold, the exact re-run
     return rc;
 }
@@ -858,23 +862,24 @@ template <int H, int KB, int VB>
 inline int launch_chunked_auto(ChunkScratch &cs, const Geo &g, const DevTables *tb, int32_t B,
                                const int32_t *d_seq, const int64_t *d_T, const int64_t *h_T,
                                const int32_t *d_pt, const uint8_t *pool, const int32_t *q_rot,
-                               int64_t *out, ins_stats *stats, int32_t *d_status, cudaStream_t s) {
+                               int64_t *out, ins_stats *stats, int32_t *d_status, cudaStream_t s,
+                               const int32_t *h_seq) {
     if constexpr (ChunkCfg<H, KB, VB>::R == 4)
         if (small_tiles<H, KB, VB>(cs, g, B, h_T))
             return launch_online_tiles<H, KB, VB, 2>(cs, g, tb, B, d_seq, d_T, h_T, d_pt, pool, q_rot, out,
-                                                     stats, d_status, s);
+                                                     stats, d_status, s, h_seq);
     return launch_online_tiles<H, KB, VB>(cs, g, tb, B, d_seq, d_T, h_T, d_pt, pool, q_rot, out, stats,
-                                          d_status, s);
+                                          d_status, s, h_seq);
 }
 
 inline int launch_online(ChunkScratch &cs, const Geo &g, const DevTables *tb, int32_t B,
                          const int32_t *d_seq, const int64_t *d_lens, const int64_t *h_lens,
                          const int32_t *d_pt, const uint8_t *pool, const int32_t *q_rot,
                          int64_t *out, ins_stats *stats, int32_t *d_status, int H,
-                         cudaStream_t s) {
+                         cudaStream_t s, const int32_t *h_seq = nullptr) {
 #define INS_CH(HH, KK, VV)                                                                      \
     return launch_chunked_auto<HH, KK, VV>(cs, g, tb, B, d_seq, d_lens, h_lens, d_pt, pool, q_rot, \
-                                           out, stats, d_status, s)
+                                           out, stats, d_status, s, h_seq)
     if (is_def_fmt(g) && g.kb == 4 && g.vb == 2) {
         switch (H) {
             case 1: INS_CH(1, 4, 2);
