@@ -101,8 +101,10 @@ def peaks():
 
 
 def traffic_per_row():
-    """DRAM bytes per scanned row of the scan kernel, from the committed ncu summary."""
-    path = os.path.join(ROOT, "profiles", "scan_ctx1m_traffic.txt")
+    """DRAM bytes per scanned row of the scan's kernels, from the committed ncu
+    summary (one launch of each kernel at 512K tokens; traffic grows with the
+    rows)."""
+    path = os.path.join(ROOT, "profiles", "scan_ctx512k_dram.txt")
     try:
         for ln in open(path):
             if ln.startswith("dram_bytes_per_row:"):
