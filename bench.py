@@ -350,8 +350,8 @@ def run_ours(args):
             "e2e": {"value": round(tot_e2e / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "us_per_step": round(e2e_ms / K * 1e3, 2)},
-            # counted by the library over the timed steps: ingress, scores,
-            # values, fold, exact re-run
+            # counted by the library over the timed steps: two small uploads,
+            # ingress, scores, values, fold, exact re-run
             "gpu_launches": launches,
             # (sequence, KV head) items of the timed scans that the exact
             # sequential kernel recomputed (0: every item took the fast path)

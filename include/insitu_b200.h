@@ -166,8 +166,10 @@ int64_t ins_cache_capacity(const ins_cache *cache);
  * ins_ingress_lanes, ins_seam, ins_seam_device_positions and ins_scan (a
  * running count, for a caller that reports what ran). The online scan is 4
  * launches with the separate kernels (scores, values, fold, exact re-run)
- * and 3 with the fused kernel (the scan, the fold, the exact re-run). No
- * reference counterpart. -1 for NULL. */
+ * and 3 with the fused kernel (the scan, the fold, the exact re-run), plus
+ * one for its small host->device upload (a kernel whose parameter carries
+ * the bytes); an ingress is 2 (its upload, the ingress). No reference
+ * counterpart. -1 for NULL. */
 int64_t ins_cache_launches(const ins_cache *cache);
 
 /* Flags of ins_ingress. */

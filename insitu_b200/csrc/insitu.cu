@@ -69,6 +69,7 @@ struct Staging {
     int cur = NSLOT - 1;
     void *h = nullptr;                  // the current slot's buffers
     void *d = nullptr;
+    int64_t *launches = nullptr;        // the cache's kernel count (an upload may be a launch)
 
     int reserve(size_t bytes) {
         cur = (cur + 1) % NSLOT;
@@ -96,7 +97,9 @@ struct Staging {
         return INS_OK;
     }
     int upload(size_t bytes, cudaStream_t s) {
-        CK(cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, s));
+        int launched = 0;
+        CK(small_upload(d, h, bytes, s, &launched));
+        if (launched && launches) *launches += 1;
         CK(cudaEventRecord(ring[cur].done, s));
         return INS_OK;
     }
@@ -399,6 +402,7 @@ int ins_cache_create(const ins_config *cfg, const ins_tables *tb, int32_t device
     if (cudaEventCreateWithFlags(&c->mirror_done, cudaEventDisableTiming) != cudaSuccess)
         return cleanup(fail(INS_ECUDA, "event creation failed"));
     c->chunk.redo_total = c->d_redo_total;
+    c->stage_a.launches = c->stage_b.launches = c->stage_c.launches = &c->chunk.launches;
     std::memset(c->h_page_table, 0xff, sizeof(int32_t) * pt);
     std::memset(c->h_seq_lens, 0, sizeof(int32_t) * cfg->max_seqs);
     c->free_pages.reserve((size_t)cfg->n_pages);
@@ -511,12 +515,9 @@ static int ingress_launch(ins_cache *c, int32_t n, const int32_t *seq_ids, const
     const int64_t warps = (int64_t)n * per_tok;
     const int wpb = 8;
     const int64_t blocks = (warps + wpb - 1) / wpb;
-    k_ingress<<<(unsigned)blocks, wpb * 32, 0, s>>>(c->g, c->d_tables, n,
-                                                    (const int64_t *)c->stage_a.d, q, k, v, q_rot,
-                                                    c->d_pool, flags, c->d_status,
-                                                    (const int2 *)((const int64_t *)c->stage_a.d + n), n_new,
-                                                    c->d_page_table, lanes);
-    CK(cudaGetLastError());
+    CK(launch_after(k_ingress, (unsigned)blocks, (unsigned)(wpb * 32), 0, s, c->g, (const DevTables *)c->d_tables,
+                    n, (const int64_t *)c->stage_a.d, q, k, v, q_rot, c->d_pool, flags, c->d_status,
+                    (const int2 *)((const int64_t *)c->stage_a.d + n), n_new, c->d_page_table, lanes));
     c->chunk.launches += 1;
     return INS_OK;
 }

@@ -70,6 +70,7 @@ __global__ void k_ingress(Geo g, const DevTables *__restrict__ tb, int32_t n,
                           int32_t *__restrict__ page_table, const uint8_t *__restrict__ lanes) {
     __shared__ uint8_t codes_sm[8][D];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    wait_prior_grid();   // launched to overlap the kernel before, which may still read the pool
     // the pages these tokens opened, (page-table index, page): the scans that
     // follow on the stream read them (nothing in this launch does)
     {

@@ -1416,6 +1416,8 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
 
     const Geo &g = a.g;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // the tile plan and the queries come from the launches before this one
+    wait_prior_grid();
     for (int i = tid; i < (1 << (2 * KB)) * 8; i += NT) {
         const int e = i >> 3;
         ctab[i] = make_double2(a.tb->k_cent_f64[e & ((1 << KB) - 1)], a.tb->k_cent_f64[e >> KB]);
@@ -2363,24 +2365,6 @@ inline cudaError_t launch_seq(const Geo &g, const DevTables *tb, int32_t B, cons
                         d_pt, pool, q_rot, out, stats, only);
 }
 
-// Launches `kernel` so that it may start while the previous kernel on the
-// stream finishes (programmatic stream serialization); the kernel calls
-// wait_prior_grid() before it reads that kernel's results.
-template <typename... KArgs, typename... Args>
-inline cudaError_t launch_after(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem,
-                                cudaStream_t s, Args &&...args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(block);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
-}
 
 // Resident CTAs of the scores (WHICH 0) or values (WHICH 1) kernel on the
 // current device: the launch grid. The dynamic-smem attribute and the
@@ -2491,11 +2475,13 @@ inline int launch_chunk_kernels(ChunkArgs &a, int32_t B, const int32_t *d_seq, c
                                 cudaStream_t s) {
     const int gA = chunk_slots<H, KB, VB, 0, RS>(), gB = chunk_slots<H, KB, VB, 1, RS>();
     if (gA < 0 || gB < 0) return INS_ECUDA;
-    k_scan_scores<H, KB, VB, RS><<<gA < a.n_tiles ? gA : a.n_tiles, CHUNK_THREADS, ScoreCfg<H, KB, VB, RS>::BYTES, s>>>(a);
-    // the values may start while the scores finish (they wait for them before
-    // reading their results)
+    // each launch may start while the one before finishes (it waits for it
+    // before reading its results)
+    const unsigned gs = (unsigned)(gA < a.n_tiles ? gA : a.n_tiles);
     const unsigned gv = (unsigned)(gB < a.n_tiles ? gB : a.n_tiles);
-    if (launch_after(k_scan_values<H, KB, VB, RS>, gv, (unsigned)CHUNK_THREADS, ChunkCfg<H, KB, VB, RS>::BYTES,
+    if (launch_after(k_scan_scores<H, KB, VB, RS>, gs, (unsigned)CHUNK_THREADS, ScoreCfg<H, KB, VB, RS>::BYTES,
+                     s, a) != cudaSuccess ||
+        launch_after(k_scan_values<H, KB, VB, RS>, gv, (unsigned)CHUNK_THREADS, ChunkCfg<H, KB, VB, RS>::BYTES,
                      s, a) != cudaSuccess ||
         fold_prepare<H>() != cudaSuccess ||
         launch_after(k_fold<H>, (unsigned)(a.n_items * a.max_blocks), (unsigned)CHUNK_THREADS,
@@ -2544,9 +2530,10 @@ inline int prepare_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, 
             d_T = (const int64_t *)(cs.desc + L.lens);
             d_seq = (const int32_t *)(cs.desc + L.seqs);
         }
-        if (cudaMemcpyAsync(cs.desc, h, L.total, cudaMemcpyHostToDevice, s) != cudaSuccess ||
-            cs.up.done(slot, s))
+        int launched = 0;
+        if (small_upload(cs.desc, h, L.total, s, &launched) != cudaSuccess || cs.up.done(slot, s))
             return INS_ECUDA;
+        cs.launches += launched;
     }
     a = ChunkArgs{};
     a.g = g;

@@ -1,9 +1,10 @@
 """The library's own count of the kernels it launched (ins_cache_launches),
-which bench.py reports as gpu_launches: one ingress per step, then the online
-scan -- 3 launches with the single-launch kernel (the scan, the fold and the
+which bench.py reports as gpu_launches: per step the upload of the ingress's
+slots and the ingress (2), then the online scan -- the upload of its tile
+plan and 3 launches with the single-launch kernel (the scan, the fold and the
 exact re-run of unproven items), or 4 with the separate launches (scores,
 values, fold, exact re-run), whether or not an item's tiles fit one fold
-block."""
+block. The small uploads are kernels whose parameter carries the bytes."""
 
 from __future__ import annotations
 
@@ -18,8 +19,8 @@ def _wire(rng, shape, scale=1.0):
     return np.clip(x, -(1 << 23), (1 << 23) - 1).astype(np.int32)
 
 
-@pytest.mark.parametrize("T,kernel,per_step", [(4096, "fused", 4), (48 * 1024, "fused", 4),
-                                               (4096, "split", 5), (48 * 1024, "split", 5)])
+@pytest.mark.parametrize("T,kernel,per_step", [(4096, "fused", 6), (48 * 1024, "fused", 6),
+                                               (4096, "split", 7), (48 * 1024, "split", 7)])
 def test_launches_per_decode_step(T, kernel, per_step):
     pytest.importorskip("torch")
     from insitu_b200 import DecodeAttention, FixedFormat, Geometry, QuantConfig
