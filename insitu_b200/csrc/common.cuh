@@ -95,31 +95,39 @@ inline cudaError_t launch_after(void (*kernel)(KArgs...), unsigned grid, unsigne
 // (__grid_constant__): up to PARAM_UPLOAD_MAX bytes, the destination 4-byte
 // aligned with room for the bytes rounded up to 4.
 constexpr int PARAM_UPLOAD_MAX = 3840;
+template <int N>
 struct ParamBlob {
     uint32_t words;
     uint32_t pad;
-    uint32_t w[PARAM_UPLOAD_MAX / 4];
+    uint32_t w[N / 4];
 };
 
-__global__ void __launch_bounds__(256) k_upload(uint32_t *__restrict__ dst, const __grid_constant__ ParamBlob b) {
+template <int N>
+__global__ void __launch_bounds__(256) k_upload(uint32_t *__restrict__ dst, const __grid_constant__ ParamBlob<N> b) {
     wait_prior_grid();                   // the kernel before may still read dst
     for (uint32_t i = threadIdx.x; i < b.words; i += blockDim.x) dst[i] = b.w[i];
 }
 
+template <int N>
+inline cudaError_t param_upload(void *dst, const void *src, size_t bytes, cudaStream_t s) {
+    ParamBlob<N> b;
+    b.words = (uint32_t)((bytes + 3) / 4);
+    b.pad = 0;
+    b.w[b.words - 1] = 0;
+    std::memcpy(b.w, src, bytes);
+    return launch_after(k_upload<N>, 1u, 256u, 0, s, reinterpret_cast<uint32_t *>(dst), b);
+}
+
 // Upload `bytes` from host memory to `dst` on `s`: as k_upload's parameter
-// when it fits (*launched = 1), else by a copy from `src` (which must then
-// stay unchanged until the copy has run).
+// when it fits (*launched = 1; a parameter of 256 bytes or of the maximum,
+// whichever holds it), else by a copy from `src` (which must then stay
+// unchanged until the copy has run).
 inline cudaError_t small_upload(void *dst, const void *src, size_t bytes, cudaStream_t s, int *launched) {
     *launched = 0;
     if (bytes == 0) return cudaSuccess;
     if (bytes <= (size_t)PARAM_UPLOAD_MAX) {
-        ParamBlob b;
-        b.words = (uint32_t)((bytes + 3) / 4);
-        b.pad = 0;
-        b.w[b.words - 1] = 0;
-        std::memcpy(b.w, src, bytes);
         *launched = 1;
-        return launch_after(k_upload, 1u, 256u, 0, s, reinterpret_cast<uint32_t *>(dst), b);
+        return bytes <= 256 ? param_upload<256>(dst, src, bytes, s) : param_upload<PARAM_UPLOAD_MAX>(dst, src, bytes, s);
     }
     return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, s);
 }
