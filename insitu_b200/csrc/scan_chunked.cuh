@@ -433,7 +433,10 @@ struct ChunkCfg {
     static constexpr size_t OFF_BCAR = OFF_BMAX + (size_t)H * CW * 8;            // int64 [H][CW]
     static constexpr size_t OFF_DB = OFF_BCAR + (size_t)H * CW * 8;              // int64 [H][CW]
     static constexpr size_t OFF_S0 = OFF_DB + (size_t)H * CW * 8;                // int32 [H][64]
-    static constexpr size_t BYTES = OFF_S0 + (size_t)H * D * 4;
+    // the next tile's V rows and norm words, staged by bulk copies
+    static constexpr size_t OFF_VB = (OFF_S0 + (size_t)H * D * 4 + 15) & ~(size_t)15;
+    static constexpr size_t OFF_NB = OFF_VB + (size_t)C * VW * 4;
+    static constexpr size_t BYTES = OFF_NB + (size_t)C * 4 + 16;
     static_assert(C % 32 == 0 && SUBT % 32 == 0 && (UNITS * H) % 32 == 0, "tile shape");
     static_assert(H == 1 || (USTR % 2 == 0 && TAB_WORDS % 2 == 0), "8-byte entries stay aligned");
     static_assert(CW <= 32, "the control phase gives one lane to each 32-row block");
@@ -1820,9 +1823,13 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
     __shared__ int4 tdesc_sm[3];
     __shared__ long long trb_sm[3];
     __shared__ int32_t pages_sm[2][PGMAX];
+    __shared__ __align__(8) uint64_t vbar;             // the staged V rows of the next tile
+    __shared__ int vlost_sm;                            // a wait on them gave up
 
     const Geo &g = a.g;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint8_t *vbuf = dyn + CF::OFF_VB;
+    const uint8_t *nbuf = dyn + CF::OFF_NB;
     // a score's offset below its block maximum, later w = v_norm * p (as int32)
     uint32_t *d_sm = reinterpret_cast<uint32_t *>(dyn + CF::OFF_S);
     uint32_t *tw = reinterpret_cast<uint32_t *>(dyn + CF::OFF_TW);
@@ -1866,34 +1873,62 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
     }
     // everything above reads only what was written before the scores launch;
     // from here on, the outputs of the launches before this one
+    // The V plane and norm words of local tile j come into shared memory by
+    // bulk copies (cp.async.bulk, no tensor map, no multicast) issued by one
+    // thread once the tile before has taken its rows out of the buffer, so
+    // they land while that tile computes. Page boundaries fall on multiples
+    // of 16 rows of a tile, so every range starts 16-byte aligned; a range
+    // rounded up to 16 bytes stays inside its plane and the buffer.
+    auto up16 = [](int x) { return (uint32_t)((x + 15) & ~15); };
+    auto stage_rows = [&](int j) {
+        const int4 t = tdesc_sm[j % 3];
+        const int nn = t.w, kv = t.x % g.n_kv, po = (int)(t.z % g.P);
+        const int npg = nn ? (po + nn + g.P - 1) / g.P : 0;
+        uint32_t bytes = 0;
+        for (int i = 0; i < npg; ++i) {
+            const int r0 = i == 0 ? po : 0, r1 = min(g.P, po + nn - i * g.P);
+            bytes += up16((r1 - r0) * VW * 4) + up16((r1 - r0) * 4);
+        }
+        mbar_arrive_tx(&vbar, bytes);
+        for (int i = 0; i < npg; ++i) {
+            const int r0 = i == 0 ? po : 0, r1 = min(g.P, po + nn - i * g.P);
+            const int row = i * g.P - po + r0;
+            const uint8_t *reg = a.pool + region_off(g, pages_sm[j & 1][i], kv);
+            bulk_g2s(dyn + CF::OFF_VB + (size_t)row * VW * 4, reg + vplane_off(g) + (int64_t)r0 * VW * 4,
+                     up16((r1 - r0) * VW * 4), &vbar);
+            bulk_g2s(dyn + CF::OFF_NB + (size_t)row * 4, reg + nplane_off(g) + (int64_t)r0 * 4, up16((r1 - r0) * 4),
+                     &vbar);
+        }
+    };
     wait_prior_grid();
+    if (tid == 0) {
+        mbar_init(&vbar, 1);
+        mbar_fence_init();
+        vlost_sm = 0;
+    }
     __syncthreads();
+    if (tid == 0 && ntl > 0) stage_rows(0);
     if (warp == WRM && ntl > 0) {
         const int4 t = tdesc_sm[0];
         const long long m = run_max_at(runmax, a, t.x, t.y, lane);
         if (lane < H) min_sm[0][lane] = m;
     }
+    int lost_at = -1;                             // the tile whose wait gave up
     for (int li = 0; li < ntl; ++li) {
         const int tile = (int)blockIdx.x + li * G;
         const int4 td = tdesc_sm[li % 3];
         const int item = td.x, c = td.y;
         const int64_t t0 = td.z;
         const int n = td.w;
-        const int kvh = item % g.n_kv;
         const int rec_idx = item * a.max_chunks + c;
-        const int poff = (int)(t0 % g.P);
         const uint32_t *sc = a.sc + (trb_sm[li % 3] + t0) * H;
 
-        // ---- 0. the tile's rows (each thread its own, first), per-tile setup ----
-        const int32_t *ptab = pages_sm[li & 1];
-        uint32_t vw[R][VW], nw[R], off[R][H];
+        // ---- 0. the tile's score offsets (each thread its own rows), setup -------
+        uint32_t off[R][H];
 #pragma unroll
         for (int r = 0; r < R; ++r) {
             const int row = r * NT + tid;
             if (row < n) {
-                int pi, lr;
-                page_row(g, poff + row, pi, lr);
-                load_vrow<VB>(g, a.pool + region_off(g, ptab[pi], kvh), lr, vw[r], nw[r]);
                 const uint32_t *src = sc + (int64_t)row * H;
                 if constexpr (H == 8) {
                     const uint4 x = __ldg(reinterpret_cast<const uint4 *>(src));
@@ -1923,26 +1958,48 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
         __syncthreads();
 
         // ---- 1. V codes, v norms and scores to shared memory ---------------------
+        // (the staged rows first: a wait that gives up reports a timeout, the
+        // launch's results are then void, and no copy is issued after it)
+        if (!vlost_sm && !mbar_wait(&vbar, (uint32_t)li & 1u)) {
+            lost_at = li;
+            if (tid == 0) atomicOr(a.status, ST_TIMEOUT);
+        }
 #pragma unroll
         for (int r = 0; r < R; ++r) {
             const int row = r * NT + tid;
             if (row < n) {
-                vn_sm[row] = (int32_t)(int16_t)(nw[r] >> 16);
+                const uint32_t *vr = reinterpret_cast<const uint32_t *>(vbuf + (size_t)row * VW * 4);
+                uint32_t vw[VW];
+                if constexpr (VB == 2) {
+                    const uint4 x = *reinterpret_cast<const uint4 *>(vr);
+                    vw[0] = x.x; vw[1] = x.y; vw[2] = x.z; vw[3] = x.w;
+                } else {
 #pragma unroll
-                for (int w = 0; w < VW; ++w) vt[w * VS + row + (row >> 4)] = vw[r][w];
+                    for (int i = 0; i < VW / 2; ++i) {
+                        const uint2 x = reinterpret_cast<const uint2 *>(vr)[i];
+                        vw[2 * i] = x.x;
+                        vw[2 * i + 1] = x.y;
+                    }
+                }
+                const uint32_t nw = *reinterpret_cast<const uint32_t *>(nbuf + (size_t)row * 4);
+                vn_sm[row] = (int32_t)(int16_t)(nw >> 16);
+#pragma unroll
+                for (int w = 0; w < VW; ++w) vt[w * VS + row + (row >> 4)] = vw[w];
 #pragma unroll
                 for (int h = 0; h < H; ++h) d_sm[h * C + row] = off[r][h];
             }
         }
+        if (lost_at >= 0) vlost_sm = 1;
         __syncthreads();
+        // the buffer is free: the next tile's rows
+        if (tid == 0 && li + 1 < ntl && !vlost_sm) stage_rows(li + 1);
 
-        // ---- 2. V codes to channel-major words; warp 1 prefetches this CTA's
-        //         next tile into L2 first ------------------------------------------
+        // ---- 2. V codes to channel-major words; warp 1 looks up the tile after
+        //         next and prefetches the next tile's score offsets into L2 -----
         if (warp == 1) {
             if (li + 2 < ntl) ahead.load(a, li + 2, lane);
             if (li + 1 < ntl) {
                 const int4 t2 = tdesc_sm[(li + 1) % 3];
-                prefetch_rows(a, t2, pages_sm[(li + 1) & 1], lane, 2);
                 const uint32_t bytes = (uint32_t)t2.w * H * 4;
                 if (lane == 0 && bytes)
                     prefetch_l2(a.sc + (trb_sm[(li + 1) % 3] + t2.z) * H, (bytes + 15) & ~15u);
@@ -2311,6 +2368,8 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
         if (warp == 1 && li + 2 < ntl) ahead.store(li + 2, lane);
         __syncthreads();                 // the next tile reuses shared memory
     }
+    // copies whose wait gave up must land before the CTA's shared memory goes
+    if (lost_at >= 0) mbar_wait(&vbar, (uint32_t)lost_at & 1u);
 }
 
 // ---------------------------------------------------------------------------
