@@ -145,14 +145,18 @@ int ins_cache_set_tiles(ins_cache *cache, int32_t mode);
 enum { INS_SCAN_FUSED = 0, INS_SCAN_SPLIT = 1 };
 int ins_cache_set_scan_kernel(ins_cache *cache, int32_t mode);
 
-/* A test of the fused scan's failure path, with no reference counterpart and
- * no use outside tests: every look-back wait gives up after `poll_limit`
- * polls (default 2^22, about a second), and the word that tile `chunk` of
- * item `item` (sequence b, KV head h: item b * n_kv + h, in the order of the
- * scan's seq_ids) publishes for query head `head` is withheld, so the tiles
- * after it wait for a word nothing writes. Their waits give up, the launch
- * still finishes, and ins_cache_status returns INS_ETIMEOUT; no GPU fault is
- * involved. item < 0 withholds nothing. */
+/* A test of the scans' failure path, with no reference counterpart and no
+ * use outside tests: every bounded wait of the online scan's look-back (fused
+ * kernel) and of its value pass's staged rows (separate launches) gives up
+ * after `poll_limit` polls (default 2^22, about a second), and tile `chunk`
+ * of item `item` (sequence b, KV head h: item b * n_kv + h, in the order of
+ * the scan's seq_ids) is held back: with the fused kernel the word it
+ * publishes for query head `head` is withheld, so the tiles after it wait
+ * for a word nothing writes; with the separate launches the bytes of its
+ * staged rows are announced 16 larger than the copies that land, so its own
+ * wait cannot complete. The waits give up, the launch still finishes, and
+ * ins_cache_status returns INS_ETIMEOUT; no GPU fault is involved. item < 0
+ * holds nothing back. */
 int ins_cache_set_wait_test(ins_cache *cache, int32_t poll_limit, int32_t item, int32_t chunk,
                             int32_t head);
 

@@ -1264,6 +1264,8 @@ int noalloc_chunked(ins_cache *c, int32_t B, const int32_t *q_rot, int64_t *out,
     x.lbw = (unsigned long long *)(p + L.lbw);
     a.item_done = (unsigned int *)(p + L.idone);
     a.scan_done = (unsigned int *)(p + L.sdone);
+    a.poll_limit = c->chunk.poll_limit;
+    a.hold_rec = -1;
     x.epoch = 1;
     x.poll_limit = c->chunk.poll_limit;
     x.hold_word = -1;

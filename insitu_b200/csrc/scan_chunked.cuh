@@ -188,6 +188,11 @@ struct ChunkArgs {
     // counters of the fold launch that reset themselves on the last arrival
     unsigned int *item_done;      // [n_items] blocks folded into each item so far
     unsigned int *scan_done;      // items finished in this launch
+    // the test of the bounded waits: polls before a wait gives up, and the
+    // tile (item * max_chunks + chunk) whose staged rows are announced 16
+    // bytes larger than the copies that land (its wait cannot complete), or -1
+    int32_t poll_limit;
+    int64_t hold_rec;
 };
 
 // Chunks of an item: one per tile_rows rows, and one (empty) for an empty item.
@@ -1278,9 +1283,9 @@ __device__ __forceinline__ void mbar_arrive_tx(uint64_t *bar, uint32_t bytes) {
 }
 // Waits for phase `parity` of the barrier to complete; gives up (false) after
 // a bounded number of polls, each of which the hardware may suspend briefly.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int limit = 1 << 22) {
     const uint32_t addr = smem_addr(bar);
-    for (int it = 0; it < (1 << 22); ++it) {
+    for (int it = 0; it < limit; ++it) {
         uint32_t done;
         asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
                      : "=r"(done) : "r"(addr), "r"(parity) : "memory");
@@ -1889,6 +1894,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
             const int r0 = i == 0 ? po : 0, r1 = min(g.P, po + nn - i * g.P);
             bytes += up16((r1 - r0) * VW * 4) + up16((r1 - r0) * 4);
         }
+        if ((int64_t)t.x * a.max_chunks + t.y == a.hold_rec) bytes += 16;   // the wait test
         mbar_arrive_tx(&vbar, bytes);
         for (int i = 0; i < npg; ++i) {
             const int r0 = i == 0 ? po : 0, r1 = min(g.P, po + nn - i * g.P);
@@ -1960,7 +1966,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
         // ---- 1. V codes, v norms and scores to shared memory ---------------------
         // (the staged rows first: a wait that gives up reports a timeout, the
         // launch's results are then void, and no copy is issued after it)
-        if (!vlost_sm && !mbar_wait(&vbar, (uint32_t)li & 1u)) {
+        if (!vlost_sm && !mbar_wait(&vbar, (uint32_t)li & 1u, a.poll_limit)) {
             lost_at = li;
             if (tid == 0) atomicOr(a.status, ST_TIMEOUT);
         }
@@ -2369,7 +2375,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
         __syncthreads();                 // the next tile reuses shared memory
     }
     // copies whose wait gave up must land before the CTA's shared memory goes
-    if (lost_at >= 0) mbar_wait(&vbar, (uint32_t)lost_at & 1u);
+    if (lost_at >= 0) mbar_wait(&vbar, (uint32_t)lost_at & 1u, a.poll_limit);
 }
 
 // ---------------------------------------------------------------------------
@@ -2627,6 +2633,10 @@ inline int prepare_chunked(ChunkScratch &cs, const Geo &g, const DevTables *tb, 
     a.status = d_status;
     a.item_done = cs.idone;
     a.scan_done = cs.sdone;
+    a.poll_limit = cs.poll_limit;
+    a.hold_rec = cs.hold_item < 0 || cs.hold_item >= n_items || cs.hold_chunk >= cs.max_chunks
+                     ? -1
+                     : (int64_t)cs.hold_item * cs.max_chunks + cs.hold_chunk;
     cs.last_items = n_items;
     return INS_OK;
 }

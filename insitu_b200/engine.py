@@ -159,7 +159,8 @@ class PagedCache:
 
     def set_wait_test(self, poll_limit: int = 1 << 22, item: int = -1, chunk: int = 0,
                       head: int = 0) -> None:
-        """Test hook of the fused scan's bounded waits (ins_cache_set_wait_test)."""
+        """Test hook of the online scan's bounded waits (ins_cache_set_wait_test):
+        the look-back of the fused kernel, the staged rows of the value pass."""
         _lib.check(self._L.ins_cache_set_wait_test(self._h, poll_limit, item, chunk, head))
 
     def recomputed(self) -> int:

@@ -484,3 +484,32 @@ def test_a_lookback_wait_that_runs_out_is_reported_and_the_context_survives():
     pc.status()
     np.testing.assert_array_equal(_np(out), want)
     np.testing.assert_array_equal(_np(st), wst)
+
+
+def test_a_staged_row_wait_that_runs_out_is_reported_and_the_context_survives():
+    """With the separate launches (the default), the value pass waits, bounded,
+    for the bulk copies of each tile's V rows. Announcing one tile's copies 16
+    bytes larger than they are leaves its wait nothing to complete on: it
+    gives up after the lowered poll limit, the launch finishes, the status is
+    INS_ETIMEOUT (DeviceTimeout), and the next scan is exact again. Every copy
+    still lands; nothing faults."""
+    from insitu_b200._lib import DeviceTimeout
+    rng = np.random.default_rng(67)
+    T = 40000
+    pc = _pc(capacity=T)
+    k, v = _wire(rng, (T, 8, 64)), _wire(rng, (T, 8, 64))
+    pc.ingress(np.zeros(T, np.int32), k, v)
+    orc = make_oracle()
+    qr = orc.rotate(_wire(rng, (1, 32, 64), 1.0 / 8.0))
+    q_rot = torch.from_numpy(qr.astype(np.int32))
+    want, wst = orc.decode_layer(qr, [orc.ingress_rows(k, v, threads=8)], threads=8)
+    pc.set_scan_kernel("split")
+    pc.set_wait_test(poll_limit=64, item=3, chunk=5, head=0)
+    pc.scan([0], q_rot)
+    with pytest.raises(DeviceTimeout):
+        pc.status()
+    pc.set_wait_test()
+    out, st = pc.scan([0], q_rot)
+    pc.status()
+    np.testing.assert_array_equal(_np(out), want)
+    np.testing.assert_array_equal(_np(st), wst)
