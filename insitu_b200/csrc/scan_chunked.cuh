@@ -629,23 +629,42 @@ __device__ void stage_entries(const ChunkArgs &a, const int (*cnt)[NR], const in
         if (lane == 0) st.ex[w][NR] = before;
     }
     __syncthreads();
-    // only the staged entries, head after head, their loads issued together
-    int off = 0;
+    // only the staged entries, all heads in one index space, eight loads a
+    // thread issued before any is stored
+    int start[H + 1];
+    start[0] = 0;
 #pragma unroll
-    for (int h = 0; h < H; ++h) {
-        const int nk = min(st.ex[h][NR], ECAP);
-        const int end = off + nk * D;
-#pragma unroll 4
-        for (int i = off + (int)threadIdx.x; i < end; i += blockDim.x) {
-            const int k = (i - off) / D, ch = (i - off) % D;
-            const SegEntry &se = a.segs[st.idx[h * ECAP + k]];
-            eS[((size_t)h * ECAP + k) * D + ch] = ldcg(&se.S[ch]);
-            if (ch == 0) {
-                st.f[h * ECAP + k] = ldcg(&se.f);
-                st.l[h * ECAP + k] = ldcg(&se.l);
+    for (int h = 0; h < H; ++h) start[h + 1] = start[h] + min(st.ex[h][NR], ECAP) * D;
+    const int tot = start[H];
+    constexpr int U = 8;
+    for (int base = (int)threadIdx.x; base < tot; base += U * (int)blockDim.x) {
+        long long v[U];
+        int dst[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int i = base + u * (int)blockDim.x;
+            dst[u] = -1;
+            if (i < tot) {
+                int h = 0, s0 = 0;
+#pragma unroll
+                for (int hh = 1; hh < H; ++hh)
+                    if (i >= start[hh]) {
+                        h = hh;
+                        s0 = start[hh];
+                    }
+                const int k = (i - s0) / D, ch = (i - s0) % D;
+                const SegEntry &se = a.segs[st.idx[h * ECAP + k]];
+                v[u] = ldcg(&se.S[ch]);
+                dst[u] = (h * ECAP + k) * D + ch;
+                if (ch == 0) {
+                    st.f[h * ECAP + k] = ldcg(&se.f);
+                    st.l[h * ECAP + k] = ldcg(&se.l);
+                }
             }
         }
-        off = end;
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (dst[u] >= 0) eS[dst[u]] = v[u];
     }
     __syncthreads();
 }
@@ -785,12 +804,26 @@ __device__ void merge_block(const ChunkArgs &a, int item, int blk, int nchunks, 
         // S0 of every tile, 16 bytes a load: [tile][head][channel]
         {
             constexpr int Q = D / 4;                   // 16-byte pieces per (tile, head)
+            constexpr int U = 8;                       // loads a thread issues before it stores
             const int n16 = nt * H * Q;
-#pragma unroll 4
-            for (int i = threadIdx.x; i < n16; i += blockDim.x) {
-                const int u = i / (H * Q), r = i % (H * Q), h = r / Q, q = r % Q;
-                const int4 x = ldcg(reinterpret_cast<const int4 *>(&recs[c0 + u].S0[h][0]) + q);
-                reinterpret_cast<int4 *>(s0_sm + ((size_t)u * H + h) * D)[q] = x;
+            for (int base = (int)threadIdx.x; base < n16; base += U * (int)blockDim.x) {
+                int4 x[U];
+#pragma unroll
+                for (int j = 0; j < U; ++j) {
+                    const int i = base + j * (int)blockDim.x;
+                    if (i < n16) {
+                        const int u = i / (H * Q), r = i % (H * Q), h = r / Q, q = r % Q;
+                        x[j] = ldcg(reinterpret_cast<const int4 *>(&recs[c0 + u].S0[h][0]) + q);
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < U; ++j) {
+                    const int i = base + j * (int)blockDim.x;
+                    if (i < n16) {
+                        const int u = i / (H * Q), r = i % (H * Q), h = r / Q, q = r % Q;
+                        reinterpret_cast<int4 *>(s0_sm + ((size_t)u * H + h) * D)[q] = x[j];
+                    }
+                }
             }
         }
         __syncthreads();
