@@ -69,6 +69,14 @@ __host__ __device__ inline int64_t nplane_off(const Geo &g) {
 // launched the ordinary way).
 __device__ __forceinline__ void wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// Lets the launch after this one (if launched with programmatic stream
+// serialization) be scheduled once every CTA of this grid has called this
+// or exited; that launch still waits (wait_prior_grid) before it reads what
+// this one writes.
+__device__ __forceinline__ void release_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Launches `kernel` so that it may start while the previous kernel on the
 // stream finishes (programmatic stream serialization); the kernel calls
 // wait_prior_grid() before it reads that kernel's results.

@@ -1549,6 +1549,9 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_scores(ChunkArgs a) {
 
     for (int li = 0; li < ntl; ++li) {
         const int tile = (int)blockIdx.x + li * G;
+        // the value launch may take SM slots from here on (it waits for this
+        // launch to finish before it reads the scores)
+        if (li == ntl - 1) release_dependents();
         if (li > 0) tile_max_out(li - 1, prev_td);
         // buffer (li + 1) & 1 was released by the barrier that ended tile li - 1
         if (li + 1 < ntl) issue(li + 1);
@@ -1955,6 +1958,7 @@ __global__ void __launch_bounds__(CHUNK_THREADS, 2) k_scan_values(ChunkArgs a) {
     int lost_at = -1;                             // the tile whose wait gave up
     for (int li = 0; li < ntl; ++li) {
         const int tile = (int)blockIdx.x + li * G;
+        if (li == ntl - 1) release_dependents();      // the fold launch may take SM slots
         const int4 td = tdesc_sm[li % 3];
         const int item = td.x, c = td.y;
         const int64_t t0 = td.z;
